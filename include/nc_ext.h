@@ -1,0 +1,52 @@
+/*
+ * nc_ext.h — side API of the B200 newch engine.
+ *
+ * These entry points have no counterpart in newch's engine/include/nc.h, whose ABI stays frozen.
+ * They sit where newch plans its optional engine/src/ext/ module (newch CLAUDE.md:83-85): device
+ * facts, data-parallel set-up (NCCL over NVLink/NVSwitch) and counters for benchmarks. A newch
+ * user needs none of them: data parallelism can also be switched on purely through the
+ * environment (NC_RANK, NC_WORLD_SIZE, NC_NCCL_ID_FILE), read by nc_init.
+ */
+#ifndef NC_EXT_H
+#define NC_EXT_H
+
+#include "nc.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Number of visible CUDA devices (0 when there is none or the driver is missing). */
+NC_API int nc_ext_device_count(void);
+/* Name of the context's device, e.g. "NVIDIA B200". */
+NC_API const char *nc_ext_device_name(const nc_ctx *ctx);
+/* Waits for all work enqueued by the context; returns its status code (kernel-found errors become
+ * NC_ERR_ARG, CUDA failures NC_ERR_STATE). */
+NC_API int nc_ext_synchronize(nc_ctx *ctx);
+/* Kernels this context has enqueued since nc_init. */
+NC_API int64_t nc_ext_launch_count(const nc_ctx *ctx);
+/* "ffma", "tf32" or "3xtf32": how fp32 GEMMs run (NC_GEMM env; force_reference forces "ffma"). */
+NC_API const char *nc_ext_gemm_mode(const nc_ctx *ctx);
+
+/* Writes an NCCL unique id (bytes) into buf; returns its length or -1. Rank 0 calls it and sends
+ * the bytes to the other ranks by any host channel. */
+NC_API int nc_ext_nccl_unique_id(void *buf, int cap);
+/* Joins the context to a data-parallel group of `world` ranks. After this, nc_optim_step averages
+ * the gradients of all ranks (one all-reduce of the flat gradient buffer) before updating.
+ * Returns NC_OK or an error status. */
+NC_API int nc_ext_dp_init(nc_ctx *ctx, int rank, int world, const void *id, int id_len);
+NC_API int nc_ext_dp_world(const nc_ctx *ctx);
+
+/* The cudaStream_t every kernel of this context runs on. */
+NC_API void *nc_ext_stream(nc_ctx *ctx);
+/* Per-kernel timing with CUDA events on the context's stream (costs a little per launch). */
+NC_API int nc_ext_timing(nc_ctx *ctx, int on);
+/* Sum of device milliseconds and the number of timed launches of kernels whose name starts with
+ * `prefix` ("" = all) since timing was switched on. */
+NC_API int nc_ext_kernel_time(nc_ctx *ctx, const char *prefix, double *ms, int64_t *count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NC_EXT_H */

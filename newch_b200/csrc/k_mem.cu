@@ -1,0 +1,296 @@
+// Memory kernels: fills, axpy, strided gather / accumulate, dtype conversion, and the per-kernel
+// CUDA-event timer used by the benchmark.
+#include <math.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "k_common.cuh"
+
+using namespace nck;
+
+// ---- timer -------------------------------------------------------------------------------------
+
+struct nck_timer {
+    struct Rec {
+        int name;
+        cudaEvent_t a, b;
+    };
+    std::vector<std::string> names;
+    std::vector<Rec> recs;
+    std::vector<cudaEvent_t> pool;
+    int open = -1;
+    double ms_done = 0;
+    std::vector<double> ms_by_name;
+    std::vector<int64_t> n_by_name;
+};
+
+static cudaEvent_t take_event(nck_timer *t) {
+    if (!t->pool.empty()) {
+        cudaEvent_t e = t->pool.back();
+        t->pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+}
+
+extern "C" void nck_timer_enable(nck_dev *d, int on) {
+    if (on && !d->timer) {
+        d->timer = new nck_timer();
+    } else if (!on && d->timer) {
+        nck_timer *t = d->timer;
+        for (auto &r : t->recs) {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+        for (auto e : t->pool) cudaEventDestroy(e);
+        delete t;
+        d->timer = nullptr;
+    }
+}
+
+extern "C" void nck_timer_begin(nck_dev *d, const char *name) {
+    nck_timer *t = d->timer;
+    if (!t || t->open >= 0) return;  // nested scopes: the outer one times them all
+    int id = -1;
+    for (size_t i = 0; i < t->names.size(); i++)
+        if (t->names[i] == name) id = (int)i;
+    if (id < 0) {
+        t->names.push_back(name);
+        t->ms_by_name.push_back(0);
+        t->n_by_name.push_back(0);
+        id = (int)t->names.size() - 1;
+    }
+    nck_timer::Rec r{id, take_event(t), take_event(t)};
+    cudaEventRecord(r.a, NCK_STREAM(d));
+    t->recs.push_back(r);
+    t->open = (int)t->recs.size() - 1;
+}
+
+extern "C" void nck_timer_end(nck_dev *d) {
+    nck_timer *t = d->timer;
+    if (!t || t->open < 0) return;
+    cudaEventRecord(t->recs[t->open].b, NCK_STREAM(d));
+    t->open = -1;
+}
+
+static void settle(nck_timer *t) {
+    for (auto &r : t->recs) {
+        float ms = 0;
+        cudaEventSynchronize(r.b);
+        cudaEventElapsedTime(&ms, r.a, r.b);
+        t->ms_by_name[r.name] += ms;
+        t->n_by_name[r.name] += 1;
+        t->pool.push_back(r.a);
+        t->pool.push_back(r.b);
+    }
+    t->recs.clear();
+}
+
+extern "C" int nck_timer_query(nck_dev *d, const char *prefix, double *ms, int64_t *count) {
+    nck_timer *t = d->timer;
+    *ms = 0;
+    *count = 0;
+    if (!t) return 5;
+    settle(t);
+    size_t lp = strlen(prefix);
+    for (size_t i = 0; i < t->names.size(); i++) {
+        if (strncmp(t->names[i].c_str(), prefix, lp) != 0) continue;
+        *ms += t->ms_by_name[i];
+        *count += t->n_by_name[i];
+    }
+    return 0;
+}
+
+extern "C" void nck_timer_reset(nck_dev *d) {
+    nck_timer *t = d->timer;
+    if (!t) return;
+    settle(t);
+    for (auto &v : t->ms_by_name) v = 0;
+    for (auto &v : t->n_by_name) v = 0;
+}
+
+// ---- fills -------------------------------------------------------------------------------------
+
+template <typename T>
+__global__ void k_fill(T *__restrict__ y, T v, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = v;
+}
+
+extern "C" void nck_fill_f32(nck_dev *d, float *y, float v, int64_t n) {
+    if (n <= 0) return;
+    Scope s(d, "fill");
+    k_fill<float><<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(y, v, n);
+    NCK_LAUNCHED(d, 1);
+}
+
+extern "C" void nck_fill_i32(nck_dev *d, int32_t *y, int32_t v, int64_t n) {
+    if (n <= 0) return;
+    Scope s(d, "fill");
+    k_fill<int32_t><<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(y, v, n);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_add_scalar_inplace(float *y, float v) { y[0] += v; }
+
+extern "C" void nck_add_scalar_inplace(nck_dev *d, float *y, float v) {
+    k_add_scalar_inplace<<<1, 1, 0, NCK_STREAM(d)>>>(y, v);
+    NCK_LAUNCHED(d, 1);
+}
+
+// y += a * x, float4 body when both pointers are 16-byte aligned
+__global__ void k_axpy(int64_t n, float a, const float *__restrict__ x, float *__restrict__ y, int vec) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (vec) {
+        int64_t n4 = n >> 2;
+        const float4 *x4 = (const float4 *)x;
+        float4 *y4 = (float4 *)y;
+        for (int64_t i = t; i < n4; i += stride) {
+            float4 xv = x4[i], yv = y4[i];
+            yv.x += a * xv.x, yv.y += a * xv.y, yv.z += a * xv.z, yv.w += a * xv.w;
+            y4[i] = yv;
+        }
+        for (int64_t i = (n4 << 2) + t; i < n; i += stride) y[i] += a * x[i];
+    } else {
+        for (int64_t i = t; i < n; i += stride) y[i] += a * x[i];
+    }
+}
+
+extern "C" void nck_axpy(nck_dev *d, int64_t n, float a, const float *x, float *y) {
+    if (n <= 0) return;
+    Scope s(d, "axpy");
+    int vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+    k_axpy<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(n, a, x, y, vec);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- strided copies ------------------------------------------------------------------------------
+
+struct Strided {
+    int nd;
+    int64_t shape[NCK_MAXD];
+    int64_t stride[NCK_MAXD];
+};
+
+// element offset of linear (row-major) index i in a strided view
+__device__ __forceinline__ int64_t strided_offset(const Strided &v, int64_t i) {
+    int64_t off = 0;
+    for (int k = v.nd - 1; k >= 0; k--) {
+        int64_t q = i / v.shape[k];
+        off += (i - q * v.shape[k]) * v.stride[k];
+        i = q;
+    }
+    return off;
+}
+
+template <typename T>
+__global__ void k_copy_strided(Strided v, const T *__restrict__ src, T *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[strided_offset(v, i)];
+}
+
+// merges dims that are laid out back to back (fewer divisions per element)
+static Strided simplify(int ndim, const int64_t *shape, const int64_t *stride) {
+    Strided v;
+    v.nd = 0;
+    for (int k = 0; k < ndim; k++) {
+        if (shape[k] == 1) continue;
+        if (v.nd > 0 && v.stride[v.nd - 1] == stride[k] * shape[k]) {
+            v.shape[v.nd - 1] *= shape[k];
+            v.stride[v.nd - 1] = stride[k];
+            continue;
+        }
+        v.shape[v.nd] = shape[k];
+        v.stride[v.nd] = stride[k];
+        v.nd++;
+    }
+    if (v.nd == 0) {
+        v.nd = 1;
+        v.shape[0] = 1;
+        v.stride[0] = 1;
+    }
+    return v;
+}
+
+extern "C" void nck_copy_strided(nck_dev *d, int es, int ndim, const int64_t *shape, const int64_t *stride,
+                                 const void *src, void *dst) {
+    int64_t n = 1;
+    for (int k = 0; k < ndim; k++) n *= shape[k];
+    if (n <= 0) return;
+    Strided v = simplify(ndim, shape, stride);
+    Scope s(d, "copy_strided");
+    cudaStream_t st = NCK_STREAM(d);
+    if (v.nd == 1 && v.stride[0] == 1) {
+        cudaMemcpyAsync(dst, src, (size_t)n * es, cudaMemcpyDeviceToDevice, st);
+        return;
+    }
+    int g = grid_for(d, n);
+    if (es == 4) k_copy_strided<int32_t><<<g, kThreads, 0, st>>>(v, (const int32_t *)src, (int32_t *)dst, n);
+    else if (es == 2) k_copy_strided<int16_t><<<g, kThreads, 0, st>>>(v, (const int16_t *)src, (int16_t *)dst, n);
+    else k_copy_strided<int8_t><<<g, kThreads, 0, st>>>(v, (const int8_t *)src, (int8_t *)dst, n);
+    NCK_LAUNCHED(d, 1);
+}
+
+// dst[view(i)] += src[i]. Every destination element is hit at most once (views of a permutation or
+// a slice), so there is no write conflict.
+__global__ void k_acc_strided(Strided v, const float *__restrict__ src, float *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[strided_offset(v, i)] += src[i];
+}
+
+extern "C" void nck_acc_strided(nck_dev *d, int ndim, const int64_t *shape, const int64_t *dst_stride,
+                                const float *src, float *dst) {
+    int64_t n = 1;
+    for (int k = 0; k < ndim; k++) n *= shape[k];
+    if (n <= 0) return;
+    Strided v = simplify(ndim, shape, dst_stride);
+    Scope s(d, "acc_strided");
+    if (v.nd == 1 && v.stride[0] == 1) {
+        nck_axpy(d, n, 1.0f, src, dst);
+        return;
+    }
+    k_acc_strided<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(v, src, dst, n);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- dtype conversion (newch ops_shape.c:463-504: truncation toward zero, saturation, NaN -> 0) -------
+
+__device__ __forceinline__ double load_as_double(const void *p, int dt, int64_t i) {
+    switch (dt) {
+    case 0: return (double)((const float *)p)[i];
+    case 1: return (double)((const int32_t *)p)[i];
+    case 3: return (double)((const int8_t *)p)[i];
+    default: return (double)((const uint8_t *)p)[i];
+    }
+}
+
+__device__ __forceinline__ double saturate(double v, double lo, double hi) {
+    if (v != v) return 0.0;
+    return v < lo ? lo : v > hi ? hi : v;
+}
+
+__global__ void k_convert(int from, int to, const void *__restrict__ src, void *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        double v = load_as_double(src, from, i);
+        if (to == 0) ((float *)dst)[i] = (float)v;
+        else if (to == 1) ((int32_t *)dst)[i] = (int32_t)saturate(v, -2147483648.0, 2147483647.0);
+        else if (to == 3) ((int8_t *)dst)[i] = (int8_t)saturate(v, -128.0, 127.0);
+        else ((uint8_t *)dst)[i] = (uint8_t)saturate(v, 0.0, 255.0);
+    }
+}
+
+extern "C" void nck_convert(nck_dev *d, int from, int to, const void *src, void *dst, int64_t n) {
+    if (n <= 0) return;
+    Scope s(d, "convert");
+    if (from == to) {
+        size_t es = (from == 0 || from == 1) ? 4 : 1;
+        cudaMemcpyAsync(dst, src, (size_t)n * es, cudaMemcpyDeviceToDevice, NCK_STREAM(d));
+        return;
+    }
+    k_convert<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(from, to, src, dst, n);
+    NCK_LAUNCHED(d, 1);
+}

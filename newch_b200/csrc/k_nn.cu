@@ -1,0 +1,645 @@
+// NN kernels: softmax / log-softmax rows, cross entropy, NLL, dropout on the engine's xoshiro256**
+// stream, batch norm, layer norm.
+//
+// Arithmetic follows newch engine/src/ops/ops_nn.c (softmax_row :22-35, cross entropy :107-149,
+// dropout :182-204, batch norm :262-349, NLL :387-416, layer norm :463-522), including its double
+// accumulators; this file is compiled without FMA contraction so the float expressions round as
+// newch's C loops do. Reductions run as fixed-shape trees and splits combined in a fixed order.
+#include <math.h>
+
+#include "k_common.cuh"
+
+using namespace nck;
+
+__device__ __forceinline__ float warp_max(float v) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---- softmax rows: one warp per row --------------------------------------------------------------------
+
+// row maximum the way newch scans it (first element, then strictly greater): NaN rows stay NaN-free
+// only if newch's are; for finite rows every order gives the same maximum
+__device__ __forceinline__ float row_max(const float *p, int64_t C, int lane) {
+    float m = -INFINITY;
+    for (int64_t c = lane; c < C; c += 32) m = fmaxf(m, p[c]);
+    return warp_max(m);
+}
+
+__global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t C, int logf_) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < rows; r += nw) {
+        const float *p = x + r * C;
+        float *q = y + r * C;
+        float m = row_max(p, C, lane);
+        float s = 0.0f;
+        for (int64_t c = lane; c < C; c += 32) s += expf(p[c] - m);
+        s = warp_sum(s);
+        if (logf_) {
+            float ls = logf(s);
+            for (int64_t c = lane; c < C; c += 32) q[c] = p[c] - m - ls;
+        } else {
+            float inv = 1.0f / s;
+            for (int64_t c = lane; c < C; c += 32) q[c] = inv * expf(p[c] - m);
+        }
+    }
+}
+
+extern "C" void nck_softmax_fwd(nck_dev *d, const float *x, float *y, int64_t rows, int64_t C, int log_form) {
+    Scope sc(d, log_form ? "log_softmax" : "softmax");
+    k_softmax_fwd<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, rows, C, log_form);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restrict__ g, float *__restrict__ gi,
+                              int64_t rows, int64_t C, int logf_) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < rows; r += nw) {
+        const float *yr = y + r * C, *gr = g + r * C;
+        float *o = gi + r * C;
+        float acc = 0.0f;
+        if (logf_) {
+            for (int64_t c = lane; c < C; c += 32) acc += gr[c];
+            acc = warp_sum(acc);
+            for (int64_t c = lane; c < C; c += 32) o[c] += gr[c] - expf(yr[c]) * acc;
+        } else {
+            for (int64_t c = lane; c < C; c += 32) acc += gr[c] * yr[c];
+            acc = warp_sum(acc);
+            for (int64_t c = lane; c < C; c += 32) o[c] += yr[c] * (gr[c] - acc);
+        }
+    }
+}
+
+extern "C" void nck_softmax_bwd(nck_dev *d, const float *y, const float *g, float *gi, int64_t rows, int64_t C,
+                                int log_form) {
+    Scope sc(d, log_form ? "log_softmax_bwd" : "softmax_bwd");
+    k_softmax_bwd<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(y, g, gi, rows, C, log_form);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- losses ----------------------------------------------------------------------------------------------
+
+// sum of n per-row terms in double (fixed tree), negated and divided: out = -sum / div (div 0 = NaN mean)
+__global__ void k_loss_combine(const float *__restrict__ terms, int64_t n, float *out, int mean) {
+    __shared__ double sm[kThreads / 32];
+    double acc = 0.0;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) acc += (double)terms[i];
+    acc = warp_sum_d(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int k = 0; k < kThreads / 32; k++) s += sm[k];
+        double loss = -s;
+        *out = mean ? (n ? (float)(loss / (double)n) : NAN) : (float)loss;
+    }
+}
+
+__device__ __forceinline__ int32_t checked_label(const int32_t *lab, int64_t i, int64_t C, int *status) {
+    int32_t l = lab[i];
+    if (l < 0 || l >= C) {
+        report(status, NCK_ERR_LABEL);
+        return 0;
+    }
+    return l;
+}
+
+__global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict__ lab, float *__restrict__ prob,
+                          float *__restrict__ terms, int64_t N, int64_t C, int *status) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < N; r += nw) {
+        const float *p = x + r * C;
+        float *q = prob + r * C;
+        float m = row_max(p, C, lane);
+        float s = 0.0f;
+        for (int64_t c = lane; c < C; c += 32) s += expf(p[c] - m);
+        float ls = logf(warp_sum(s));
+        int32_t l = checked_label(lab, r, C, status);
+        for (int64_t c = lane; c < C; c += 32) {
+            float lp = p[c] - m - ls;
+            if (c == l) terms[r] = lp;
+            q[c] = expf(lp);
+        }
+    }
+}
+
+extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t *lab, float *prob, float *loss,
+                                      int64_t N, int64_t C) {
+    Scope sc(d, "cross_entropy");
+    float *terms = (float *)d->scratch;
+    if (N > 0) k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status);
+    k_loss_combine<<<1, kThreads, 0, NCK_STREAM(d)>>>(terms, N, loss, 1);
+    NCK_LAUNCHED(d, 2);
+}
+
+__global__ void k_ce_bwd(const float *__restrict__ prob, const int32_t *__restrict__ lab,
+                         const float *__restrict__ gloss, float *__restrict__ gi, int64_t N, int64_t C) {
+    float s = gloss[0] / (float)(N ? N : 1);
+    int64_t n = N * C;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = t / C, c = t - i * C;
+        float v = gi[t] + s * prob[t];
+        int32_t l = lab[i];
+        if (c == l) v -= s;
+        gi[t] = v;
+    }
+}
+
+extern "C" void nck_cross_entropy_bwd(nck_dev *d, const float *prob, const int32_t *lab, const float *gloss, float *gi,
+                                      int64_t N, int64_t C) {
+    if (N * C <= 0) return;
+    Scope sc(d, "cross_entropy_bwd");
+    k_ce_bwd<<<grid_for(d, N * C), kThreads, 0, NCK_STREAM(d)>>>(prob, lab, gloss, gi, N, C);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_nll_terms(const float *__restrict__ x, const int32_t *__restrict__ lab, float *__restrict__ terms,
+                            int64_t N, int64_t C, int *status) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < N; i += (int64_t)gridDim.x * blockDim.x)
+        terms[i] = x[i * C + checked_label(lab, i, C, status)];
+}
+
+extern "C" void nck_nll_fwd(nck_dev *d, const float *x, const int32_t *lab, float *loss, int64_t N, int64_t C,
+                            int sum) {
+    Scope sc(d, "nll_loss");
+    float *terms = (float *)d->scratch;
+    if (N > 0) k_nll_terms<<<grid_for(d, N), kThreads, 0, NCK_STREAM(d)>>>(x, lab, terms, N, C, d->status);
+    k_loss_combine<<<1, kThreads, 0, NCK_STREAM(d)>>>(terms, N, loss, !sum);
+    NCK_LAUNCHED(d, 2);
+}
+
+__global__ void k_nll_bwd(const int32_t *__restrict__ lab, const float *__restrict__ gloss, float *__restrict__ gi,
+                          int64_t N, int64_t C, int sum) {
+    float g = gloss[0];
+    float s = sum ? g : g / (float)(N ? N : 1);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < N; i += (int64_t)gridDim.x * blockDim.x)
+        gi[i * C + lab[i]] -= s;
+}
+
+extern "C" void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, int64_t N, int64_t C,
+                            int sum) {
+    if (N <= 0) return;
+    Scope sc(d, "nll_loss_bwd");
+    k_nll_bwd<<<grid_for(d, N), kThreads, 0, NCK_STREAM(d)>>>(lab, gloss, gi, N, C, sum);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- dropout on the xoshiro256** stream ------------------------------------------------------------------
+//
+// Block b owns draws [b * 16384, (b + 1) * 16384); its thread t owns the 64 draws starting at
+// t * 64 inside that. Jump tables (uploaded once): tab[k] = T^(2^(6 + k)) for k < 36, T the 256x256
+// GF(2) transition matrix of xoshiro256**, stored by column (image of each state bit).
+//   block base  = prod over set bits k of b   of T^(16384 * 2^k) = tab[8 + k]
+//   thread start = doubling prefix over the block: state[t] = T^(64 * 2^r) state[t - 2^r] = tab[r]
+
+constexpr int kDropDraws = 64;                      // draws per thread
+constexpr int kDropThreads = 256;                   // threads per block
+constexpr int kDropBlock = kDropDraws * kDropThreads;  // 16384 draws per block
+constexpr int kRngTables = 36;
+
+__device__ ulonglong4 *g_rng_tab;  // device copy of the jump matrices (kRngTables x 256 columns)
+
+// once per device and process: the tables never change
+extern "C" int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes) {
+    static int done[128];
+    if (bytes != (size_t)kRngTables * 256 * 32 || d->device < 0 || d->device >= 128) return 1;
+    if (done[d->device]) return 0;
+    void *dev = nullptr;
+    if (cudaMalloc(&dev, bytes) != cudaSuccess) return 1;
+    if (cudaMemcpy(dev, tables, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return 1;
+    if (cudaMemcpyToSymbol(g_rng_tab, &dev, sizeof dev) != cudaSuccess) return 1;
+    done[d->device] = 1;
+    return 0;
+}
+
+// out = M v for a 256x256 bit matrix by columns: each lane XORs 8 columns, the warp XOR-reduces.
+// Every lane returns the full product.
+__device__ __forceinline__ ulonglong4 warp_matvec(const ulonglong4 *__restrict__ M, const ulonglong4 &v, int lane) {
+    int w = lane >> 3;
+    unsigned long long word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+    unsigned byte = (unsigned)(word >> ((lane & 7) * 8)) & 0xffu;
+    ulonglong4 acc = make_ulonglong4(0, 0, 0, 0);
+    for (int i = 0; i < 8; i++) {
+        if ((byte >> i) & 1u) {
+            ulonglong4 c = M[lane * 8 + i];
+            acc.x ^= c.x, acc.y ^= c.y, acc.z ^= c.z, acc.w ^= c.w;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        acc.x ^= __shfl_xor_sync(0xffffffffu, acc.x, o);
+        acc.y ^= __shfl_xor_sync(0xffffffffu, acc.y, o);
+        acc.z ^= __shfl_xor_sync(0xffffffffu, acc.z, o);
+        acc.w ^= __shfl_xor_sync(0xffffffffu, acc.w, o);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ unsigned long long rotl64(unsigned long long x, int k) { return (x << k) | (x >> (64 - k)); }
+
+__global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
+                                                              float *__restrict__ y, uint32_t *__restrict__ bits,
+                                                              int64_t n, float p) {
+    __shared__ ulonglong4 st[kDropThreads];
+    __shared__ uint32_t mb[kDropBlock / 32];
+    const ulonglong4 *tab = g_rng_tab;
+    int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (warp == 0) {
+        ulonglong4 v = s0;
+        unsigned long long b = blockIdx.x;
+        for (int k = 0; b; k++, b >>= 1)
+            if (b & 1) v = warp_matvec(tab + (size_t)(8 + k) * 256, v, lane);
+        if (lane == 0) st[0] = v;
+    }
+    __syncthreads();
+    for (int r = 0; r < 8; r++) {
+        int cnt = 1 << r;
+        for (int t = cnt + warp; t < 2 * cnt; t += kDropThreads / 32) {
+            ulonglong4 v = warp_matvec(tab + (size_t)r * 256, st[t - cnt], lane);
+            if (lane == 0) st[t] = v;
+        }
+        __syncthreads();
+    }
+    // 64 draws: uniform u = (r >> 40) * 2^-24 (exact), kept when u >= p
+    unsigned long long s[4] = {st[tid].x, st[tid].y, st[tid].z, st[tid].w};
+    uint32_t w0 = 0, w1 = 0;
+    for (int i = 0; i < kDropDraws; i++) {
+        unsigned long long r = rotl64(s[1] * 5ull, 7) * 9ull;
+        unsigned long long t = s[1] << 17;
+        s[2] ^= s[0];
+        s[3] ^= s[1];
+        s[1] ^= s[2];
+        s[0] ^= s[3];
+        s[2] ^= t;
+        s[3] = rotl64(s[3], 45);
+        float u = (float)(r >> 40) * (1.0f / 16777216.0f);
+        uint32_t keep = u >= p ? 1u : 0u;
+        if (i < 32) w0 |= keep << i;
+        else w1 |= keep << (i - 32);
+    }
+    mb[2 * tid] = w0;
+    mb[2 * tid + 1] = w1;
+    __syncthreads();
+    float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+    int64_t base = (int64_t)blockIdx.x * kDropBlock;
+    for (int j = tid; j < kDropBlock; j += kDropThreads) {
+        int64_t e = base + j;
+        if (e < n) {
+            float m = (mb[j >> 5] >> (j & 31)) & 1u ? keepv : 0.0f;
+            y[e] = x[e] * m;
+        }
+    }
+    int64_t words = (n + 31) / 32;
+    for (int w = tid; w < kDropBlock / 32; w += kDropThreads) {
+        int64_t gw = (int64_t)blockIdx.x * (kDropBlock / 32) + w;
+        if (gw < words) bits[gw] = mb[w];
+    }
+}
+
+extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits,
+                                int64_t n, float p) {
+    if (n <= 0) return;
+    Scope sc(d, "dropout");
+    ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
+    int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
+    k_dropout_fwd<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(s0, x, y, bits, n, p);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_dropout_bwd(const float *__restrict__ g, const uint32_t *__restrict__ bits, float *__restrict__ gi,
+                              int64_t n, float p) {
+    float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float m = (bits[i >> 5] >> (i & 31)) & 1u ? keepv : 0.0f;
+        gi[i] += g[i] * m;
+    }
+}
+
+extern "C" void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p) {
+    if (n <= 0) return;
+    Scope sc(d, "dropout_bwd");
+    k_dropout_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, bits, gi, n, p);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- batch norm over x [N, C, S] -----------------------------------------------------------------------
+//
+// Per-channel statistics: grid (C, splits); each block sums its samples' planes in double, a
+// finalize kernel combines the splits in order. Variance from the double sums of x and x^2.
+
+__device__ __forceinline__ void block_sum2(double &a, double &b, double *sm) {
+    a = warp_sum_d(a);
+    b = warp_sum_d(b);
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) sm[w] = a, sm[32 + w] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0, t = 0;
+        for (int k = 0; k < nw; k++) s += sm[k], t += sm[32 + k];
+        a = s, b = t;
+    }
+}
+
+__global__ void k_bn_stats(const float *__restrict__ x, double *__restrict__ part, int64_t N, int64_t C, int64_t S,
+                           int64_t per_split) {
+    __shared__ double sm[64];
+    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    double s = 0.0, ss = 0.0;
+    for (int64_t n = n0; n < n1; n++) {
+        const float *p = x + (n * C + c) * S;
+        for (int64_t j = threadIdx.x; j < S; j += blockDim.x) {
+            double v = (double)p[j];
+            s += v;
+            ss += v * v;
+        }
+    }
+    block_sum2(s, ss, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = s;
+        part[(blockIdx.y * C + c) * 2 + 1] = ss;
+    }
+}
+
+__global__ void k_bn_finalize(const double *__restrict__ part, int splits, int64_t C, int64_t M, float *mean,
+                              float *invstd, float *rm, float *rv, float mom, float eps) {
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
+        double s = 0.0, ss = 0.0;
+        for (int k = 0; k < splits; k++) s += part[(k * C + c) * 2], ss += part[(k * C + c) * 2 + 1];
+        double mu = s / (double)M;
+        double dev = ss - s * mu; /* sum of squared deviations */
+        if (dev < 0.0) dev = 0.0;
+        mean[c] = (float)mu;
+        invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)eps));
+        rm[c] = (1.0f - mom) * rm[c] + mom * (float)mu;
+        rv[c] = (1.0f - mom) * rv[c] + mom * (float)(dev / (double)(M - 1));
+    }
+}
+
+__global__ void k_bn_eval_stats(const float *__restrict__ rm, const float *__restrict__ rv, float *mean, float *invstd,
+                                int64_t C, float eps) {
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
+        mean[c] = rm[c];
+        invstd[c] = 1.0f / sqrtf(rv[c] + eps);
+    }
+}
+
+// y = x * a + d per channel, a = w * invstd, d = b - mean * a; one block row per (n, c) plane
+__global__ void k_bn_norm(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
+                          const float *__restrict__ mean, const float *__restrict__ invstd, float *__restrict__ y,
+                          int64_t NC, int64_t C, int64_t S) {
+    for (int64_t plane = blockIdx.x; plane < NC; plane += gridDim.x) {
+        int64_t c = plane % C;
+        float a = w[c] * invstd[c], dd = b[c] - mean[c] * a;
+        const float *p = x + plane * S;
+        float *q = y + plane * S;
+        if ((S & 3) == 0 && (((uintptr_t)p | (uintptr_t)q) & 15) == 0) {
+            for (int64_t j = threadIdx.x; j < S / 4; j += blockDim.x) {
+                float4 v = ((const float4 *)p)[j];
+                v.x = v.x * a + dd, v.y = v.y * a + dd, v.z = v.z * a + dd, v.w = v.w * a + dd;
+                ((float4 *)q)[j] = v;
+            }
+        } else {
+            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) q[j] = p[j] * a + dd;
+        }
+    }
+}
+
+static int64_t bn_splits(const nck_dev *d, int64_t N, int64_t C) {
+    int64_t want = ((int64_t)d->sm_count * 4 + C - 1) / C;
+    if (want < 1) want = 1;
+    return want > N ? N : want;
+}
+
+static int norm_threads(int64_t S) { return S >= 1024 ? 256 : S >= 256 ? 128 : 64; }
+
+extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
+                                 float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
+                                 float eps) {
+    Scope sc(d, "bn_fwd");
+    int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
+    splits = (N + per - 1) / per;
+    double *part = (double *)d->scratch;
+    dim3 g1((unsigned)C, (unsigned)splits);
+    k_bn_stats<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
+    k_bn_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, mean, invstd, rm, rv,
+                                                                   mom, eps);
+    int64_t planes = N * C;
+    int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
+    k_bn_norm<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    NCK_LAUNCHED(d, 3);
+}
+
+extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
+                                float *invstd, const float *rm, const float *rv, int64_t N, int64_t C, int64_t S,
+                                float eps) {
+    Scope sc(d, "bn_fwd");
+    k_bn_eval_stats<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(rm, rv, mean, invstd, C, eps);
+    int64_t planes = N * C;
+    if (planes > 0) {
+        int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
+        k_bn_norm<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    }
+    NCK_LAUNCHED(d, 2);
+}
+
+// backward sums per channel: sg = sum g, sgx = sum g * xhat (float products, double sums)
+__global__ void k_bn_bwd_sums(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ mean,
+                              const float *__restrict__ invstd, double *__restrict__ part, int64_t N, int64_t C,
+                              int64_t S, int64_t per_split) {
+    __shared__ double sm[64];
+    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    float mu = mean[c], is = invstd[c];
+    double sg = 0.0, sgx = 0.0;
+    for (int64_t n = n0; n < n1; n++) {
+        const float *p = x + (n * C + c) * S, *q = g + (n * C + c) * S;
+        for (int64_t j = threadIdx.x; j < S; j += blockDim.x) {
+            float gv = q[j];
+            sg += gv;
+            sgx += gv * (p[j] - mu) * is;
+        }
+    }
+    block_sum2(sg, sgx, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = sg;
+        part[(blockIdx.y * C + c) * 2 + 1] = sgx;
+    }
+}
+
+__global__ void k_bn_bwd_finalize(const double *__restrict__ part, int splits, int64_t C, int64_t M,
+                                  float *__restrict__ gw, float *__restrict__ gb, float *__restrict__ coef) {
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
+        double sg = 0.0, sgx = 0.0;
+        for (int k = 0; k < splits; k++) sg += part[(k * C + c) * 2], sgx += part[(k * C + c) * 2 + 1];
+        if (gw) gw[c] += (float)sgx;
+        if (gb) gb[c] += (float)sg;
+        coef[2 * c] = (float)(sg / (double)M);
+        coef[2 * c + 1] = (float)(sgx / (double)M);
+    }
+}
+
+__global__ void k_bn_bwd_dx(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ g,
+                            const float *__restrict__ mean, const float *__restrict__ invstd,
+                            const float *__restrict__ coef, float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
+                            int training) {
+    for (int64_t plane = blockIdx.x; plane < NC; plane += gridDim.x) {
+        int64_t c = plane % C;
+        float mu = mean[c], is = invstd[c], k = w[c] * is, mg = coef[2 * c], mgx = coef[2 * c + 1];
+        const float *p = x + plane * S, *q = g + plane * S;
+        float *o = gx + plane * S;
+        if (training)
+            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) o[j] += k * (q[j] - mg - (p[j] - mu) * is * mgx);
+        else
+            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) o[j] += k * q[j];
+    }
+}
+
+extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean,
+                           const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
+                           int training) {
+    Scope sc(d, "bn_bwd");
+    int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
+    splits = (N + per - 1) / per;
+    double *part = (double *)d->scratch;
+    float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
+    dim3 g1((unsigned)C, (unsigned)splits);
+    k_bn_bwd_sums<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
+    k_bn_bwd_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, gw, gb, coef);
+    int launched = 2;
+    if (gx) {
+        int64_t planes = N * C;
+        int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
+        k_bn_bwd_dx<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx, planes, C, S,
+                                                                    training);
+        launched++;
+    }
+    NCK_LAUNCHED(d, launched);
+}
+
+// ---- layer norm over rows of D: one warp per row -------------------------------------------------------
+
+__global__ void k_ln_fwd(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
+                         float *__restrict__ y, float *__restrict__ stats, int64_t R, int64_t D, float eps) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < R; r += nw) {
+        const float *p = x + r * D;
+        double s = 0.0;
+        for (int64_t i = lane; i < D; i += 32) s += (double)p[i];
+        s = warp_sum_d(s);
+        double mean = s / (double)D;
+        double ss = 0.0;
+        for (int64_t i = lane; i < D; i += 32) {
+            double dv = (double)p[i] - mean;
+            ss += dv * dv;
+        }
+        ss = warp_sum_d(ss);
+        float rstd = (float)(1.0 / sqrt(ss / (double)D + (double)eps));
+        float fm = (float)mean;
+        if (lane == 0) stats[2 * r] = fm, stats[2 * r + 1] = rstd;
+        float *q = y + r * D;
+        for (int64_t i = lane; i < D; i += 32) {
+            float v = (p[i] - fm) * rstd;
+            q[i] = (w ? v * w[i] : v) + (b ? b[i] : 0.0f);
+        }
+    }
+}
+
+extern "C" void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats,
+                           int64_t R, int64_t D, float eps) {
+    Scope sc(d, "ln_fwd");
+    k_ln_fwd<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, D, eps);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_ln_bwd_dx(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ g,
+                            const float *__restrict__ stats, float *__restrict__ gx, int64_t R, int64_t D) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < R; r += nw) {
+        const float *p = x + r * D, *q = g + r * D;
+        float mean = stats[2 * r], rstd = stats[2 * r + 1];
+        double sg = 0.0, sgx = 0.0;
+        for (int64_t i = lane; i < D; i += 32) {
+            float xhat = (p[i] - mean) * rstd, gi = w ? q[i] * w[i] : q[i];
+            sg += gi;
+            sgx += gi * xhat;
+        }
+        sg = warp_sum_d(sg);
+        sgx = warp_sum_d(sgx);
+        float mg = (float)(sg / (double)D), mgx = (float)(sgx / (double)D);
+        float *o = gx + r * D;
+        for (int64_t i = lane; i < D; i += 32) {
+            float xhat = (p[i] - mean) * rstd, gi = w ? q[i] * w[i] : q[i];
+            o[i] += rstd * (gi - mg - xhat * mgx);
+        }
+    }
+}
+
+// weight / bias grads: column sums over rows of g * xhat and g, split over row ranges
+__global__ void k_ln_bwd_wb(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ stats,
+                            float *__restrict__ part, int64_t R, int64_t D, int64_t rows_per) {
+    __shared__ float sw[8][33], sb[8][33];
+    int64_t i = blockIdx.x * 32 + threadIdx.x;
+    int64_t r0 = blockIdx.y * rows_per, r1 = r0 + rows_per < R ? r0 + rows_per : R;
+    float aw = 0.0f, ab = 0.0f;
+    if (i < D)
+        for (int64_t r = r0 + threadIdx.y; r < r1; r += 8) {
+            float gv = g[r * D + i];
+            aw += gv * ((x[r * D + i] - stats[2 * r]) * stats[2 * r + 1]);
+            ab += gv;
+        }
+    sw[threadIdx.y][threadIdx.x] = aw;
+    sb[threadIdx.y][threadIdx.x] = ab;
+    __syncthreads();
+    if (threadIdx.y == 0 && i < D) {
+        float a = 0.0f, b = 0.0f;
+        for (int k = 0; k < 8; k++) a += sw[k][threadIdx.x], b += sb[k][threadIdx.x];
+        part[(blockIdx.y * 2) * D + i] = a;
+        part[(blockIdx.y * 2 + 1) * D + i] = b;
+    }
+}
+
+__global__ void k_ln_bwd_wb_combine(const float *__restrict__ part, int splits, int64_t D, float *gw, float *gb) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < D; i += (int64_t)gridDim.x * blockDim.x) {
+        float a = 0.0f, b = 0.0f;
+        for (int k = 0; k < splits; k++) a += part[(2 * k) * D + i], b += part[(2 * k + 1) * D + i];
+        if (gw) gw[i] += a;
+        if (gb) gb[i] += b;
+    }
+}
+
+extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
+                           float *gw, float *gb, int64_t R, int64_t D) {
+    Scope sc(d, "ln_bwd");
+    int launched = 0;
+    if (gx) {
+        k_ln_bwd_dx<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, R, D);
+        launched++;
+    }
+    if (gw || gb) {
+        int64_t col_blocks = (D + 31) / 32;
+        int64_t splits = ((int64_t)d->sm_count * 4 + col_blocks - 1) / col_blocks;
+        if (splits > R / 16 + 1) splits = R / 16 + 1;
+        int64_t maxs = (int64_t)d->scratch_bytes / (2 * D * (int64_t)sizeof(float));
+        if (splits > maxs) splits = maxs;
+        if (splits < 1) splits = 1;
+        int64_t per = (R + splits - 1) / splits;
+        splits = (R + per - 1) / per;
+        float *part = (float *)d->scratch;
+        dim3 grid((unsigned)col_blocks, (unsigned)splits), block(32, 8);
+        k_ln_bwd_wb<<<grid, block, 0, NCK_STREAM(d)>>>(x, g, stats, part, R, D, per);
+        k_ln_bwd_wb_combine<<<grid_for(d, D), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, D, gw, gb);
+        launched += 2;
+    }
+    NCK_LAUNCHED(d, launched);
+}

@@ -1,0 +1,221 @@
+// Reductions: axis sums / means / max / argmax and their gradients, column sums for bias
+// gradients, sums of squares for gradient clipping. Every output is produced by one thread, one
+// warp or a fixed split followed by an in-order combine: results do not depend on scheduling.
+#include <math.h>
+
+#include "k_common.cuh"
+
+using namespace nck;
+
+// ---- per-output sums ---------------------------------------------------------------------------------
+
+// inner == 1: one warp per output row, lanes stride the row, a fixed shuffle tree combines them
+__global__ void k_rowsum(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t R, float scale) {
+    int lane = threadIdx.x & 31;
+    int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp; r < rows; r += nwarps) {
+        const float *p = x + r * R;
+        float s = 0.0f;
+        for (int64_t i = lane; i < R; i += 32) s += p[i];
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) y[r] = scale * s;
+    }
+}
+
+// inner > 1: one thread per (outer, inner) column, rows added in order with the scale fused
+__global__ void k_colsum_strided(const float *__restrict__ x, float *__restrict__ y, int64_t outer, int64_t R,
+                                 int64_t inner, float scale) {
+    int64_t n = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t o = t / inner, i = t - o * inner;
+        const float *p = x + o * R * inner + i;
+        float acc = 0.0f;
+        for (int64_t r = 0; r < R; r++) acc = fmaf(scale, p[r * inner], acc);
+        y[t] = acc;
+    }
+}
+
+extern "C" void nck_reduce_sum(nck_dev *d, const float *x, float *y, int64_t outer, int64_t R, int64_t inner,
+                               float scale) {
+    int64_t n = outer * inner;
+    if (n <= 0) return;
+    Scope sc(d, "reduce_sum");
+    if (R == 0) {
+        cudaMemsetAsync(y, 0, (size_t)n * sizeof(float), NCK_STREAM(d));
+        return;
+    }
+    if (inner == 1) {
+        k_rowsum<<<grid_for(d, n * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, n, R, scale);
+    } else {
+        k_colsum_strided<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(x, y, outer, R, inner, scale);
+    }
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_reduce_sum_i32(const int32_t *__restrict__ x, int32_t *__restrict__ y, int64_t outer, int64_t R,
+                                 int64_t inner) {
+    int64_t n = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t o = t / inner, i = t - o * inner;
+        int64_t s = 0;
+        for (int64_t r = 0; r < R; r++) s += x[(o * R + r) * inner + i];
+        y[t] = (int32_t)s;
+    }
+}
+
+extern "C" void nck_reduce_sum_i32(nck_dev *d, const int32_t *x, int32_t *y, int64_t outer, int64_t R,
+                                   int64_t inner) {
+    int64_t n = outer * inner;
+    if (n <= 0) return;
+    Scope sc(d, "reduce_sum_i32");
+    k_reduce_sum_i32<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(x, y, outer, R, inner);
+    NCK_LAUNCHED(d, 1);
+}
+
+// first maximum wins (strictly greater replaces), as newch's reduce (ops_reduce.c:101-108)
+__global__ void k_reduce_max(const float *__restrict__ x, float *__restrict__ y, int32_t *__restrict__ arg,
+                             int64_t outer, int64_t R, int64_t inner) {
+    int64_t n = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t o = t / inner, i = t - o * inner;
+        const float *p = x + o * R * inner + i;
+        float bv = p[0];
+        int32_t best = 0;
+        for (int64_t r = 1; r < R; r++) {
+            float v = p[r * inner];
+            if (v > bv) bv = v, best = (int32_t)r;
+        }
+        arg[t] = best;
+        if (y) y[t] = bv;
+    }
+}
+
+extern "C" void nck_reduce_max(nck_dev *d, const float *x, float *y, int32_t *arg, int64_t outer, int64_t R,
+                               int64_t inner) {
+    int64_t n = outer * inner;
+    if (n <= 0) return;
+    Scope sc(d, y ? "reduce_max" : "argmax");
+    k_reduce_max<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(x, y, arg, outer, R, inner);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- gradients --------------------------------------------------------------------------------------
+
+__global__ void k_reduce_sum_bwd(const float *__restrict__ g, float *__restrict__ gi, int64_t outer, int64_t R,
+                                 int64_t inner, float scale) {
+    int64_t n = outer * R * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = t % inner, o = t / (R * inner);
+        float gv = g[o * inner + i];
+        gi[t] = inner == 1 ? gi[t] + scale * gv : fmaf(scale, gv, gi[t]);
+    }
+}
+
+extern "C" void nck_reduce_sum_bwd(nck_dev *d, const float *g, float *gi, int64_t outer, int64_t R, int64_t inner,
+                                   float scale) {
+    int64_t n = outer * R * inner;
+    if (n <= 0) return;
+    Scope sc(d, "reduce_sum_bwd");
+    k_reduce_sum_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, gi, outer, R, inner, scale);
+    NCK_LAUNCHED(d, 1);
+}
+
+__global__ void k_reduce_max_bwd(const float *__restrict__ g, const int32_t *__restrict__ arg, float *__restrict__ gi,
+                                 int64_t outer, int64_t R, int64_t inner) {
+    int64_t n = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+        int64_t o = t / inner, i = t - o * inner;
+        gi[(o * R + arg[t]) * inner + i] += g[t];
+    }
+}
+
+extern "C" void nck_reduce_max_bwd(nck_dev *d, const float *g, const int32_t *arg, float *gi, int64_t outer, int64_t R,
+                                   int64_t inner) {
+    int64_t n = outer * inner;
+    if (n <= 0) return;
+    Scope sc(d, "reduce_max_bwd");
+    k_reduce_max_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, arg, gi, outer, R, inner);
+    NCK_LAUNCHED(d, 1);
+}
+
+// ---- column sums of a [M, N] matrix (bias gradients): split M, combine the partials in order ----------
+
+constexpr int kColRows = 8;  // threadIdx.y extent
+
+__global__ void k_colsum_partial(const float *__restrict__ x, float *__restrict__ part, int64_t M, int64_t N,
+                                 int64_t rows_per_split) {
+    __shared__ float sm[kColRows][33];
+    int64_t n = blockIdx.x * 32 + threadIdx.x;
+    int64_t m0 = blockIdx.y * rows_per_split, m1 = m0 + rows_per_split < M ? m0 + rows_per_split : M;
+    float acc = 0.0f;
+    if (n < N)
+        for (int64_t m = m0 + threadIdx.y; m < m1; m += kColRows) acc += x[m * N + n];
+    sm[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && n < N) {
+        float s = sm[0][threadIdx.x];
+        for (int k = 1; k < kColRows; k++) s += sm[k][threadIdx.x];
+        part[blockIdx.y * N + n] = s;
+    }
+}
+
+__global__ void k_colsum_combine(const float *__restrict__ part, float *__restrict__ gy, int64_t N, int splits) {
+    for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
+        float s = gy[n];
+        for (int k = 0; k < splits; k++) s += part[k * N + n];
+        gy[n] = s;
+    }
+}
+
+extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N) {
+    if (M <= 0 || N <= 0) return;
+    Scope sc(d, "colsum");
+    int64_t col_blocks = (N + 31) / 32;
+    int64_t want = (int64_t)d->sm_count * 4;
+    int64_t splits = want / col_blocks;
+    if (splits < 1) splits = 1;
+    if (splits > M / 64 + 1) splits = M / 64 + 1;
+    if (splits * N * (int64_t)sizeof(float) > (int64_t)d->scratch_bytes) splits = (int64_t)d->scratch_bytes / (N * 4);
+    if (splits < 1) splits = 1;
+    int64_t rows_per = (M + splits - 1) / splits;
+    splits = (M + rows_per - 1) / rows_per;
+    float *part = (float *)d->scratch;
+    dim3 grid((unsigned)col_blocks, (unsigned)splits), block(32, kColRows);
+    k_colsum_partial<<<grid, block, 0, NCK_STREAM(d)>>>(x, part, M, N, rows_per);
+    k_colsum_combine<<<grid_for(d, N), kThreads, 0, NCK_STREAM(d)>>>(part, gy, N, (int)splits);
+    NCK_LAUNCHED(d, 2);
+}
+
+// ---- sum of squares (double) ---------------------------------------------------------------------------
+
+__global__ void k_sumsq_partial(const float *__restrict__ x, int64_t n, double *__restrict__ part) {
+    __shared__ double sm[kThreads / 32];
+    double acc = 0.0;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        acc += (double)x[i] * (double)x[i];
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int k = 0; k < kThreads / 32; k++) s += sm[k];
+        part[blockIdx.x] = s;
+    }
+}
+
+__global__ void k_sumsq_combine(const double *__restrict__ part, int nb, double *out, int accumulate) {
+    double s = accumulate ? *out : 0.0;
+    for (int k = 0; k < nb; k++) s += part[k];
+    *out = s;
+}
+
+extern "C" void nck_sumsq(nck_dev *d, const float *x, int64_t n, double *out, int accumulate) {
+    Scope sc(d, "sumsq");
+    int nb = n > 0 ? grid_for(d, n, kThreads, 4) : 1;
+    double *part = (double *)d->scratch;
+    if (n > 0) k_sumsq_partial<<<nb, kThreads, 0, NCK_STREAM(d)>>>(x, n, part);
+    else cudaMemsetAsync(part, 0, sizeof(double), NCK_STREAM(d));
+    k_sumsq_combine<<<1, 1, 0, NCK_STREAM(d)>>>(part, nb, out, accumulate);
+    NCK_LAUNCHED(d, 2);
+}

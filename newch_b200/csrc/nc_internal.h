@@ -1,0 +1,266 @@
+/* Internal definitions of the B200 engine (host C11). Not installed.
+ *
+ * The engine keeps newch's execution model (engine/src/core/nc_internal.h:34-105 of newch): eager
+ * ops through one entry point, a tape of nodes walked newest-first for backward, a step arena reset
+ * in O(1). What differs is where things live:
+ *   - tensor data is device memory (B200 HBM): a device step arena for temporaries, the CUDA
+ *     stream-ordered pool for persistent tensors;
+ *   - tensor headers, tape nodes and op-private records are host memory in a host step arena;
+ *   - host views of device data are explicit mirrors with a coherence state per data owner.
+ */
+#ifndef NC_INTERNAL_H
+#define NC_INTERNAL_H
+
+#include "../../include/nc.h"
+#include "../../include/nc_ext.h"
+#include "nck.h"
+
+#include <stdarg.h>
+#include <string.h>
+
+#define NC_DEV_ALIGN 256        /* device allocations: TMA / vector loads / coalescing friendly */
+#define NC_HOST_ALIGN 64
+#define NC_MAX_INPUTS 6
+#define NC_MIN_DEV_CHUNK ((size_t)64 << 20)
+#define NC_HOST_CHUNK ((size_t)1 << 20)
+#define NC_MIRROR_SMALL 4096    /* owners up to this many bytes keep an eager host mirror */
+
+/* ---- tensor ----------------------------------------------------------------------------------- */
+
+enum {
+    NC_TF_REQUIRES_GRAD = 1u << 0,
+    NC_TF_PERSISTENT = 1u << 1,
+    NC_TF_OWNS_DATA = 1u << 2,
+    NC_TF_GRAD_CLEARED = 1u << 3,
+    NC_TF_ON_TAPE = 1u << 4,
+};
+
+/* coherence of an owner's host mirror */
+enum {
+    NC_COH_HOST_VALID = 1u << 0, /* mirror equals device data */
+    NC_COH_HOST_DIRTY = 1u << 1, /* mirror handed out: may hold writes the device has not seen */
+};
+
+typedef struct nc_node nc_node;
+
+struct nc_tensor {
+    nc_ctx *ctx;
+    nc_dtype dtype;
+    int ndim;
+    uint32_t flags;
+    int64_t shape[NC_MAX_DIMS];
+    int64_t stride[NC_MAX_DIMS];
+    void *data;        /* device address of logical element 0 */
+    nc_tensor *grad;   /* contiguous f32, same logical shape */
+    nc_node *node;
+    nc_tensor *owner;  /* views: the tensor whose data this aliases */
+    const char *name;
+    /* owners only */
+    size_t bytes;      /* size of the data allocation */
+    void *host;        /* host mirror of the whole allocation (NULL until needed) */
+    uint32_t coh;
+    int host_pinned;   /* mirror came from cudaMallocHost */
+};
+
+/* ---- op registry ------------------------------------------------------------------------------ */
+
+enum { NC_OPF_ELEMENTWISE = 1u << 0, NC_OPF_REDUCTION = 1u << 1, NC_OPF_VIEW = 1u << 2, NC_OPF_NONDIFF = 1u << 3 };
+
+typedef struct {
+    int64_t i[NC_MAX_DIMS + 2];
+    float f[4];
+} nc_op_params;
+
+typedef struct nc_op_def {
+    const char *name;
+    uint32_t flags;
+    int kind;
+    nc_status (*infer)(nc_node *n, nc_dtype *dt, int *ndim, int64_t *shape);
+    int (*view)(nc_node *n, int ndim, const int64_t *shape);
+    nc_status (*forward)(nc_node *n);
+    void (*backward)(nc_node *n);
+} nc_op_def;
+
+struct nc_node {
+    const nc_op_def *op;
+    nc_tensor *in[NC_MAX_INPUTS];
+    int n_in;
+    nc_tensor *out;
+    nc_op_params p;
+    void *saved;       /* op-private host record (host arena); may point at device scratch */
+    nc_node *prev;
+    uint32_t mark;
+    int released;
+};
+
+#define NC_OP_LIST(X)                                                          \
+    X(add) X(sub) X(mul) X(div)                                                \
+    X(neg) X(exp) X(log) X(sqrt) X(relu) X(sigmoid) X(tanh)                    \
+    X(scale) X(add_scalar) X(pow_scalar)                                       \
+    X(leaky_relu) X(relu6) X(hardsigmoid) X(hardswish) X(silu) X(gelu)         \
+    X(gelu_tanh)                                                               \
+    X(matmul) X(linear)                                                        \
+    X(sum) X(mean) X(max) X(argmax)                                            \
+    X(reshape) X(transpose) X(contiguous) X(detach) X(index_select)            \
+    X(log_softmax) X(softmax) X(cross_entropy)                                 \
+    X(conv2d) X(max_pool2d) X(avg_pool2d) X(dropout) X(batch_norm)             \
+    X(linear_int8) X(nll_loss) X(compare) X(cat) X(to_dtype)                   \
+    X(bmm) X(layer_norm) X(masked_fill) X(slice)
+
+#define NC_DECLARE_OP(name) extern const nc_op_def nc_op_##name;
+NC_OP_LIST(NC_DECLARE_OP)
+#undef NC_DECLARE_OP
+
+int nc__op_count(void);
+const nc_op_def *nc__op_at(int i);
+
+nc_tensor *nc__apply(const nc_op_def *op, nc_tensor **in, int n_in, const nc_op_params *p);
+
+/* ---- context ---------------------------------------------------------------------------------- */
+
+typedef struct nc_hchunk {
+    struct nc_hchunk *next;
+    size_t cap, used;
+    unsigned char *base;
+} nc_hchunk;
+
+typedef struct {
+    char *base;
+    size_t cap, used;
+} nc_dchunk;
+
+typedef struct {
+    char *p;
+    size_t size;
+} nc_dfree;
+
+
+struct nc_ctx {
+    /* device */
+    nck_dev dev;
+    char device_name[128];
+    int device_ok;
+
+    /* device step arena: bump chunks + best-fit free list of released blocks */
+    nc_dchunk *dchunks;
+    int n_dchunks, cap_dchunks;
+    int cur_dchunk;
+    nc_dfree *dfree;
+    int n_dfree, cap_dfree;
+    size_t dchunk_min;
+    size_t arena_in_use, arena_reserved, arena_peak;
+
+    /* host step arena for headers, nodes and op records */
+    nc_hchunk *hchunks, *hcur;
+
+    /* persistent device blocks (open-addressing set of device pointers) */
+    size_t persistent_bytes;
+    void **pmem;
+    size_t pmem_cap, pmem_n;
+
+    /* backward temporaries of the node being processed */
+    void *bwd_tmp[64];
+    size_t bwd_tmp_size[64];
+    int bwd_tmp_n;
+    int bwd_logging;
+    int grad_alloc;
+    uint32_t mark_epoch;
+
+    int persistent_depth;
+    int grad_enabled;
+    nc_node *tape;
+
+    nc_status status;
+    char err[256];
+
+    uint64_t rng[4];
+    nc_cpu_info cpu;
+    int n_threads;
+    int force_reference;
+
+    /* pinned staging ring for small uploads */
+    unsigned char *stage;
+    size_t stage_cap, stage_pos;
+    void *stage_events[8];
+    int stage_slot;
+
+    /* data parallel */
+    int dp_rank, dp_world;
+    void *nccl_comm;
+
+    /* scratch double accumulators etc. */
+    double *dscratch;
+};
+
+void *nc__arena_alloc(nc_ctx *ctx, size_t bytes);             /* device, step lifetime */
+void nc__arena_free(nc_ctx *ctx, void *p, size_t bytes);
+void *nc__persistent_alloc(nc_ctx *ctx, size_t bytes);        /* device */
+void nc__persistent_free(nc_ctx *ctx, void *p, size_t bytes);
+void *nc__alloc(nc_ctx *ctx, size_t bytes, int persistent);
+void *nc__meta_alloc(nc_ctx *ctx, size_t bytes, int persistent); /* host headers/records */
+void nc__meta_free(nc_ctx *ctx, void *p, int persistent);
+int nc__is_persistent_mode(const nc_ctx *ctx);
+
+void nc__error(nc_ctx *ctx, nc_status code, const char *fmt, ...);
+/* checks the last CUDA call; on failure records NC_ERR_STATE and returns 0 */
+int nc__cuda_ok(nc_ctx *ctx, int cuda_err, const char *what);
+/* waits for the stream, folds kernel-found errors into the context status; returns 1 if ok */
+int nc__sync(nc_ctx *ctx);
+
+uint64_t nc__rng_next(nc_ctx *ctx);
+float nc__rand_uniform01(nc_ctx *ctx);
+float nc__rand_normal(nc_ctx *ctx);
+/* advances the context stream by n draws without producing them */
+void nc__rng_skip(nc_ctx *ctx, uint64_t n);
+int nc__rng_device_init(nc_ctx *ctx);
+
+void nc__detect_cpu(nc_cpu_info *info);
+
+/* host <-> device */
+void nc__upload(nc_ctx *ctx, void *dst, const void *src, size_t bytes);
+void nc__download(nc_ctx *ctx, void *dst, const void *src, size_t bytes); /* synchronous */
+
+/* ---- tensor helpers --------------------------------------------------------------------------- */
+
+size_t nc__dtype_size(nc_dtype dt);
+const char *nc__dtype_name(nc_dtype dt);
+int64_t nc__shape_numel(int ndim, const int64_t *shape);
+void nc__contig_strides(int ndim, const int64_t *shape, int64_t *stride);
+int nc__norm_axis(int axis, int ndim);
+int nc__same_shape(const nc_tensor *a, const nc_tensor *b);
+const char *nc__shape_str(int ndim, const int64_t *shape, char *buf, size_t size);
+int nc__expect_f32(const nc_node *n, int i);
+
+nc_tensor *nc__tensor_new(nc_ctx *ctx, nc_dtype dt, int ndim, const int64_t *shape, int persistent);
+nc_tensor *nc__tensor_alias(const nc_tensor *src, int persistent);
+static inline nc_tensor *nc__owner(nc_tensor *t) { return t->owner ? t->owner : t; }
+
+nc_tensor *nc__grad_buf(nc_tensor *t);
+static inline int nc__needs_grad(const nc_tensor *t) { return (t->flags & NC_TF_REQUIRES_GRAD) != 0; }
+
+/* device pointer to t's element 0 after pushing any host writes to the device */
+void *nc__dev(nc_tensor *t);
+/* t (its owner) is about to be written by a kernel: host mirror no longer valid */
+void nc__dev_write(nc_tensor *t);
+/* contiguous device f32 data of t (a copy in the arena when t is a strided view) */
+const float *nc__contig_f32(nc_tensor *t);
+/* contiguous device data of any dtype */
+const void *nc__contig(nc_tensor *t);
+/* host copy of t's contiguous data (mirror when valid, else a download); NULL on error */
+const void *nc__host_view(nc_tensor *t);
+
+void nc__bcast_strides(const nc_tensor *t, int ndim, const int64_t *shape, int64_t *out);
+void nc__bcast_strides_shape(int tn, const int64_t *tshape, int ndim, const int64_t *shape, int64_t *out);
+
+static inline nck_dev *nc__k(nc_ctx *ctx) { return &ctx->dev; }
+
+/* GEMM entry point for ops (same contract as the newch kernel table's gemm_f32, newch
+ * engine/src/kernels/kernels.h:34-41, plus batch strides) */
+void nc__gemm(nc_ctx *ctx, int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
+              int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc);
+void nc__gemm_batched(nc_ctx *ctx, const nck_gemm_args *a);
+
+/* data parallel: all-reduce of a device float buffer, averaged over ranks */
+int nc__dp_allreduce_mean(nc_ctx *ctx, float *buf, int64_t n);
+
+#endif /* NC_INTERNAL_H */

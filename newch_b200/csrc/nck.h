@@ -1,0 +1,217 @@
+/* Launch interface between the C11 host engine and the sm_100a kernels.
+ *
+ * Plain C: every launcher takes the device context (stream, status word, SM count) and raw device
+ * pointers with sizes. Nothing here knows about tensors, autograd or the arena. Each launcher
+ * enqueues its kernels on d->stream and adds the number of kernels it launched to d->launches.
+ * Sizes are int64 element counts unless noted. Launchers never synchronize.
+ */
+#ifndef NCK_H
+#define NCK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct nck_timer nck_timer;
+
+typedef struct nck_dev {
+    void *stream;      /* cudaStream_t */
+    int *status;       /* device word: first kernel-detected error code (0 = ok) */
+    int *status_host;  /* pinned mirror read at sync points */
+    int device;
+    int sm_count;
+    int64_t launches;  /* kernels enqueued so far */
+    int gemm_mode;     /* NCK_GEMM_* */
+    nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
+    void *scratch;     /* device scratch for split reductions (owned by the context) */
+    size_t scratch_bytes;
+} nck_dev;
+
+/* kernel-detected error codes written to *status (first one wins) */
+enum { NCK_OK = 0, NCK_ERR_INDEX = 1, NCK_ERR_LABEL = 2 };
+
+enum { NCK_GEMM_FFMA = 0, NCK_GEMM_TF32 = 1, NCK_GEMM_3XTF32 = 2 };
+
+/* ---- timing (bench instrumentation) ------------------------------------------------------ */
+void nck_timer_enable(nck_dev *d, int on);
+void nck_timer_begin(nck_dev *d, const char *name);
+void nck_timer_end(nck_dev *d);
+/* total milliseconds and launch count for kernels whose name starts with `prefix` ("" = all) */
+int nck_timer_query(nck_dev *d, const char *prefix, double *ms, int64_t *count);
+void nck_timer_reset(nck_dev *d);
+
+/* ---- memory helpers ---------------------------------------------------------------------- */
+void nck_fill_f32(nck_dev *d, float *y, float v, int64_t n);
+void nck_fill_i32(nck_dev *d, int32_t *y, int32_t v, int64_t n);
+void nck_add_scalar_inplace(nck_dev *d, float *y, float v); /* y[0] += v */
+/* y[i] += a * x[i] */
+void nck_axpy(nck_dev *d, int64_t n, float a, const float *x, float *y);
+/* dst (contiguous, element size es) = src viewed through shape/stride (elements) */
+void nck_copy_strided(nck_dev *d, int es, int ndim, const int64_t *shape, const int64_t *stride, const void *src,
+                      void *dst);
+/* dst viewed through shape/dst_stride += src (contiguous): backward of a strided view */
+void nck_acc_strided(nck_dev *d, int ndim, const int64_t *shape, const int64_t *dst_stride, const float *src,
+                     float *dst);
+/* dtype conversion (reference dtype codes: 0 f32, 1 i32, 3 i8, 4 u8); saturating, NaN -> 0 */
+void nck_convert(nck_dev *d, int from, int to, const void *src, void *dst, int64_t n);
+
+/* ---- elementwise --------------------------------------------------------------------------- */
+enum {
+    NCK_UN_NEG, NCK_UN_EXP, NCK_UN_LOG, NCK_UN_SQRT, NCK_UN_RELU, NCK_UN_SIGMOID, NCK_UN_TANH, NCK_UN_SCALE,
+    NCK_UN_ADD_SCALAR, NCK_UN_POW, NCK_UN_LEAKY_RELU, NCK_UN_RELU6, NCK_UN_HARDSIGMOID, NCK_UN_HARDSWISH,
+    NCK_UN_SILU, NCK_UN_GELU, NCK_UN_GELU_TANH
+};
+void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, float *y, int64_t n);
+/* gi += g * d/dx f(x) (y = f(x) for kinds that use it) */
+void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, const float *y, const float *g, float *gi,
+                   int64_t n);
+
+enum { NCK_BIN_ADD, NCK_BIN_SUB, NCK_BIN_MUL, NCK_BIN_DIV };
+#define NCK_MAXD 6
+typedef struct {
+    int ndim;
+    int64_t shape[NCK_MAXD];
+    int64_t sa[NCK_MAXD], sb[NCK_MAXD], so[NCK_MAXD]; /* element strides, 0 = broadcast */
+} nck_bcast;
+void nck_binary_fwd(nck_dev *d, int kind, const nck_bcast *bc, const float *a, const float *b, float *o);
+/* same-shape contiguous fast path */
+void nck_binary_fwd_flat(nck_dev *d, int kind, const float *a, const float *b, float *o, int64_t n);
+/* gradient of input `which` (0 = a, 1 = b) accumulated into gx whose shape broadcasts to bc->shape;
+ * gx_stride gives gx's strides over the output dims (0 on broadcast dims). g is contiguous. */
+void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast *bc, const float *g, const float *a,
+                    const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel);
+/* compare: a, b f32 or i32 (type flags), result i32 */
+void nck_compare(nck_dev *d, int op, const nck_bcast *bc, const void *a, int a_i32, const void *b, int b_i32,
+                 int32_t *o);
+/* out = mask ? v : x with mask i32 broadcast (strides in bc->sb), x strides in bc->sa, out contiguous */
+void nck_masked_fill_fwd(nck_dev *d, const nck_bcast *bc, const float *x, const int32_t *m, float v, float *o);
+void nck_masked_fill_bwd(nck_dev *d, const nck_bcast *bc, const float *g, const int32_t *m, float *gx);
+
+/* ---- reductions ---------------------------------------------------------------------------- */
+/* x viewed as [outer, R, inner], contiguous. mean: scale = 1/R. */
+void nck_reduce_sum(nck_dev *d, const float *x, float *y, int64_t outer, int64_t R, int64_t inner, float scale);
+void nck_reduce_sum_i32(nck_dev *d, const int32_t *x, int32_t *y, int64_t outer, int64_t R, int64_t inner);
+/* max value (may be NULL) and first argmax index */
+void nck_reduce_max(nck_dev *d, const float *x, float *y, int32_t *arg, int64_t outer, int64_t R, int64_t inner);
+/* gy[n] += sum_m x[m, n] for a contiguous [M, N] matrix (bias gradients) */
+void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N);
+void nck_reduce_sum_bwd(nck_dev *d, const float *g, float *gi, int64_t outer, int64_t R, int64_t inner,
+                        float scale);
+void nck_reduce_max_bwd(nck_dev *d, const float *g, const int32_t *arg, float *gi, int64_t outer, int64_t R,
+                        int64_t inner);
+/* fills *out (double, device) with sum of squares of n floats; accumulates when `accumulate` */
+void nck_sumsq(nck_dev *d, const float *x, int64_t n, double *out, int accumulate);
+
+/* ---- nn ------------------------------------------------------------------------------------- */
+/* rows x C, contiguous. log_form: log-softmax. */
+void nck_softmax_fwd(nck_dev *d, const float *x, float *y, int64_t rows, int64_t C, int log_form);
+void nck_softmax_bwd(nck_dev *d, const float *y, const float *g, float *gi, int64_t rows, int64_t C, int log_form);
+/* cross entropy: prob = softmax rows (saved), loss = mean -log p[label] (double accumulation) */
+void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t *lab, float *prob, float *loss, int64_t N,
+                           int64_t C);
+void nck_cross_entropy_bwd(nck_dev *d, const float *prob, const int32_t *lab, const float *gloss, float *gi,
+                           int64_t N, int64_t C);
+void nck_nll_fwd(nck_dev *d, const float *x, const int32_t *lab, float *loss, int64_t N, int64_t C, int sum);
+void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, int64_t N, int64_t C, int sum);
+/* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i */
+void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits, int64_t n,
+                     float p);
+void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p);
+/* one-time upload of the xoshiro256** jump tables (host-computed) */
+int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes);
+
+/* batch norm over x [N, C, S] */
+void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
+                      float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom, float eps);
+void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
+                     float *invstd, const float *rm, const float *rv, int64_t N, int64_t C, int64_t S, float eps);
+void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean, const float *invstd,
+                float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S, int training);
+/* layer norm over rows of D */
+void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats, int64_t R,
+                int64_t D, float eps);
+void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
+                float *gw, float *gb, int64_t R, int64_t D);
+
+/* ---- gather / scatter ------------------------------------------------------------------------ */
+void nck_index_select(nck_dev *d, const void *x, const int32_t *idx, void *y, int64_t B, int64_t N,
+                      int64_t row_bytes);
+void nck_index_select_bwd(nck_dev *d, const float *g, const int32_t *idx, float *gx, int64_t B, int64_t N,
+                          int64_t row);
+/* cat / split along a [outer, len*inner] view */
+void nck_cat_part(nck_dev *d, const void *x, void *y, int64_t outer, int64_t row_bytes, int64_t out_row_bytes,
+                  int64_t off_bytes);
+void nck_cat_part_bwd(nck_dev *d, const float *g, float *gx, int64_t outer, int64_t row, int64_t out_row,
+                      int64_t off);
+
+/* ---- convolution / pooling (NCHW) ---------------------------------------------------------- */
+typedef struct {
+    int64_t N, C, H, W, OC, KH, KW, OH, OW;
+    int sh, sw, ph, pw, dh, dw;
+    int64_t G;
+} nck_conv;
+/* col [n][g][Cg*KH*KW][OH*OW] for samples [n0, n0+nb) */
+void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float *col, int64_t n0, int64_t nb);
+/* dx[n] += fold(col[n]) */
+void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb);
+/* gb[oc] += sum over n, l of g[n, oc, l] */
+void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_t N, int64_t OC, int64_t L);
+/* direct convolution for few input channels per group (Cg*KH*KW <= 64) */
+void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
+void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
+void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx);
+#define NCK_DW_MAX_TAPS 25 /* nck_dw_dw handles kernels up to 5x5 */
+void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
+void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max);
+void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx, int is_max);
+
+/* ---- GEMM -------------------------------------------------------------------------------------- */
+/* C_b = alpha * op(A_b) op(B_b) + beta * C_b for b in [0, batch); row-major; ta/tb as the newch kernel
+ * table (ta: A stored K x M). With reduce_batch, C = alpha * sum_b op(A_b) op(B_b) + beta * C. */
+typedef struct {
+    int ta, tb;
+    int64_t M, N, K;
+    float alpha, beta;
+    const float *A;
+    int64_t lda, sA;
+    const float *B;
+    int64_t ldb, sB;
+    float *C;
+    int64_t ldc, sC;
+    int64_t batch;
+    int reduce_batch;
+    const float *bias; /* optional: C[m, n] = alpha * acc + bias[n] (or bias[m] with bias_per_row) + beta * C */
+    int bias_per_row;
+} nck_gemm_args;
+void nck_gemm(nck_dev *d, const nck_gemm_args *a);
+
+/* ---- optimizers -------------------------------------------------------------------------------- */
+typedef struct {
+    float *w;
+    const float *g;
+    float *m, *v;
+    int64_t n;
+} nck_param_seg;
+enum { NCK_OPT_SGD, NCK_OPT_ADAM, NCK_OPT_ADAMW, NCK_OPT_RMSPROP };
+typedef struct {
+    int kind;
+    float lr, momentum, weight_decay, beta1, beta2, eps, gs, bc1, bc2;
+    int eps_inside_sqrt;
+} nck_opt_hyper;
+/* one launch for all parameter segments; segs is a host array, copied into the launch */
+void nck_optim_step(nck_dev *d, const nck_opt_hyper *h, const nck_param_seg *segs, int nseg);
+
+/* ---- int8 quantization -------------------------------------------------------------------------- */
+void nck_quantize_rows(nck_dev *d, const float *x, int8_t *q, float *scale, int64_t rows, int64_t cols);
+/* y[r, o] = (float)acc * xs[r] * ws[o] + b[o], acc = sum_k xq[r,k] * wq[o,k] (exact int32) */
+void nck_qlinear(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, const float *b,
+                 float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NCK_H */

@@ -1,0 +1,207 @@
+"""Replays a recorded nc.h call sequence (a workload trace) against any library with the newch C ABI.
+
+A trace is what the unchanged newch Python package called for one benchmark configuration (see
+newch_b200/workloads/record_traces.py). Replaying it against the B200 library runs exactly the
+calls a newch user's script makes; replaying it against the reference engine reproduces the
+reference's results for the same calls. Handles are re-bound to whatever pointers the library under
+test returns, host buffers are rebuilt from the trace's blobs (seeded synthetic inputs are
+regenerated), and every scalar result and copied-out buffer is kept for comparison.
+"""
+
+from __future__ import annotations
+
+import base64
+import ctypes
+import gzip
+import json
+import zlib
+from ctypes import c_char_p, c_int64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+from . import capi, synth
+
+WORKLOADS = Path(__file__).resolve().parent / "workloads"
+
+
+class ReplayMismatch(RuntimeError):
+    pass
+
+
+class Trace:
+    def __init__(self, path):
+        path = Path(path)
+        if not path.exists():
+            path = WORKLOADS / f"{path}.json.gz"
+        with gzip.open(path, "rt") as f:
+            t = json.load(f)
+        if t.get("format") != "nc-trace-1":
+            raise ValueError(f"{path}: not an nc trace")
+        self.path = path
+        self.meta = t["meta"]
+        self.calls = t["calls"]
+        self.blobs = t["blobs"]
+        self.marks = t["marks"]
+        self.step_ends = t["step_ends"]
+
+    def blob(self, bid: str, seed_offset: int = 0) -> np.ndarray:
+        b = self.blobs[bid]
+        if "gen" in b:
+            spec = synth.with_seed_offset(b["gen"], seed_offset) if seed_offset else b["gen"]
+            return np.frombuffer(synth.generate(spec).tobytes(), dtype=np.uint8).copy()
+        return np.frombuffer(zlib.decompress(base64.b64decode(b["zlib"])), dtype=np.uint8).copy()
+
+    def steps(self):
+        """(start, end) call ranges of the training/inference steps, each ending with nc_step_end."""
+        begin = self.marks.get("train_begin", 0)
+        out, start = [], begin
+        for e in self.step_ends:
+            if e >= begin:
+                out.append((start, e + 1))
+                start = e + 1
+        return out
+
+    def golden_items(self):
+        """Scalar results the reference returned from nc_item during the steps (the losses)."""
+        b, e = self.marks.get("train_begin", 0), self.marks.get("train_end", len(self.calls))
+        return [c[2] for c in self.calls[b:e] if c[0] == "nc_item"]
+
+    def golden_outputs(self):
+        """Buffers the reference copied out after the steps (final parameters / predictions)."""
+        e = self.marks.get("train_end", len(self.calls))
+        out = []
+        for c in self.calls[e:]:
+            if c[0] == "nc_copy_to" and len(c) > 3:
+                out.append(c[3])
+        return out
+
+    def output_bytes(self, entry) -> bytes | None:
+        if "out" in entry:
+            return self.blob(entry["out"]).tobytes()
+        return None
+
+
+_STRUCTS = {"nc_init": capi.Config}
+
+
+class Replayer:
+    """Executes trace calls on `lib`. `seed_offset` regenerates synthetic inputs with another seed
+    (per-rank data shards); `check` raises when a call's success differs from the recording."""
+
+    def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True):
+        self.lib = lib
+        self.trace = trace
+        self.check = check
+        self.h: dict = {}
+        self.items: list = []    # (call index, value) of nc_item results
+        self.outputs: list = []  # (call index, bytes) of nc_copy_to results
+        self._keep: list = []
+        self._blobs: dict = {}
+        self.seed_offset = seed_offset
+        self._fns = {name: getattr(lib, name) for name in {c[0] for c in trace.calls}}
+        self._prepared = [self._prepare(i, c) for i, c in enumerate(trace.calls)]
+
+    # -- preparation: everything that does not depend on live handles is built once ------------
+    def _blob_ptr(self, bid):
+        arr = self._blobs.get(bid)
+        if arr is None:
+            arr = self.trace.blob(bid, self.seed_offset)
+            self._blobs[bid] = arr
+        return arr.ctypes.data
+
+    def _prepare(self, idx, call):
+        name, args, ret = call[0], call[1], call[2]
+        extra = call[3] if len(call) > 3 else None
+        conv = []
+        fn = self._fns[name]
+        argtypes = capi.SIGNATURES[name][1] if name in capi.SIGNATURES else []
+        for k, a in enumerate(args):
+            t = argtypes[k] if k < len(argtypes) else None
+            if a is None:
+                conv.append((0, None))
+            elif isinstance(a, dict):
+                if "h" in a:
+                    conv.append((1, a["h"]))
+                elif "s" in a:
+                    arr = (c_int64 * max(len(a["s"]), 1))(*a["s"])
+                    self._keep.append(arr)
+                    conv.append((0, arr))
+                elif "b" in a:
+                    conv.append((0, self._blob_ptr(a["b"])))
+                elif "o" in a:
+                    conv.append((2, int(a["o"])))
+                elif "hl" in a:
+                    conv.append((3, list(a["hl"])))
+                elif "st" in a:
+                    st_t = t if isinstance(t, type) and issubclass(t, ctypes.Structure) else _STRUCTS.get(name)
+                    if st_t is None and t is not None and hasattr(t, "_type_"):
+                        st_t = t._type_
+                    obj = st_t(*a["st"])
+                    self._keep.append(obj)
+                    conv.append((0, ctypes.byref(obj) if name == "nc_init" else obj))
+                elif "str" in a:
+                    conv.append((0, a["str"].encode()))
+                elif "strs" in a:
+                    arr = (c_char_p * max(len(a["strs"]), 1))(*[s.encode() for s in a["strs"]])
+                    self._keep.append(arr)
+                    conv.append((0, arr))
+                elif "f" in a:
+                    conv.append((0, float(a["f"])))
+                else:
+                    raise ValueError(f"call {idx} {name}: unknown argument {a}")
+            else:
+                conv.append((0, a))
+        ret_h = ret["h"] if isinstance(ret, dict) and "h" in ret else None
+        ret_null = ret is None and capi.SIGNATURES.get(name, (None,))[0] is c_void_p and name not in (
+            "nc_data_f32", "nc_data_i32", "nc_optim_state")
+        out_h = extra.get("out_h") if isinstance(extra, dict) else None
+        return (fn, name, conv, ret_h, ret_null, out_h)
+
+    # -- execution --------------------------------------------------------------------------
+    def run(self, start: int = 0, end: int | None = None) -> None:
+        h = self.h
+        prepared = self._prepared
+        end = len(prepared) if end is None else end
+        for i in range(start, end):
+            fn, name, conv, ret_h, ret_null, out_h = prepared[i]
+            vals = []
+            outbuf = None
+            for kind, v in conv:
+                if kind == 0:
+                    vals.append(v)
+                elif kind == 1:
+                    vals.append(h[v])
+                elif kind == 2:
+                    outbuf = (ctypes.c_char * v)() if name == "nc_copy_to" else (c_void_p * 1)()
+                    vals.append(outbuf)
+                else:
+                    vals.append((c_void_p * max(len(v), 1))(*[h[x] if x is not None else None for x in v]))
+            r = fn(*vals)
+            if ret_h is not None:
+                if not r:
+                    raise ReplayMismatch(f"call {i} {name}: returned NULL where the reference succeeded: "
+                                         f"{self._error()}")
+                h[ret_h] = r
+            elif ret_null and r and self.check:
+                raise ReplayMismatch(f"call {i} {name}: succeeded where the reference returned NULL")
+            if out_h is not None:
+                h[out_h] = outbuf[0]
+            if name == "nc_item":
+                self.items.append((i, r))
+            elif name == "nc_copy_to" and outbuf is not None:
+                self.outputs.append((i, bytes(outbuf)))
+
+    def _error(self) -> str:
+        ctx = self.h.get(1)  # nc_init is every trace's first call
+        try:
+            return self.lib.nc_error(ctx).decode(errors="replace") if ctx else "?"
+        except Exception:  # pragma: no cover - diagnostics only
+            return "?"
+
+    def run_all(self) -> None:
+        self.run(0, None)
+
+    @property
+    def ctx(self):
+        return self.h.get(1)
