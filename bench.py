@@ -1,0 +1,352 @@
+#!/usr/bin/env python3
+"""Training-step throughput of the B200 newch engine (train samples/sec), with its roofline and the
+reference engine's multithreaded CPU path timed on the same host.
+
+The workload is a recorded nc.h call sequence of the unchanged newch Python package (see
+newch_b200/workloads/record_traces.py): by default configuration 2 of the baseline, the two-block
+CNN trained through compile/fit with AdamW at batch 512 per GPU. One timed step replays exactly the
+calls newch's fit() makes for one batch (forward, cross entropy, zero_grad, backward, optimizer step,
+loss.item(), step_end) through the C ABI.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config cfg2]
+
+Multi-GPU: launched by torch.distributed.run, one process per GPU; each rank trains on its own data
+shard and the engine all-reduces the flat gradient buffer over NCCL before every update (weak
+scaling). Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from newch_b200 import capi, replay  # noqa: E402
+
+METRIC = "train samples/sec at 1/2/4/8 B200 (CNN, transformer); % HBM/tensor roofline"
+REF_LIB = REPO / "oracle" / "_ref" / "libnc_ref.so"
+BATCH = {"cfg1": 64, "cfg2": 512, "cfg3": 256, "cfg4": 64, "cfg5": 8192, "cfg2_stream": 512}
+DESC = {
+    "cfg1": "small CNN step (Conv16+ReLU+MaxPool+Linear, log_softmax+nll, Adam), batch 64",
+    "cfg2": "two-block CNN via compile/fit (Conv32/64+BN+ReLU+Pool, Dropout, Linear 3136-128-10, AdamW), "
+            "batch 512 per GPU",
+    "cfg3": "depthwise-separable MobileNet-style step (Adam), batch 256 per GPU",
+    "cfg4": "causal char TransformerEncoder LM step (4 layers, d 256, T 128, AdamW), batch 64 per GPU",
+    "cfg5": "int8 quantize_ MLP inference, 8192 rows",
+}
+E2E_TRACE = {"cfg2": "cfg2_stream"}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.25)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.out = self.proc.communicate(timeout=5)[0]
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def load_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def step_io_bytes(trace: replay.Trace, start: int, end: int):
+    """Host->device and device->host bytes of one step's calls (inputs uploaded, results read)."""
+    h2d = d2h = 0
+    for c in trace.calls[start:end]:
+        name, args = c[0], c[1]
+        if name in ("nc_from_data", "nc_copy_from"):
+            for a in args:
+                if isinstance(a, dict) and "b" in a:
+                    h2d += trace.blobs[a["b"]]["n"]
+        elif name == "nc_item":
+            d2h += 4
+        elif name == "nc_copy_to":
+            d2h += int(args[2])
+    return h2d, d2h
+
+
+class Run:
+    """A trace replayed on the B200 engine: prologue and recorded steps once, then the last recorded
+    step repeated."""
+
+    def __init__(self, lib, trace_name: str, rank: int, world: int, pg, pinned: bool = False):
+        self.lib = lib
+        self.trace = replay.Trace(trace_name)
+        self.rep = replay.Replayer(lib, self.trace, seed_offset=rank * 7919, pinned=pinned)
+        self.rep.run(0, 1)  # nc_init
+        self.ctx = self.rep.ctx
+        if not self.ctx or not lib.nc_ok(self.ctx):
+            raise RuntimeError(f"nc_init failed: {lib.nc_error(self.ctx) if self.ctx else 'NULL'}")
+        if world > 1:
+            import torch
+            import torch.distributed as dist
+            buf = (ctypes.c_char * 512)()
+            n = lib.nc_ext_nccl_unique_id(buf, 512) if rank == 0 else 0
+            t = torch.zeros(513, dtype=torch.uint8)
+            if rank == 0:
+                t[0] = n
+                t[1:1 + n] = torch.frombuffer(bytearray(buf.raw[:n]), dtype=torch.uint8)
+            dist.broadcast(t, 0, group=pg)
+            n = int(t[0])
+            idb = bytes(t[1:1 + n].tolist())
+            st = lib.nc_ext_dp_init(self.ctx, rank, world, idb, n)
+            if st != 0:
+                raise RuntimeError(f"dp init failed: {lib.nc_error(self.ctx)}")
+        steps = self.trace.steps()
+        self.rep.run(1, steps[-1][1])  # model set-up and every recorded step
+        self.step = steps[-1]
+
+    def one(self):
+        self.rep.run(*self.step)
+
+
+def timed_steps(run: Run, k: int, stream, flush):
+    """Device time of k steps (CUDA events on the engine's stream), L2 flushed between steps."""
+    import torch
+    evs = []
+    for _ in range(k):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run.one()
+        b.record(stream)
+        evs.append((a, b))
+        with torch.cuda.stream(stream):
+            flush.zero_()
+    torch.cuda.synchronize()
+    run.lib.nc_ext_synchronize(run.ctx)
+    return sum(a.elapsed_time(b) for a, b in evs) / 1e3
+
+
+def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
+    lib, ctx = run.lib, run.ctx
+    lib.nc_ext_timing(ctx, 1)
+    lib.nc_ext_timing_reset(ctx)
+    for _ in range(steps):
+        run.one()
+    table = capi.kernel_table(lib, ctx)
+    lib.nc_ext_timing(ctx, 0)
+    total = sum(t[1] for t in table) or 1.0
+    name, ms, cnt, fl, by = max(table, key=lambda t: t[1])
+    per_launch_ms = ms / max(cnt, 1)
+    if fl > 0:
+        achieved = fl / max(cnt, 1) / (per_launch_ms / 1e3) / 1e12
+        peak, unit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
+    else:
+        achieved = by / max(cnt, 1) / (per_launch_ms / 1e3) / 1e9
+        peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+    traffic = None
+    tf = REPO / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(name)
+    kernels = sorted(table, key=lambda t: -t[1])[:8]
+    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "traffic": traffic, "peak_src": peaks["src"] + " (MEASURED_PEAKS.json)",
+            "share_of_step_kernel_time": round(ms / total, 3), "launches_per_step": cnt / steps,
+            "top_kernels": [{"name": t[0], "ms_per_step": round(t[1] / steps, 4), "share": round(t[1] / total, 3)}
+                            for t in kernels]}
+
+
+def cpu_reference(trace_name: str, budget_s: float, max_steps: int, warmup: int = 1):
+    """The reference engine (its multithreaded AVX2 tier, all host cores) replaying the same trace."""
+    lib = capi.load(REF_LIB)
+    tr = replay.Trace(trace_name)
+    rep = replay.Replayer(lib, tr)
+    steps = tr.steps()
+    rep.run(0, steps[-1][1])
+    s = steps[-1]
+    for _ in range(warmup):
+        rep.run(*s)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_steps and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        rep.run(*s)
+        times.append(time.perf_counter() - t0)
+    ctx = rep.ctx
+    cores = lib.nc_num_threads(ctx)
+    backend = lib.nc_kernel_backend(ctx).decode()
+    return times, cores, backend
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--no-extras", action="store_true", help="skip e2e, roofline and CPU baseline")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    cfg = args.config
+    batch = BATCH.get(cfg, 1)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        if not REF_LIB.exists():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnc_ref.so was not built"}))
+            return 0
+        times, cores, backend = cpu_reference(cfg, budget_s=120.0, max_steps=max(args.steps, 1),
+                                               warmup=max(args.warmup, 1))
+        t = sum(times)
+        value = batch * len(times) / t
+        out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "samples/s", "n_gpus": 0,
+               "steps": len(times), "warmup": args.warmup, "ms_per_step": round(1e3 * t / len(times), 3),
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+               "data": "synthetic (seeded, MNIST-shaped)",
+               "config": {"workload": f"{cfg}: {DESC.get(cfg, cfg)}", "global_batch": batch, "per_gpu_batch": batch},
+               "cpu_baseline": {"value": round(value, 3), "unit": "samples/s", "cores": cores, "kind": "reference",
+                                "sample": f"{len(times)} {cfg} steps, newch engine ({backend} tier) built from its "
+                                          f"sources, same recorded calls"},
+               "e2e": {"value": round(value, 3), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": 0}}
+        print(json.dumps(out), flush=True)
+        return 0
+
+    os.environ["NC_DEVICE"] = str(local)
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+        pg = dist.group.WORLD
+    lib = capi.load_b200()
+    if lib.nc_ext_device_count() < 1:
+        raise SystemExit("no CUDA device")
+
+    run = Run(lib, cfg, rank, world, pg)
+    stream = torch.cuda.ExternalStream(lib.nc_ext_stream(run.ctx), device=torch.device("cuda", local))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+    for _ in range(args.warmup):
+        run.one()
+    lib.nc_ext_synchronize(run.ctx)
+    if pg:
+        dist.barrier(pg)
+    torch.cuda.synchronize()
+    l0 = lib.nc_ext_launch_count(run.ctx)
+    with Clocks(local) as clk:
+        secs = timed_steps(run, args.steps, stream, flush)
+    launches = (lib.nc_ext_launch_count(run.ctx) - l0) // max(args.steps, 1)
+    if pg:
+        dist.barrier(pg)
+        t = torch.tensor([secs], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+        secs = float(t[0])
+    if not lib.nc_ok(run.ctx):
+        raise SystemExit(f"engine error: {lib.nc_error(run.ctx).decode()}")
+    value = batch * world * args.steps / secs
+
+    e2e = None
+    rl = None
+    cpu = None
+    if not args.no_extras:
+        et = E2E_TRACE.get(cfg, cfg)
+        erun = Run(lib, et, rank, world, pg, pinned=True)
+        estream = torch.cuda.ExternalStream(lib.nc_ext_stream(erun.ctx), device=torch.device("cuda", local))
+        for _ in range(max(args.warmup, 3)):
+            erun.one()
+        ek = max(10, min(args.steps, 200))
+        if pg:
+            dist.barrier(pg)
+        esecs = timed_steps(erun, ek, estream, flush)
+        if pg:
+            t = torch.tensor([esecs], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+            esecs = float(t[0])
+        h2d, d2h = step_io_bytes(erun.trace, *erun.step)
+        e2e = {"value": round(batch * world * ek / esecs, 3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "trace": et, "steps": ek}
+        if rank == 0:
+            rl = roofline(run, load_peaks())
+            if world == 1 and REF_LIB.exists():
+                times, cores, backend = cpu_reference(cfg, budget_s=20.0, max_steps=30)
+                cpu = {"value": round(batch * len(times) / sum(times), 3), "unit": "samples/s", "cores": cores,
+                       "kind": "reference",
+                       "sample": f"{len(times)} steps of {cfg} (median {1e3 * statistics.median(times):.1f} ms), "
+                                 f"newch engine {backend} tier built from its sources, same recorded calls"}
+    if rank == 0:
+        out = {"metric": METRIC, "value": round(value, 3), "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": round(1e3 * secs / args.steps, 4), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, MNIST-shaped)",
+               "config": {"workload": f"{cfg}: {DESC.get(cfg, cfg)}", "global_batch": batch * world,
+                          "per_gpu_batch": batch, "parallelism": f"dp{world}",
+                          "gemm": lib.nc_ext_gemm_mode(run.ctx).decode(),
+                          "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+                          "driver": "recorded newch fit() call sequence replayed through the nc.h C ABI"},
+               "gpu_launches": int(launches), "clocks": clk.summary(), "e2e": e2e, "roofline": rl,
+               "cpu_baseline": cpu}
+        print(json.dumps(out), flush=True)
+    if pg:
+        dist.barrier(pg)
+        dist.destroy_process_group()
+    os._exit(0)  # engine contexts go with the process
+
+
+if __name__ == "__main__":
+    sys.exit(main())

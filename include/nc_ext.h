@@ -44,6 +44,13 @@ NC_API int nc_ext_timing(nc_ctx *ctx, int on);
 /* Sum of device milliseconds and the number of timed launches of kernels whose name starts with
  * `prefix` ("" = all) since timing was switched on. */
 NC_API int nc_ext_kernel_time(nc_ctx *ctx, const char *prefix, double *ms, int64_t *count);
+/* Timed kernel class i (0-based): its name, total device milliseconds, launches and the algorithmic
+ * work of those launches (FLOPs, and bytes that must move: each logical input read once, each
+ * output written once). Returns 0 when i is past the last class. */
+NC_API int nc_ext_kernel_entry(nc_ctx *ctx, int i, const char **name, double *ms, int64_t *count, double *flops,
+                               double *bytes);
+/* Clears the accumulated timings (timing stays on). */
+NC_API void nc_ext_timing_reset(nc_ctx *ctx);
 
 #ifdef __cplusplus
 }

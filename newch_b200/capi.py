@@ -168,7 +168,22 @@ EXT_SIGNATURES: dict = {
     "nc_ext_stream": (c_void_p, [P]),
     "nc_ext_timing": (c_int, [P, c_int]),
     "nc_ext_kernel_time": (c_int, [P, c_char_p, POINTER(ctypes.c_double), POINTER(c_int64)]),
+    "nc_ext_kernel_entry": (c_int, [P, c_int, POINTER(c_char_p), POINTER(ctypes.c_double), POINTER(c_int64),
+                                    POINTER(ctypes.c_double), POINTER(ctypes.c_double)]),
+    "nc_ext_timing_reset": (None, [P]),
 }
+
+
+def kernel_table(lib, ctx) -> list:
+    """[(name, ms, launches, flops, bytes)] of the timed kernel classes (timing must be on)."""
+    out, i = [], 0
+    name, ms, cnt = c_char_p(), ctypes.c_double(), c_int64()
+    fl, by = ctypes.c_double(), ctypes.c_double()
+    while lib.nc_ext_kernel_entry(ctx, i, ctypes.byref(name), ctypes.byref(ms), ctypes.byref(cnt), ctypes.byref(fl),
+                                  ctypes.byref(by)):
+        out.append((name.value.decode(), ms.value, cnt.value, fl.value, by.value))
+        i += 1
+    return out
 
 PKG_DIR = Path(__file__).resolve().parent
 REPO_DIR = PKG_DIR.parent

@@ -547,3 +547,16 @@ int nc_ext_kernel_time(nc_ctx *ctx, const char *prefix, double *ms, int64_t *cou
     nc__sync(ctx);
     return nck_timer_query(&ctx->dev, prefix ? prefix : "", ms, count);
 }
+
+int nc_ext_kernel_entry(nc_ctx *ctx, int i, const char **name, double *ms, int64_t *count, double *flops,
+                        double *bytes) {
+    if (!ctx->device_ok) return 0;
+    nc__sync(ctx);
+    return nck_timer_entry(&ctx->dev, i, name, ms, count, flops, bytes);
+}
+
+void nc_ext_timing_reset(nc_ctx *ctx) {
+    if (!ctx->device_ok) return;
+    nc__sync(ctx);
+    nck_timer_reset(&ctx->dev);
+}

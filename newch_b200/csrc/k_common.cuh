@@ -27,8 +27,8 @@ __device__ __forceinline__ void report(int *status, int code) { atomicCAS(status
 // RAII timing scope: when the device has a timer, brackets the launches inside with CUDA events.
 struct Scope {
     nck_dev *d;
-    Scope(nck_dev *dev, const char *name) : d(dev) {
-        if (d->timer) nck_timer_begin(d, name);
+    Scope(nck_dev *dev, const char *name, double flops = 0.0, double bytes = 0.0) : d(dev) {
+        if (d->timer) nck_timer_begin(d, name, flops, bytes);
     }
     ~Scope() {
         if (d->timer) nck_timer_end(d);

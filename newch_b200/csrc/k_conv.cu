@@ -28,7 +28,7 @@ __global__ void k_im2col(nck_conv g, const float *__restrict__ x, float *__restr
 extern "C" void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float *col, int64_t n0, int64_t nb) {
     int64_t total = nb * g->C * g->KH * g->KW * g->OH * g->OW;
     if (total <= 0) return;
-    Scope sc(d, "im2col");
+    Scope sc(d, "im2col", 0.0, 4.0 * (nb * g->C * g->H * g->W + total));
     k_im2col<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, col, n0, nb);
     NCK_LAUNCHED(d, 1);
 }
@@ -64,7 +64,7 @@ __global__ void k_col2im(nck_conv g, const float *__restrict__ col, float *__res
 extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb) {
     int64_t total = nb * g->C * g->H * g->W;
     if (total <= 0) return;
-    Scope sc(d, "col2im");
+    Scope sc(d, "col2im", 0.0, 4.0 * (nb * g->C * g->KH * g->KW * g->OH * g->OW + 2 * total));
     k_col2im<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
     NCK_LAUNCHED(d, 1);
 }
@@ -146,7 +146,8 @@ extern "C" void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *
                                     float *y) {
     int64_t L = g->OH * g->OW;
     if (g->N * g->G * L <= 0) return;
-    Scope sc(d, "conv_direct");
+    Scope sc(d, "conv_direct", 2.0 * g->N * g->OC * L * (g->C / g->G) * g->KH * g->KW,
+             4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L));
     int64_t bx = (L + kThreads - 1) / kThreads;
     if (bx > 64) bx = 64;
     dim3 grid((unsigned)bx, (unsigned)(g->N * g->G));
@@ -182,7 +183,7 @@ __global__ void k_dw_fwd(nck_conv g, const float *__restrict__ x, const float *_
 extern "C" void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y) {
     int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
-    Scope sc(d, "dw_fwd");
+    Scope sc(d, "dw_fwd", 2.0 * total * g->KH * g->KW, 4.0 * (g->N * g->C * g->H * g->W + total));
     k_dw_fwd<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
     NCK_LAUNCHED(d, 1);
 }
@@ -216,7 +217,8 @@ __global__ void k_dw_dx(nck_conv g, const float *__restrict__ gy, const float *_
 extern "C" void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx) {
     int64_t total = g->N * g->C * g->H * g->W;
     if (total <= 0) return;
-    Scope sc(d, "dw_dx");
+    Scope sc(d, "dw_dx", 2.0 * g->N * g->C * g->OH * g->OW * g->KH * g->KW,
+             4.0 * (g->N * g->C * g->OH * g->OW + 2 * total));
     k_dw_dx<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, w, gx);
     NCK_LAUNCHED(d, 1);
 }
@@ -271,7 +273,8 @@ extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const f
     int KK = (int)(g->KH * g->KW);
     if (g->N * g->C <= 0 || KK <= 0) return;
     if (KK > NCK_DW_MAX_TAPS) return; /* the caller takes the im2col path for larger kernels */
-    Scope sc(d, "dw_dw");
+    Scope sc(d, "dw_dw", 2.0 * g->N * g->C * g->OH * g->OW * KK,
+             4.0 * (g->N * g->C * (g->H * g->W + g->OH * g->OW)));
     int64_t splits = ((int64_t)d->sm_count * 4 + g->C - 1) / g->C;
     if (splits > g->N) splits = g->N;
     if (splits < 1) splits = 1;
@@ -319,7 +322,8 @@ __global__ void k_pool_fwd(nck_conv g, const float *__restrict__ x, float *__res
 extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max) {
     int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
-    Scope sc(d, is_max ? "max_pool" : "avg_pool");
+    Scope sc(d, is_max ? "max_pool" : "avg_pool", 0.0,
+             4.0 * (g->N * g->C * g->H * g->W + (is_max ? 2 : 1) * total));
     k_pool_fwd<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
     NCK_LAUNCHED(d, 1);
 }
@@ -365,7 +369,8 @@ __global__ void k_pool_bwd_gather(nck_conv g, const float *__restrict__ gy, cons
 
 extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx,
                              int is_max) {
-    Scope sc(d, is_max ? "max_pool_bwd" : "avg_pool_bwd");
+    Scope sc(d, is_max ? "max_pool_bwd" : "avg_pool_bwd", 0.0,
+             4.0 * ((is_max ? 2 : 1) * g->N * g->C * g->OH * g->OW + 2 * g->N * g->C * g->H * g->W));
     if (is_max && g->sh >= g->KH && g->sw >= g->KW) {
         int64_t total = g->N * g->C * g->OH * g->OW;
         if (total <= 0) return;

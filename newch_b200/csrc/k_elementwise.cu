@@ -135,7 +135,7 @@ static const char *unary_name(int kind, int bwd) {
 
 extern "C" void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, float *y, int64_t n) {
     if (n <= 0) return;
-    Scope sc(d, unary_name(kind, 0));
+    Scope sc(d, unary_name(kind, 0), 0.0, 8.0 * n);
     int vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
     k_unary_fwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, n, vec);
     NCK_LAUNCHED(d, 1);
@@ -144,7 +144,9 @@ extern "C" void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, flo
 extern "C" void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, const float *y, const float *g,
                               float *gi, int64_t n) {
     if (n <= 0) return;
-    Scope sc(d, unary_name(kind, 1));
+    /* reads x, g and the accumulator (and y where the derivative uses it), writes the accumulator */
+    int uses_y = kind == NCK_UN_EXP || kind == NCK_UN_SQRT || kind == NCK_UN_SIGMOID || kind == NCK_UN_TANH;
+    Scope sc(d, unary_name(kind, 1), 0.0, (16.0 + (uses_y ? 4.0 : 0.0)) * n);
     int vec = (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)gi) & 15) == 0;
     k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec);
     NCK_LAUNCHED(d, 1);

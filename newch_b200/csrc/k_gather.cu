@@ -25,7 +25,7 @@ __global__ void k_index_select(const char *__restrict__ x, const int32_t *__rest
 extern "C" void nck_index_select(nck_dev *d, const void *x, const int32_t *idx, void *y, int64_t B, int64_t N,
                                  int64_t row_bytes) {
     if (B <= 0 || row_bytes <= 0) return;
-    Scope sc(d, "index_select");
+    Scope sc(d, "index_select", 0.0, 2.0 * B * row_bytes + 4.0 * B);
     int64_t units = (row_bytes & 15) == 0 ? row_bytes / 16 : row_bytes;
     k_index_select<<<grid_for(d, B * units), kThreads, 0, NCK_STREAM(d)>>>((const char *)x, idx, (char *)y, B, N,
                                                                            row_bytes, d->status);

@@ -208,7 +208,10 @@ __global__ void k_sgemm_combine(GemmP p, int64_t nout) {
 
 extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (a->M <= 0 || a->N <= 0 || a->batch <= 0) return;
-    Scope sc(d, "gemm_f32");
+    double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
+    double nC = (a->reduce_batch ? 1.0 : (double)a->batch) * (a->beta != 0.0f ? 2.0 : 1.0);
+    Scope sc(d, "gemm_f32", 2.0 * a->M * a->N * a->K * a->batch,
+             4.0 * (nA * a->M * a->K + nB * a->K * a->N + nC * a->M * a->N));
     GemmP p;
     p.ta = a->ta, p.tb = a->tb, p.M = a->M, p.N = a->N, p.K = a->K, p.alpha = a->alpha, p.beta = a->beta;
     p.A = a->A, p.lda = a->lda, p.sA = a->sA, p.B = a->B, p.ldb = a->ldb, p.sB = a->sB;

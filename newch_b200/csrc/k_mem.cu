@@ -21,8 +21,7 @@ struct nck_timer {
     std::vector<Rec> recs;
     std::vector<cudaEvent_t> pool;
     int open = -1;
-    double ms_done = 0;
-    std::vector<double> ms_by_name;
+    std::vector<double> ms_by_name, flops_by_name, bytes_by_name;
     std::vector<int64_t> n_by_name;
 };
 
@@ -52,7 +51,7 @@ extern "C" void nck_timer_enable(nck_dev *d, int on) {
     }
 }
 
-extern "C" void nck_timer_begin(nck_dev *d, const char *name) {
+extern "C" void nck_timer_begin(nck_dev *d, const char *name, double flops, double bytes) {
     nck_timer *t = d->timer;
     if (!t || t->open >= 0) return;  // nested scopes: the outer one times them all
     int id = -1;
@@ -61,9 +60,13 @@ extern "C" void nck_timer_begin(nck_dev *d, const char *name) {
     if (id < 0) {
         t->names.push_back(name);
         t->ms_by_name.push_back(0);
+        t->flops_by_name.push_back(0);
+        t->bytes_by_name.push_back(0);
         t->n_by_name.push_back(0);
         id = (int)t->names.size() - 1;
     }
+    t->flops_by_name[id] += flops;
+    t->bytes_by_name[id] += bytes;
     nck_timer::Rec r{id, take_event(t), take_event(t)};
     cudaEventRecord(r.a, NCK_STREAM(d));
     t->recs.push_back(r);
@@ -105,11 +108,41 @@ extern "C" int nck_timer_query(nck_dev *d, const char *prefix, double *ms, int64
     return 0;
 }
 
+extern "C" int nck_timer_work(nck_dev *d, const char *prefix, double *flops, double *bytes) {
+    nck_timer *t = d->timer;
+    *flops = 0;
+    *bytes = 0;
+    if (!t) return 5;
+    size_t lp = strlen(prefix);
+    for (size_t i = 0; i < t->names.size(); i++) {
+        if (strncmp(t->names[i].c_str(), prefix, lp) != 0) continue;
+        *flops += t->flops_by_name[i];
+        *bytes += t->bytes_by_name[i];
+    }
+    return 0;
+}
+
+extern "C" int nck_timer_entry(nck_dev *d, int i, const char **name, double *ms, int64_t *count, double *flops,
+                               double *bytes) {
+    nck_timer *t = d->timer;
+    if (!t) return 0;
+    settle(t);
+    if (i < 0 || i >= (int)t->names.size()) return 0;
+    *name = t->names[i].c_str();
+    *ms = t->ms_by_name[i];
+    *count = t->n_by_name[i];
+    *flops = t->flops_by_name[i];
+    *bytes = t->bytes_by_name[i];
+    return 1;
+}
+
 extern "C" void nck_timer_reset(nck_dev *d) {
     nck_timer *t = d->timer;
     if (!t) return;
     settle(t);
     for (auto &v : t->ms_by_name) v = 0;
+    for (auto &v : t->flops_by_name) v = 0;
+    for (auto &v : t->bytes_by_name) v = 0;
     for (auto &v : t->n_by_name) v = 0;
 }
 

@@ -55,7 +55,7 @@ __global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y
 }
 
 extern "C" void nck_softmax_fwd(nck_dev *d, const float *x, float *y, int64_t rows, int64_t C, int log_form) {
-    Scope sc(d, log_form ? "log_softmax" : "softmax");
+    Scope sc(d, log_form ? "log_softmax" : "softmax", 0.0, 8.0 * rows * C);
     k_softmax_fwd<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, rows, C, log_form);
     NCK_LAUNCHED(d, 1);
 }
@@ -82,7 +82,7 @@ __global__ void k_softmax_bwd(const float *__restrict__ y, const float *__restri
 
 extern "C" void nck_softmax_bwd(nck_dev *d, const float *y, const float *g, float *gi, int64_t rows, int64_t C,
                                 int log_form) {
-    Scope sc(d, log_form ? "log_softmax_bwd" : "softmax_bwd");
+    Scope sc(d, log_form ? "log_softmax_bwd" : "softmax_bwd", 0.0, 16.0 * rows * C);
     k_softmax_bwd<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(y, g, gi, rows, C, log_form);
     NCK_LAUNCHED(d, 1);
 }
@@ -136,7 +136,7 @@ __global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict
 
 extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t *lab, float *prob, float *loss,
                                       int64_t N, int64_t C) {
-    Scope sc(d, "cross_entropy");
+    Scope sc(d, "cross_entropy", 0.0, 8.0 * N * C + 4.0 * N);
     float *terms = (float *)d->scratch;
     if (N > 0) k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status);
     k_loss_combine<<<1, kThreads, 0, NCK_STREAM(d)>>>(terms, N, loss, 1);
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, con
 extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits,
                                 int64_t n, float p) {
     if (n <= 0) return;
-    Scope sc(d, "dropout");
+    Scope sc(d, "dropout", 0.0, 8.0 * n + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
     k_dropout_fwd<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(s0, x, y, bits, n, p);
@@ -327,7 +327,7 @@ __global__ void k_dropout_bwd(const float *__restrict__ g, const uint32_t *__res
 
 extern "C" void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p) {
     if (n <= 0) return;
-    Scope sc(d, "dropout_bwd");
+    Scope sc(d, "dropout_bwd", 0.0, 12.0 * n + n / 8.0);
     k_dropout_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, bits, gi, n, p);
     NCK_LAUNCHED(d, 1);
 }
@@ -425,7 +425,7 @@ static int norm_threads(int64_t S) { return S >= 1024 ? 256 : S >= 256 ? 128 : 6
 extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                                  float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
                                  float eps) {
-    Scope sc(d, "bn_fwd");
+    Scope sc(d, "bn_fwd", 0.0, 8.0 * N * C * S);
     int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
@@ -506,7 +506,7 @@ __global__ void k_bn_bwd_dx(const float *__restrict__ x, const float *__restrict
 extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean,
                            const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
                            int training) {
-    Scope sc(d, "bn_bwd");
+    Scope sc(d, "bn_bwd", 0.0, (gx ? 16.0 : 8.0) * N * C * S);
     int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
@@ -556,7 +556,7 @@ __global__ void k_ln_fwd(const float *__restrict__ x, const float *__restrict__ 
 
 extern "C" void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats,
                            int64_t R, int64_t D, float eps) {
-    Scope sc(d, "ln_fwd");
+    Scope sc(d, "ln_fwd", 0.0, 8.0 * R * D);
     k_ln_fwd<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, D, eps);
     NCK_LAUNCHED(d, 1);
 }
@@ -620,7 +620,7 @@ __global__ void k_ln_bwd_wb_combine(const float *__restrict__ part, int splits, 
 
 extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
                            float *gw, float *gb, int64_t R, int64_t D) {
-    Scope sc(d, "ln_bwd");
+    Scope sc(d, "ln_bwd", 0.0, (gx ? 16.0 : 8.0) * R * D);
     int launched = 0;
     if (gx) {
         k_ln_bwd_dx<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, R, D);

@@ -69,7 +69,11 @@ __global__ void k_optim(nck_opt_hyper h, SegTable t) {
 }  // namespace
 
 extern "C" void nck_optim_step(nck_dev *d, const nck_opt_hyper *h, const nck_param_seg *segs, int nseg) {
-    Scope sc(d, "optim");
+    int64_t total = 0;
+    for (int i = 0; i < nseg; i++) total += segs[i].n;
+    /* Adam/AdamW: read w, g, m, v and write w, m, v (28 bytes per parameter); SGD/RMSprop less */
+    double per = h->kind == NCK_OPT_ADAM || h->kind == NCK_OPT_ADAMW ? 28.0 : 20.0;
+    Scope sc(d, "optim", 0.0, per * total);
     for (int s0 = 0; s0 < nseg; s0 += kMaxSeg) {
         SegTable t;
         t.n = nseg - s0 < kMaxSeg ? nseg - s0 : kMaxSeg;

@@ -32,7 +32,7 @@ __global__ void k_quantize_rows(const float *__restrict__ x, int8_t *__restrict_
 
 extern "C" void nck_quantize_rows(nck_dev *d, const float *x, int8_t *q, float *scale, int64_t rows, int64_t cols) {
     if (rows <= 0) return;
-    Scope sc(d, "quantize_rows");
+    Scope sc(d, "quantize_rows", 0.0, 5.0 * rows * cols + 4.0 * rows);
     k_quantize_rows<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, q, scale, rows, cols);
     NCK_LAUNCHED(d, 1);
 }
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(256) k_qgemm(const int8_t *__restrict__ A, con
 extern "C" void nck_qlinear(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
                             const float *b, float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out) {
     if (M <= 0 || N <= 0) return;
-    Scope sc(d, "qgemm_i8");
+    Scope sc(d, "qgemm_i8", 2.0 * M * N * K, (double)M * K + (double)N * K + 4.0 * M * N);
     int vec = K % 16 == 0 && (((uintptr_t)xq | (uintptr_t)wq) & 15) == 0;
     dim3 grid((unsigned)((N + QBN - 1) / QBN), (unsigned)((M + QBM - 1) / QBM));
     k_qgemm<<<grid, 256, 0, NCK_STREAM(d)>>>(xq, wq, xs, ws, b, y, acc_out, M, N, K, vec);

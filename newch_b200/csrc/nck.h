@@ -37,10 +37,16 @@ enum { NCK_GEMM_FFMA = 0, NCK_GEMM_TF32 = 1, NCK_GEMM_3XTF32 = 2 };
 
 /* ---- timing (bench instrumentation) ------------------------------------------------------ */
 void nck_timer_enable(nck_dev *d, int on);
-void nck_timer_begin(nck_dev *d, const char *name);
+/* flops / bytes: the algorithmic work of the launches in this scope (0 when not accounted) */
+void nck_timer_begin(nck_dev *d, const char *name, double flops, double bytes);
 void nck_timer_end(nck_dev *d);
 /* total milliseconds and launch count for kernels whose name starts with `prefix` ("" = all) */
 int nck_timer_query(nck_dev *d, const char *prefix, double *ms, int64_t *count);
+/* algorithmic work recorded for those kernels */
+int nck_timer_work(nck_dev *d, const char *prefix, double *flops, double *bytes);
+/* name, total ms, launches, flops, bytes of timed kernel class i (0 .. n-1); returns 0 past the end */
+int nck_timer_entry(nck_dev *d, int i, const char **name, double *ms, int64_t *count, double *flops,
+                    double *bytes);
 void nck_timer_reset(nck_dev *d);
 
 /* ---- memory helpers ---------------------------------------------------------------------- */

@@ -89,10 +89,11 @@ class Replayer:
     """Executes trace calls on `lib`. `seed_offset` regenerates synthetic inputs with another seed
     (per-rank data shards); `check` raises when a call's success differs from the recording."""
 
-    def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True):
+    def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True, pinned: bool = False):
         self.lib = lib
         self.trace = trace
         self.check = check
+        self.pinned = pinned  # host inputs in page-locked memory (as a data loader would stage them)
         self.h: dict = {}
         self.items: list = []    # (call index, value) of nc_item results
         self.outputs: list = []  # (call index, bytes) of nc_copy_to results
@@ -107,6 +108,12 @@ class Replayer:
         arr = self._blobs.get(bid)
         if arr is None:
             arr = self.trace.blob(bid, self.seed_offset)
+            if self.pinned:
+                import torch  # page-locked host allocation only
+                t = torch.empty(max(arr.size, 1), dtype=torch.uint8, pin_memory=True)
+                t.numpy()[: arr.size] = arr
+                self._keep.append(t)
+                arr = t.numpy()
             self._blobs[bid] = arr
         return arr.ctypes.data
 
