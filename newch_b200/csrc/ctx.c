@@ -41,8 +41,11 @@ int nc__sync(nc_ctx *ctx) {
     int code = *(volatile int *)ctx->dev.status_host;
     if (code != NCK_OK) {
         *(volatile int *)ctx->dev.status_host = NCK_OK;
-        nc__error(ctx, NC_ERR_ARG, code == NCK_ERR_LABEL ? "a label is outside [0, C) (found on the device)"
-                                                         : "an index is out of range (found on the device)");
+        if (code == NCK_ERR_LABEL) nc__error(ctx, NC_ERR_ARG, "a label is outside [0, C) (found on the device)");
+        else if (code == NCK_ERR_INDEX) nc__error(ctx, NC_ERR_ARG, "an index is out of range (found on the device)");
+        else if (code == NCK_ERR_PIPELINE)
+            nc__error(ctx, NC_ERR_STATE, "a tensor-core pipeline wait timed out (kernel gave up, results invalid)");
+        else nc__error(ctx, NC_ERR_STATE, "a kernel failed to launch");
         return 0;
     }
     return ctx->status == NC_OK;
@@ -319,13 +322,17 @@ static uint64_t splitmix64(uint64_t *x) {
     return z ^ (z >> 31);
 }
 
+/* FP32 contraction mode. Default 3xTF32 on tcgen05 (hi*hi + hi*lo + lo*hi with fp32 accumulation:
+ * fp32-class results at tensor-core speed); NC_GEMM=tf32 trades accuracy (rel ~1e-3) for a third of
+ * the MMAs; NC_GEMM=ffma (and force_reference) selects the CUDA-core kernel whose per-element
+ * summation order is fixed. */
 static int gemm_mode_from_env(int force_reference) {
     if (force_reference) return NCK_GEMM_FFMA;
     const char *m = getenv("NC_GEMM");
-    if (!m || !*m) return NCK_GEMM_FFMA;
+    if (!m || !*m) return NCK_GEMM_3XTF32;
     if (!strcmp(m, "tf32")) return NCK_GEMM_TF32;
-    if (!strcmp(m, "3xtf32")) return NCK_GEMM_3XTF32;
-    return NCK_GEMM_FFMA;
+    if (!strcmp(m, "ffma")) return NCK_GEMM_FFMA;
+    return NCK_GEMM_3XTF32;
 }
 
 int nc__dp_env_init(nc_ctx *ctx); /* dp.c */

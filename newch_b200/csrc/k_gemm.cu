@@ -208,6 +208,7 @@ __global__ void k_sgemm_combine(GemmP p, int64_t nout) {
 
 extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (a->M <= 0 || a->N <= 0 || a->batch <= 0) return;
+    if (d->gemm_mode != NCK_GEMM_FFMA && nck_gemm_tc(d, a)) return;
     double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
     double nC = (a->reduce_batch ? 1.0 : (double)a->batch) * (a->beta != 0.0f ? 2.0 : 1.0);
     Scope sc(d, "gemm_f32", 2.0 * a->M * a->N * a->K * a->batch,

@@ -31,7 +31,7 @@ typedef struct nck_dev {
 } nck_dev;
 
 /* kernel-detected error codes written to *status (first one wins) */
-enum { NCK_OK = 0, NCK_ERR_INDEX = 1, NCK_ERR_LABEL = 2 };
+enum { NCK_OK = 0, NCK_ERR_INDEX = 1, NCK_ERR_LABEL = 2, NCK_ERR_PIPELINE = 3, NCK_ERR_LAUNCH = 4 };
 
 enum { NCK_GEMM_FFMA = 0, NCK_GEMM_TF32 = 1, NCK_GEMM_3XTF32 = 2 };
 
@@ -193,6 +193,9 @@ typedef struct {
     int bias_per_row;
 } nck_gemm_args;
 void nck_gemm(nck_dev *d, const nck_gemm_args *a);
+/* tensor-core path (tcgen05 kind::tf32 via TMA); returns 0 when the operands do not meet its
+ * alignment rules, leaving the GEMM to the caller */
+int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a);
 
 /* ---- optimizers -------------------------------------------------------------------------------- */
 typedef struct {

@@ -3,7 +3,8 @@ on the B200 engine and on the reference engine (CPU), step by step.
 
 Checked: every nc_item result (the per-step losses, BatchNorm's num_batches_tracked), and the copied-out
 results after training (final parameters, or the int8 model's logits). Losses must agree to 1e-5
-relative. Final parameters after Adam are compared normwise against the reference with a
+relative on the CUDA-core GEMM path (NC_GEMM=ffma) and to 1e-3 relative on the tensor-core paths
+(3xTF32, the default, and TF32), whose contractions round differently from the reference's loops. Final parameters after Adam are compared normwise against the reference with a
 tolerance for Adam's normalisation: for a parameter whose true gradient is zero (a conv bias in front
 of BatchNorm, the key bias of attention), the update lr * m / sqrt(v) is the sign of rounding noise and
 can differ by up to 2 * lr per step between any two correct implementations; every other parameter
@@ -29,7 +30,16 @@ def run(lib, name):
     return t, r
 
 
-def compare(name):
+LOSS_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 1e-3}
+
+
+@pytest.fixture(params=["ffma", "3xtf32", "tf32"])
+def mode(request, monkeypatch):
+    monkeypatch.setenv("NC_GEMM", request.param)
+    return request.param
+
+
+def compare(name, mode="ffma"):
     ref = capi.load(REF_LIB)
     gpu = capi.load_b200()
     t, rg = run(gpu, name)
@@ -38,7 +48,7 @@ def compare(name):
     gi, ri = [v for _, v in rg.items], [v for _, v in rr.items]
     assert len(gi) == len(ri)
     for a, b in zip(gi, ri):
-        assert a == pytest.approx(b, rel=1e-5, abs=1e-6)
+        assert a == pytest.approx(b, rel=LOSS_TOL[mode], abs=1e-6), (mode, gi, ri)
     assert len(rg.outputs) == len(rr.outputs)
     base = name.replace("_small", "")
     steps = len(t.steps())
@@ -56,17 +66,18 @@ def compare(name):
 
 
 @pytest.mark.parametrize("name", ["cfg1_small", "cfg2_small", "cfg3_small", "cfg4_small", "cfg5_small"])
-def test_small_configs(name):
-    compare(name)
+def test_small_configs(name, mode):
+    compare(name, mode)
 
 
 @pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg2_stream", "cfg3", "cfg4", "cfg5"])
-def test_full_size_configs(name):
-    compare(name)
+def test_full_size_configs(name, mode):
+    compare(name, mode)
 
 
-def test_full_size_against_recorded_losses():
+def test_full_size_against_recorded_losses(monkeypatch):
     """The B200 replay of config 2 reproduces the losses newch itself logged when the trace was made."""
+    monkeypatch.setenv("NC_GEMM", "ffma")
     gpu = capi.load_b200()
     t, r = run(gpu, "cfg2")
     got = [v for _, v in r.items]
