@@ -12,11 +12,58 @@
 #include "nc_internal.h"
 
 #include <cuda_runtime_api.h>
+#include <dlfcn.h>
 #include <nccl.h>
+#include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <time.h>
 #include <unistd.h>
+
+/* NCCL is opened on first use, not linked: a process that never joins a data-parallel group never
+ * loads it, and a process that also hosts another NCCL user (a framework that bundles its own
+ * libnccl.so.2) shares whichever copy that user loaded first instead of pinning an older one. */
+static struct {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *);
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
+    ncclResult_t (*CommAbort)(ncclComm_t);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    const char *(*GetErrorString)(ncclResult_t);
+    int ok;
+} nccl_fn;
+static pthread_once_t nccl_once = PTHREAD_ONCE_INIT;
+
+static void nccl_open(void) {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return;
+#define NC_NCCL_SYM(field, name) *(void **)&nccl_fn.field = dlsym(h, name)
+    NC_NCCL_SYM(GetUniqueId, "ncclGetUniqueId");
+    NC_NCCL_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+    NC_NCCL_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+    NC_NCCL_SYM(CommAbort, "ncclCommAbort");
+    NC_NCCL_SYM(CommDestroy, "ncclCommDestroy");
+    NC_NCCL_SYM(AllReduce, "ncclAllReduce");
+    NC_NCCL_SYM(GetErrorString, "ncclGetErrorString");
+#undef NC_NCCL_SYM
+    nccl_fn.ok = nccl_fn.GetUniqueId && nccl_fn.CommInitRankConfig && nccl_fn.CommGetAsyncError &&
+                 nccl_fn.CommAbort && nccl_fn.CommDestroy && nccl_fn.AllReduce && nccl_fn.GetErrorString;
+}
+
+static int nccl_loaded(void) {
+    pthread_once(&nccl_once, nccl_open);
+    return nccl_fn.ok;
+}
+
+#define ncclGetUniqueId(...) (nccl_loaded() ? nccl_fn.GetUniqueId(__VA_ARGS__) : ncclSystemError)
+#define ncclCommInitRankConfig(...) (nccl_loaded() ? nccl_fn.CommInitRankConfig(__VA_ARGS__) : ncclSystemError)
+#define ncclCommGetAsyncError(...) (nccl_loaded() ? nccl_fn.CommGetAsyncError(__VA_ARGS__) : ncclSystemError)
+#define ncclCommAbort(...) (nccl_loaded() ? nccl_fn.CommAbort(__VA_ARGS__) : ncclSystemError)
+#define ncclCommDestroy(...) (nccl_loaded() ? nccl_fn.CommDestroy(__VA_ARGS__) : ncclSystemError)
+#define ncclAllReduce(...) (nccl_loaded() ? nccl_fn.AllReduce(__VA_ARGS__) : ncclSystemError)
+#define ncclGetErrorString(r) (nccl_loaded() ? nccl_fn.GetErrorString(r) : "libnccl.so.2 could not be loaded")
 
 static double now_s(void) {
     struct timespec ts;

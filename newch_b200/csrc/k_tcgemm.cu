@@ -1,16 +1,26 @@
 // FP32-input GEMM on the 5th-generation tensor cores: tcgen05.mma kind::tf32, operands staged in
-// shared memory by TMA (128-byte swizzle, no multicast), accumulator in tensor memory, one CTA per
-// 128 x 128 output tile.
+// shared memory by TMA (128-byte swizzle, no multicast), accumulators in tensor memory.
 //
-// Roles in a 128-thread CTA: thread 0 issues the TMA loads of a 4-stage ring (3 in 3xTF32 mode), thread 32 issues the
-// MMAs (4 x K=8 per 32-deep stage) and commits each stage back to the loader, then all four warps
-// read the accumulator rows out of TMEM (warp w owns lanes 32w .. 32w+31 = tile rows) and apply the
-// epilogue C = alpha * acc + bias + beta * C, or store raw partial tiles when the reduction range is
-// split. In 3xTF32 mode two more warps split every staged fp32 tile into a TF32-exact high part and
-// the remainder, and the MMA thread accumulates hi*hi + hi*lo + lo*hi: close to fp32 accuracy.
+// Orientation. The kernel computes D[i][j] = sum_k P[i][k] * Q[j][k] with the 128 rows i of a tile
+// on the 128 TMEM lanes, and stores D[i][j] at out[j * ldo + i]. The host passes P = op(B)^T and
+// Q = op(A), so i runs along C's contiguous dimension (n) and every warp store of the epilogue
+// writes 32 consecutive floats. The tile width BN (Q rows per tile) is chosen per GEMM among
+// 32, 64, 96, 128 to fit M (64 output channels use a 64-wide tile, 288 a 96-wide one).
 //
-// Every wait on an mbarrier gives up after 2 s of device time and records an error in the context's
-// status word, so a broken pipeline cannot hang the GPU.
+// Persistent CTAs, one per SM, walk a static list of work units (tile, output batch, reduction slice)
+// with warp-specialised roles:
+//   warps 0-3  epilogue: tcgen05.ld of the accumulator rows (warp w owns lanes 32w..32w+31), alpha /
+//              bias / beta, coalesced stores (or raw partial tiles when the reduction is split)
+//   warp 4     TMA loader (one thread) feeding an S-stage mbarrier ring, K in steps of 32 (128 B)
+//   warp 5     MMA issuer (one thread): 4 MMAs of K = 8 per stage, commits each stage back to the
+//              loader and each finished tile to the epilogue
+//   warps 6-7  3xTF32 only: split every staged fp32 tile into its TF32 head (top 19 bits) and the
+//              remainder; the MMA thread then accumulates head*head + head*rest + rest*head
+// Two accumulators in TMEM let the epilogue of one tile overlap the main loop of the next.
+//
+// Every mbarrier wait gives up after 2 s of device time and records an error in the status word; a
+// role that gave up stops, the loader waits (bounded) for its copies in flight, the MMA thread for
+// its MMAs, and the CTA frees its TMEM and returns.
 #include <cuda.h>
 #include <string.h>
 
@@ -18,28 +28,31 @@
 
 using namespace nck;
 
-
 namespace {
 
-constexpr int TM = 128, TN = 128, TK = 32;  // tile; TK fp32 = 128 bytes = one swizzle row
-constexpr int kTileBytes = TM * TK * 4;      // 16 KiB per operand per stage
-constexpr uint64_t kWaitNs = 2000000000ull;   // an mbarrier wait gives up after 2 s of device time
-constexpr int kErrPipeline = 3;              // status code for a wait that gave up
+constexpr int TM = 128, TK = 32;          // tile rows (TMEM lanes); K per stage (32 fp32 = 128 B)
+constexpr int kMaxBN = 128;               // widest tile (Q rows per tile)
+constexpr int kStageA = TM * TK;          // floats per P stage (16 KiB)
+constexpr int kStageB = kMaxBN * TK;      // floats per Q stage (16 KiB)
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr int kErrPipeline = 3;
+constexpr int kEpiWarps = 4, kLoadWarp = 4, kMmaWarp = 5, kSplitWarp0 = 6;
 
 struct TcParams {
-    int64_t M, N, K;
+    int64_t R, Cq, K;      // P rows (original N), Q rows (original M), depth
+    int BN;                // tile width along Q
     float alpha, beta;
     float *C;
     int64_t ldc, sC;
     const float *bias;
-    int bias_row;
+    int bias_q;            // bias indexed by the Q row (original row m); else by the P row (column n)
     int64_t batch;
-    int reduce, splits;
-    int64_t bper, kper;
-    float *part;
-    int a_mn, b_mn;      // operand stored MN-major (transposed relative to K-major)
-    int a_bat, b_bat;    // operand has a batch coordinate (3-D tensor map)
-    int three;           // 3xTF32
+    int reduce, splits;    // reduce: the batch is summed; splits: slices of the reduction range
+    int64_t bper, kper;    // batches per slice (reduce), K per slice (otherwise)
+    int64_t tiles_r, tiles_q, units;
+    float *part;           // partial tiles [unit slice][Cq][R] when splits > 1
+    int p_mn, q_mn;        // operand stored MN-major
+    int p_bat, q_bat;      // operand has a batch coordinate (3-D tensor map)
     int *status;
 };
 
@@ -63,7 +76,7 @@ __device__ __forceinline__ uint64_t now_ns() {
     return t;
 }
 
-// returns false when the bounded wait gave up (the error goes to the status word)
+// false when the bounded wait gave up (the error goes to the status word)
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status) {
     uint32_t addr = smem_u32(bar);
     uint64_t start = 0;
@@ -115,15 +128,24 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo_bytes, uin
     return d;
 }
 
-// instruction descriptor: D f32, A/B tf32, dense, M = 128, N = 128
-__device__ __forceinline__ uint32_t idesc_tf32(int a_mn, int b_mn) {
+// K-offset descriptor of one stage buffer for the k-th 8-deep MMA step
+__device__ __forceinline__ uint64_t stage_desc(uint32_t base, int mn, int k) {
+    // K-major: 128 B rows of 32 K values, 8-row atoms 1024 B apart; step k moves 32 B along the row
+    if (!mn) return sdesc(base + k * 32, 16, 1024, 2);
+    // MN-major: 128 B rows of 32 M/N values, one row per K; 4-row atoms 512 B apart (SBO), 32-wide
+    // blocks 4 KiB apart (LBO); step k moves 8 rows
+    return sdesc(base + k * 1024, 4096, 512, 1);
+}
+
+// instruction descriptor: D f32, A/B tf32, dense, M = 128, N = bn
+__device__ __forceinline__ uint32_t idesc_tf32(int a_mn, int b_mn, int bn) {
     uint32_t d = 0;
     d |= 1u << 4;               // D format F32
     d |= 2u << 7;               // A format TF32
     d |= 2u << 10;              // B format TF32
     d |= (uint32_t)a_mn << 15;  // A major
     d |= (uint32_t)b_mn << 16;  // B major
-    d |= (uint32_t)(TN >> 3) << 17;
+    d |= (uint32_t)(bn >> 3) << 17;
     d |= (uint32_t)(TM >> 4) << 24;
     return d;
 }
@@ -141,211 +163,254 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-// K-offset descriptors of one stage buffer for the k-th 8-deep MMA step
-__device__ __forceinline__ uint64_t stage_desc(uint32_t base, int mn, int k) {
-    // K-major: 128 B rows of 32 K values, 8-row atoms 1024 B apart; step k moves 32 B along the row
-    if (!mn) return sdesc(base + k * 32, 16, 1024, 2);
-    // MN-major: 128 B rows of 32 M/N values, one row per K; 4-row atoms 512 B apart (SBO), 32-wide
-    // blocks 4 KiB apart (LBO); step k moves 8 rows
-    return sdesc(base + k * 1024, 4096, 512, 1);
-}
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
 template <int S>
 struct Smem {
-    float a[S][TM * TK];
-    float b[S][TN * TK];
-    uint64_t full[S], empty[S], ready[S], lo_free[S], accum;
+    float a[S][kStageA];
+    float b[S][kStageB];
+    uint64_t full[S], empty[S], ready[S];
+    uint64_t tfull[2], tempty[2], mma_done;
     uint32_t tmem;
 };
 
 template <int S>
 struct SmemLo {
-    float a[S][TM * TK];
-    float b[S][TN * TK];
+    float a[S][kStageA];
+    float b[S][kStageB];
 };
 
-__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+// A work unit: tile (tr, tq), output batch ob (or 0 when the batch is summed), reduction slice sl.
+struct Unit {
+    int64_t r0, q0, ob, sl, b0, b1, k0, k1, steps;
+};
 
-// S pipeline stages; THREE selects 3xTF32 (two extra warps split the staged tiles)
+__device__ __forceinline__ Unit unit_of(const TcParams &p, int64_t u) {
+    Unit w;
+    int64_t tiles = p.tiles_r * p.tiles_q;
+    int64_t t = u % tiles, z = u / tiles;
+    w.r0 = (t % p.tiles_r) * TM;
+    w.q0 = (t / p.tiles_r) * p.BN;
+    if (p.reduce) {
+        w.ob = 0, w.sl = z;
+        w.b0 = z * p.bper;
+        w.b1 = w.b0 + p.bper < p.batch ? w.b0 + p.bper : p.batch;
+        w.k0 = 0, w.k1 = p.K;
+    } else {
+        w.ob = z / p.splits, w.sl = z % p.splits;
+        w.b0 = w.ob, w.b1 = w.ob + 1;
+        w.k0 = w.sl * p.kper;
+        w.k1 = w.k0 + p.kper < p.K ? w.k0 + p.kper : p.K;
+    }
+    int64_t kt = (w.k1 - w.k0 + TK - 1) / TK;
+    w.steps = (w.b1 - w.b0) * kt;
+    return w;
+}
+
 template <int S, bool THREE>
-__global__ void __launch_bounds__(THREE ? 192 : 128, 1) k_tcgemm(const __grid_constant__ CUtensorMap tmA,
-                                                                 const __grid_constant__ CUtensorMap tmB, TcParams p) {
-    constexpr int kStages = S;
+__global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_constant__ CUtensorMap tmP,
+                                                                 const __grid_constant__ CUtensorMap tmQ, TcParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // 1024-byte alignment of the stage buffers (the swizzle pattern follows address bits)
     Smem<S> &s = *reinterpret_cast<Smem<S> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     SmemLo<S> *lo = THREE ? reinterpret_cast<SmemLo<S> *>(reinterpret_cast<unsigned char *>(&s) +
                                                           ((sizeof(Smem<S>) + 1023) & ~(size_t)1023))
                           : nullptr;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t n0 = (int64_t)blockIdx.x * TN, m0 = (int64_t)blockIdx.y * TM, z = blockIdx.z;
-
-    int64_t b0, b1, k0 = 0, k1 = p.K, ob;
-    if (p.reduce) {
-        b0 = z * p.bper;
-        b1 = b0 + p.bper < p.batch ? b0 + p.bper : p.batch;
-        ob = 0;
-    } else {
-        ob = z / p.splits;
-        int64_t sl = z % p.splits;
-        b0 = ob, b1 = ob + 1;
-        k0 = sl * p.kper;
-        k1 = k0 + p.kper < p.K ? k0 + p.kper : p.K;
-    }
-    const int64_t kt_n = (k1 - k0 + TK - 1) / TK;
-    const int64_t T = (b1 > b0 ? b1 - b0 : 0) * kt_n;
+    const int BN = p.BN;
+    const uint32_t tcols = BN * 2 <= 32 ? 32 : BN * 2 <= 64 ? 64 : BN * 2 <= 128 ? 128 : 256;
+    const uint32_t stage_bytes = (uint32_t)(TM + BN) * TK * 4;
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; i++) {
+        for (int i = 0; i < S; i++) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
-            mbar_init(&s.ready[i], 64);   // the two split warps (3xTF32)
-            mbar_init(&s.lo_free[i], 1);
+            mbar_init(&s.ready[i], 64);
         }
-        mbar_init(&s.accum, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s.tfull[i], 1);
+            mbar_init(&s.tempty[i], kEpiWarps);
+        }
+        mbar_init(&s.mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem)),
-                     "r"(TN));
+                     "r"(tcols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = s.tmem;
-    bool ok = true;
-    if (tid == 0) {
-    }
 
-    if (tid == 0) {
-        // ---- loader --------------------------------------------------------------------------
-        for (int64_t t = 0; t < T && ok; t++) {
-            int st = (int)(t % kStages);
-            uint32_t ph = (uint32_t)((t / kStages) & 1);
-            if (t >= kStages) ok = mbar_wait(&s.empty[st], ph ^ 1, p.status);
-            if (!ok) break;
-            int64_t b = b0 + t / kt_n;
-            int kk = (int)(k0 + (t % kt_n) * TK);
-            mbar_expect_tx(&s.full[st], 2 * kTileBytes);
-            if (!p.a_mn) {
-                if (p.a_bat) tma_3d(s.a[st], &tmA, kk, (int)m0, (int)b, &s.full[st]);
-                else tma_2d(s.a[st], &tmA, kk, (int)m0, &s.full[st]);
-            } else {
-                for (int j = 0; j < 4; j++) {
-                    if (p.a_bat) tma_3d(s.a[st] + j * 1024, &tmA, (int)m0 + 32 * j, kk, (int)b, &s.full[st]);
-                    else tma_2d(s.a[st] + j * 1024, &tmA, (int)m0 + 32 * j, kk, &s.full[st]);
+    if (warp == kLoadWarp) {
+        if (lane == 0) {
+            // ---- loader ------------------------------------------------------------------------------
+            int64_t it = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                Unit w = unit_of(p, u);
+                int64_t kt = (w.k1 - w.k0 + TK - 1) / TK;
+                for (int64_t t = 0; t < w.steps; t++, it++) {
+                    int st = (int)(it % S);
+                    uint32_t ph = (uint32_t)((it / S) & 1);
+                    if (it >= S && !(ok = mbar_wait(&s.empty[st], ph ^ 1, p.status))) break;
+                    int b = (int)(w.b0 + t / kt);
+                    int kk = (int)(w.k0 + (t % kt) * TK);
+                    mbar_expect_tx(&s.full[st], stage_bytes);
+                    if (!p.p_mn) {
+                        if (p.p_bat) tma_3d(s.a[st], &tmP, kk, (int)w.r0, b, &s.full[st]);
+                        else tma_2d(s.a[st], &tmP, kk, (int)w.r0, &s.full[st]);
+                    } else {
+                        for (int j = 0; j < TM / 32; j++) {
+                            if (p.p_bat) tma_3d(s.a[st] + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, b, &s.full[st]);
+                            else tma_2d(s.a[st] + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, &s.full[st]);
+                        }
+                    }
+                    if (!p.q_mn) {
+                        if (p.q_bat) tma_3d(s.b[st], &tmQ, kk, (int)w.q0, b, &s.full[st]);
+                        else tma_2d(s.b[st], &tmQ, kk, (int)w.q0, &s.full[st]);
+                    } else {
+                        for (int j = 0; j < BN / 32; j++) {
+                            if (p.q_bat) tma_3d(s.b[st] + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, b, &s.full[st]);
+                            else tma_2d(s.b[st] + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
+                        }
+                    }
                 }
             }
-            if (!p.b_mn) {
-                if (p.b_bat) tma_3d(s.b[st], &tmB, kk, (int)n0, (int)b, &s.full[st]);
-                else tma_2d(s.b[st], &tmB, kk, (int)n0, &s.full[st]);
-            } else {
-                for (int j = 0; j < 4; j++) {
-                    if (p.b_bat) tma_3d(s.b[st] + j * 1024, &tmB, (int)n0 + 32 * j, kk, (int)b, &s.full[st]);
-                    else tma_2d(s.b[st] + j * 1024, &tmB, (int)n0 + 32 * j, kk, &s.full[st]);
+            // no copy may still be landing in shared memory when the CTA exits
+            int64_t first = it > S ? it - S : 0;
+            for (int64_t j = first; j < it; j++)
+                if (!mbar_wait(&s.full[j % S], (uint32_t)((j / S) & 1), p.status)) break;
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            // ---- MMA issuer ----------------------------------------------------------------------------
+            const uint32_t idesc = idesc_tf32(p.p_mn, p.q_mn, BN);
+            int64_t it = 0, local = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, local++) {
+                Unit w = unit_of(p, u);
+                int acc = (int)(local & 1);
+                if (local >= 2 && !(ok = mbar_wait(&s.tempty[acc], (uint32_t)(((local >> 1) & 1) ^ 1), p.status)))
+                    break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t d = tmem + (uint32_t)acc * (tcols / 2);
+                for (int64_t t = 0; t < w.steps; t++, it++) {
+                    int st = (int)(it % S);
+                    uint32_t ph = (uint32_t)((it / S) & 1);
+                    if (!(ok = mbar_wait(THREE ? &s.ready[st] : &s.full[st], ph, p.status))) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    uint32_t ab = smem_u32(s.a[st]), bb = smem_u32(s.b[st]);
+                    for (int k = 0; k < TK / 8; k++) {
+                        uint32_t accum = (t > 0 || k > 0) ? 1u : 0u;
+                        mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, accum);
+                        if (THREE) {
+                            uint32_t al = smem_u32(lo->a[st]), bl = smem_u32(lo->b[st]);
+                            mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bl, p.q_mn, k), idesc, 1u);
+                            mma_tf32(d, stage_desc(al, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, 1u);
+                        }
+                    }
+                    mma_commit(&s.empty[st]);  // the loader may refill this stage once these MMAs read it
                 }
+                if (ok) mma_commit(&s.tfull[acc]);
             }
+            // every MMA issued has completed before the CTA frees tensor memory
+            mma_commit(&s.mma_done);
+            mbar_wait(&s.mma_done, 0, p.status);
         }
-    } else if (tid == 32) {
-        // ---- MMA issuer -------------------------------------------------------------------------
-        const uint32_t idesc = idesc_tf32(p.a_mn, p.b_mn);
-        for (int64_t t = 0; t < T && ok; t++) {
-            int st = (int)(t % kStages);
-            uint32_t ph = (uint32_t)((t / kStages) & 1);
-            ok = mbar_wait(THREE ? &s.ready[st] : &s.full[st], ph, p.status);
-            if (!ok) break;
-            asm volatile("tcgen05.fence::after_thread_sync;");
-            uint32_t ab = smem_u32(s.a[st]), bb = smem_u32(s.b[st]);
-            for (int k = 0; k < TK / 8; k++) {
-                uint32_t acc = (t > 0 || k > 0) ? 1u : 0u;
-                mma_tf32(tmem, stage_desc(ab, p.a_mn, k), stage_desc(bb, p.b_mn, k), idesc, acc);
-                if (THREE) {
-                    uint32_t al = smem_u32(lo->a[st]), bl = smem_u32(lo->b[st]);
-                    mma_tf32(tmem, stage_desc(ab, p.a_mn, k), stage_desc(bl, p.b_mn, k), idesc, 1u);
-                    mma_tf32(tmem, stage_desc(al, p.a_mn, k), stage_desc(bb, p.b_mn, k), idesc, 1u);
+    } else if (THREE && warp >= kSplitWarp0) {
+        // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head -------------
+        const int t2 = tid - kSplitWarp0 * 32;  // 0 .. 63
+        const int nb = BN * TK / 4;
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+            Unit w = unit_of(p, u);
+            for (int64_t t = 0; t < w.steps; t++, it++) {
+                int st = (int)(it % S);
+                uint32_t ph = (uint32_t)((it / S) & 1);
+                if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
+                float4 *ah = reinterpret_cast<float4 *>(s.a[st]), *al = reinterpret_cast<float4 *>(lo->a[st]);
+                for (int i = t2; i < TM * TK / 4; i += 64) {
+                    float4 v = ah[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+                    ah[i] = h;
+                    al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
                 }
+                float4 *bh = reinterpret_cast<float4 *>(s.b[st]), *bl = reinterpret_cast<float4 *>(lo->b[st]);
+                for (int i = t2; i < nb; i += 64) {
+                    float4 v = bh[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+                    bh[i] = h;
+                    bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+                mbar_arrive(&s.ready[st]);
             }
-            mma_commit(&s.empty[st]);  // the loader may refill this stage once these MMAs have read it
-            if (THREE) mma_commit(&s.lo_free[st]);
         }
-        mma_commit(&s.accum);
-    } else if (THREE && warp >= 4) {
-        // ---- 3xTF32 split: hi = x with the low 13 mantissa bits cleared, lo = x - hi --------------
-        const int t2 = tid - 128;  // 0 .. 63
-        for (int64_t t = 0; t < T && ok; t++) {
-            int st = (int)(t % kStages);
-            uint32_t ph = (uint32_t)((t / kStages) & 1);
-            ok = mbar_wait(&s.full[st], ph, p.status);
-            if (ok && t >= kStages) ok = mbar_wait(&s.lo_free[st], ph ^ 1, p.status);
-            if (!ok) break;
-            float4 *ah = reinterpret_cast<float4 *>(s.a[st]), *bh = reinterpret_cast<float4 *>(s.b[st]);
-            float4 *al = reinterpret_cast<float4 *>(lo->a[st]), *bl = reinterpret_cast<float4 *>(lo->b[st]);
-            for (int i = t2; i < TM * TK / 4; i += 64) {
-                float4 v = ah[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                ah[i] = h;
-                al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-                float4 u = bh[i], g = make_float4(tf32_hi(u.x), tf32_hi(u.y), tf32_hi(u.z), tf32_hi(u.w));
-                bh[i] = g;
-                bl[i] = make_float4(u.x - g.x, u.y - g.y, u.z - g.z, u.w - g.w);
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
-            mbar_arrive(&s.ready[st]);
-        }
-    }
-
-    // ---- epilogue: warps 0-3, row m0 + 32 * warp + lane -----------------------------------------------
-    if (warp < 4) {
-        __syncwarp();
-        bool have = mbar_wait(&s.accum, 0, p.status);
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const int64_t m = m0 + warp * 32 + lane;
+    } else if (warp < kEpiWarps) {
+        // ---- epilogue: accumulator lane i = P row r0 + 32 * warp + lane ---------------------------------
+        int64_t local = 0;
         const bool partial = p.splits > 1;
-        float *out = partial ? p.part + z * p.M * p.N : p.C + ob * p.sC;
-        const int64_t ldo = partial ? p.N : p.ldc;
-        for (int c0 = 0; c0 < TN; c0 += 16) {
-            uint32_t r[16];
-            uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                "[%16];"
-                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                  "=r"(r[15])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (!have || m >= p.M) continue;
-            float *row = out + m * ldo;
-            for (int j = 0; j < 16; j++) {
-                int64_t n = n0 + c0 + j;
-                if (n >= p.N) break;
-                float acc = __uint_as_float(r[j]);
-                if (partial) {
-                    row[n] = acc;
-                } else {
-                    float v = p.alpha * acc;
-                    if (p.bias) v = v + (p.bias_row ? p.bias[m] : p.bias[n]);
-                    if (p.beta != 0.0f) v = fmaf(p.beta, row[n], v);
-                    row[n] = v;
+        for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x, local++) {
+            Unit w = unit_of(p, u);
+            int acc = (int)(local & 1);
+            if (!mbar_wait(&s.tfull[acc], (uint32_t)((local >> 1) & 1), p.status)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int64_t i = w.r0 + warp * 32 + lane;
+            // partial tiles: slice-major [ob][slice][Cq][R] (ob = 0 when the batch is summed)
+            float *out = partial ? p.part + (w.ob * p.splits + w.sl) * p.R * p.Cq : p.C + w.ob * p.sC;
+            const int64_t ldo = partial ? p.R : p.ldc;
+            const bool live = i < p.R;
+            const float bias_i = (!partial && p.bias && !p.bias_q && live) ? p.bias[i] : 0.0f;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)acc * (tcols / 2) + (uint32_t)c0;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                      "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                      "=r"(r[14]), "=r"(r[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (!live) continue;
+#pragma unroll
+                for (int jj = 0; jj < 16; jj++) {
+                    int64_t j = w.q0 + c0 + jj;
+                    if (j >= p.Cq) break;
+                    float a = __uint_as_float(r[jj]);
+                    float *dst = out + j * ldo + i;
+                    if (partial) {
+                        *dst = a;
+                    } else {
+                        float v = p.alpha * a;
+                        if (p.bias) v = v + (p.bias_q ? p.bias[j] : bias_i);
+                        if (p.beta != 0.0f) v = fmaf(p.beta, *dst, v);
+                        *dst = v;
+                    }
                 }
             }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.tempty[acc]);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TN));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
 }
 
+// C = alpha * (sum of the slices' partial tiles) + bias + beta * C, slices added in a fixed order
 __global__ void k_tc_combine(TcParams p, int64_t nout) {
-    int64_t MN = p.M * p.N, total = nout * MN;
+    int64_t MN = p.R * p.Cq, total = nout * MN;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ob = t / MN, r = t - ob * MN, m = r / p.N, n = r - m * p.N;
+        int64_t ob = t / MN, r = t - ob * MN, m = r / p.R, n = r - m * p.R;
         const float *src = p.part + ob * p.splits * MN + r;
         float s = 0.0f;
         for (int k = 0; k < p.splits; k++) s += src[k * MN];
         float *c = p.C + ob * p.sC + m * p.ldc + n;
         float v = p.alpha * s;
-        if (p.bias) v = v + (p.bias_row ? p.bias[m] : p.bias[n]);
+        if (p.bias) v = v + (p.bias_q ? p.bias[m] : p.bias[n]);
         if (p.beta != 0.0f) v = fmaf(p.beta, *c, v);
         *c = v;
     }
@@ -372,7 +437,7 @@ EncodeTiled encoder() {
     return fn;
 }
 
-// operand view: `inner` elements contiguous (lda stride between outer rows), optional batch dim
+// operand view: `inner` elements contiguous (ld elements between outer rows), optional batch dim
 bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
               int64_t bstride, int box_inner, int box_outer, bool mn_major) {
     EncodeTiled enc = encoder();
@@ -385,8 +450,7 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, (void *)base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -396,7 +460,31 @@ size_t smem_bytes() {
     return 1024 + base + (THREE ? sizeof(SmemLo<S>) : 0);
 }
 
-constexpr int kStagesTf32 = 4, kStages3x = 3;
+constexpr int kStagesTf32 = 6, kStages3x = 3;
+
+// tile width along Q: the fewest wasted columns, counting ~32 columns of per-tile overhead
+int pick_bn(int64_t cq) {
+    int best = 128;
+    int64_t best_cost = INT64_MAX;
+    for (int bn = 32; bn <= kMaxBN; bn += 32) {
+        int64_t tiles = (cq + bn - 1) / bn, cost = tiles * (bn + 32);
+        if (cost < best_cost) best_cost = cost, best = bn;
+    }
+    return best;
+}
+
+template <int S, bool THREE>
+bool set_smem_attr() {
+    static int done = 0;
+    if (done) return true;
+    if (cudaFuncSetAttribute(k_tcgemm<S, THREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bytes<S, THREE>()) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    done = 1;
+    return true;
+}
 
 }  // namespace
 
@@ -405,39 +493,43 @@ constexpr int kStagesTf32 = 4, kStages3x = 3;
 extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
     if (a->M <= 0 || a->N <= 0 || a->batch <= 0 || a->K <= 0) return 0;
     if (a->M > INT32_MAX || a->N > INT32_MAX || a->K > INT32_MAX || a->batch > INT32_MAX) return 0;
-    int three = d->gemm_mode == NCK_GEMM_3XTF32;
-    int a_mn = a->ta, b_mn = !a->tb;
-    int a_bat = a->batch > 1 && a->sA != 0, b_bat = a->batch > 1 && a->sB != 0;
+    const int three = d->gemm_mode == NCK_GEMM_3XTF32;
+    // P = op(B)^T (rows n), Q = op(A) (rows m)
+    const int p_mn = !a->tb, q_mn = a->ta;
+    const int p_bat = a->batch > 1 && a->sB != 0, q_bat = a->batch > 1 && a->sA != 0;
     if ((uintptr_t)a->A % 16 || (uintptr_t)a->B % 16 || a->lda % 4 || a->ldb % 4) return 0;
-    if ((a_bat && a->sA % 4) || (b_bat && a->sB % 4)) return 0;
-    CUtensorMap ma, mb;
-    // A: K-major [M][K] (ta = 0) or MN-major [K][M]
-    bool okA = !a_mn ? make_map(&ma, a->A, a->K, a->M, a->lda, a_bat ? a->batch : 1, a->sA, TK, TM, false)
-                     : make_map(&ma, a->A, a->M, a->K, a->lda, a_bat ? a->batch : 1, a->sA, 32, TK, true);
-    // B: op(B) is K x N; K-major when stored [N][K] (tb = 1), MN-major when stored [K][N]
-    bool okB = !b_mn ? make_map(&mb, a->B, a->K, a->N, a->ldb, b_bat ? a->batch : 1, a->sB, TK, TN, false)
-                     : make_map(&mb, a->B, a->N, a->K, a->ldb, b_bat ? a->batch : 1, a->sB, 32, TK, true);
-    if (!okA || !okB) return 0;
+    if ((p_bat && a->sB % 4) || (q_bat && a->sA % 4)) return 0;
+    const int bn = pick_bn(a->M);
+    CUtensorMap mp, mq;
+    bool okP = !p_mn ? make_map(&mp, a->B, a->K, a->N, a->ldb, p_bat ? a->batch : 1, a->sB, TK, TM, false)
+                     : make_map(&mp, a->B, a->N, a->K, a->ldb, p_bat ? a->batch : 1, a->sB, 32, TK, true);
+    bool okQ = !q_mn ? make_map(&mq, a->A, a->K, a->M, a->lda, q_bat ? a->batch : 1, a->sA, TK, bn, false)
+                     : make_map(&mq, a->A, a->M, a->K, a->lda, q_bat ? a->batch : 1, a->sA, 32, TK, true);
+    if (!okP || !okQ) return 0;
 
     TcParams p;
     memset(&p, 0, sizeof p);
-    p.M = a->M, p.N = a->N, p.K = a->K, p.alpha = a->alpha, p.beta = a->beta;
-    p.C = a->C, p.ldc = a->ldc, p.sC = a->sC, p.bias = a->bias, p.bias_row = a->bias_per_row;
+    p.R = a->N, p.Cq = a->M, p.K = a->K, p.BN = bn, p.alpha = a->alpha, p.beta = a->beta;
+    p.C = a->C, p.ldc = a->ldc, p.sC = a->sC, p.bias = a->bias, p.bias_q = a->bias_per_row;
     p.batch = a->batch, p.reduce = a->reduce_batch && a->batch > 1;
-    p.a_mn = a_mn, p.b_mn = b_mn, p.a_bat = a_bat, p.b_bat = b_bat, p.three = three, p.status = d->status;
+    p.p_mn = p_mn, p.q_mn = q_mn, p.p_bat = p_bat, p.q_bat = q_bat, p.status = d->status;
+    p.tiles_r = (a->N + TM - 1) / TM, p.tiles_q = (a->M + bn - 1) / bn;
 
-    int64_t tiles = ((a->M + TM - 1) / TM) * ((a->N + TN - 1) / TN);
-    int64_t nout = p.reduce ? 1 : a->batch;
-    int64_t target = (int64_t)d->sm_count;
-    int64_t maxpart = (int64_t)(d->scratch_bytes / sizeof(float)) / (a->M * a->N * nout);
+    const int64_t tiles = p.tiles_r * p.tiles_q, nout = p.reduce ? 1 : a->batch;
+    const int64_t sms = d->sm_count > 0 ? d->sm_count : 148;
+    const int64_t maxpart = (int64_t)(d->scratch_bytes / sizeof(float)) / (a->M * a->N * nout);
     int64_t splits = 1;
-    if (tiles * nout < target) {
-        splits = (target + tiles * nout - 1) / (tiles * nout);
-        int64_t cap = p.reduce ? a->batch : (a->K + 4 * TK - 1) / (4 * TK);
+    if (p.reduce) {
+        // the batch sum: enough slices to occupy every SM, each slice a run of whole samples
+        splits = (sms + tiles - 1) / tiles;
+        if (splits > a->batch) splits = a->batch;
+    } else if (tiles * nout < sms) {
+        splits = (sms + tiles * nout - 1) / (tiles * nout);
+        int64_t cap = (a->K + 4 * TK - 1) / (4 * TK);
         if (splits > cap) splits = cap;
-        if (splits > maxpart) splits = maxpart;
-        if (splits < 1) splits = 1;
     }
+    if (splits > maxpart) splits = maxpart;
+    if (splits < 1) splits = 1;
     if (p.reduce) {
         p.bper = (a->batch + splits - 1) / splits;
         splits = (a->batch + p.bper - 1) / p.bper;
@@ -449,30 +541,18 @@ extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
     }
     p.splits = (int)splits;
     p.part = (float *)d->scratch;
-    if (nout * splits > 65535) return 0;
+    p.units = tiles * nout * splits;
 
-    size_t smem = three ? smem_bytes<kStages3x, true>() : smem_bytes<kStagesTf32, false>();
-    static int attr_set[2] = {0, 0};
-    if (!attr_set[three]) {
-        cudaError_t e = three ? cudaFuncSetAttribute(k_tcgemm<kStages3x, true>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                              : cudaFuncSetAttribute(k_tcgemm<kStagesTf32, false>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return 0;
-        }
-        attr_set[three] = 1;
-    }
-    double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
-    double nC = (double)nout * (a->beta != 0.0f ? 2.0 : 1.0);
+    if (three ? !set_smem_attr<kStages3x, true>() : !set_smem_attr<kStagesTf32, false>()) return 0;
+    const size_t smem = three ? smem_bytes<kStages3x, true>() : smem_bytes<kStagesTf32, false>();
+    const double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
+    const double nC = (double)nout * (a->beta != 0.0f ? 2.0 : 1.0);
     Scope sc(d, three ? "gemm_3xtf32_tc" : "gemm_tf32_tc", 2.0 * a->M * a->N * a->K * a->batch,
              4.0 * (nA * a->M * a->K + nB * a->K * a->N + nC * a->M * a->N));
-    dim3 grid((unsigned)((a->N + TN - 1) / TN), (unsigned)((a->M + TM - 1) / TM), (unsigned)(nout * splits));
-    if (three) k_tcgemm<kStages3x, true><<<grid, 192, smem, NCK_STREAM(d)>>>(ma, mb, p);
-    else k_tcgemm<kStagesTf32, false><<<grid, 128, smem, NCK_STREAM(d)>>>(ma, mb, p);
-    cudaError_t le = cudaGetLastError();
-    if (le != cudaSuccess) {
+    const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
+    if (three) k_tcgemm<kStages3x, true><<<grid, 256, smem, NCK_STREAM(d)>>>(mp, mq, p);
+    else k_tcgemm<kStagesTf32, false><<<grid, 192, smem, NCK_STREAM(d)>>>(mp, mq, p);
+    if (cudaGetLastError() != cudaSuccess) {
         /* a launch that never ran: report it through the status word like a kernel-found error */
         *(volatile int *)d->status_host = NCK_ERR_LAUNCH;
         return 1;
