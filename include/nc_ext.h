@@ -52,6 +52,28 @@ NC_API int nc_ext_kernel_entry(nc_ctx *ctx, int i, const char **name, double *ms
 /* Clears the accumulated timings (timing stays on). */
 NC_API void nc_ext_timing_reset(nc_ctx *ctx);
 
+/* Cross-entropy forward on caller-owned device buffers that allocates nothing. It has no
+ * counterpart in newch; the arithmetic is the engine's nc_cross_entropy (newch
+ * engine/src/ops/ops_nn.c:107-149): prob[rows, classes] = softmax(logits) and
+ * *loss = -mean(log prob[r, labels[r]]), with the mean summed in double in a fixed order.
+ *
+ * For callers that must not have device memory allocated on their behalf while they run (a runtime
+ * that owns and accounts for the whole device pool, a latency-critical loop, a process at its
+ * memory limit): the only scratch is a static device array of NC_EXT_CE_NOALLOC_MAX_ROWS floats.
+ * All pointers are device pointers; `stream` is a cudaStream_t (NULL = the legacy default stream).
+ * The call is asynchronous. Returns NC_OK, NC_ERR_ARG (rows < 0, rows > NC_EXT_CE_NOALLOC_MAX_ROWS,
+ * classes <= 0, or a NULL pointer; nothing is launched) or NC_ERR_STATE (CUDA set-up or launch
+ * failure).
+ * - The first call on a device (made with that device current) looks up the static array's address;
+ *   make it before any stream capture begins.
+ * - *status must start at zero; a label outside [0, classes) sets it to 2 (that row's label is
+ *   read as class 0). The static array needs no initialisation.
+ * - Calls on one device share the static array: calls that can run at the same time (on streams
+ *   with no ordering between them) race on it. Calls ordered on one stream are safe. */
+#define NC_EXT_CE_NOALLOC_MAX_ROWS 262144
+NC_API int nc_ext_cross_entropy_fwd_noalloc(const float *logits, const int32_t *labels, int64_t rows,
+                                            int64_t classes, float *prob, float *loss, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -171,6 +171,8 @@ EXT_SIGNATURES: dict = {
     "nc_ext_kernel_entry": (c_int, [P, c_int, POINTER(c_char_p), POINTER(ctypes.c_double), POINTER(c_int64),
                                     POINTER(ctypes.c_double), POINTER(ctypes.c_double)]),
     "nc_ext_timing_reset": (None, [P]),
+    "nc_ext_cross_entropy_fwd_noalloc": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                                 c_void_p]),
 }
 
 

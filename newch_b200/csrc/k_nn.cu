@@ -9,6 +9,10 @@
 
 #include "k_common.cuh"
 
+#include <mutex>
+
+#include "../../include/nc_ext.h"
+
 using namespace nck;
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -141,6 +145,75 @@ extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t 
     if (N > 0) k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status);
     k_loss_combine<<<1, kThreads, 0, NCK_STREAM(d)>>>(terms, N, loss, 1);
     NCK_LAUNCHED(d, 2);
+}
+
+// ---- cross entropy on caller-owned buffers, with no allocation ------------------------------------------
+//
+// Some callers cannot let a library allocate device memory while they run: a runtime that owns the
+// whole device pool and accounts for every byte itself, a latency-critical loop in which an
+// allocator call (and the device synchronisation it may imply) would stall the stream, or a process
+// at its memory limit, where a failed allocation half-way through a step would leave it half done.
+// nc_ext_cross_entropy_fwd_noalloc serves them. It runs the same two kernels as the engine's cross
+// entropy (per-row log-probabilities, then the fixed-order double sum of the label terms) but keeps
+// the per-row terms in the fixed static array below instead of the context's scratch buffer, so it
+// needs no nc_ctx and allocates nothing.
+//
+// - Size limit: rows <= NC_EXT_CE_NOALLOC_MAX_ROWS (1 MiB of float terms); larger calls are rejected
+//   with NC_ERR_ARG before anything is launched.
+// - Set-up: the first call on each device (with that device current) looks up the array's device
+//   address with cudaGetSymbolAddress and caches it with the SM count. Make that first call before
+//   any stream capture begins.
+// - Nothing in the array has to start at zero: each call writes terms[0, rows) before reading them.
+//   The caller's status word must start at zero; a label outside [0, classes) sets it to 2.
+// - The array is shared by every call on a device: two calls whose kernels can overlap (different
+//   streams with no ordering between them) race on it and may return wrong losses. Calls ordered on
+//   one stream are safe.
+static __device__ __align__(256) float g_ce_terms_static[NC_EXT_CE_NOALLOC_MAX_ROWS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+struct NoAllocDevice {
+    float *terms;
+    int sm_count;
+    bool ready;
+};
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Address of the static terms array and the SM count of the current device, looked up once.
+const NoAllocDevice *noalloc_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice &e = g_noalloc_dev[dev];
+    if (!e.ready) {
+        void *p = nullptr;
+        int sms = 0;
+        if (cudaGetSymbolAddress(&p, g_ce_terms_static) != cudaSuccess || !p) return nullptr;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return nullptr;
+        e.terms = (float *)p;
+        e.sm_count = sms;
+        e.ready = true;
+    }
+    return &e;
+}
+}  // namespace
+
+extern "C" NC_API int nc_ext_cross_entropy_fwd_noalloc(const float *logits, const int32_t *labels, int64_t rows,
+                                                       int64_t classes, float *prob, float *loss, int *status,
+                                                       void *stream) {
+    if (rows < 0 || rows > NC_EXT_CE_NOALLOC_MAX_ROWS || classes <= 0) return NC_ERR_ARG;
+    if (!loss || !status || (rows > 0 && (!logits || !labels || !prob))) return NC_ERR_ARG;
+    const NoAllocDevice *dev = noalloc_device();
+    if (!dev) return NC_ERR_STATE;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (rows > 0) {
+        int64_t want = (rows * 32 + kThreads - 1) / kThreads, cap = (int64_t)dev->sm_count * 8;
+        int grid = (int)(want < cap ? want : cap);
+        k_ce_rows<<<grid, kThreads, 0, st>>>(logits, labels, prob, dev->terms, rows, classes, status);
+    }
+    k_loss_combine<<<1, kThreads, 0, st>>>(dev->terms, rows, loss, 1);
+    return cudaGetLastError() == cudaSuccess ? NC_OK : NC_ERR_STATE;
 }
 
 __global__ void k_ce_bwd(const float *__restrict__ prob, const int32_t *__restrict__ lab,
