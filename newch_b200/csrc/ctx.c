@@ -370,6 +370,10 @@ nc_ctx *nc_init(const nc_config *cfg) {
     ctx->dev.device = dev;
     ctx->dev.sm_count = prop.multiProcessorCount;
     ctx->dev.gemm_mode = gemm_mode_from_env(c.force_reference);
+    {
+        const char *cv = getenv("NC_CONV");
+        ctx->dev.conv_implicit = cv && !strcmp(cv, "implicit");
+    }
     cudaStream_t s;
     if (!nc__cuda_ok(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return ctx;
     ctx->dev.stream = s;

@@ -9,55 +9,82 @@
 
 using namespace nck;
 
+// Unfold and fold run one (sample, channel) plane per block: index arithmetic inside a plane is 32-bit
+// (a plane is far below 2^31 elements), each thread owns output positions of the plane, and for a
+// fixed tap the threads of a warp touch consecutive addresses.
+
 // col[n - n0][c * KH * KW + ki * KW + kj][oy * OW + ox] for samples n0 .. n0 + nb
-__global__ void k_im2col(nck_conv g, const float *__restrict__ x, float *__restrict__ col, int64_t n0, int64_t nb) {
-    int64_t L = g.OH * g.OW, KK = g.KH * g.KW, rows = g.C * KK;
-    int64_t total = nb * rows * L;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t l = t % L, rr = t / L;
-        int64_t row = rr % rows, n = rr / rows + n0;
-        int64_t c = row / KK, kk = row - c * KK, ki = kk / g.KW, kj = kk - ki * g.KW;
-        int64_t oy = l / g.OW, ox = l - oy * g.OW;
-        int64_t iy = oy * g.sh - g.ph + ki * g.dh, ix = ox * g.sw - g.pw + kj * g.dw;
-        float v = 0.0f;
-        if (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W) v = x[((n * g.C + c) * g.H + iy) * g.W + ix];
-        col[t] = v;
+__global__ void __launch_bounds__(128) k_im2col(nck_conv g, const float *__restrict__ x, float *__restrict__ col,
+                                                int64_t n0, int64_t nb) {
+    const int L = (int)(g.OH * g.OW), OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
+    const int KH = (int)g.KH, KW = (int)g.KW, KK = KH * KW;
+    const int64_t planes = nb * g.C;
+    for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+        const float *xp = x + (n0 * g.C + pl) * (int64_t)H * W;  // planes of samples n0.. are consecutive
+        float *cp = col + pl * (int64_t)KK * L;
+        for (int l = threadIdx.x; l < L; l += blockDim.x) {
+            int oy = l / OW, ox = l - oy * OW;
+            int iy0 = oy * g.sh - g.ph, ix0 = ox * g.sw - g.pw;
+            for (int ki = 0; ki < KH; ki++) {
+                int iy = iy0 + ki * g.dh;
+                bool rowok = iy >= 0 && iy < H;
+                for (int kj = 0; kj < KW; kj++) {
+                    int ix = ix0 + kj * g.dw;
+                    float v = (rowok && ix >= 0 && ix < W) ? __ldg(xp + iy * W + ix) : 0.0f;
+                    cp[(ki * KW + kj) * L + l] = v;
+                }
+            }
+        }
     }
+}
+
+static int plane_grid(const nck_dev *d, int64_t planes) {
+    int64_t cap = (int64_t)(d->sm_count > 0 ? d->sm_count : 148) * 16;
+    return (int)(planes < cap ? (planes > 0 ? planes : 1) : cap);
 }
 
 extern "C" void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float *col, int64_t n0, int64_t nb) {
     int64_t total = nb * g->C * g->KH * g->KW * g->OH * g->OW;
     if (total <= 0) return;
     Scope sc(d, "im2col", 0.0, 4.0 * (nb * g->C * g->H * g->W + total));
-    k_im2col<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, col, n0, nb);
+    k_im2col<<<plane_grid(d, nb * g->C), 128, 0, NCK_STREAM(d)>>>(*g, x, col, n0, nb);
     NCK_LAUNCHED(d, 1);
 }
 
-// dx[n, c, iy, ix] += sum over (ki, kj) hitting it of col[n][c, ki, kj][oy, ox]
-__global__ void k_col2im(nck_conv g, const float *__restrict__ col, float *__restrict__ dx, int64_t n0, int64_t nb) {
-    int64_t L = g.OH * g.OW, KK = g.KH * g.KW;
-    int64_t total = nb * g.C * g.H * g.W;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ix = t % g.W, r = t / g.W;
-        int64_t iy = r % g.H;
-        r /= g.H;
-        int64_t c = r % g.C, n = r / g.C;
-        const float *cb = col + (n * g.C + c) * KK * L;
-        float acc = 0.0f;
-        for (int64_t ki = 0; ki < g.KH; ki++) {
-            int64_t ty = iy + g.ph - ki * g.dh;
-            if (ty < 0 || ty % g.sh) continue;
-            int64_t oy = ty / g.sh;
-            if (oy >= g.OH) continue;
-            for (int64_t kj = 0; kj < g.KW; kj++) {
-                int64_t tx = ix + g.pw - kj * g.dw;
-                if (tx < 0 || tx % g.sw) continue;
-                int64_t ox = tx / g.sw;
-                if (ox >= g.OW) continue;
-                acc += cb[(ki * g.KW + kj) * L + oy * g.OW + ox];
+// dx[n, c, iy, ix] += sum over the taps (ki, kj) whose window covers it of col[n][c, ki, kj][oy, ox],
+// taps in (ki, kj) order
+__global__ void __launch_bounds__(128) k_col2im(nck_conv g, const float *__restrict__ col, float *__restrict__ dx,
+                                                int64_t n0, int64_t nb) {
+    const int L = (int)(g.OH * g.OW), OH = (int)g.OH, OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
+    const int KH = (int)g.KH, KW = (int)g.KW, KK = KH * KW, HW = H * W;
+    const int64_t planes = nb * g.C;
+    for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+        const float *cb = col + pl * (int64_t)KK * L;
+        float *dp = dx + (n0 * g.C + pl) * (int64_t)HW;
+        for (int t = threadIdx.x; t < HW; t += blockDim.x) {
+            int iy = t / W, ix = t - iy * W;
+            float acc = 0.0f;
+            for (int ki = 0; ki < KH; ki++) {
+                int oy = iy + g.ph - ki * g.dh;  // divided by the stride below (unit stride: as is)
+                if (oy < 0) continue;
+                if (g.sh != 1) {
+                    if (oy % g.sh) continue;
+                    oy /= g.sh;
+                }
+                if (oy >= OH) continue;
+                for (int kj = 0; kj < KW; kj++) {
+                    int ox = ix + g.pw - kj * g.dw;
+                    if (ox < 0) continue;
+                    if (g.sw != 1) {
+                        if (ox % g.sw) continue;
+                        ox /= g.sw;
+                    }
+                    if (ox >= OW) continue;
+                    acc += __ldg(cb + (ki * KW + kj) * L + oy * OW + ox);
+                }
             }
+            dp[t] += acc;
         }
-        dx[((n + n0) * g.C + c) * g.H * g.W + iy * g.W + ix] += acc;
     }
 }
 
@@ -65,21 +92,35 @@ extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, floa
     int64_t total = nb * g->C * g->H * g->W;
     if (total <= 0) return;
     Scope sc(d, "col2im", 0.0, 4.0 * (nb * g->C * g->KH * g->KW * g->OH * g->OW + 2 * total));
-    k_col2im<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+    k_col2im<<<plane_grid(d, nb * g->C), 128, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
     NCK_LAUNCHED(d, 1);
 }
 
 // ---- per-channel sums over [N, C, S] (bias gradients) -----------------------------------------------
+//
+// Block (c, split) sums the planes of channel c for its run of samples with four independent
+// accumulators per thread (float4 loads when the plane is 16-byte aligned); the splits are then
+// added in order.
 
 __global__ void k_chan_sum_partial(const float *__restrict__ x, float *__restrict__ part, int64_t N, int64_t C,
                                    int64_t S, int64_t per_split) {
     __shared__ float sm[kThreads / 32];
     int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
-    float acc = 0.0f;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    const bool vec = (S & 3) == 0 && ((uintptr_t)x & 15) == 0;
     for (int64_t n = n0; n < n1; n++) {
         const float *p = x + (n * C + c) * S;
-        for (int64_t j = threadIdx.x; j < S; j += blockDim.x) acc += p[j];
+        if (vec) {
+            const float4 *q = reinterpret_cast<const float4 *>(p);
+            for (int64_t j = threadIdx.x; j < S / 4; j += blockDim.x) {
+                float4 v = __ldg(q + j);
+                a0 += v.x, a1 += v.y, a2 += v.z, a3 += v.w;
+            }
+        } else {
+            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) a0 += __ldg(p + j);
+        }
     }
+    float acc = (a0 + a1) + (a2 + a3);
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -100,8 +141,8 @@ __global__ void k_chan_sum_combine(const float *__restrict__ part, int splits, i
 
 extern "C" void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_t N, int64_t OC, int64_t L) {
     if (N * OC * L <= 0) return;
-    Scope sc(d, "conv_bias_grad");
-    int64_t splits = ((int64_t)d->sm_count * 4 + OC - 1) / OC;
+    Scope sc(d, "conv_bias_grad", 0.0, 4.0 * (N * OC * L + 2 * OC));
+    int64_t splits = ((int64_t)d->sm_count * 8 + OC - 1) / OC;
     if (splits > N) splits = N;
     if (splits < 1) splits = 1;
     int64_t per = (N + splits - 1) / splits;
@@ -116,43 +157,173 @@ extern "C" void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_
 // ---- direct convolution: each thread reads its receptive field once and produces every output
 // channel of its group at that position (Cg * KH * KW <= 32, OCg <= 64) ---------------------------------
 
-__global__ void k_conv_direct(nck_conv g, const float *__restrict__ x, const float *__restrict__ w,
-                              const float *__restrict__ b, float *__restrict__ y) {
-    __shared__ float ws[64 * 32];
-    int64_t Cg = g.C / g.G, OCg = g.OC / g.G, KK = g.KH * g.KW, CKK = Cg * KK, L = g.OH * g.OW;
-    int64_t ng = blockIdx.y;  // (n, group)
-    int64_t n = ng / g.G, gi = ng % g.G;
-    for (int64_t i = threadIdx.x; i < OCg * CKK; i += blockDim.x) ws[i] = w[gi * OCg * CKK + i];
-    __syncthreads();
-    for (int64_t l = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; l < L; l += (int64_t)gridDim.x * blockDim.x) {
-        int64_t oy = l / g.OW, ox = l - oy * g.OW;
-        float in[32];
-        for (int64_t k = 0; k < CKK; k++) {
-            int64_t c = k / KK, kk = k - c * KK, ki = kk / g.KW, kj = kk - ki * g.KW;
-            int64_t iy = oy * g.sh - g.ph + ki * g.dh, ix = ox * g.sw - g.pw + kj * g.dw;
-            in[k] = (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W)
-                        ? x[((n * g.C + gi * Cg + c) * g.H + iy) * g.W + ix]
-                        : 0.0f;
+// Tap table of one group: for tap k = (c, ki, kj) the input offset c*H*W + ki*dh*W + kj*dw and the
+// row / column displacement ki*dh - ph, kj*dw - pw (shared memory, built once per block).
+struct Taps {
+    int off[32], dy[32], dx[32];
+};
+
+__device__ __forceinline__ void build_taps(const nck_conv &g, int CKK, Taps &t) {
+    const int KK = (int)(g.KH * g.KW), KW = (int)g.KW, HW = (int)(g.H * g.W);
+    for (int k = threadIdx.x; k < CKK; k += blockDim.x) {
+        int c = k / KK, kk = k - c * KK, ki = kk / KW, kj = kk - ki * KW;
+        t.dy[k] = ki * g.dh - g.ph;
+        t.dx[k] = kj * g.dw - g.pw;
+        t.off[k] = c * HW + t.dy[k] * (int)g.W + t.dx[k];
+    }
+}
+
+// receptive field of output position (oy, ox) for the first KT taps (k < CKK live), zero outside
+template <int KT>
+__device__ __forceinline__ void gather_taps(const float *xg, const Taps &t, int CKK, int oy, int ox, int sh, int sw,
+                                            int H, int W, float (&in)[KT]) {
+    const int iy0 = oy * sh, ix0 = ox * sw, base = iy0 * W + ix0;
+#pragma unroll
+    for (int k = 0; k < KT; k++) {
+        float v = 0.0f;
+        if (k < CKK) {
+            int iy = iy0 + t.dy[k], ix = ix0 + t.dx[k];
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = __ldg(xg + base + t.off[k]);
         }
-        for (int64_t o = 0; o < OCg; o++) {
-            float acc = b ? b[gi * OCg + o] : 0.0f;
-            for (int64_t k = 0; k < CKK; k++) acc = fmaf(ws[o * CKK + k], in[k], acc);
-            y[(n * g.OC + gi * OCg + o) * L + l] = acc;
+        in[k] = v;
+    }
+}
+
+// y[n, g*OCg + o, l] = bias + sum over taps k in order of w[o, k] * in[k] (fused multiply-adds);
+// block (l-chunk, n * G + group), one output position per thread
+template <int KT>
+__global__ void __launch_bounds__(256) k_conv_direct(nck_conv g, const float *__restrict__ x,
+                                                     const float *__restrict__ w, const float *__restrict__ b,
+                                                     float *__restrict__ y) {
+    __shared__ float ws[64 * 32];
+    __shared__ Taps taps;
+    const int Cg = (int)(g.C / g.G), OCg = (int)(g.OC / g.G), CKK = Cg * (int)(g.KH * g.KW);
+    const int L = (int)(g.OH * g.OW), OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
+    const int64_t ng = blockIdx.y, n = ng / g.G, gi = ng % g.G;
+    for (int i = threadIdx.x; i < OCg * CKK; i += blockDim.x) ws[i] = w[gi * OCg * CKK + i];
+    build_taps(g, CKK, taps);
+    __syncthreads();
+    const float *xg = x + (n * g.C + gi * Cg) * (int64_t)H * W;
+    float *yg = y + (n * g.OC + gi * OCg) * (int64_t)L;
+    for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < L; l += gridDim.x * blockDim.x) {
+        int oy = l / OW, ox = l - oy * OW;
+        float in[KT];
+        gather_taps<KT>(xg, taps, CKK, oy, ox, g.sh, g.sw, H, W, in);
+        for (int o = 0; o < OCg; o++) {
+            float acc = b ? __ldg(b + gi * OCg + o) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < KT; k++)
+                if (k < CKK) acc = fmaf(ws[o * CKK + k], in[k], acc);
+            yg[(int64_t)o * L + l] = acc;
         }
     }
 }
 
 extern "C" void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b,
                                     float *y) {
-    int64_t L = g->OH * g->OW;
+    int64_t L = g->OH * g->OW, CKK = (g->C / g->G) * g->KH * g->KW;
     if (g->N * g->G * L <= 0) return;
-    Scope sc(d, "conv_direct", 2.0 * g->N * g->OC * L * (g->C / g->G) * g->KH * g->KW,
-             4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L));
+    Scope sc(d, "conv_direct", 2.0 * g->N * g->OC * L * CKK, 4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L));
     int64_t bx = (L + kThreads - 1) / kThreads;
     if (bx > 64) bx = 64;
     dim3 grid((unsigned)bx, (unsigned)(g->N * g->G));
-    k_conv_direct<<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
+    if (CKK <= 9) k_conv_direct<9><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
+    else if (CKK <= 16) k_conv_direct<16><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
+    else k_conv_direct<32><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
     NCK_LAUNCHED(d, 1);
+}
+
+// ---- direct weight gradient for few taps per group (Cg * KH * KW <= 32) --------------------------------
+//
+// dW[g*OCg + o, k] += sum over samples n and positions l of dY[n, g*OCg + o, l] * in_k(n, l). Block
+// (split, group * oc-chunk) walks its slice of the flattened (n, l) positions, one per thread, with
+// OW_ output channels x KT taps of accumulators in registers; warp shuffles and shared memory reduce
+// them to one partial per block, and the splits are added in order by k_direct_dw_combine.
+template <int KT, int OCW>
+__global__ void __launch_bounds__(128) k_direct_dw_partial(nck_conv g, const float *__restrict__ x,
+                                                           const float *__restrict__ gy, float *__restrict__ part,
+                                                           int64_t per_split) {
+    __shared__ Taps taps;
+    __shared__ float red[4][OCW * KT];
+    const int Cg = (int)(g.C / g.G), OCg = (int)(g.OC / g.G), CKK = Cg * (int)(g.KH * g.KW);
+    const int L = (int)(g.OH * g.OW), OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
+    const int chunks = (OCg + OCW - 1) / OCW;
+    const int gi = blockIdx.y / chunks, o0 = (blockIdx.y % chunks) * OCW;
+    build_taps(g, CKK, taps);
+    __syncthreads();
+    float acc[OCW][KT];
+#pragma unroll
+    for (int o = 0; o < OCW; o++)
+#pragma unroll
+        for (int k = 0; k < KT; k++) acc[o][k] = 0.0f;
+    const int64_t total = g.N * (int64_t)L, p0 = blockIdx.x * per_split;
+    const int64_t p1 = p0 + per_split < total ? p0 + per_split : total;
+    for (int64_t p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        int64_t n = p / L;
+        int l = (int)(p - n * L), oy = l / OW, ox = l - oy * OW;
+        float in[KT];
+        gather_taps<KT>(x + (n * g.C + gi * Cg) * (int64_t)H * W, taps, CKK, oy, ox, g.sh, g.sw, H, W, in);
+        const float *gp = gy + (n * g.OC + gi * OCg + o0) * (int64_t)L + l;
+#pragma unroll
+        for (int o = 0; o < OCW; o++) {
+            float gv = (o0 + o < OCg) ? __ldg(gp + (int64_t)o * L) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < KT; k++) acc[o][k] = fmaf(gv, in[k], acc[o][k]);
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 0; o < OCW; o++)
+#pragma unroll
+        for (int k = 0; k < KT; k++) {
+            float v = acc[o][k];
+            for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+            if (lane == 0) red[warp][o * KT + k] = v;
+        }
+    __syncthreads();
+    for (int i = threadIdx.x; i < OCW * KT; i += blockDim.x) {
+        int o = i / KT, k = i - o * KT;
+        if (o0 + o < OCg && k < CKK) {
+            float v = ((red[0][i] + red[1][i]) + red[2][i]) + red[3][i];
+            part[((int64_t)blockIdx.x * g.OC + gi * OCg + o0 + o) * CKK + k] = v;
+        }
+    }
+}
+
+__global__ void k_direct_dw_combine(const float *__restrict__ part, int splits, int64_t n, float *__restrict__ gw) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float s = gw[i];
+        for (int k = 0; k < splits; k++) s += part[k * n + i];
+        gw[i] = s;
+    }
+}
+
+template <int KT, int OCW>
+static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
+    const int64_t OCg = g->OC / g->G, CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
+    const int64_t chunks = (OCg + OCW - 1) / OCW, total = g->N * L, wsz = g->OC * CKK;
+    int64_t splits = ((int64_t)d->sm_count * 8 + g->G * chunks - 1) / (g->G * chunks);
+    int64_t maxs = (int64_t)(d->scratch_bytes / sizeof(float)) / wsz;
+    if (splits > maxs) splits = maxs;
+    if (splits > (total + 127) / 128) splits = (total + 127) / 128;
+    if (splits < 1) splits = 1;
+    int64_t per = (total + splits - 1) / splits;
+    splits = (total + per - 1) / per;
+    float *part = (float *)d->scratch;
+    dim3 grid((unsigned)splits, (unsigned)(g->G * chunks));
+    k_direct_dw_partial<KT, OCW><<<grid, 128, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
+    k_direct_dw_combine<<<grid_for(d, wsz), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
+    NCK_LAUNCHED(d, 2);
+}
+
+extern "C" void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
+    int64_t CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
+    if (g->N * L <= 0 || CKK <= 0) return;
+    Scope sc(d, "conv_direct_dw", 2.0 * g->N * g->OC * L * CKK,
+             4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L + 2 * g->OC * CKK));
+    if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
+    else if (CKK <= 16) direct_dw_launch<16, 4>(d, g, x, gy, gw);
+    else direct_dw_launch<32, 2>(d, g, x, gy, gw);
 }
 
 // ---- depthwise (groups == C == OC) ---------------------------------------------------------------

@@ -270,16 +270,19 @@ extern "C" void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, 
 
 // ---- dropout on the xoshiro256** stream ------------------------------------------------------------------
 //
-// Block b owns draws [b * 16384, (b + 1) * 16384); its thread t owns the 64 draws starting at
-// t * 64 inside that. Jump tables (uploaded once): tab[k] = T^(2^(6 + k)) for k < 36, T the 256x256
-// GF(2) transition matrix of xoshiro256**, stored by column (image of each state bit).
-//   block base  = prod over set bits k of b   of T^(16384 * 2^k) = tab[8 + k]
+// Block b owns draws [b * 8192, (b + 1) * 8192); its thread t owns the 64 draws starting at t * 64
+// inside that. Jump tables (uploaded once): tab[k] = T^(2^(6 + k)) for k < 36, T the 256x256 GF(2)
+// transition matrix of xoshiro256**, stored by column (image of each state bit).
+//   block base  = prod over set bits k of b   of T^(8192 * 2^k) = tab[7 + k]
 //   thread start = doubling prefix over the block: state[t] = T^(64 * 2^r) state[t - 2^r] = tab[r]
+// The seven prefix matrices (56 KiB) are staged in shared memory: the block applies them 127 times.
 
-constexpr int kDropDraws = 64;                      // draws per thread
-constexpr int kDropThreads = 256;                   // threads per block
-constexpr int kDropBlock = kDropDraws * kDropThreads;  // 16384 draws per block
+constexpr int kDropDraws = 64;                         // draws per thread
+constexpr int kDropLog = 7;                            // log2 threads per block
+constexpr int kDropThreads = 1 << kDropLog;            // 128 threads per block
+constexpr int kDropBlock = kDropDraws * kDropThreads;  // 8192 draws per block
 constexpr int kRngTables = 36;
+constexpr size_t kDropSmem = (size_t)kDropLog * 256 * sizeof(ulonglong4);
 
 __device__ ulonglong4 *g_rng_tab;  // device copy of the jump matrices (kRngTables x 256 columns)
 
@@ -299,15 +302,14 @@ extern "C" int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t 
 // out = M v for a 256x256 bit matrix by columns: each lane XORs 8 columns, the warp XOR-reduces.
 // Every lane returns the full product.
 __device__ __forceinline__ ulonglong4 warp_matvec(const ulonglong4 *__restrict__ M, const ulonglong4 &v, int lane) {
-    int w = lane >> 3;
-    unsigned long long word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
-    unsigned byte = (unsigned)(word >> ((lane & 7) * 8)) & 0xffu;
+    // lane owns columns c = 32 i + lane (i < 8): consecutive lanes read consecutive columns
+    const unsigned long long words[4] = {v.x, v.y, v.z, v.w};
     ulonglong4 acc = make_ulonglong4(0, 0, 0, 0);
+#pragma unroll
     for (int i = 0; i < 8; i++) {
-        if ((byte >> i) & 1u) {
-            ulonglong4 c = M[lane * 8 + i];
-            acc.x ^= c.x, acc.y ^= c.y, acc.z ^= c.z, acc.w ^= c.w;
-        }
+        ulonglong4 c = M[i * 32 + lane];
+        unsigned long long m = 0ull - ((words[i >> 1] >> ((i & 1) * 32 + lane)) & 1ull);
+        acc.x ^= c.x & m, acc.y ^= c.y & m, acc.z ^= c.z & m, acc.w ^= c.w & m;
     }
     for (int o = 16; o; o >>= 1) {
         acc.x ^= __shfl_xor_sync(0xffffffffu, acc.x, o);
@@ -323,22 +325,24 @@ __device__ __forceinline__ unsigned long long rotl64(unsigned long long x, int k
 __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
                                                               float *__restrict__ y, uint32_t *__restrict__ bits,
                                                               int64_t n, float p) {
+    extern __shared__ ulonglong4 ptab[];  // kDropLog prefix matrices
     __shared__ ulonglong4 st[kDropThreads];
     __shared__ uint32_t mb[kDropBlock / 32];
     const ulonglong4 *tab = g_rng_tab;
     int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < kDropLog * 256; i += kDropThreads) ptab[i] = tab[i];
     if (warp == 0) {
         ulonglong4 v = s0;
         unsigned long long b = blockIdx.x;
         for (int k = 0; b; k++, b >>= 1)
-            if (b & 1) v = warp_matvec(tab + (size_t)(8 + k) * 256, v, lane);
+            if (b & 1) v = warp_matvec(tab + (size_t)(kDropLog + k) * 256, v, lane);
         if (lane == 0) st[0] = v;
     }
     __syncthreads();
-    for (int r = 0; r < 8; r++) {
+    for (int r = 0; r < kDropLog; r++) {
         int cnt = 1 << r;
         for (int t = cnt + warp; t < 2 * cnt; t += kDropThreads / 32) {
-            ulonglong4 v = warp_matvec(tab + (size_t)r * 256, st[t - cnt], lane);
+            ulonglong4 v = warp_matvec(ptab + r * 256, st[t - cnt], lane);
             if (lane == 0) st[t] = v;
         }
         __syncthreads();
@@ -385,7 +389,12 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
     Scope sc(d, "dropout", 0.0, 8.0 * n + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
-    k_dropout_fwd<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(s0, x, y, bits, n, p);
+    static int attr_done = 0;
+    if (!attr_done) {
+        cudaFuncSetAttribute(k_dropout_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDropSmem);
+        attr_done = 1;
+    }
+    k_dropout_fwd<<<(unsigned)blocks, kDropThreads, kDropSmem, NCK_STREAM(d)>>>(s0, x, y, bits, n, p);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -423,19 +432,51 @@ __device__ __forceinline__ void block_sum2(double &a, double &b, double *sm) {
     }
 }
 
-__global__ void k_bn_stats(const float *__restrict__ x, double *__restrict__ part, int64_t N, int64_t C, int64_t S,
-                           int64_t per_split) {
+// One block per (channel, run of samples). The block's elements are walked as a flat list of float4
+// (planes of a multiple of 4 floats) or floats, two independent double accumulator pairs per thread
+// and loads unrolled so that enough bytes are in flight to keep HBM busy.
+template <int V>
+__device__ __forceinline__ void bn_load(const float *p, int64_t i, float (&v)[V]) {
+    if constexpr (V == 4) {
+        float4 q = __ldg(reinterpret_cast<const float4 *>(p) + i);
+        v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+    } else {
+        v[0] = __ldg(p + i);
+    }
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) k_bn_stats(const float *__restrict__ x, double *__restrict__ part, int64_t N,
+                                                  int64_t C, int64_t S, int64_t per_split) {
     __shared__ double sm[64];
-    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
-    double s = 0.0, ss = 0.0;
-    for (int64_t n = n0; n < n1; n++) {
-        const float *p = x + (n * C + c) * S;
-        for (int64_t j = threadIdx.x; j < S; j += blockDim.x) {
-            double v = (double)p[j];
-            s += v;
-            ss += v * v;
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const int SV = (int)(S / V);
+    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
+    double s0 = 0.0, q0 = 0.0, s1 = 0.0, q1 = 0.0;
+    int t = threadIdx.x;
+    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
+        int u = t + blockDim.x;
+        int na = t / SV, nb = u / SV;
+        float va[V], vb[V];
+        bn_load<V>(x + ((n0 + na) * C + c) * S, t - na * SV, va);
+        bn_load<V>(x + ((n0 + nb) * C + c) * S, u - nb * SV, vb);
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            double a = (double)va[k], b = (double)vb[k];
+            s0 += a, q0 += a * a, s1 += b, q1 += b * b;
         }
     }
+    if (t < total) {
+        int na = t / SV;
+        float va[V];
+        bn_load<V>(x + ((n0 + na) * C + c) * S, t - na * SV, va);
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            double a = (double)va[k];
+            s0 += a, q0 += a * a;
+        }
+    }
+    double s = s0 + s1, ss = q0 + q1;
     block_sum2(s, ss, sm);
     if (threadIdx.x == 0) {
         part[(blockIdx.y * C + c) * 2] = s;
@@ -466,49 +507,64 @@ __global__ void k_bn_eval_stats(const float *__restrict__ rm, const float *__res
     }
 }
 
-// y = x * a + d per channel, a = w * invstd, d = b - mean * a; one block row per (n, c) plane
-__global__ void k_bn_norm(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ b,
-                          const float *__restrict__ mean, const float *__restrict__ invstd, float *__restrict__ y,
-                          int64_t NC, int64_t C, int64_t S) {
-    for (int64_t plane = blockIdx.x; plane < NC; plane += gridDim.x) {
-        int64_t c = plane % C;
-        float a = w[c] * invstd[c], dd = b[c] - mean[c] * a;
-        const float *p = x + plane * S;
-        float *q = y + plane * S;
-        if ((S & 3) == 0 && (((uintptr_t)p | (uintptr_t)q) & 15) == 0) {
-            for (int64_t j = threadIdx.x; j < S / 4; j += blockDim.x) {
-                float4 v = ((const float4 *)p)[j];
-                v.x = v.x * a + dd, v.y = v.y * a + dd, v.z = v.z * a + dd, v.w = v.w * a + dd;
-                ((float4 *)q)[j] = v;
-            }
+// y = x * a + d per channel, a = w * invstd, d = b - mean * a; flat over all elements (V = 4: float4
+// items, planes of a multiple of 4 floats)
+template <int V>
+__global__ void __launch_bounds__(256) k_bn_norm(const float *__restrict__ x, const float *__restrict__ w,
+                                                 const float *__restrict__ b, const float *__restrict__ mean,
+                                                 const float *__restrict__ invstd, float *__restrict__ y, int64_t NC,
+                                                 int64_t C, int64_t S) {
+    const int64_t SV = S / V, total = NC * SV;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c = total <= 0x7fffffff ? (int64_t)(((uint32_t)i / (uint32_t)SV) % (uint32_t)C) : (i / SV) % C;
+        float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
+        if constexpr (V == 4) {
+            float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            v.x = v.x * a + dd, v.y = v.y * a + dd, v.z = v.z * a + dd, v.w = v.w * a + dd;
+            reinterpret_cast<float4 *>(y)[i] = v;
         } else {
-            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) q[j] = p[j] * a + dd;
+            y[i] = __ldg(x + i) * a + dd;
         }
     }
 }
 
-static int64_t bn_splits(const nck_dev *d, int64_t N, int64_t C) {
-    int64_t want = ((int64_t)d->sm_count * 4 + C - 1) / C;
+static bool bn_vec4(int64_t S, const void *p, const void *q, const void *r) {
+    return (S & 3) == 0 && (((uintptr_t)p | (uintptr_t)q | (uintptr_t)r) & 15) == 0;
+}
+
+static int flat_grid(const nck_dev *d, int64_t items) {
+    int64_t want = (items + 255) / 256, cap = (int64_t)(d->sm_count > 0 ? d->sm_count : 148) * 16;
+    if (want > cap) want = cap;
+    return want < 1 ? 1 : (int)want;
+}
+
+// runs of samples per channel: about 8 blocks per SM, and at most 2^30 elements per block (the
+// statistics kernels index a block's elements with 32-bit integers)
+static int64_t bn_splits(const nck_dev *d, int64_t N, int64_t C, int64_t S) {
+    int64_t want = ((int64_t)d->sm_count * 8 + C - 1) / C;
+    int64_t need = (N * S + ((int64_t)1 << 30) - 1) >> 30;
+    if (want < need) want = need;
     if (want < 1) want = 1;
     return want > N ? N : want;
 }
 
-static int norm_threads(int64_t S) { return S >= 1024 ? 256 : S >= 256 ? 128 : 64; }
 
 extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                                  float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
                                  float eps) {
     Scope sc(d, "bn_fwd", 0.0, 8.0 * N * C * S);
-    int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
+    int64_t splits = bn_splits(d, N, C, S), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     dim3 g1((unsigned)C, (unsigned)splits);
-    k_bn_stats<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
+    const bool v4 = bn_vec4(S, x, y, x);
+    if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
+    else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
     k_bn_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, mean, invstd, rm, rv,
                                                                    mom, eps);
     int64_t planes = N * C;
-    int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
-    k_bn_norm<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    if (v4) k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
     NCK_LAUNCHED(d, 3);
 }
 
@@ -518,29 +574,54 @@ extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, cons
     Scope sc(d, "bn_fwd");
     k_bn_eval_stats<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(rm, rv, mean, invstd, C, eps);
     int64_t planes = N * C;
-    if (planes > 0) {
-        int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
-        k_bn_norm<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    if (planes * S > 0) {
+        if (bn_vec4(S, x, y, x))
+            k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+        else
+            k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
     }
     NCK_LAUNCHED(d, 2);
 }
 
-// backward sums per channel: sg = sum g, sgx = sum g * xhat (float products, double sums)
-__global__ void k_bn_bwd_sums(const float *__restrict__ x, const float *__restrict__ g, const float *__restrict__ mean,
-                              const float *__restrict__ invstd, double *__restrict__ part, int64_t N, int64_t C,
-                              int64_t S, int64_t per_split) {
+// backward sums per channel: sg = sum g, sgx = sum g * xhat (float products, double sums); same
+// walk as the statistics kernel
+template <int V>
+__global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x, const float *__restrict__ g,
+                                                     const float *__restrict__ mean, const float *__restrict__ invstd,
+                                                     double *__restrict__ part, int64_t N, int64_t C, int64_t S,
+                                                     int64_t per_split) {
     __shared__ double sm[64];
-    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
-    float mu = mean[c], is = invstd[c];
-    double sg = 0.0, sgx = 0.0;
-    for (int64_t n = n0; n < n1; n++) {
-        const float *p = x + (n * C + c) * S, *q = g + (n * C + c) * S;
-        for (int64_t j = threadIdx.x; j < S; j += blockDim.x) {
-            float gv = q[j];
-            sg += gv;
-            sgx += gv * (p[j] - mu) * is;
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const float mu = mean[c], is = invstd[c];
+    const int SV = (int)(S / V);
+    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
+    double g0 = 0.0, h0 = 0.0, g1 = 0.0, h1 = 0.0;
+    int t = threadIdx.x;
+    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
+        int u = t + blockDim.x;
+        int na = t / SV, nb = u / SV;
+        int64_t oa = ((n0 + na) * C + c) * S, ob = ((n0 + nb) * C + c) * S;
+        float xa[V], ga[V], xb[V], gb[V];
+        bn_load<V>(x + oa, t - na * SV, xa);
+        bn_load<V>(g + oa, t - na * SV, ga);
+        bn_load<V>(x + ob, u - nb * SV, xb);
+        bn_load<V>(g + ob, u - nb * SV, gb);
+#pragma unroll
+        for (int k = 0; k < V; k++) {
+            g0 += ga[k], h0 += ga[k] * (xa[k] - mu) * is;
+            g1 += gb[k], h1 += gb[k] * (xb[k] - mu) * is;
         }
     }
+    if (t < total) {
+        int na = t / SV;
+        int64_t oa = ((n0 + na) * C + c) * S;
+        float xa[V], ga[V];
+        bn_load<V>(x + oa, t - na * SV, xa);
+        bn_load<V>(g + oa, t - na * SV, ga);
+#pragma unroll
+        for (int k = 0; k < V; k++) g0 += ga[k], h0 += ga[k] * (xa[k] - mu) * is;
+    }
+    double sg = g0 + g1, sgx = h0 + h1;
     block_sum2(sg, sgx, sm);
     if (threadIdx.x == 0) {
         part[(blockIdx.y * C + c) * 2] = sg;
@@ -560,19 +641,32 @@ __global__ void k_bn_bwd_finalize(const double *__restrict__ part, int splits, i
     }
 }
 
-__global__ void k_bn_bwd_dx(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ g,
-                            const float *__restrict__ mean, const float *__restrict__ invstd,
-                            const float *__restrict__ coef, float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
-                            int training) {
-    for (int64_t plane = blockIdx.x; plane < NC; plane += gridDim.x) {
-        int64_t c = plane % C;
-        float mu = mean[c], is = invstd[c], k = w[c] * is, mg = coef[2 * c], mgx = coef[2 * c + 1];
-        const float *p = x + plane * S, *q = g + plane * S;
-        float *o = gx + plane * S;
-        if (training)
-            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) o[j] += k * (q[j] - mg - (p[j] - mu) * is * mgx);
-        else
-            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) o[j] += k * q[j];
+// gx += k * (g - mean(g) - xhat * mean(g * xhat)) in training, gx += k * g in eval; flat walk
+template <int V>
+__global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, const float *__restrict__ w,
+                                                   const float *__restrict__ g, const float *__restrict__ mean,
+                                                   const float *__restrict__ invstd, const float *__restrict__ coef,
+                                                   float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
+                                                   int training) {
+    const int64_t SV = S / V, total = NC * SV;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c = total <= 0x7fffffff ? (int64_t)(((uint32_t)i / (uint32_t)SV) % (uint32_t)C) : (i / SV) % C;
+        float mu = __ldg(mean + c), is = __ldg(invstd + c), k = __ldg(w + c) * is;
+        float mg = __ldg(coef + 2 * c), mgx = __ldg(coef + 2 * c + 1);
+        float xv[V], gv[V], ov[V];
+        bn_load<V>(x, i, xv);
+        bn_load<V>(g, i, gv);
+        if constexpr (V == 4) {
+            float4 o = reinterpret_cast<float4 *>(gx)[i];
+            ov[0] = o.x, ov[1] = o.y, ov[2] = o.z, ov[3] = o.w;
+        } else {
+            ov[0] = gx[i];
+        }
+#pragma unroll
+        for (int e = 0; e < V; e++)
+            ov[e] += training ? k * (gv[e] - mg - (xv[e] - mu) * is * mgx) : k * gv[e];
+        if constexpr (V == 4) reinterpret_cast<float4 *>(gx)[i] = make_float4(ov[0], ov[1], ov[2], ov[3]);
+        else gx[i] = ov[0];
     }
 }
 
@@ -580,19 +674,24 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
                            const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
                            int training) {
     Scope sc(d, "bn_bwd", 0.0, (gx ? 16.0 : 8.0) * N * C * S);
-    int64_t splits = bn_splits(d, N, C), per = (N + splits - 1) / splits;
+    int64_t splits = bn_splits(d, N, C, S), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     dim3 g1((unsigned)C, (unsigned)splits);
-    k_bn_bwd_sums<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
+    const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
+    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
+    else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
     k_bn_bwd_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, gw, gb, coef);
     int launched = 2;
     if (gx) {
         int64_t planes = N * C;
-        int blocks = (int)(planes < (int64_t)d->sm_count * 16 ? planes : (int64_t)d->sm_count * 16);
-        k_bn_bwd_dx<<<blocks, norm_threads(S), 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx, planes, C, S,
-                                                                    training);
+        if (v4)
+            k_bn_bwd_dx<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
+                                                                                   planes, C, S, training);
+        else
+            k_bn_bwd_dx<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
+                                                                               planes, C, S, training);
         launched++;
     }
     NCK_LAUNCHED(d, launched);

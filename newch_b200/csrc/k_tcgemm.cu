@@ -11,10 +11,10 @@
 // with warp-specialised roles:
 //   warps 0-3  epilogue: tcgen05.ld of the accumulator rows (warp w owns lanes 32w..32w+31), alpha /
 //              bias / beta, coalesced stores (or raw partial tiles when the reduction is split)
-//   warp 4     TMA loader (one thread) feeding an S-stage mbarrier ring, K in steps of 32 (128 B)
+//   warp 4     TMA loader (one thread) feeding a ring of up to 8 stages, K in steps of 32 (128 B)
 //   warp 5     MMA issuer (one thread): 4 MMAs of K = 8 per stage, commits each stage back to the
 //              loader and each finished tile to the epilogue
-//   warps 6-7  3xTF32 only: split every staged fp32 tile into its TF32 head (top 19 bits) and the
+//   warps 6-13 3xTF32 only: split every staged fp32 tile into its TF32 head (top 19 bits) and the
 //              remainder; the MMA thread then accumulates head*head + head*rest + rest*head
 // Two accumulators in TMEM let the epilogue of one tile overlap the main loop of the next.
 //
@@ -25,22 +25,21 @@
 #include <string.h>
 
 #include "k_common.cuh"
+#include "k_tcgen05.cuh"
 
 using namespace nck;
 
 namespace {
 
-constexpr int TM = 128, TK = 32;          // tile rows (TMEM lanes); K per stage (32 fp32 = 128 B)
-constexpr int kMaxBN = 128;               // widest tile (Q rows per tile)
-constexpr int kStageA = TM * TK;          // floats per P stage (16 KiB)
-constexpr int kStageB = kMaxBN * TK;      // floats per Q stage (16 KiB)
-constexpr uint64_t kWaitNs = 2000000000ull;
-constexpr int kErrPipeline = 3;
-constexpr int kEpiWarps = 4, kLoadWarp = 4, kMmaWarp = 5, kSplitWarp0 = 6;
+using namespace tc;
+
+constexpr int kEpiWarps = 4, kLoadWarp = 4, kMmaWarp = 5, kSplitWarp0 = 6, kSplitThreads = 256;
+constexpr int kThreadsTf32 = kSplitWarp0 * 32, kThreads3x = kThreadsTf32 + kSplitThreads;
 
 struct TcParams {
     int64_t R, Cq, K;      // P rows (original N), Q rows (original M), depth
     int BN;                // tile width along Q
+    int stages;            // ring depth (as many as shared memory holds, at most kMaxStages)
     float alpha, beta;
     float *C;
     int64_t ldc, sC;
@@ -55,50 +54,6 @@ struct TcParams {
     int p_bat, q_bat;      // operand has a batch coordinate (3-D tensor map)
     int *status;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ uint64_t now_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// false when the bounded wait gave up (the error goes to the status word)
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status) {
-    uint32_t addr = smem_u32(bar);
-    uint64_t start = 0;
-    for (uint32_t i = 0;; i++) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred P;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, P;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if ((i & 1023) == 0) {
-            uint64_t t = now_ns();
-            if (!start) start = t;
-            else if (t - start > kWaitNs) break;
-        }
-    }
-    report(status, kErrPipeline);
-    return false;
-}
 
 __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
     asm volatile(
@@ -116,68 +71,13 @@ __device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int c0
         : "memory");
 }
 
-// shared memory matrix descriptor, version 1 (sm100); layout 2 = 128-byte swizzle in 16-byte units
-// (K-major tiles), layout 1 = 128-byte swizzle in 32-byte units (the only MN-major form for tf32)
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFF);
-    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
-    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
-    d |= (uint64_t)1 << 46;  // version
-    d |= (uint64_t)layout << 61;
-    return d;
-}
 
-// K-offset descriptor of one stage buffer for the k-th 8-deep MMA step
-__device__ __forceinline__ uint64_t stage_desc(uint32_t base, int mn, int k) {
-    // K-major: 128 B rows of 32 K values, 8-row atoms 1024 B apart; step k moves 32 B along the row
-    if (!mn) return sdesc(base + k * 32, 16, 1024, 2);
-    // MN-major: 128 B rows of 32 M/N values, one row per K; 4-row atoms 512 B apart (SBO), 32-wide
-    // blocks 4 KiB apart (LBO); step k moves 8 rows
-    return sdesc(base + k * 1024, 4096, 512, 1);
-}
-
-// instruction descriptor: D f32, A/B tf32, dense, M = 128, N = bn
-__device__ __forceinline__ uint32_t idesc_tf32(int a_mn, int b_mn, int bn) {
-    uint32_t d = 0;
-    d |= 1u << 4;               // D format F32
-    d |= 2u << 7;               // A format TF32
-    d |= 2u << 10;              // B format TF32
-    d |= (uint32_t)a_mn << 15;  // A major
-    d |= (uint32_t)b_mn << 16;  // B major
-    d |= (uint32_t)(bn >> 3) << 17;
-    d |= (uint32_t)(TM >> 4) << 24;
-    return d;
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
-
-template <int S>
-struct Smem {
-    float a[S][kStageA];
-    float b[S][kStageB];
-    uint64_t full[S], empty[S], ready[S];
+// Barriers sit in the first KiB of dynamic shared memory; the stage buffers follow, 1 KiB aligned:
+// [P stages][Q stages] and in 3xTF32 mode [P rests][Q rests], `stages` of each.
+struct Bars {
+    uint64_t full[kMaxStages], empty[kMaxStages], ready[kMaxStages];
     uint64_t tfull[2], tempty[2], mma_done;
     uint32_t tmem;
-};
-
-template <int S>
-struct SmemLo {
-    float a[S][kStageA];
-    float b[S][kStageB];
 };
 
 // A work unit: tile (tr, tq), output batch ob (or 0 when the batch is summed), reduction slice sl.
@@ -207,14 +107,18 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int64_t u) {
     return w;
 }
 
-template <int S, bool THREE>
-__global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_constant__ CUtensorMap tmP,
+template <bool THREE>
+__global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm(const __grid_constant__ CUtensorMap tmP,
                                                                  const __grid_constant__ CUtensorMap tmQ, TcParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    Smem<S> &s = *reinterpret_cast<Smem<S> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    SmemLo<S> *lo = THREE ? reinterpret_cast<SmemLo<S> *>(reinterpret_cast<unsigned char *>(&s) +
-                                                          ((sizeof(Smem<S>) + 1023) & ~(size_t)1023))
-                          : nullptr;
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                            ~(uintptr_t)1023);
+    Bars &s = *reinterpret_cast<Bars *>(base);
+    const int S = p.stages, sbq = p.BN * TK;
+    float *const ring_a = reinterpret_cast<float *>(base + 1024);
+    float *const ring_b = ring_a + S * kStageA;
+    float *const rest_a = ring_b + S * sbq;  // 3xTF32 only
+    float *const rest_b = rest_a + S * kStageA;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int BN = p.BN;
     const uint32_t tcols = BN * 2 <= 32 ? 32 : BN * 2 <= 64 ? 64 : BN * 2 <= 128 ? 128 : 256;
@@ -224,7 +128,7 @@ __global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_co
         for (int i = 0; i < S; i++) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
-            mbar_init(&s.ready[i], 64);
+            mbar_init(&s.ready[i], kSplitThreads);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&s.tfull[i], 1);
@@ -259,21 +163,21 @@ __global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_co
                     int kk = (int)(w.k0 + (t % kt) * TK);
                     mbar_expect_tx(&s.full[st], stage_bytes);
                     if (!p.p_mn) {
-                        if (p.p_bat) tma_3d(s.a[st], &tmP, kk, (int)w.r0, b, &s.full[st]);
-                        else tma_2d(s.a[st], &tmP, kk, (int)w.r0, &s.full[st]);
+                        if (p.p_bat) tma_3d(ring_a + st * kStageA, &tmP, kk, (int)w.r0, b, &s.full[st]);
+                        else tma_2d(ring_a + st * kStageA, &tmP, kk, (int)w.r0, &s.full[st]);
                     } else {
                         for (int j = 0; j < TM / 32; j++) {
-                            if (p.p_bat) tma_3d(s.a[st] + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, b, &s.full[st]);
-                            else tma_2d(s.a[st] + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, &s.full[st]);
+                            if (p.p_bat) tma_3d(ring_a + st * kStageA + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, b, &s.full[st]);
+                            else tma_2d(ring_a + st * kStageA + j * 1024, &tmP, (int)w.r0 + 32 * j, kk, &s.full[st]);
                         }
                     }
                     if (!p.q_mn) {
-                        if (p.q_bat) tma_3d(s.b[st], &tmQ, kk, (int)w.q0, b, &s.full[st]);
-                        else tma_2d(s.b[st], &tmQ, kk, (int)w.q0, &s.full[st]);
+                        if (p.q_bat) tma_3d(ring_b + st * sbq, &tmQ, kk, (int)w.q0, b, &s.full[st]);
+                        else tma_2d(ring_b + st * sbq, &tmQ, kk, (int)w.q0, &s.full[st]);
                     } else {
                         for (int j = 0; j < BN / 32; j++) {
-                            if (p.q_bat) tma_3d(s.b[st] + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, b, &s.full[st]);
-                            else tma_2d(s.b[st] + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
+                            if (p.q_bat) tma_3d(ring_b + st * sbq + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, b, &s.full[st]);
+                            else tma_2d(ring_b + st * sbq + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
                         }
                     }
                 }
@@ -301,12 +205,12 @@ __global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_co
                     uint32_t ph = (uint32_t)((it / S) & 1);
                     if (!(ok = mbar_wait(THREE ? &s.ready[st] : &s.full[st], ph, p.status))) break;
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    uint32_t ab = smem_u32(s.a[st]), bb = smem_u32(s.b[st]);
+                    uint32_t ab = smem_u32(ring_a + st * kStageA), bb = smem_u32(ring_b + st * sbq);
                     for (int k = 0; k < TK / 8; k++) {
                         uint32_t accum = (t > 0 || k > 0) ? 1u : 0u;
                         mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, accum);
                         if (THREE) {
-                            uint32_t al = smem_u32(lo->a[st]), bl = smem_u32(lo->b[st]);
+                            uint32_t al = smem_u32(rest_a + st * kStageA), bl = smem_u32(rest_b + st * sbq);
                             mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bl, p.q_mn, k), idesc, 1u);
                             mma_tf32(d, stage_desc(al, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, 1u);
                         }
@@ -321,7 +225,7 @@ __global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_co
         }
     } else if (THREE && warp >= kSplitWarp0) {
         // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head -------------
-        const int t2 = tid - kSplitWarp0 * 32;  // 0 .. 63
+        const int t2 = tid - kSplitWarp0 * 32;  // 0 .. kSplitThreads - 1
         const int nb = BN * TK / 4;
         int64_t it = 0;
         bool ok = true;
@@ -331,14 +235,14 @@ __global__ void __launch_bounds__(THREE ? 256 : 192, 1) k_tcgemm(const __grid_co
                 int st = (int)(it % S);
                 uint32_t ph = (uint32_t)((it / S) & 1);
                 if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
-                float4 *ah = reinterpret_cast<float4 *>(s.a[st]), *al = reinterpret_cast<float4 *>(lo->a[st]);
-                for (int i = t2; i < TM * TK / 4; i += 64) {
+                float4 *ah = reinterpret_cast<float4 *>(ring_a + st * kStageA), *al = reinterpret_cast<float4 *>(rest_a + st * kStageA);
+                for (int i = t2; i < TM * TK / 4; i += kSplitThreads) {
                     float4 v = ah[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
                     ah[i] = h;
                     al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
                 }
-                float4 *bh = reinterpret_cast<float4 *>(s.b[st]), *bl = reinterpret_cast<float4 *>(lo->b[st]);
-                for (int i = t2; i < nb; i += 64) {
+                float4 *bh = reinterpret_cast<float4 *>(ring_b + st * sbq), *bl = reinterpret_cast<float4 *>(rest_b + st * sbq);
+                for (int i = t2; i < nb; i += kSplitThreads) {
                     float4 v = bh[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
                     bh[i] = h;
                     bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
@@ -454,13 +358,16 @@ bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer,
     return r == CUDA_SUCCESS;
 }
 
-template <int S, bool THREE>
-size_t smem_bytes() {
-    size_t base = (sizeof(Smem<S>) + 1023) & ~(size_t)1023;
-    return 1024 + base + (THREE ? sizeof(SmemLo<S>) : 0);
+// stages that fit: per stage a P tile (16 KiB) and a Q tile (BN * 128 B), doubled in 3xTF32 mode
+int ring_stages(int bn, bool three) {
+    size_t per = (size_t)(kStageA + bn * TK) * 4 * (three ? 2 : 1);
+    size_t n = (kSmemLimit - 2048) / per;
+    return (int)(n > (size_t)kMaxStages ? kMaxStages : n);
 }
 
-constexpr int kStagesTf32 = 6, kStages3x = 3;
+size_t smem_bytes(int bn, bool three, int stages) {
+    return 2048 + (size_t)stages * (kStageA + bn * TK) * 4 * (three ? 2 : 1);
+}
 
 // tile width along Q: the fewest wasted columns, counting ~32 columns of per-tile overhead
 int pick_bn(int64_t cq) {
@@ -473,12 +380,11 @@ int pick_bn(int64_t cq) {
     return best;
 }
 
-template <int S, bool THREE>
+template <bool THREE>
 bool set_smem_attr() {
     static int done = 0;
     if (done) return true;
-    if (cudaFuncSetAttribute(k_tcgemm<S, THREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem_bytes<S, THREE>()) != cudaSuccess) {
+    if (cudaFuncSetAttribute(k_tcgemm<THREE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -543,15 +449,16 @@ extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
     p.part = (float *)d->scratch;
     p.units = tiles * nout * splits;
 
-    if (three ? !set_smem_attr<kStages3x, true>() : !set_smem_attr<kStagesTf32, false>()) return 0;
-    const size_t smem = three ? smem_bytes<kStages3x, true>() : smem_bytes<kStagesTf32, false>();
+    if (three ? !set_smem_attr<true>() : !set_smem_attr<false>()) return 0;
+    p.stages = ring_stages(bn, three);
+    const size_t smem = smem_bytes(bn, three, p.stages);
     const double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
     const double nC = (double)nout * (a->beta != 0.0f ? 2.0 : 1.0);
     Scope sc(d, three ? "gemm_3xtf32_tc" : "gemm_tf32_tc", 2.0 * a->M * a->N * a->K * a->batch,
              4.0 * (nA * a->M * a->K + nB * a->K * a->N + nC * a->M * a->N));
     const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
-    if (three) k_tcgemm<kStages3x, true><<<grid, 256, smem, NCK_STREAM(d)>>>(mp, mq, p);
-    else k_tcgemm<kStagesTf32, false><<<grid, 192, smem, NCK_STREAM(d)>>>(mp, mq, p);
+    if (three) k_tcgemm<true><<<grid, kThreads3x, smem, NCK_STREAM(d)>>>(mp, mq, p);
+    else k_tcgemm<false><<<grid, kThreadsTf32, smem, NCK_STREAM(d)>>>(mp, mq, p);
     if (cudaGetLastError() != cudaSuccess) {
         /* a launch that never ran: report it through the status word like a kernel-found error */
         *(volatile int *)d->status_host = NCK_ERR_LAUNCH;

@@ -25,6 +25,7 @@ typedef struct nck_dev {
     int sm_count;
     int64_t launches;  /* kernels enqueued so far */
     int gemm_mode;     /* NCK_GEMM_* */
+    int conv_implicit; /* 1: convolutions try the implicit-GEMM kernels before unfolding (NC_CONV=implicit) */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
     size_t scratch_bytes;
@@ -167,6 +168,13 @@ void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int6
 void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_t N, int64_t OC, int64_t L);
 /* direct convolution for few input channels per group (Cg*KH*KW <= 64) */
 void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
+/* implicit-GEMM convolution on tcgen05 (groups 1): mode 0 y = conv(x) + bias (in = x, q = w),
+ * 1 gx += conv-transpose(gy) for unit strides (in = gy, q = w), 2 gw += dY x taps (in = x, q = gy).
+ * Returns 0, launching nothing, for a convolution it does not handle. */
+int nck_conv_implicit(nck_dev *d, int mode, const nck_conv *g, const float *in, const float *q, float *out,
+                      const float *bias);
+/* gw[oc, k] += sum over n, l of gy[n, oc, l] * x-tap k at l (same eligibility as the direct forward) */
+void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw);
 void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
 void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx);
 #define NCK_DW_MAX_TAPS 25 /* nck_dw_dw handles kernels up to 5x5 */

@@ -142,6 +142,7 @@ static nc_status conv_fwd(nc_node *n) {
         gemm_fwd(ctx, &g, Wt, X, g.C * HW, HW, B, Y, g.N);
         return NC_OK;
     }
+    if (nck_conv_implicit(nc__k(ctx), 0, &g, X, Wt, Y, B)) return NC_OK; /* tensor cores, no unfolded copy */
     int64_t CKKL = g.C * g.KH * g.KW * L, nbmax = chunk_samples(&g);
     float *col = (float *)nc__arena_alloc(ctx, (size_t)(nbmax * CKKL) * sizeof(float));
     if (!col) return NC_ERR_OOM;
@@ -207,6 +208,19 @@ static void conv_bwd(nc_node *n) {
             return;
         }
         gx = NULL; /* larger depthwise kernels: dW through the grouped im2col path below */
+    }
+    if (gw && use_direct(&g)) {
+        /* few taps per group: dW straight from x and dY, no unfolded copy */
+        nck_conv_direct_dw(nc__k(ctx), &g, X, G, (float *)gw->data);
+        gw = NULL;
+        if (!gx) return;
+    }
+    if (!is_pointwise(&g)) {
+        /* tensor cores straight from x and dY (dX for unit strides); what is not handled here takes
+         * the unfolded path below */
+        if (gw && nck_conv_implicit(nc__k(ctx), 2, &g, X, G, (float *)gw->data, NULL)) gw = NULL;
+        if (gx && nck_conv_implicit(nc__k(ctx), 1, &g, G, Wt, (float *)gx->data, NULL)) gx = NULL;
+        if (!gw && !gx) return;
     }
     if (is_pointwise(&g)) {
         if (gw) gemm_dw(ctx, &g, G, X, g.C * HW, HW, (float *)gw->data, g.N);

@@ -1,0 +1,106 @@
+"""Convolution forward, dX, dW and dB on the B200 engine against the numpy oracle (float64), over
+geometries that exercise the implicit-GEMM tensor-core path (groups 1, more than 32 taps): strides,
+padding, dilation, non-square kernels, position counts that are not a multiple of the 128-row
+tile, channel counts above one 128-wide tile, reductions split across CTAs. Unit-stride dX runs on
+the implicit path too; strided dX and the FFMA mode take the unfolded path, checked the same way.
+
+Every case runs on both convolution paths: unfolded (im2col + GEMM + col2im) and implicit
+(NC_CONV=implicit). Tolerances (normwise, max|err| / max|ref|): FFMA and 3xTF32 1e-5, TF32 2e-3."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from nchelp import Eng, rel_err, seeded
+
+pytestmark = pytest.mark.gpu
+TOL = {"ffma": 1e-5, "3xtf32": 1e-5, "tf32": 2e-3}
+
+# (N, C, H, W), (OC, KH, KW), stride, pad, dilation
+GEOMS = [
+    ((3, 4, 9, 11), (5, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((3, 8, 14, 14), (16, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((2, 16, 13, 17), (40, 3, 3), (2, 2), (1, 1), (1, 1)),
+    ((2, 12, 12, 12), (24, 5, 5), (1, 1), (2, 2), (1, 1)),
+    ((2, 8, 15, 15), (20, 3, 3), (1, 1), (2, 2), (2, 2)),
+    ((1, 32, 7, 7), (200, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((4, 64, 6, 5), (33, 1, 3), (1, 1), (0, 1), (1, 1)),
+    ((2, 150, 5, 6), (20, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((16, 32, 14, 14), (64, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((5, 20, 10, 9), (12, 3, 2), (1, 2), (0, 1), (1, 1)),
+]
+
+
+@pytest.fixture(params=["ffma", "tf32", "3xtf32"])
+def mode(request, monkeypatch):
+    monkeypatch.setenv("NC_GEMM", request.param)
+    return request.param
+
+
+@pytest.fixture(params=["unfolded", "implicit"], autouse=True)
+def conv_path(request, monkeypatch):
+    """NC_CONV=implicit: tensor-core convolutions gathered straight from x / dY (no unfolded copy)."""
+    monkeypatch.setenv("NC_CONV", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("xs,wk,stride,pad,dil", GEOMS)
+def test_conv_forward_and_grads(mode, xs, wk, stride, pad, dil):
+    import ncoracle as O
+
+    ws = (wk[0], xs[1], wk[1], wk[2])
+    X, W, B = seeded(1, xs), seeded(2, ws, 0.3), seeded(3, (wk[0],))
+    with Eng("b200") as e:
+        assert e.L.nc_ext_gemm_mode(e.ctx).decode() == mode
+        x, w, b = e.param(X), e.param(W), e.param(B)
+        y = e.check(e.L.nc_conv2d_ex(x, w, b, stride[0], stride[1], pad[0], pad[1], dil[0], dil[1], 1))
+        out = e.np(y)
+        G = seeded(4, out.shape)
+        e.backward_with(y, G)
+        dx, dw, db = e.grad(x), e.grad(w), e.grad(b)
+        assert e.ok(), e.err()
+    y_ref = O.conv2d(X, W, B, stride=stride, pad=pad, dil=dil)
+    dx_ref, dw_ref, db_ref = O.conv2d_grads(X, W, G, stride=stride, pad=pad, dil=dil)
+    tol = TOL[mode]
+    assert rel_err(out, y_ref) < tol
+    assert rel_err(dx, dx_ref) < tol
+    assert rel_err(dw, dw_ref) < tol
+    assert rel_err(db, db_ref) < 1e-5
+
+
+def test_conv_grads_accumulate(mode):
+    """Two backward passes add into the same gradients (dX and dW accumulate, never overwrite)."""
+    import ncoracle as O
+
+    xs, ws = (4, 16, 10, 10), (24, 16, 3, 3)
+    X, W = seeded(5, xs), seeded(6, ws, 0.3)
+    with Eng("b200") as e:
+        x, w = e.param(X), e.param(W)
+        for seed in (7, 8):
+            y = e.check(e.L.nc_conv2d_ex(x, w, None, 1, 1, 1, 1, 1, 1, 1))
+            e.backward_with(y, seeded(seed, e.shape(y)))
+        dx, dw = e.grad(x), e.grad(w)
+        shape_y = e.shape(y)
+    G = seeded(7, shape_y) + seeded(8, shape_y)
+    dx_ref, dw_ref, _ = O.conv2d_grads(X, W, G, pad=(1, 1))
+    assert rel_err(dx, dx_ref) < TOL[mode]
+    assert rel_err(dw, dw_ref) < TOL[mode]
+
+
+def test_conv_large_batch_against_unfolded_path(monkeypatch):
+    """cfg2's second convolution at batch 128: implicit (3xTF32) against the unfolded FFMA path."""
+    xs, ws = (128, 32, 14, 14), (64, 32, 3, 3)
+    X, W, B = seeded(9, xs), seeded(10, ws, 0.2), seeded(11, (64,))
+    res = {}
+    for m in ("ffma", "3xtf32"):
+        monkeypatch.setenv("NC_GEMM", m)
+        with Eng("b200") as e:
+            x, w, b = e.param(X), e.param(W), e.param(B)
+            y = e.check(e.L.nc_conv2d_ex(x, w, b, 1, 1, 1, 1, 1, 1, 1))
+            G = seeded(12, e.shape(y))
+            out = e.np(y)
+            e.backward_with(y, G)
+            res[m] = (out, e.grad(x), e.grad(w), e.grad(b))
+    for a, r in zip(res["3xtf32"], res["ffma"]):
+        assert rel_err(a, r) < 1e-5
