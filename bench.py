@@ -18,7 +18,6 @@ scaling). Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
-import ctypes
 import json
 import os
 import statistics
@@ -34,6 +33,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 from newch_b200 import capi, replay  # noqa: E402
+from newch_b200 import dist as dist_host  # noqa: E402
 
 METRIC = "train samples/sec at 1/2/4/8 B200 (CNN, transformer); % HBM/tensor roofline"
 REF_LIB = REPO / "oracle" / "_ref" / "libnc_ref.so"
@@ -136,26 +136,13 @@ class Run:
     def __init__(self, lib, trace_name: str, rank: int, world: int, pg, pinned: bool = False):
         self.lib = lib
         self.trace = replay.Trace(trace_name)
-        self.rep = replay.Replayer(lib, self.trace, seed_offset=rank * 7919, pinned=pinned)
+        self.rep = replay.Replayer(lib, self.trace, seed_offset=dist_host.shard_seed_offset(rank), pinned=pinned)
         self.rep.run(0, 1)  # nc_init
         self.ctx = self.rep.ctx
         if not self.ctx or not lib.nc_ok(self.ctx):
             raise RuntimeError(f"nc_init failed: {lib.nc_error(self.ctx) if self.ctx else 'NULL'}")
         if world > 1:
-            import torch
-            import torch.distributed as dist
-            buf = (ctypes.c_char * 512)()
-            n = lib.nc_ext_nccl_unique_id(buf, 512) if rank == 0 else 0
-            t = torch.zeros(513, dtype=torch.uint8)
-            if rank == 0:
-                t[0] = n
-                t[1:1 + n] = torch.frombuffer(bytearray(buf.raw[:n]), dtype=torch.uint8)
-            dist.broadcast(t, 0, group=pg)
-            n = int(t[0])
-            idb = bytes(t[1:1 + n].tolist())
-            st = lib.nc_ext_dp_init(self.ctx, rank, world, idb, n)
-            if st != 0:
-                raise RuntimeError(f"dp init failed: {lib.nc_error(self.ctx)}")
+            dist_host.join_engine_group(lib, self.ctx, pg, rank, world)
         steps = self.trace.steps()
         self.rep.run(1, steps[-1][1])  # model set-up and every recorded step
         self.step = steps[-1]
@@ -274,7 +261,8 @@ def main() -> int:
     torch.cuda.set_device(local)
     pg = None
     if world > 1:
-        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+        os.environ.setdefault("NC_DP_TIMEOUT", "60")  # a rank that never joins ends the run, not hangs it
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
         pg = dist.group.WORLD
     lib = capi.load_b200()
     if lib.nc_ext_device_count() < 1:
@@ -322,8 +310,9 @@ def main() -> int:
         h2d, d2h = step_io_bytes(erun.trace, *erun.step)
         e2e = {"value": round(batch * world * ek / esecs, 3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "trace": et, "steps": ek}
+        # every rank steps (each step all-reduces gradients); rank 0 reports its kernel table
+        rl = roofline(run, load_peaks())
         if rank == 0:
-            rl = roofline(run, load_peaks())
             if world == 1 and REF_LIB.exists():
                 times, cores, backend = cpu_reference(cfg, budget_s=20.0, max_steps=30)
                 cpu = {"value": round(batch * len(times) / sum(times), 3), "unit": "samples/s", "cores": cores,
