@@ -52,15 +52,25 @@ extern "C" void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float 
 }
 
 // dx[n, c, iy, ix] += sum over the taps (ki, kj) whose window covers it of col[n][c, ki, kj][oy, ox],
-// taps in (ki, kj) order
-__global__ void __launch_bounds__(128) k_col2im(nck_conv g, const float *__restrict__ col, float *__restrict__ dx,
+// taps in (ki, kj) order. STAGE: the plane's contiguous KH*KW*L slab of col is first copied to shared
+// memory with 16-byte loads (full-bandwidth reads), and the gathers read shared memory.
+template <bool STAGE>
+__global__ void __launch_bounds__(256) k_col2im(nck_conv g, const float *__restrict__ col, float *__restrict__ dx,
                                                 int64_t n0, int64_t nb) {
+    extern __shared__ float slab[];
     const int L = (int)(g.OH * g.OW), OH = (int)g.OH, OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
     const int KH = (int)g.KH, KW = (int)g.KW, KK = KH * KW, HW = H * W;
     const int64_t planes = nb * g.C;
     for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
         const float *cb = col + pl * (int64_t)KK * L;
         float *dp = dx + (n0 * g.C + pl) * (int64_t)HW;
+        if (STAGE) {
+            __syncthreads();  // the previous plane's reads are done
+            const float4 *src = reinterpret_cast<const float4 *>(cb);
+            for (int i = threadIdx.x; i < KK * L / 4; i += blockDim.x) reinterpret_cast<float4 *>(slab)[i] = __ldg(src + i);
+            __syncthreads();
+        }
+        const float *sb = STAGE ? slab : cb;
         for (int t = threadIdx.x; t < HW; t += blockDim.x) {
             int iy = t / W, ix = t - iy * W;
             float acc = 0.0f;
@@ -80,7 +90,7 @@ __global__ void __launch_bounds__(128) k_col2im(nck_conv g, const float *__restr
                         ox /= g.sw;
                     }
                     if (ox >= OW) continue;
-                    acc += __ldg(cb + (ki * KW + kj) * L + oy * OW + ox);
+                    acc += STAGE ? sb[(ki * KW + kj) * L + oy * OW + ox] : __ldg(sb + (ki * KW + kj) * L + oy * OW + ox);
                 }
             }
             dp[t] += acc;
@@ -92,7 +102,14 @@ extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, floa
     int64_t total = nb * g->C * g->H * g->W;
     if (total <= 0) return;
     Scope sc(d, "col2im", 0.0, 4.0 * (nb * g->C * g->KH * g->KW * g->OH * g->OW + 2 * total));
-    k_col2im<<<plane_grid(d, nb * g->C), 128, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+    const int64_t slab = g->KH * g->KW * g->OH * g->OW;
+    const size_t bytes = (size_t)slab * sizeof(float);
+    if (slab % 4 == 0 && ((uintptr_t)col & 15) == 0 && bytes <= 48 * 1024) {
+        int64_t planes = nb * g->C, cap = (int64_t)d->sm_count * 8;
+        k_col2im<true><<<(int)(planes < cap ? planes : cap), 256, bytes, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+    } else {
+        k_col2im<false><<<plane_grid(d, nb * g->C), 256, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+    }
     NCK_LAUNCHED(d, 1);
 }
 
@@ -102,22 +119,34 @@ extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, floa
 // accumulators per thread (float4 loads when the plane is 16-byte aligned); the splits are then
 // added in order.
 
-__global__ void k_chan_sum_partial(const float *__restrict__ x, float *__restrict__ part, int64_t N, int64_t C,
-                                   int64_t S, int64_t per_split) {
+template <int V>
+__global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restrict__ x, float *__restrict__ part,
+                                                          int64_t N, int64_t C, int64_t S, int64_t per_split) {
     __shared__ float sm[kThreads / 32];
-    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const int SV = (int)(S / V);
+    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-    const bool vec = (S & 3) == 0 && ((uintptr_t)x & 15) == 0;
-    for (int64_t n = n0; n < n1; n++) {
-        const float *p = x + (n * C + c) * S;
-        if (vec) {
-            const float4 *q = reinterpret_cast<const float4 *>(p);
-            for (int64_t j = threadIdx.x; j < S / 4; j += blockDim.x) {
-                float4 v = __ldg(q + j);
-                a0 += v.x, a1 += v.y, a2 += v.z, a3 += v.w;
-            }
+    int t = threadIdx.x;
+    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
+        const int u = t + blockDim.x, na = t / SV, nb = u / SV;
+        const float *pa = x + ((n0 + na) * C + c) * S, *pb = x + ((n0 + nb) * C + c) * S;
+        if (V == 4) {
+            float4 va = __ldg(reinterpret_cast<const float4 *>(pa) + (t - na * SV));
+            float4 vb = __ldg(reinterpret_cast<const float4 *>(pb) + (u - nb * SV));
+            a0 += va.x + va.y, a1 += va.z + va.w, a2 += vb.x + vb.y, a3 += vb.z + vb.w;
         } else {
-            for (int64_t j = threadIdx.x; j < S; j += blockDim.x) a0 += __ldg(p + j);
+            a0 += __ldg(pa + (t - na * SV)), a2 += __ldg(pb + (u - nb * SV));
+        }
+    }
+    if (t < total) {
+        const int na = t / SV;
+        const float *pa = x + ((n0 + na) * C + c) * S;
+        if (V == 4) {
+            float4 va = __ldg(reinterpret_cast<const float4 *>(pa) + (t - na * SV));
+            a0 += va.x + va.y, a1 += va.z + va.w;
+        } else {
+            a0 += __ldg(pa + (t - na * SV));
         }
     }
     float acc = (a0 + a1) + (a2 + a3);
@@ -143,13 +172,18 @@ extern "C" void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_
     if (N * OC * L <= 0) return;
     Scope sc(d, "conv_bias_grad", 0.0, 4.0 * (N * OC * L + 2 * OC));
     int64_t splits = ((int64_t)d->sm_count * 8 + OC - 1) / OC;
+    int64_t need = (N * L + ((int64_t)1 << 30) - 1) >> 30; /* a block walks at most 2^30 elements */
+    if (splits < need) splits = need;
     if (splits > N) splits = N;
     if (splits < 1) splits = 1;
     int64_t per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)OC, (unsigned)splits);
-    k_chan_sum_partial<<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per);
+    if (L % 4 == 0 && ((uintptr_t)g & 15) == 0)
+        k_chan_sum_partial<4><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per);
+    else
+        k_chan_sum_partial<1><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per);
     k_chan_sum_combine<<<grid_for(d, OC), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, OC, gb);
     NCK_LAUNCHED(d, 2);
 }
@@ -290,11 +324,15 @@ __global__ void __launch_bounds__(128) k_direct_dw_partial(nck_conv g, const flo
     }
 }
 
+// one warp per weight: lanes add strided runs of the slices, then a fixed shuffle tree
 __global__ void k_direct_dw_combine(const float *__restrict__ part, int splits, int64_t n, float *__restrict__ gw) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        float s = gw[i];
-        for (int k = 0; k < splits; k++) s += part[k * n + i];
-        gw[i] = s;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; i < n; i += warps) {
+        float s = 0.0f;
+        for (int k = lane; k < splits; k += 32) s += __ldg(part + k * n + i);
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) gw[i] += s;
     }
 }
 
@@ -312,7 +350,7 @@ static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, cons
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)splits, (unsigned)(g->G * chunks));
     k_direct_dw_partial<KT, OCW><<<grid, 128, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
-    k_direct_dw_combine<<<grid_for(d, wsz), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
+    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
     NCK_LAUNCHED(d, 2);
 }
 
@@ -460,25 +498,30 @@ extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const f
 
 // ---- pooling ---------------------------------------------------------------------------------------------
 
+// Pooling kernels index with I = uint32_t when every index fits (the common case: integer division
+// is several times cheaper than with 64-bit operands), else int64_t.
+template <typename I>
 __global__ void k_pool_fwd(nck_conv g, const float *__restrict__ x, float *__restrict__ y, int32_t *__restrict__ arg,
                            int is_max) {
-    int64_t total = g.N * g.C * g.OH * g.OW;
-    float inv = 1.0f / (float)(g.KH * g.KW);
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ox = t % g.OW, r = t / g.OW;
-        int64_t oy = r % g.OH, plane = r / g.OH;
-        const float *xp = x + plane * g.H * g.W;
+    const I OW = (I)g.OW, OH = (I)g.OH, H = (I)g.H, W = (I)g.W, KH = (I)g.KH, KW = (I)g.KW;
+    const I total = (I)(g.N * g.C) * OH * OW;
+    const float inv = 1.0f / (float)(g.KH * g.KW);
+    for (I t = blockIdx.x * (I)blockDim.x + threadIdx.x; t < total; t += (I)gridDim.x * blockDim.x) {
+        I r = t / OW, ox = t - r * OW;
+        I plane = r / OH, oy = r - plane * OH;
+        const float *xp = x + (int64_t)plane * H * W;
         float best = -INFINITY, acc = 0.0f;
         int32_t bi = -1;
-        for (int64_t ki = 0; ki < g.KH; ki++) {
-            int64_t iy = oy * g.sh - g.ph + ki;
-            if (iy < 0 || iy >= g.H) continue;
-            for (int64_t kj = 0; kj < g.KW; kj++) {
-                int64_t ix = ox * g.sw - g.pw + kj;
-                if (ix < 0 || ix >= g.W) continue;
-                float v = xp[iy * g.W + ix];
+        const int64_t iy0 = (int64_t)oy * g.sh - g.ph, ix0 = (int64_t)ox * g.sw - g.pw;
+        for (I ki = 0; ki < KH; ki++) {
+            int64_t iy = iy0 + (int64_t)ki;
+            if (iy < 0 || iy >= (int64_t)H) continue;
+            for (I kj = 0; kj < KW; kj++) {
+                int64_t ix = ix0 + (int64_t)kj;
+                if (ix < 0 || ix >= (int64_t)W) continue;
+                float v = __ldg(xp + iy * (int64_t)W + ix);
                 acc += v;
-                if (v > best || bi < 0) best = v, bi = (int32_t)(iy * g.W + ix);
+                if (v > best || bi < 0) best = v, bi = (int32_t)(iy * (int64_t)W + ix);
             }
         }
         if (is_max) {
@@ -490,41 +533,49 @@ __global__ void k_pool_fwd(nck_conv g, const float *__restrict__ x, float *__res
     }
 }
 
+static bool small_index(int64_t n) { return n > 0 && n < ((int64_t)1 << 31); }
+
 extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max) {
     int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
     Scope sc(d, is_max ? "max_pool" : "avg_pool", 0.0,
              4.0 * (g->N * g->C * g->H * g->W + (is_max ? 2 : 1) * total));
-    k_pool_fwd<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
+    if (small_index(g->N * g->C * g->H * g->W) && small_index(total))
+        k_pool_fwd<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
+    else
+        k_pool_fwd<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
     NCK_LAUNCHED(d, 1);
 }
 
 // windows that do not overlap: each output adds its gradient to the one input it came from
+template <typename I>
 __global__ void k_maxpool_bwd_scatter(nck_conv g, const float *__restrict__ gy, const int32_t *__restrict__ arg,
                                       float *__restrict__ gx) {
-    int64_t per = g.OH * g.OW, total = g.N * g.C * per;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x)
-        gx[(t / per) * g.H * g.W + arg[t]] += gy[t];
+    const I per = (I)(g.OH * g.OW), total = (I)(g.N * g.C) * per, hw = (I)(g.H * g.W);
+    for (I t = blockIdx.x * (I)blockDim.x + threadIdx.x; t < total; t += (I)gridDim.x * blockDim.x)
+        gx[(int64_t)(t / per) * hw + __ldg(arg + t)] += __ldg(gy + t);
 }
 
 // general windows: each input gathers from the outputs whose window holds it, in output order
+template <typename I>
 __global__ void k_pool_bwd_gather(nck_conv g, const float *__restrict__ gy, const int32_t *__restrict__ arg,
                                   float *__restrict__ gx, int is_max) {
-    int64_t total = g.N * g.C * g.H * g.W;
-    float inv = 1.0f / (float)(g.KH * g.KW);
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ix = t % g.W, r = t / g.W;
-        int64_t iy = r % g.H, plane = r / g.H;
-        int32_t self = (int32_t)(iy * g.W + ix);
-        const float *gp = gy + plane * g.OH * g.OW;
-        const int32_t *ap = is_max ? arg + plane * g.OH * g.OW : nullptr;
+    const I W = (I)g.W, H = (I)g.H;
+    const I total = (I)(g.N * g.C) * H * W;
+    const float inv = 1.0f / (float)(g.KH * g.KW);
+    for (I t = blockIdx.x * (I)blockDim.x + threadIdx.x; t < total; t += (I)gridDim.x * blockDim.x) {
+        I r = t / W, ix = t - r * W;
+        I plane = r / H, iy = r - plane * H;
+        int32_t self = (int32_t)(iy * W + ix);
+        const float *gp = gy + (int64_t)plane * g.OH * g.OW;
+        const int32_t *ap = is_max ? arg + (int64_t)plane * g.OH * g.OW : nullptr;
         float acc = gx[t];
-        int64_t oy0 = iy + g.ph - (g.KH - 1);
+        int64_t oy0 = (int64_t)iy + g.ph - (g.KH - 1);
         oy0 = oy0 <= 0 ? 0 : (oy0 + g.sh - 1) / g.sh;
-        int64_t oy1 = (iy + g.ph) / g.sh;
-        int64_t ox0 = ix + g.pw - (g.KW - 1);
+        int64_t oy1 = ((int64_t)iy + g.ph) / g.sh;
+        int64_t ox0 = (int64_t)ix + g.pw - (g.KW - 1);
         ox0 = ox0 <= 0 ? 0 : (ox0 + g.sw - 1) / g.sw;
-        int64_t ox1 = (ix + g.pw) / g.sw;
+        int64_t ox1 = ((int64_t)ix + g.pw) / g.sw;
         for (int64_t oy = oy0; oy <= oy1 && oy < g.OH; oy++)
             for (int64_t ox = ox0; ox <= ox1 && ox < g.OW; ox++) {
                 int64_t o = oy * g.OW + ox;
@@ -545,11 +596,17 @@ extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, con
     if (is_max && g->sh >= g->KH && g->sw >= g->KW) {
         int64_t total = g->N * g->C * g->OH * g->OW;
         if (total <= 0) return;
-        k_maxpool_bwd_scatter<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx);
+        if (small_index(g->N * g->C * g->H * g->W))
+            k_maxpool_bwd_scatter<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx);
+        else
+            k_maxpool_bwd_scatter<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx);
     } else {
         int64_t total = g->N * g->C * g->H * g->W;
         if (total <= 0) return;
-        k_pool_bwd_gather<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
+        if (small_index(total))
+            k_pool_bwd_gather<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
+        else
+            k_pool_bwd_gather<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
     }
     NCK_LAUNCHED(d, 1);
 }

@@ -259,6 +259,39 @@ __global__ void k_binary_bwd(int kind, int which, KeptRed kr, const float *__res
     }
 }
 
+// no broadcast and every operand laid out like gx: gx[i] += d/dx f at element i
+__global__ void k_binary_bwd_flat(int kind, int which, const float *__restrict__ g, const float *__restrict__ a,
+                                  const float *__restrict__ b, float *__restrict__ gx, int64_t n, int vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const bool ab = kind == NCK_BIN_MUL || kind == NCK_BIN_DIV;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = n >> 2;
+        for (int64_t i = t; i < n4; i += stride) {
+            float4 gv = __ldg((const float4 *)g + i), o = ((float4 *)gx)[i];
+            float4 av = ab ? __ldg((const float4 *)a + i) : make_float4(0, 0, 0, 0);
+            float4 bv = ab ? __ldg((const float4 *)b + i) : make_float4(0, 0, 0, 0);
+            o.x = o.x + bin_grad(kind, which, gv.x, av.x, bv.x);
+            o.y = o.y + bin_grad(kind, which, gv.y, av.y, bv.y);
+            o.z = o.z + bin_grad(kind, which, gv.z, av.z, bv.z);
+            o.w = o.w + bin_grad(kind, which, gv.w, av.w, bv.w);
+            ((float4 *)gx)[i] = o;
+        }
+        done = n4 << 2;
+    }
+    for (int64_t i = done + t; i < n; i += stride)
+        gx[i] = gx[i] + bin_grad(kind, which, g[i], ab ? a[i] : 0.0f, ab ? b[i] : 0.0f);
+}
+
+static bool contiguous_like(const KeptRed &kr, const int64_t *st) {
+    int64_t expect = 1;
+    for (int k = kr.nk - 1; k >= 0; k--) {
+        if (st[k] != expect) return false;
+        expect *= kr.kshape[k];
+    }
+    return true;
+}
+
 extern "C" void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast *bc, const float *g, const float *a,
                                const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel) {
     if (gx_numel <= 0 || bc_numel(bc) <= 0) return;
@@ -279,6 +312,15 @@ extern "C" void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast 
         }
     }
     Scope sc(d, "binary_bwd");
+    const bool ab = kind == NCK_BIN_MUL || kind == NCK_BIN_DIV;
+    if (kr.nr == 0 && contiguous_like(kr, kr.kso) && contiguous_like(kr, kr.ksx) &&
+        (!ab || (contiguous_like(kr, kr.ksa) && contiguous_like(kr, kr.ksb)))) {
+        int vec = (((uintptr_t)g | (uintptr_t)gx | (ab ? ((uintptr_t)a | (uintptr_t)b) : 0)) & 15) == 0;
+        k_binary_bwd_flat<<<grid_for(d, vec ? (gx_numel + 3) / 4 : gx_numel), kThreads, 0, NCK_STREAM(d)>>>(
+            kind, which, g, a, b, gx, gx_numel, vec);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     k_binary_bwd<<<grid_for(d, gx_numel), kThreads, 0, NCK_STREAM(d)>>>(kind, which, kr, g, a, b, gx, gx_numel);
     NCK_LAUNCHED(d, 1);
 }

@@ -36,14 +36,71 @@ __global__ void k_colsum_strided(const float *__restrict__ x, float *__restrict_
     }
 }
 
+// few long rows (a full-tensor sum): block (slice, row) sums a contiguous slice with four
+// accumulators and a fixed tree; k_rowsum_combine adds the slices of a row in order
+__global__ void __launch_bounds__(256) k_rowsum_split(const float *__restrict__ x, float *__restrict__ part, int64_t R,
+                                                      int64_t per, int vec) {
+    __shared__ float sm[8];
+    const int64_t r = blockIdx.y, s0 = blockIdx.x * per, s1 = s0 + per < R ? s0 + per : R;
+    const float *p = x + r * R;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    if (vec) {  // per and the row base are multiples of 4 floats
+        const float4 *q = reinterpret_cast<const float4 *>(p + s0);
+        const int64_t n4 = (s1 - s0) / 4;
+        for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+            float4 v = __ldg(q + i);
+            a0 += v.x, a1 += v.y, a2 += v.z, a3 += v.w;
+        }
+        for (int64_t i = s0 + n4 * 4 + threadIdx.x; i < s1; i += blockDim.x) a0 += __ldg(p + i);
+    } else {
+        for (int64_t i = s0 + threadIdx.x; i < s1; i += blockDim.x) a0 += __ldg(p + i);
+    }
+    float acc = (a0 + a1) + (a2 + a3);
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) t += sm[k];
+        part[r * gridDim.x + blockIdx.x] = t;
+    }
+}
+
+__global__ void k_rowsum_combine(const float *__restrict__ part, int splits, int64_t rows, float *__restrict__ y,
+                                 float scale) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        float s = 0.0f;
+        for (int k = lane; k < splits; k += 32) s += part[r * splits + k];
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) y[r] = scale * s;
+    }
+}
+
 extern "C" void nck_reduce_sum(nck_dev *d, const float *x, float *y, int64_t outer, int64_t R, int64_t inner,
                                float scale) {
     int64_t n = outer * inner;
     if (n <= 0) return;
-    Scope sc(d, "reduce_sum");
+    Scope sc(d, "reduce_sum", 0.0, 4.0 * (n * R + n));
     if (R == 0) {
         cudaMemsetAsync(y, 0, (size_t)n * sizeof(float), NCK_STREAM(d));
         return;
+    }
+    const int64_t sms = d->sm_count > 0 ? d->sm_count : 148;
+    if (inner == 1 && n < sms * 4 && R >= 65536) {
+        int64_t splits = (sms * 8 + n - 1) / n;
+        int64_t per = ((R + splits - 1) / splits + 3) / 4 * 4;
+        splits = (R + per - 1) / per;
+        if (n * splits * (int64_t)sizeof(float) <= (int64_t)d->scratch_bytes && splits <= 65535) {
+            float *part = (float *)d->scratch;
+            const int vec = (R % 4 == 0) && (((uintptr_t)x & 15) == 0);
+            dim3 grid((unsigned)splits, (unsigned)n);
+            k_rowsum_split<<<grid, 256, 0, NCK_STREAM(d)>>>(x, part, R, per, vec);
+            k_rowsum_combine<<<grid_for(d, n * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, n, y, scale);
+            NCK_LAUNCHED(d, 2);
+            return;
+        }
     }
     if (inner == 1) {
         k_rowsum<<<grid_for(d, n * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, n, R, scale);

@@ -151,6 +151,9 @@ static nc_status conv_fwd(nc_node *n) {
         nck_im2col(nc__k(ctx), &g, X, col, n0, nb);
         gemm_fwd(ctx, &g, Wt, col, CKKL, L, B, Y + n0 * g.OC * L, nb);
     }
+    /* one chunk held the whole batch: the unfolded input stays valid in the step arena until step end
+     * and the weight gradient reads it instead of unfolding x again */
+    if (nbmax >= g.N) n->saved = col;
     return NC_OK;
 }
 
@@ -228,6 +231,12 @@ static void conv_bwd(nc_node *n) {
         return;
     }
     int64_t CKKL = g.C * g.KH * g.KW * L, nbmax = chunk_samples(&g);
+    const float *fwd_col = nbmax >= g.N ? (const float *)n->saved : NULL; /* x unfolded by the forward */
+    if (gw && fwd_col) {
+        gemm_dw(ctx, &g, G, fwd_col, CKKL, L, (float *)gw->data, g.N);
+        gw = NULL;
+        if (!gx) return;
+    }
     float *col = (float *)nc__arena_alloc(ctx, (size_t)(nbmax * CKKL) * sizeof(float));
     if (!col) return;
     for (int64_t n0 = 0; n0 < g.N; n0 += nbmax) {
