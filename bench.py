@@ -179,7 +179,11 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     total = sum(t[1] for t in table) or 1.0
     name, ms, cnt, fl, by = max(table, key=lambda t: t[1])
     per_launch_ms = ms / max(cnt, 1)
-    if fl > 0:
+    # the binding roof: a kernel with FLOPs is tensor-bound only when its arithmetic takes longer at the
+    # tensor peak than its algorithmic bytes take at the HBM peak
+    t_tensor = fl / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = by / (peaks["hbm_gbs"] * 1e9)
+    if fl > 0 and t_tensor >= t_hbm:
         achieved = fl / max(cnt, 1) / (per_launch_ms / 1e3) / 1e12
         peak, unit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
     else:
@@ -190,8 +194,12 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(name)
     kernels = sorted(table, key=lambda t: -t[1])[:8]
+    sec = max(per_launch_ms, 1e-9) / 1e3
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic, "peak_src": peaks["src"] + " (MEASURED_PEAKS.json)",
+            "algorithmic_bytes_per_launch": round(by / max(cnt, 1)), "flops_per_launch": round(fl / max(cnt, 1)),
+            "achieved_gbs": round(by / max(cnt, 1) / sec / 1e9, 1),
+            "achieved_tflops": round(fl / max(cnt, 1) / sec / 1e12, 2),
             "share_of_step_kernel_time": round(ms / total, 3), "launches_per_step": cnt / steps,
             "top_kernels": [{"name": t[0], "ms_per_step": round(t[1] / steps, 4), "share": round(t[1] / total, 3)}
                             for t in kernels]}

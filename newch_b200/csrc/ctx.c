@@ -393,6 +393,8 @@ nc_ctx *nc_init(const nc_config *cfg) {
     ctx->dev.status = (int *)st_dev;
     ctx->dev.scratch_bytes = (size_t)64 << 20;
     if (!nc__cuda_ok(ctx, cudaMalloc(&ctx->dev.scratch, ctx->dev.scratch_bytes), "scratch")) return ctx;
+    if (!nc__cuda_ok(ctx, cudaMalloc((void **)&ctx->dev.counters, 256), "counters")) return ctx;
+    if (!nc__cuda_ok(ctx, cudaMemset(ctx->dev.counters, 0, 256), "counters")) return ctx;
     void *stage = NULL;
     if (cudaHostAlloc(&stage, NC_STAGE_BYTES, cudaHostAllocDefault) == cudaSuccess) {
         ctx->stage = (unsigned char *)stage;
@@ -431,6 +433,7 @@ void nc_free_ctx(nc_ctx *ctx) {
             if (ctx->stage_events[i]) cudaEventDestroy((cudaEvent_t)ctx->stage_events[i]);
         if (ctx->stage) cudaFreeHost(ctx->stage);
         if (ctx->dev.scratch) cudaFree(ctx->dev.scratch);
+        if (ctx->dev.counters) cudaFree(ctx->dev.counters);
         if (ctx->dev.status_host) cudaFreeHost(ctx->dev.status_host);
         nck_timer_enable(&ctx->dev, 0);
         cudaStreamDestroy(s);

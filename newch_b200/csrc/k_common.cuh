@@ -24,6 +24,23 @@ inline int grid_for(const nck_dev *d, int64_t n, int threads = kThreads, int per
 // Records a kernel-detected error (first one wins). The host reads it at its next synchronization.
 __device__ __forceinline__ void report(int *status, int code) { atomicCAS(status, 0, code); }
 
+// True in the one block of the grid that finishes last: every block's thread 0 publishes its
+// partial result, fences and counts itself in; the block that makes the count complete sees all the
+// partials (read them with ld.global.cg) and re-arms the counter to 0 for the next launch.
+__device__ __forceinline__ bool last_block_done(unsigned *counter) {
+    __shared__ bool last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        last = atomicAdd(counter, 1u) == total - 1;
+        if (last) atomicExch(counter, 0u);
+    }
+    __syncthreads();
+    if (last) __threadfence();
+    return last;
+}
+
 // RAII timing scope: when the device has a timer, brackets the launches inside with CUDA events.
 struct Scope {
     nck_dev *d;

@@ -121,7 +121,8 @@ extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, floa
 
 template <int V>
 __global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restrict__ x, float *__restrict__ part,
-                                                          int64_t N, int64_t C, int64_t S, int64_t per_split) {
+                                                          int64_t N, int64_t C, int64_t S, int64_t per_split,
+                                                          float *__restrict__ gb, unsigned *counter) {
     __shared__ float sm[kThreads / 32];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const int SV = (int)(S / V);
@@ -158,13 +159,12 @@ __global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restric
         for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += sm[k];
         part[blockIdx.y * C + c] = s;
     }
-}
-
-__global__ void k_chan_sum_combine(const float *__restrict__ part, int splits, int64_t C, float *__restrict__ gb) {
-    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
-        float s = gb[c];
-        for (int k = 0; k < splits; k++) s += part[k * C + c];
-        gb[c] = s;
+    if (last_block_done(counter)) {  // gb[c] += the splits of channel c, in order
+        for (int64_t cc = threadIdx.x; cc < C; cc += blockDim.x) {
+            float t = gb[cc];
+            for (int k = 0; k < (int)gridDim.y; k++) t += __ldcg(part + k * C + cc);
+            gb[cc] = t;
+        }
     }
 }
 
@@ -181,11 +181,10 @@ extern "C" void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)OC, (unsigned)splits);
     if (L % 4 == 0 && ((uintptr_t)g & 15) == 0)
-        k_chan_sum_partial<4><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per);
+        k_chan_sum_partial<4><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per, gb, d->counters);
     else
-        k_chan_sum_partial<1><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per);
-    k_chan_sum_combine<<<grid_for(d, OC), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, OC, gb);
-    NCK_LAUNCHED(d, 2);
+        k_chan_sum_partial<1><<<grid, kThreads, 0, NCK_STREAM(d)>>>(g, part, N, OC, L, per, gb, d->counters);
+    NCK_LAUNCHED(d, 1);
 }
 
 // ---- direct convolution: each thread reads its receptive field once and produces every output
@@ -535,12 +534,53 @@ __global__ void k_pool_fwd(nck_conv g, const float *__restrict__ x, float *__res
 
 static bool small_index(int64_t n) { return n > 0 && n < ((int64_t)1 << 31); }
 
+// 2x2 max pooling with stride 2 and no padding, input width a multiple of 4: a thread reads one float4
+// from each of the two input rows of a window pair and writes two adjacent outputs (taps in newch's
+// order, the first maximum kept)
+__device__ __forceinline__ void max4(float a, float b, float c, float d, int32_t ia, int32_t W, float &best,
+                                     int32_t &bi) {
+    best = a, bi = ia;
+    if (b > best) best = b, bi = ia + 1;
+    if (c > best) best = c, bi = ia + W;
+    if (d > best) best = d, bi = ia + W + 1;
+}
+
+__global__ void __launch_bounds__(256) k_maxpool2x2(const float *__restrict__ x, float *__restrict__ y,
+                                                    int32_t *__restrict__ arg, uint32_t planes, uint32_t H, uint32_t W,
+                                                    uint32_t OH, uint32_t OW) {
+    const uint32_t pairs = (OW + 1) / 2, total = planes * OH * pairs;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = t / pairs, q = t - r * pairs, pl = r / OH, oy = r - pl * OH;
+        const float *r0 = x + (size_t)pl * H * W + (size_t)(2 * oy) * W;
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(r0) + q);
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(r0 + W) + q);
+        const int32_t i0 = (int32_t)(2 * oy * W + 4 * q);
+        const size_t o = (size_t)pl * OH * OW + (size_t)oy * OW + 2 * q;
+        float best;
+        int32_t bi;
+        max4(a.x, a.y, b.x, b.y, i0, (int32_t)W, best, bi);
+        y[o] = best;
+        arg[o] = bi;
+        if (2 * q + 1 < OW) {
+            max4(a.z, a.w, b.z, b.w, i0 + 2, (int32_t)W, best, bi);
+            y[o + 1] = best;
+            arg[o + 1] = bi;
+        }
+    }
+}
+
 extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max) {
     int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
     Scope sc(d, is_max ? "max_pool" : "avg_pool", 0.0,
              4.0 * (g->N * g->C * g->H * g->W + (is_max ? 2 : 1) * total));
-    if (small_index(g->N * g->C * g->H * g->W) && small_index(total))
+    const int64_t planes = g->N * g->C;
+    if (is_max && g->KH == 2 && g->KW == 2 && g->sh == 2 && g->sw == 2 && g->ph == 0 && g->pw == 0 && g->W % 4 == 0 &&
+        ((uintptr_t)x & 15) == 0 && small_index(planes * g->H * g->W)) {
+        const int64_t items = planes * g->OH * ((g->OW + 1) / 2);
+        k_maxpool2x2<<<grid_for(d, items), 256, 0, NCK_STREAM(d)>>>(x, y, arg, (uint32_t)planes, (uint32_t)g->H,
+                                                                  (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW);
+    } else if (small_index(g->N * g->C * g->H * g->W) && small_index(total))
         k_pool_fwd<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
     else
         k_pool_fwd<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);

@@ -190,6 +190,8 @@ __global__ void __launch_bounds__(kIcThreads, 1) k_convgemm(IcParams p) {
         // each thread issues all of its loads for a stage before it splits and stores any of them ----
         const int pt = tid - kProdWarp0 * 32, grp = pt >> 7, tt = pt & 127;
         int64_t it = 0;
+        int pst = 0;
+        uint32_t pph = 0;
         bool ok = true;
         for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
             Unit w = unit_of(p, u);
@@ -209,9 +211,12 @@ __global__ void __launch_bounds__(kIcThreads, 1) k_convgemm(IcParams p) {
                 }
             }
             for (int64_t ks = 0; ks < ksteps; ks++, it++) {
+                // stage and phase of step it, advanced by counting (every step, the other group's too)
+                const int st = pst;
+                const uint32_t ph = pph;
+                if (++pst == S) pst = 0, pph ^= 1;
                 if ((it & 1) != grp) continue;
-                const int st = (int)(it % S);
-                if (it >= S && !(ok = mbar_wait(&s.empty[st], (uint32_t)(((it / S) & 1) ^ 1), p.status))) break;
+                if (it >= S && !(ok = mbar_wait(&s.empty[st], ph ^ 1, p.status))) break;
                 const int k0 = (int)(w.k_lo + ks * TK);
                 float *ta = ring_a + st * kStageA, *ra = rest_a + st * kStageA;
                 float *tb = ring_b + st * sbq, *rb = rest_b + st * sbq;
@@ -309,6 +314,12 @@ __global__ void __launch_bounds__(kIcThreads, 1) k_convgemm(IcParams p) {
         if (lane == 0) {
             // ---- MMA issuer ----------------------------------------------------------------------------
             const uint32_t idesc = idesc_tf32(0, 0, BN);
+            const uint64_t dA = stage_desc(smem_u32(ring_a), 0, 0), dB = stage_desc(smem_u32(ring_b), 0, 0);
+            const uint32_t stA = (uint32_t)(kStageA * 4) >> 4, stB = (uint32_t)(sbq * 4) >> 4;
+            const uint64_t restA = (uint64_t)((smem_u32(rest_a) - smem_u32(ring_a)) >> 4);
+            const uint64_t restB = (uint64_t)((smem_u32(rest_b) - smem_u32(ring_b)) >> 4);
+            int st = 0;
+            uint32_t ph = 0;
             int64_t it = 0, local = 0;
             bool ok = true;
             for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, local++) {
@@ -320,21 +331,22 @@ __global__ void __launch_bounds__(kIcThreads, 1) k_convgemm(IcParams p) {
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t d = tmem + (uint32_t)acc * (tcols / 2);
                 for (int64_t ks = 0; ks < ksteps; ks++, it++) {
-                    const int st = (int)(it % S);
-                    if (!(ok = mbar_wait(&s.full[st], (uint32_t)((it / S) & 1), p.status))) break;
+                    if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    const uint32_t ab = smem_u32(ring_a + st * kStageA), bb = smem_u32(ring_b + st * sbq);
-                    const uint32_t al = smem_u32(rest_a + st * kStageA), bl = smem_u32(rest_b + st * sbq);
+                    // descriptors by addition: only the start-address field moves
+                    const uint64_t a0 = dA + (uint64_t)(st * stA), b0 = dB + (uint64_t)(st * stB);
 #pragma unroll
                     for (int k = 0; k < TK / 8; k++) {
                         const uint32_t accum = (ks > 0 || k > 0) ? 1u : 0u;
-                        mma_tf32(d, stage_desc(ab, 0, k), stage_desc(bb, 0, k), idesc, accum);
+                        const uint64_t ak = a0 + (uint64_t)(2 * k), bk = b0 + (uint64_t)(2 * k);
+                        mma_tf32(d, ak, bk, idesc, accum);
                         if (three) {
-                            mma_tf32(d, stage_desc(ab, 0, k), stage_desc(bl, 0, k), idesc, 1u);
-                            mma_tf32(d, stage_desc(al, 0, k), stage_desc(bb, 0, k), idesc, 1u);
+                            mma_tf32(d, ak, bk + restB, idesc, 1u);
+                            mma_tf32(d, ak + restA, bk, idesc, 1u);
                         }
                     }
                     mma_commit(&s.empty[st]);
+                    if (++st == S) st = 0, ph ^= 1;
                 }
                 if (ok) mma_commit(&s.tfull[acc]);
             }

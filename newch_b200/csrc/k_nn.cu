@@ -445,9 +445,31 @@ __device__ __forceinline__ void bn_load(const float *p, int64_t i, float (&v)[V]
     }
 }
 
+// per-channel statistics -> mean, invstd and running statistics (unbiased variance), splits in order
+struct BnFwdFin {
+    float *mean, *invstd, *rm, *rv;
+    float mom, eps;
+    int splits;
+};
+
+__device__ void bn_fwd_finalize(const double *part, int64_t C, int64_t M, const BnFwdFin &f) {
+    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+        double s = 0.0, ss = 0.0;
+        for (int k = 0; k < f.splits; k++) s += __ldcg(part + (k * C + c) * 2), ss += __ldcg(part + (k * C + c) * 2 + 1);
+        double mu = s / (double)M;
+        double dev = ss - s * mu; /* sum of squared deviations */
+        if (dev < 0.0) dev = 0.0;
+        f.mean[c] = (float)mu;
+        f.invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)f.eps));
+        f.rm[c] = (1.0f - f.mom) * f.rm[c] + f.mom * (float)mu;
+        f.rv[c] = (1.0f - f.mom) * f.rv[c] + f.mom * (float)(dev / (double)(M - 1));
+    }
+}
+
 template <int V>
 __global__ void __launch_bounds__(256) k_bn_stats(const float *__restrict__ x, double *__restrict__ part, int64_t N,
-                                                  int64_t C, int64_t S, int64_t per_split) {
+                                                  int64_t C, int64_t S, int64_t per_split, BnFwdFin fin,
+                                                  unsigned *counter) {
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const int SV = (int)(S / V);
@@ -482,21 +504,7 @@ __global__ void __launch_bounds__(256) k_bn_stats(const float *__restrict__ x, d
         part[(blockIdx.y * C + c) * 2] = s;
         part[(blockIdx.y * C + c) * 2 + 1] = ss;
     }
-}
-
-__global__ void k_bn_finalize(const double *__restrict__ part, int splits, int64_t C, int64_t M, float *mean,
-                              float *invstd, float *rm, float *rv, float mom, float eps) {
-    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
-        double s = 0.0, ss = 0.0;
-        for (int k = 0; k < splits; k++) s += part[(k * C + c) * 2], ss += part[(k * C + c) * 2 + 1];
-        double mu = s / (double)M;
-        double dev = ss - s * mu; /* sum of squared deviations */
-        if (dev < 0.0) dev = 0.0;
-        mean[c] = (float)mu;
-        invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)eps));
-        rm[c] = (1.0f - mom) * rm[c] + mom * (float)mu;
-        rv[c] = (1.0f - mom) * rv[c] + mom * (float)(dev / (double)(M - 1));
-    }
+    if (last_block_done(counter)) bn_fwd_finalize(part, C, N * S, fin);
 }
 
 __global__ void k_bn_eval_stats(const float *__restrict__ rm, const float *__restrict__ rv, float *mean, float *invstd,
@@ -558,14 +566,13 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
     double *part = (double *)d->scratch;
     dim3 g1((unsigned)C, (unsigned)splits);
     const bool v4 = bn_vec4(S, x, y, x);
-    if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
-    else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per);
-    k_bn_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, mean, invstd, rm, rv,
-                                                                   mom, eps);
+    const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits};
+    if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
+    else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     int64_t planes = N * C;
     if (v4) k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
     else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
-    NCK_LAUNCHED(d, 3);
+    NCK_LAUNCHED(d, 2);
 }
 
 extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
@@ -585,11 +592,28 @@ extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, cons
 
 // backward sums per channel: sg = sum g, sgx = sum g * xhat (float products, double sums); same
 // walk as the statistics kernel
+// backward sums -> weight / bias gradients and the two means the input gradient needs
+struct BnBwdFin {
+    float *gw, *gb, *coef;
+    int splits;
+};
+
+__device__ void bn_bwd_finalize(const double *part, int64_t C, int64_t M, const BnBwdFin &f) {
+    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+        double sg = 0.0, sgx = 0.0;
+        for (int k = 0; k < f.splits; k++) sg += __ldcg(part + (k * C + c) * 2), sgx += __ldcg(part + (k * C + c) * 2 + 1);
+        if (f.gw) f.gw[c] += (float)sgx;
+        if (f.gb) f.gb[c] += (float)sg;
+        f.coef[2 * c] = (float)(sg / (double)M);
+        f.coef[2 * c + 1] = (float)(sgx / (double)M);
+    }
+}
+
 template <int V>
 __global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x, const float *__restrict__ g,
                                                      const float *__restrict__ mean, const float *__restrict__ invstd,
                                                      double *__restrict__ part, int64_t N, int64_t C, int64_t S,
-                                                     int64_t per_split) {
+                                                     int64_t per_split, BnBwdFin fin, unsigned *counter) {
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const float mu = mean[c], is = invstd[c];
@@ -627,18 +651,7 @@ __global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x
         part[(blockIdx.y * C + c) * 2] = sg;
         part[(blockIdx.y * C + c) * 2 + 1] = sgx;
     }
-}
-
-__global__ void k_bn_bwd_finalize(const double *__restrict__ part, int splits, int64_t C, int64_t M,
-                                  float *__restrict__ gw, float *__restrict__ gb, float *__restrict__ coef) {
-    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
-        double sg = 0.0, sgx = 0.0;
-        for (int k = 0; k < splits; k++) sg += part[(k * C + c) * 2], sgx += part[(k * C + c) * 2 + 1];
-        if (gw) gw[c] += (float)sgx;
-        if (gb) gb[c] += (float)sg;
-        coef[2 * c] = (float)(sg / (double)M);
-        coef[2 * c + 1] = (float)(sgx / (double)M);
-    }
+    if (last_block_done(counter)) bn_bwd_finalize(part, C, N * S, fin);
 }
 
 // gx += k * (g - mean(g) - xhat * mean(g * xhat)) in training, gx += k * g in eval; flat walk
@@ -680,10 +693,10 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     dim3 g1((unsigned)C, (unsigned)splits);
     const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
-    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
-    else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per);
-    k_bn_bwd_finalize<<<grid_for(d, C), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, C, N * S, gw, gb, coef);
-    int launched = 2;
+    const BnBwdFin fin = {gw, gb, coef, (int)splits};
+    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
+    else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
+    int launched = 1;
     if (gx) {
         int64_t planes = N * C;
         if (v4)

@@ -150,17 +150,16 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
     if (warp == kLoadWarp) {
         if (lane == 0) {
             // ---- loader ------------------------------------------------------------------------------
+            // stage, phase, batch and K position advance by counting: no division per K step
             int64_t it = 0;
+            int st = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
                 Unit w = unit_of(p, u);
-                int64_t kt = (w.k1 - w.k0 + TK - 1) / TK;
+                int b = (int)w.b0, kk = (int)w.k0;
                 for (int64_t t = 0; t < w.steps; t++, it++) {
-                    int st = (int)(it % S);
-                    uint32_t ph = (uint32_t)((it / S) & 1);
                     if (it >= S && !(ok = mbar_wait(&s.empty[st], ph ^ 1, p.status))) break;
-                    int b = (int)(w.b0 + t / kt);
-                    int kk = (int)(w.k0 + (t % kt) * TK);
                     mbar_expect_tx(&s.full[st], stage_bytes);
                     if (!p.p_mn) {
                         if (p.p_bat) tma_3d(ring_a + st * kStageA, &tmP, kk, (int)w.r0, b, &s.full[st]);
@@ -180,6 +179,9 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                             else tma_2d(ring_b + st * sbq + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
                         }
                     }
+                    if (++st == S) st = 0, ph ^= 1;
+                    kk += TK;
+                    if (kk >= w.k1) kk = (int)w.k0, b++;
                 }
             }
             // no copy may still be landing in shared memory when the CTA exits
@@ -191,7 +193,14 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
         if (lane == 0) {
             // ---- MMA issuer ----------------------------------------------------------------------------
             const uint32_t idesc = idesc_tf32(p.p_mn, p.q_mn, BN);
+            const uint64_t dA = stage_desc(smem_u32(ring_a), p.p_mn, 0), dB = stage_desc(smem_u32(ring_b), p.q_mn, 0);
+            const uint32_t stA = (uint32_t)(kStageA * 4) >> 4, stB = (uint32_t)(sbq * 4) >> 4;
+            const uint32_t kA = p.p_mn ? 64u : 2u, kB = p.q_mn ? 64u : 2u;  // 8 K rows (MN-major) or 32 B
+            const uint64_t restA = (uint64_t)((smem_u32(rest_a) - smem_u32(ring_a)) >> 4);
+            const uint64_t restB = (uint64_t)((smem_u32(rest_b) - smem_u32(ring_b)) >> 4);
             int64_t it = 0, local = 0;
+            int st = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, local++) {
                 Unit w = unit_of(p, u);
@@ -201,21 +210,23 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t d = tmem + (uint32_t)acc * (tcols / 2);
                 for (int64_t t = 0; t < w.steps; t++, it++) {
-                    int st = (int)(it % S);
-                    uint32_t ph = (uint32_t)((it / S) & 1);
                     if (!(ok = mbar_wait(THREE ? &s.ready[st] : &s.full[st], ph, p.status))) break;
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    uint32_t ab = smem_u32(ring_a + st * kStageA), bb = smem_u32(ring_b + st * sbq);
+                    // descriptors by addition: the start address (bits 0-13, in 16-byte units) is the only
+                    // field that moves between stages and K steps
+                    const uint64_t a0 = dA + (uint64_t)(st * stA), b0 = dB + (uint64_t)(st * stB);
+#pragma unroll
                     for (int k = 0; k < TK / 8; k++) {
-                        uint32_t accum = (t > 0 || k > 0) ? 1u : 0u;
-                        mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, accum);
+                        const uint32_t accum = (t > 0 || k > 0) ? 1u : 0u;
+                        const uint64_t ak = a0 + (uint64_t)(k * kA), bk = b0 + (uint64_t)(k * kB);
+                        mma_tf32(d, ak, bk, idesc, accum);
                         if (THREE) {
-                            uint32_t al = smem_u32(rest_a + st * kStageA), bl = smem_u32(rest_b + st * sbq);
-                            mma_tf32(d, stage_desc(ab, p.p_mn, k), stage_desc(bl, p.q_mn, k), idesc, 1u);
-                            mma_tf32(d, stage_desc(al, p.p_mn, k), stage_desc(bb, p.q_mn, k), idesc, 1u);
+                            mma_tf32(d, ak, bk + restB, idesc, 1u);
+                            mma_tf32(d, ak + restA, bk, idesc, 1u);
                         }
                     }
                     mma_commit(&s.empty[st]);  // the loader may refill this stage once these MMAs read it
+                    if (++st == S) st = 0, ph ^= 1;
                 }
                 if (ok) mma_commit(&s.tfull[acc]);
             }
@@ -227,13 +238,12 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
         // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head -------------
         const int t2 = tid - kSplitWarp0 * 32;  // 0 .. kSplitThreads - 1
         const int nb = BN * TK / 4;
-        int64_t it = 0;
+        int st = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
             Unit w = unit_of(p, u);
-            for (int64_t t = 0; t < w.steps; t++, it++) {
-                int st = (int)(it % S);
-                uint32_t ph = (uint32_t)((it / S) & 1);
+            for (int64_t t = 0; t < w.steps; t++) {
                 if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
                 float4 *ah = reinterpret_cast<float4 *>(ring_a + st * kStageA), *al = reinterpret_cast<float4 *>(rest_a + st * kStageA);
                 for (int i = t2; i < TM * TK / 4; i += kSplitThreads) {
@@ -249,6 +259,7 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
                 mbar_arrive(&s.ready[st]);
+                if (++st == S) st = 0, ph ^= 1;
             }
         }
     } else if (warp < kEpiWarps) {

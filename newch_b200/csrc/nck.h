@@ -28,6 +28,7 @@ typedef struct nck_dev {
     int conv_implicit; /* 1: convolutions try the implicit-GEMM kernels before unfolding (NC_CONV=implicit) */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
+    unsigned *counters; /* device counters for last-block-finishes reductions; each user leaves it at 0 */
     size_t scratch_bytes;
 } nck_dev;
 
