@@ -56,7 +56,7 @@ extern "C" void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float 
 // memory with 16-byte loads (full-bandwidth reads), and the gathers read shared memory.
 template <bool STAGE>
 __global__ void __launch_bounds__(256) k_col2im(nck_conv g, const float *__restrict__ col, float *__restrict__ dx,
-                                                int64_t n0, int64_t nb) {
+                                                int64_t n0, int64_t nb, int accum) {
     extern __shared__ float slab[];
     const int L = (int)(g.OH * g.OW), OH = (int)g.OH, OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
     const int KH = (int)g.KH, KW = (int)g.KW, KK = KH * KW, HW = H * W;
@@ -93,12 +93,13 @@ __global__ void __launch_bounds__(256) k_col2im(nck_conv g, const float *__restr
                     acc += STAGE ? sb[(ki * KW + kj) * L + oy * OW + ox] : __ldg(sb + (ki * KW + kj) * L + oy * OW + ox);
                 }
             }
-            dp[t] += acc;
+            dp[t] = (accum ? dp[t] : 0.0f) + acc;
         }
     }
 }
 
-extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb) {
+extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb,
+                           int acc) {
     int64_t total = nb * g->C * g->H * g->W;
     if (total <= 0) return;
     Scope sc(d, "col2im", 0.0, 4.0 * (nb * g->C * g->KH * g->KW * g->OH * g->OW + 2 * total));
@@ -106,9 +107,9 @@ extern "C" void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, floa
     const size_t bytes = (size_t)slab * sizeof(float);
     if (slab % 4 == 0 && ((uintptr_t)col & 15) == 0 && bytes <= 48 * 1024) {
         int64_t planes = nb * g->C, cap = (int64_t)d->sm_count * 8;
-        k_col2im<true><<<(int)(planes < cap ? planes : cap), 256, bytes, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+        k_col2im<true><<<(int)(planes < cap ? planes : cap), 256, bytes, NCK_STREAM(d)>>>(*g, col, dx, n0, nb, acc);
     } else {
-        k_col2im<false><<<plane_grid(d, nb * g->C), 256, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb);
+        k_col2im<false><<<plane_grid(d, nb * g->C), 256, 0, NCK_STREAM(d)>>>(*g, col, dx, n0, nb, acc);
     }
     NCK_LAUNCHED(d, 1);
 }
@@ -629,10 +630,40 @@ __global__ void k_pool_bwd_gather(nck_conv g, const float *__restrict__ gy, cons
     }
 }
 
+// Non-overlapping windows (stride >= kernel) into a fresh gradient buffer: each input element lies in
+// at most one window, so it is stored once: the window's gradient where it was the maximum (max) or
+// gy / (KH*KW) (average), 0 elsewhere; the same values zero-fill plus scatter would leave.
+__global__ void k_pool_bwd_set(nck_conv g, const float *__restrict__ gy, const int32_t *__restrict__ arg,
+                               float *__restrict__ gx, int is_max) {
+    const uint32_t W = (uint32_t)g.W, H = (uint32_t)g.H, OH = (uint32_t)g.OH, OW = (uint32_t)g.OW;
+    const uint32_t total = (uint32_t)(g.N * g.C) * H * W;
+    const float inv = 1.0f / (float)(g.KH * g.KW);
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = t / W, ix = t - r * W, plane = r / H, iy = r - plane * H;
+        const uint32_t ty = iy + (uint32_t)g.ph, tx = ix + (uint32_t)g.pw;
+        const uint32_t oy = ty / (uint32_t)g.sh, ox = tx / (uint32_t)g.sw;
+        float v = 0.0f;
+        if (ty - oy * (uint32_t)g.sh < (uint32_t)g.KH && tx - ox * (uint32_t)g.sw < (uint32_t)g.KW && oy < OH &&
+            ox < OW) {
+            const size_t o = (size_t)plane * OH * OW + (size_t)oy * OW + ox;
+            if (is_max) v = __ldg(arg + o) == (int32_t)(iy * W + ix) ? __ldg(gy + o) : 0.0f;
+            else v = __ldg(gy + o) * inv;
+        }
+        gx[t] = v;
+    }
+}
+
 extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx,
-                             int is_max) {
+                             int is_max, int acc) {
     Scope sc(d, is_max ? "max_pool_bwd" : "avg_pool_bwd", 0.0,
              4.0 * ((is_max ? 2 : 1) * g->N * g->C * g->OH * g->OW + 2 * g->N * g->C * g->H * g->W));
+    const int64_t in_total = g->N * g->C * g->H * g->W;
+    if (!acc && g->sh >= g->KH && g->sw >= g->KW && small_index(in_total)) {
+        k_pool_bwd_set<<<grid_for(d, in_total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
+    if (!acc) cudaMemsetAsync(gx, 0, (size_t)in_total * sizeof(float), NCK_STREAM(d));
     if (is_max && g->sh >= g->KH && g->sw >= g->KW) {
         int64_t total = g->N * g->C * g->OH * g->OW;
         if (total <= 0) return;

@@ -436,14 +436,23 @@ int stages_for(int bn, bool three, int K) {
 // Implicit-GEMM convolution (mode 0 forward, 1 dX, 2 dW). Returns 0 without launching anything when
 // the convolution is not one it handles (groups != 1, dX with a stride, too many taps, the FFMA GEMM
 // mode), and the caller takes the unfolded path.
-extern "C" int nck_conv_implicit(nck_dev *d, int mode, const nck_conv *g, const float *in, const float *q, float *out,
-                                 const float *bias) {
+extern "C" int nck_conv_implicit_supported(const nck_dev *d, int mode, const nck_conv *g) {
     if (!d->conv_implicit || d->gemm_mode == NCK_GEMM_FFMA || g->G != 1) return 0;
     if (mode == IC_DX && (g->sh != 1 || g->sw != 1)) return 0;
     const int64_t KK = g->KH * g->KW, L = g->OH * g->OW, HW = g->H * g->W;
     const int64_t K = (mode == IC_DX ? g->OC : g->C) * KK;
     if (K <= 0 || K > kMaxTaps || g->N <= 0 || L <= 0) return 0;
     if (g->C * HW > INT32_MAX / 2 || g->OC * L > INT32_MAX / 2 || g->C * KK * g->OC > INT32_MAX / 2) return 0;
+    const int64_t npos = mode == IC_DX ? g->N * HW : g->N * L;
+    if (npos >= ((int64_t)1 << 31)) return 0; /* positions index in 32 bits */
+    return stages_for(pick_bn_ic(mode == IC_DX ? g->C : g->OC), d->gemm_mode == NCK_GEMM_3XTF32, (int)K) >= 2;
+}
+
+extern "C" int nck_conv_implicit(nck_dev *d, int mode, const nck_conv *g, const float *in, const float *q, float *out,
+                                 const float *bias) {
+    if (!nck_conv_implicit_supported(d, mode, g)) return 0;
+    const int64_t KK = g->KH * g->KW, L = g->OH * g->OW, HW = g->H * g->W;
+    const int64_t K = (mode == IC_DX ? g->OC : g->C) * KK;
     const bool three = d->gemm_mode == NCK_GEMM_3XTF32;
 
     IcParams p;

@@ -101,13 +101,13 @@ __global__ void k_unary_fwd(int kind, float s, const float *__restrict__ x, floa
 }
 
 __global__ void k_unary_bwd(int kind, float s, const float *__restrict__ x, const float *__restrict__ y,
-                            const float *__restrict__ g, float *__restrict__ gi, int64_t n, int vec) {
+                            const float *__restrict__ g, float *__restrict__ gi, int64_t n, int vec, int acc) {
     int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (vec) {
         int64_t n4 = n >> 2;
         for (int64_t i = t; i < n4; i += stride) {
             float4 xv = ((const float4 *)x)[i], yv = ((const float4 *)y)[i], gv = ((const float4 *)g)[i];
-            float4 o = ((float4 *)gi)[i];
+            float4 o = acc ? ((float4 *)gi)[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             o.x = accumulate(kind, s, o.x, gv.x, unary_grad(kind, s, xv.x, yv.x, gv.x));
             o.y = accumulate(kind, s, o.y, gv.y, unary_grad(kind, s, xv.y, yv.y, gv.y));
             o.z = accumulate(kind, s, o.z, gv.z, unary_grad(kind, s, xv.z, yv.z, gv.z));
@@ -115,10 +115,10 @@ __global__ void k_unary_bwd(int kind, float s, const float *__restrict__ x, cons
             ((float4 *)gi)[i] = o;
         }
         for (int64_t i = (n4 << 2) + t; i < n; i += stride)
-            gi[i] = accumulate(kind, s, gi[i], g[i], unary_grad(kind, s, x[i], y[i], g[i]));
+            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad(kind, s, x[i], y[i], g[i]));
     } else {
         for (int64_t i = t; i < n; i += stride)
-            gi[i] = accumulate(kind, s, gi[i], g[i], unary_grad(kind, s, x[i], y[i], g[i]));
+            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad(kind, s, x[i], y[i], g[i]));
     }
 }
 
@@ -142,13 +142,13 @@ extern "C" void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, flo
 }
 
 extern "C" void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, const float *y, const float *g,
-                              float *gi, int64_t n) {
+                              float *gi, int acc, int64_t n) {
     if (n <= 0) return;
     /* reads x, g and the accumulator (and y where the derivative uses it), writes the accumulator */
     int uses_y = kind == NCK_UN_EXP || kind == NCK_UN_SQRT || kind == NCK_UN_SIGMOID || kind == NCK_UN_TANH;
-    Scope sc(d, unary_name(kind, 1), 0.0, (16.0 + (uses_y ? 4.0 : 0.0)) * n);
+    Scope sc(d, unary_name(kind, 1), 0.0, (12.0 + (acc ? 4.0 : 0.0) + (uses_y ? 4.0 : 0.0)) * n);
     int vec = (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)gi) & 15) == 0;
-    k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec);
+    k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec, acc);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -261,14 +261,14 @@ __global__ void k_binary_bwd(int kind, int which, KeptRed kr, const float *__res
 
 // no broadcast and every operand laid out like gx: gx[i] += d/dx f at element i
 __global__ void k_binary_bwd_flat(int kind, int which, const float *__restrict__ g, const float *__restrict__ a,
-                                  const float *__restrict__ b, float *__restrict__ gx, int64_t n, int vec) {
+                                  const float *__restrict__ b, float *__restrict__ gx, int64_t n, int vec, int acc) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     const bool ab = kind == NCK_BIN_MUL || kind == NCK_BIN_DIV;
     int64_t done = 0;
     if (vec) {
         const int64_t n4 = n >> 2;
         for (int64_t i = t; i < n4; i += stride) {
-            float4 gv = __ldg((const float4 *)g + i), o = ((float4 *)gx)[i];
+            float4 gv = __ldg((const float4 *)g + i), o = acc ? ((float4 *)gx)[i] : make_float4(0, 0, 0, 0);
             float4 av = ab ? __ldg((const float4 *)a + i) : make_float4(0, 0, 0, 0);
             float4 bv = ab ? __ldg((const float4 *)b + i) : make_float4(0, 0, 0, 0);
             o.x = o.x + bin_grad(kind, which, gv.x, av.x, bv.x);
@@ -280,7 +280,7 @@ __global__ void k_binary_bwd_flat(int kind, int which, const float *__restrict__
         done = n4 << 2;
     }
     for (int64_t i = done + t; i < n; i += stride)
-        gx[i] = gx[i] + bin_grad(kind, which, g[i], ab ? a[i] : 0.0f, ab ? b[i] : 0.0f);
+        gx[i] = (acc ? gx[i] : 0.0f) + bin_grad(kind, which, g[i], ab ? a[i] : 0.0f, ab ? b[i] : 0.0f);
 }
 
 static bool contiguous_like(const KeptRed &kr, const int64_t *st) {
@@ -293,8 +293,12 @@ static bool contiguous_like(const KeptRed &kr, const int64_t *st) {
 }
 
 extern "C" void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast *bc, const float *g, const float *a,
-                               const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel) {
-    if (gx_numel <= 0 || bc_numel(bc) <= 0) return;
+                               const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel, int acc) {
+    if (gx_numel <= 0) return;
+    if (bc_numel(bc) <= 0) {
+        if (!acc) cudaMemsetAsync(gx, 0, (size_t)gx_numel * sizeof(float), NCK_STREAM(d));
+        return;
+    }
     KeptRed kr;
     kr.nk = kr.nr = 0;
     kr.R = 1;
@@ -317,10 +321,11 @@ extern "C" void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast 
         (!ab || (contiguous_like(kr, kr.ksa) && contiguous_like(kr, kr.ksb)))) {
         int vec = (((uintptr_t)g | (uintptr_t)gx | (ab ? ((uintptr_t)a | (uintptr_t)b) : 0)) & 15) == 0;
         k_binary_bwd_flat<<<grid_for(d, vec ? (gx_numel + 3) / 4 : gx_numel), kThreads, 0, NCK_STREAM(d)>>>(
-            kind, which, g, a, b, gx, gx_numel, vec);
+            kind, which, g, a, b, gx, gx_numel, vec, acc);
         NCK_LAUNCHED(d, 1);
         return;
     }
+    if (!acc) cudaMemsetAsync(gx, 0, (size_t)gx_numel * sizeof(float), NCK_STREAM(d));
     k_binary_bwd<<<grid_for(d, gx_numel), kThreads, 0, NCK_STREAM(d)>>>(kind, which, kr, g, a, b, gx, gx_numel);
     NCK_LAUNCHED(d, 1);
 }

@@ -193,6 +193,28 @@ __global__ void k_axpy(int64_t n, float a, const float *__restrict__ x, float *_
     }
 }
 
+__global__ void k_axpy_set(int64_t n, float a, const float *__restrict__ x, float *__restrict__ y, int vec) {
+    int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = n >> 2;
+        for (int64_t i = t; i < n4; i += stride) {
+            float4 xv = __ldg((const float4 *)x + i);
+            ((float4 *)y)[i] = make_float4(0.0f + a * xv.x, 0.0f + a * xv.y, 0.0f + a * xv.z, 0.0f + a * xv.w);
+        }
+        done = n4 << 2;
+    }
+    for (int64_t i = done + t; i < n; i += stride) y[i] = 0.0f + a * x[i];
+}
+
+extern "C" void nck_axpy_set(nck_dev *d, int64_t n, float a, const float *x, float *y) {
+    if (n <= 0) return;
+    Scope s(d, "axpy", 0.0, 8.0 * n);
+    int vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+    k_axpy_set<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(n, a, x, y, vec);
+    NCK_LAUNCHED(d, 1);
+}
+
 extern "C" void nck_axpy(nck_dev *d, int64_t n, float a, const float *x, float *y) {
     if (n <= 0) return;
     Scope s(d, "axpy");

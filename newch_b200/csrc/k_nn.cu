@@ -399,18 +399,19 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
 }
 
 __global__ void k_dropout_bwd(const float *__restrict__ g, const uint32_t *__restrict__ bits, float *__restrict__ gi,
-                              int64_t n, float p) {
+                              int64_t n, float p, int acc) {
     float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float m = (bits[i >> 5] >> (i & 31)) & 1u ? keepv : 0.0f;
-        gi[i] += g[i] * m;
+        gi[i] = (acc ? gi[i] : 0.0f) + g[i] * m;
     }
 }
 
-extern "C" void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p) {
+extern "C" void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p,
+                                int acc) {
     if (n <= 0) return;
-    Scope sc(d, "dropout_bwd", 0.0, 12.0 * n + n / 8.0);
-    k_dropout_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, bits, gi, n, p);
+    Scope sc(d, "dropout_bwd", 0.0, (acc ? 12.0 : 8.0) * n + n / 8.0);
+    k_dropout_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, bits, gi, n, p, acc);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -660,7 +661,7 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
                                                    const float *__restrict__ g, const float *__restrict__ mean,
                                                    const float *__restrict__ invstd, const float *__restrict__ coef,
                                                    float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
-                                                   int training) {
+                                                   int training, int acc) {
     const int64_t SV = S / V, total = NC * SV;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t c = total <= 0x7fffffff ? (int64_t)(((uint32_t)i / (uint32_t)SV) % (uint32_t)C) : (i / SV) % C;
@@ -669,7 +670,10 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
         float xv[V], gv[V], ov[V];
         bn_load<V>(x, i, xv);
         bn_load<V>(g, i, gv);
-        if constexpr (V == 4) {
+        if (!acc) {
+#pragma unroll
+            for (int e = 0; e < V; e++) ov[e] = 0.0f;
+        } else if constexpr (V == 4) {
             float4 o = reinterpret_cast<float4 *>(gx)[i];
             ov[0] = o.x, ov[1] = o.y, ov[2] = o.z, ov[3] = o.w;
         } else {
@@ -685,8 +689,8 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
 
 extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean,
                            const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
-                           int training) {
-    Scope sc(d, "bn_bwd", 0.0, (gx ? 16.0 : 8.0) * N * C * S);
+                           int training, int acc_gx) {
+    Scope sc(d, "bn_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * N * C * S);
     int64_t splits = bn_splits(d, N, C, S), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
@@ -701,10 +705,10 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
         int64_t planes = N * C;
         if (v4)
             k_bn_bwd_dx<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
-                                                                                   planes, C, S, training);
+                                                                                   planes, C, S, training, acc_gx);
         else
             k_bn_bwd_dx<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
-                                                                               planes, C, S, training);
+                                                                               planes, C, S, training, acc_gx);
         launched++;
     }
     NCK_LAUNCHED(d, launched);

@@ -236,6 +236,10 @@ nc_tensor *nc__tensor_alias(const nc_tensor *src, int persistent);
 static inline nc_tensor *nc__owner(nc_tensor *t) { return t->owner ? t->owner : t; }
 
 nc_tensor *nc__grad_buf(nc_tensor *t);
+/* The gradient buffer for a writer that sets every element of it: a new (or zero_grad-cleared)
+ * buffer of a temporary comes back without zero-filling and *acc = 0 (the writer stores); otherwise
+ * *acc = 1 (the writer adds). Persistent tensors always get a zero-filled buffer and *acc = 1. */
+nc_tensor *nc__grad_buf_acc(nc_tensor *t, int *acc);
 static inline int nc__needs_grad(const nc_tensor *t) { return (t->flags & NC_TF_REQUIRES_GRAD) != 0; }
 
 /* device pointer to t's element 0 after pushing any host writes to the device */

@@ -57,6 +57,8 @@ void nck_fill_i32(nck_dev *d, int32_t *y, int32_t v, int64_t n);
 void nck_add_scalar_inplace(nck_dev *d, float *y, float v); /* y[0] += v */
 /* y[i] += a * x[i] */
 void nck_axpy(nck_dev *d, int64_t n, float a, const float *x, float *y);
+/* y = a * x (the first writer of a fresh gradient buffer) */
+void nck_axpy_set(nck_dev *d, int64_t n, float a, const float *x, float *y);
 /* dst (contiguous, element size es) = src viewed through shape/stride (elements) */
 void nck_copy_strided(nck_dev *d, int es, int ndim, const int64_t *shape, const int64_t *stride, const void *src,
                       void *dst);
@@ -66,6 +68,10 @@ void nck_acc_strided(nck_dev *d, int ndim, const int64_t *shape, const int64_t *
 /* dtype conversion (reference dtype codes: 0 f32, 1 i32, 3 i8, 4 u8); saturating, NaN -> 0 */
 void nck_convert(nck_dev *d, int from, int to, const void *src, void *dst, int64_t n);
 
+/* Gradient launchers with an `acc` argument: acc = 1 adds into the gradient buffer; acc = 0 means the
+ * buffer was handed over without zero-filling (a fresh gradient) and the launcher stores every
+ * element (or zero-fills first when its kernel only touches some). */
+
 /* ---- elementwise --------------------------------------------------------------------------- */
 enum {
     NCK_UN_NEG, NCK_UN_EXP, NCK_UN_LOG, NCK_UN_SQRT, NCK_UN_RELU, NCK_UN_SIGMOID, NCK_UN_TANH, NCK_UN_SCALE,
@@ -74,7 +80,7 @@ enum {
 };
 void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, float *y, int64_t n);
 /* gi += g * d/dx f(x) (y = f(x) for kinds that use it) */
-void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, const float *y, const float *g, float *gi,
+void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, const float *y, const float *g, float *gi, int acc,
                    int64_t n);
 
 enum { NCK_BIN_ADD, NCK_BIN_SUB, NCK_BIN_MUL, NCK_BIN_DIV };
@@ -90,7 +96,7 @@ void nck_binary_fwd_flat(nck_dev *d, int kind, const float *a, const float *b, f
 /* gradient of input `which` (0 = a, 1 = b) accumulated into gx whose shape broadcasts to bc->shape;
  * gx_stride gives gx's strides over the output dims (0 on broadcast dims). g is contiguous. */
 void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast *bc, const float *g, const float *a,
-                    const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel);
+                    const float *b, float *gx, const int64_t *gx_stride, int64_t gx_numel, int acc);
 /* compare: a, b f32 or i32 (type flags), result i32 */
 void nck_compare(nck_dev *d, int op, const nck_bcast *bc, const void *a, int a_i32, const void *b, int b_i32,
                  int32_t *o);
@@ -127,7 +133,7 @@ void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, 
 /* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i */
 void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits, int64_t n,
                      float p);
-void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p);
+void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p, int acc);
 /* one-time upload of the xoshiro256** jump tables (host-computed) */
 int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes);
 
@@ -137,7 +143,7 @@ void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b
 void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                      float *invstd, const float *rm, const float *rv, int64_t N, int64_t C, int64_t S, float eps);
 void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean, const float *invstd,
-                float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S, int training);
+                float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S, int training, int acc_gx);
 /* layer norm over rows of D */
 void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats, int64_t R,
                 int64_t D, float eps);
@@ -164,7 +170,7 @@ typedef struct {
 /* col [n][g][Cg*KH*KW][OH*OW] for samples [n0, n0+nb) */
 void nck_im2col(nck_dev *d, const nck_conv *g, const float *x, float *col, int64_t n0, int64_t nb);
 /* dx[n] += fold(col[n]) */
-void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb);
+void nck_col2im(nck_dev *d, const nck_conv *g, const float *col, float *dx, int64_t n0, int64_t nb, int acc);
 /* gb[oc] += sum over n, l of g[n, oc, l] */
 void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_t N, int64_t OC, int64_t L);
 /* direct convolution for few input channels per group (Cg*KH*KW <= 64) */
@@ -174,6 +180,8 @@ void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *x, const fl
  * Returns 0, launching nothing, for a convolution it does not handle. */
 int nck_conv_implicit(nck_dev *d, int mode, const nck_conv *g, const float *in, const float *q, float *out,
                       const float *bias);
+/* whether nck_conv_implicit would take this convolution (nothing is launched) */
+int nck_conv_implicit_supported(const nck_dev *d, int mode, const nck_conv *g);
 /* gw[oc, k] += sum over n, l of gy[n, oc, l] * x-tap k at l (same eligibility as the direct forward) */
 void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw);
 void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
@@ -181,7 +189,7 @@ void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, f
 #define NCK_DW_MAX_TAPS 25 /* nck_dw_dw handles kernels up to 5x5 */
 void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
 void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max);
-void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx, int is_max);
+void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx, int is_max, int acc);
 
 /* ---- GEMM -------------------------------------------------------------------------------------- */
 /* C_b = alpha * op(A_b) op(B_b) + beta * C_b for b in [0, batch); row-major; ta/tb as the newch kernel

@@ -11,6 +11,8 @@
  */
 #include "nc_internal.h"
 
+#include <cuda_runtime_api.h>
+
 #include <math.h>
 #include <stdio.h>
 
@@ -190,6 +192,13 @@ static void gemm_dx(nc_ctx *ctx, const nck_conv *g, const float *W, const float 
     }
 }
 
+/* a fresh (not zero-filled) gradient buffer about to be added into: zero it first */
+static void zero_if_fresh(nc_ctx *ctx, nc_tensor *gt, int *acc) {
+    if (*acc) return;
+    nc__cuda_ok(ctx, cudaMemsetAsync(gt->data, 0, gt->bytes, (cudaStream_t)ctx->dev.stream), "memset");
+    *acc = 1;
+}
+
 static void conv_bwd(nc_node *n) {
     nc_tensor *x = n->in[0], *w = n->in[1], *b = n->n_in > 2 ? n->in[2] : NULL;
     nc_ctx *ctx = x->ctx;
@@ -197,14 +206,18 @@ static void conv_bwd(nc_node *n) {
     const float *G = (const float *)n->out->grad->data;
     const float *X = nc__contig_f32(x), *Wt = nc__contig_f32(w);
     if (!X || !Wt) return;
-    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf(x) : NULL;
+    int acc_gx = 1; /* 0: gx is a fresh buffer, not zero-filled, that the path below must store whole */
+    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf_acc(x, &acc_gx) : NULL;
     nc_tensor *gw = nc__needs_grad(w) ? nc__grad_buf(w) : NULL;
     nc_tensor *gb = b && nc__needs_grad(b) ? nc__grad_buf(b) : NULL;
     int64_t L = g.OH * g.OW, HW = g.H * g.W;
     if (!g.N) return;
     if (gb) nck_conv_bias_grad(nc__k(ctx), G, (float *)gb->data, g.N, g.OC, L);
     if (is_depthwise(&g)) {
-        if (gx) nck_dw_dx(nc__k(ctx), &g, G, Wt, (float *)gx->data);
+        if (gx) {
+            zero_if_fresh(ctx, gx, &acc_gx);
+            nck_dw_dx(nc__k(ctx), &g, G, Wt, (float *)gx->data);
+        }
         if (!gw) return;
         if (g.KH * g.KW <= NCK_DW_MAX_TAPS) {
             nck_dw_dw(nc__k(ctx), &g, X, G, (float *)gw->data, NULL);
@@ -222,12 +235,13 @@ static void conv_bwd(nc_node *n) {
         /* tensor cores straight from x and dY (dX for unit strides); what is not handled here takes
          * the unfolded path below */
         if (gw && nck_conv_implicit(nc__k(ctx), 2, &g, X, G, (float *)gw->data, NULL)) gw = NULL;
+        if (gx && !acc_gx && nck_conv_implicit_supported(nc__k(ctx), 1, &g)) zero_if_fresh(ctx, gx, &acc_gx);
         if (gx && nck_conv_implicit(nc__k(ctx), 1, &g, G, Wt, (float *)gx->data, NULL)) gx = NULL;
         if (!gw && !gx) return;
     }
     if (is_pointwise(&g)) {
         if (gw) gemm_dw(ctx, &g, G, X, g.C * HW, HW, (float *)gw->data, g.N);
-        if (gx) gemm_dx(ctx, &g, Wt, G, (float *)gx->data, g.C * HW, HW, 1.0f, g.N);
+        if (gx) gemm_dx(ctx, &g, Wt, G, (float *)gx->data, g.C * HW, HW, acc_gx ? 1.0f : 0.0f, g.N);
         return;
     }
     int64_t CKKL = g.C * g.KH * g.KW * L, nbmax = chunk_samples(&g);
@@ -247,7 +261,7 @@ static void conv_bwd(nc_node *n) {
         }
         if (gx) {
             gemm_dx(ctx, &g, Wt, G + n0 * g.OC * L, col, CKKL, L, 0.0f, nb);
-            nck_col2im(nc__k(ctx), &g, col, (float *)gx->data, n0, nb);
+            nck_col2im(nc__k(ctx), &g, col, (float *)gx->data, n0, nb, acc_gx);
         }
     }
 }
@@ -307,12 +321,15 @@ static nc_status pool_fwd(nc_node *n) {
 
 static void pool_bwd(nc_node *n) {
     nc_tensor *x = n->in[0];
-    nc_tensor *gt = nc__grad_buf(x);
+    int acc;
+    nc_tensor *gt = nc__grad_buf_acc(x, &acc);
     if (!gt) return;
     nck_conv g = geom(n, n->p.i[4], n->p.i[5], 0);
     if (nc_numel(n->out))
         nck_pool_bwd(nc__k(x->ctx), &g, (const float *)n->out->grad->data, (const int32_t *)n->saved,
-                     (float *)gt->data, n->op->kind == POOL_MAX);
+                     (float *)gt->data, n->op->kind == POOL_MAX, acc);
+    else if (!acc)
+        zero_if_fresh(x->ctx, gt, &acc);
 }
 
 const nc_op_def nc_op_max_pool2d = {"max_pool2d", 0, POOL_MAX, pool_infer, NULL, pool_fwd, pool_bwd};

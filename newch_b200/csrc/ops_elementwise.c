@@ -63,17 +63,18 @@ static void binary_bwd(nc_node *n) {
     for (int which = 0; which < 2; which++) {
         nc_tensor *x = n->in[which];
         if (!nc__needs_grad(x)) continue;
-        nc_tensor *gx = nc__grad_buf(x);
+        int acc;
+        nc_tensor *gx = nc__grad_buf_acc(x, &acc);
         if (!gx) return;
         int64_t sgx[NC_MAX_DIMS];
         nc__bcast_strides_shape(x->ndim, x->shape, o->ndim, o->shape, sgx);
         if ((n->op->kind == BIN_ADD || n->op->kind == BIN_SUB) && nc__same_shape(x, o)) {
-            nck_axpy(k, nc_numel(o), (n->op->kind == BIN_SUB && which == 1) ? -1.0f : 1.0f,
-                     (const float *)o->grad->data, (float *)gx->data);
+            (acc ? nck_axpy : nck_axpy_set)(k, nc_numel(o), (n->op->kind == BIN_SUB && which == 1) ? -1.0f : 1.0f,
+                                            (const float *)o->grad->data, (float *)gx->data);
             continue;
         }
         nck_binary_bwd(k, n->op->kind, which, &bc, (const float *)o->grad->data, (const float *)a->data,
-                       (const float *)b->data, (float *)gx->data, sgx, nc_numel(x));
+                       (const float *)b->data, (float *)gx->data, sgx, nc_numel(x), acc);
     }
 }
 
@@ -114,11 +115,12 @@ static nc_status unary_fwd(nc_node *n) {
 
 static void unary_bwd(nc_node *n) {
     nc_tensor *in = n->in[0];
-    nc_tensor *gt = nc__grad_buf(in);
     const float *x = nc__contig_f32(in);
+    int acc;
+    nc_tensor *gt = x ? nc__grad_buf_acc(in, &acc) : NULL;
     if (!gt || !x) return;
     nck_unary_bwd(nc__k(in->ctx), n->op->kind, n->p.f[0], x, (const float *)n->out->data,
-                  (const float *)n->out->grad->data, (float *)gt->data, nc_numel(in));
+                  (const float *)n->out->grad->data, (float *)gt->data, acc, nc_numel(in));
 }
 
 #define UNARY_OP(nm, KIND) \

@@ -87,14 +87,18 @@ static void matmul_bwd(nc_node *n) {
     mm_dims(n, &M, &K, &N);
     const float *g = (const float *)n->out->grad->data;
     if (nc__needs_grad(a)) {
-        nc_tensor *ga = nc__grad_buf(a);
         gemm_operand B = as_gemm(b, K, N);
-        if (ga && B.p) nc__gemm(a->ctx, 0, !B.trans, M, K, N, 1.0f, g, N, B.p, B.ld, 1.0f, (float *)ga->data, K);
+        int acc;
+        nc_tensor *ga = B.p ? nc__grad_buf_acc(a, &acc) : NULL;
+        if (ga && B.p)
+            nc__gemm(a->ctx, 0, !B.trans, M, K, N, 1.0f, g, N, B.p, B.ld, acc ? 1.0f : 0.0f, (float *)ga->data, K);
     }
     if (nc__needs_grad(b)) {
-        nc_tensor *gb = nc__grad_buf(b);
         gemm_operand A = a_operand(a, M, K);
-        if (gb && A.p) nc__gemm(a->ctx, !A.trans, 0, K, N, M, 1.0f, A.p, A.ld, g, N, 1.0f, (float *)gb->data, N);
+        int acc;
+        nc_tensor *gb = A.p ? nc__grad_buf_acc(b, &acc) : NULL;
+        if (gb && A.p)
+            nc__gemm(a->ctx, !A.trans, 0, K, N, M, 1.0f, A.p, A.ld, g, N, acc ? 1.0f : 0.0f, (float *)gb->data, N);
     }
 }
 
@@ -310,9 +314,10 @@ static void linear_bwd(nc_node *n) {
     int64_t in = w->shape[1], out = w->shape[0], M = in ? nc_numel(x) / in : 0;
     const float *g = (const float *)n->out->grad->data;
     if (nc__needs_grad(x)) {
-        nc_tensor *gx = nc__grad_buf(x);
         const float *W = nc__contig_f32(w);
-        if (gx && W) nc__gemm(x->ctx, 0, 0, M, in, out, 1.0f, g, out, W, in, 1.0f, (float *)gx->data, in);
+        int acc;
+        nc_tensor *gx = W ? nc__grad_buf_acc(x, &acc) : NULL;
+        if (gx && W) nc__gemm(x->ctx, 0, 0, M, in, out, 1.0f, g, out, W, in, acc ? 1.0f : 0.0f, (float *)gx->data, in);
     }
     if (nc__needs_grad(w)) {
         nc_tensor *gw = nc__grad_buf(w);

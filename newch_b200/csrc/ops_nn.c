@@ -163,12 +163,13 @@ static nc_status dropout_fwd(nc_node *n) {
 }
 
 static void dropout_bwd(nc_node *n) {
-    nc_tensor *gt = nc__grad_buf(n->in[0]);
+    int acc;
+    nc_tensor *gt = nc__grad_buf_acc(n->in[0], &acc);
     if (!gt) return;
     int64_t N = nc_numel(n->out);
     if (N)
         nck_dropout_bwd(nc__k(gt->ctx), (const float *)n->out->grad->data, (const uint32_t *)n->saved,
-                        (float *)gt->data, N, n->p.f[0]);
+                        (float *)gt->data, N, n->p.f[0], acc);
 }
 
 const nc_op_def nc_op_dropout = {"dropout", NC_OPF_ELEMENTWISE, 0, dropout_infer, NULL, dropout_fwd, dropout_bwd};
@@ -256,12 +257,13 @@ static void bn_bwd(nc_node *n) {
     const bn_saved *sv = (const bn_saved *)n->saved;
     const float *X = nc__contig_f32(x), *w = nc__contig_f32(n->in[1]);
     if (!X || !w) return;
-    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf(x) : NULL;
+    int acc_gx = 1;
+    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf_acc(x, &acc_gx) : NULL;
     nc_tensor *gw = nc__needs_grad(n->in[1]) ? nc__grad_buf(n->in[1]) : NULL;
     nc_tensor *gb = nc__needs_grad(n->in[2]) ? nc__grad_buf(n->in[2]) : NULL;
     nck_bn_bwd(nc__k(x->ctx), X, w, (const float *)n->out->grad->data, sv->mean, sv->invstd,
                gx ? (float *)gx->data : NULL, gw ? (float *)gw->data : NULL, gb ? (float *)gb->data : NULL, N, C, S,
-               (int)n->p.i[0]);
+               (int)n->p.i[0], acc_gx);
 }
 
 const nc_op_def nc_op_batch_norm = {"batch_norm", 0, 0, bn_infer, NULL, bn_fwd, bn_bwd};

@@ -35,8 +35,11 @@ static nc_status copy_fwd(nc_node *n) {
 }
 
 static void flat_bwd(nc_node *n) {
-    nc_tensor *gt = nc__grad_buf(n->in[0]);
-    if (gt) nck_axpy(nc__k(gt->ctx), nc_numel(gt), 1.0f, (const float *)n->out->grad->data, (float *)gt->data);
+    int acc;
+    nc_tensor *gt = nc__grad_buf_acc(n->in[0], &acc);
+    if (gt)
+        (acc ? nck_axpy : nck_axpy_set)(nc__k(gt->ctx), nc_numel(gt), 1.0f, (const float *)n->out->grad->data,
+                                        (float *)gt->data);
 }
 
 /* ---- reshape ------------------------------------------------------------------------------------ */

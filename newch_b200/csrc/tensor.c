@@ -503,6 +503,25 @@ nc_tensor *nc__grad_buf(nc_tensor *t) {
     return t->grad;
 }
 
+nc_tensor *nc__grad_buf_acc(nc_tensor *t, int *acc) {
+    *acc = 1;
+    if (t->flags & NC_TF_PERSISTENT) return nc__grad_buf(t);
+    nc_ctx *ctx = t->ctx;
+    if (t->grad) {
+        nc__dev_write(t->grad);
+        if (t->flags & NC_TF_GRAD_CLEARED) {
+            t->flags &= ~NC_TF_GRAD_CLEARED;
+            *acc = 0;
+        }
+        return t->grad;
+    }
+    ctx->grad_alloc = 1;
+    t->grad = nc__tensor_new(ctx, NC_F32, t->ndim, t->shape, 0);
+    ctx->grad_alloc = 0;
+    if (t->grad) *acc = 0;
+    return t->grad;
+}
+
 /* ---- printing --------------------------------------------------------------------------------- */
 
 void nc_print(const nc_tensor *t) {
