@@ -653,11 +653,42 @@ __global__ void k_pool_bwd_set(nck_conv g, const float *__restrict__ gy, const i
     }
 }
 
+// the same for 2x2 max pooling with stride 2, no padding, width a multiple of 4: a thread stores four
+// consecutive inputs of one row (two windows) with one 16-byte write
+__global__ void __launch_bounds__(256) k_maxpool2x2_bwd_set(const float *__restrict__ gy,
+                                                            const int32_t *__restrict__ arg, float *__restrict__ gx,
+                                                            uint32_t planes, uint32_t H, uint32_t W, uint32_t OH,
+                                                            uint32_t OW) {
+    const uint32_t quads = W / 4, total = planes * H * quads;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = t / quads, q = t - r * quads, pl = r / H, iy = r - pl * H, oy = iy >> 1;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (oy < OH) {
+            const size_t o = (size_t)pl * OH * OW + (size_t)oy * OW + 2 * q;
+            const int32_t i0 = (int32_t)(iy * W + 4 * q), a0 = __ldg(arg + o), a1 = __ldg(arg + o + 1);
+            const float g0 = __ldg(gy + o), g1 = __ldg(gy + o + 1);
+            v.x = a0 == i0 ? g0 : 0.0f;
+            v.y = a0 == i0 + 1 ? g0 : 0.0f;
+            v.z = a1 == i0 + 2 ? g1 : 0.0f;
+            v.w = a1 == i0 + 3 ? g1 : 0.0f;
+        }
+        reinterpret_cast<float4 *>(gx + (size_t)pl * H * W + (size_t)iy * W)[q] = v;
+    }
+}
+
 extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx,
                              int is_max, int acc) {
     Scope sc(d, is_max ? "max_pool_bwd" : "avg_pool_bwd", 0.0,
              4.0 * ((is_max ? 2 : 1) * g->N * g->C * g->OH * g->OW + 2 * g->N * g->C * g->H * g->W));
     const int64_t in_total = g->N * g->C * g->H * g->W;
+    if (!acc && is_max && g->KH == 2 && g->KW == 2 && g->sh == 2 && g->sw == 2 && g->ph == 0 && g->pw == 0 &&
+        g->W % 4 == 0 && ((uintptr_t)gx & 15) == 0 && small_index(in_total)) {
+        const int64_t items = in_total / 4;
+        k_maxpool2x2_bwd_set<<<grid_for(d, items), 256, 0, NCK_STREAM(d)>>>(
+            gy, arg, gx, (uint32_t)(g->N * g->C), (uint32_t)g->H, (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     if (!acc && g->sh >= g->KH && g->sw >= g->KW && small_index(in_total)) {
         k_pool_bwd_set<<<grid_for(d, in_total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
         NCK_LAUNCHED(d, 1);
