@@ -224,7 +224,8 @@ __device__ __forceinline__ void gather_taps(const float *xg, const Taps &t, int 
 }
 
 // y[n, g*OCg + o, l] = bias + sum over taps k in order of w[o, k] * in[k] (fused multiply-adds);
-// block (l-chunk, n * G + group), one output position per thread
+// block (position chunk, group): a grid-stride walk over the flattened (n, l) positions, one output
+// position per thread per step; the group's weights and tap table are staged once per block
 template <int KT>
 __global__ void __launch_bounds__(256) k_conv_direct(nck_conv g, const float *__restrict__ x,
                                                      const float *__restrict__ w, const float *__restrict__ b,
@@ -233,14 +234,16 @@ __global__ void __launch_bounds__(256) k_conv_direct(nck_conv g, const float *__
     __shared__ Taps taps;
     const int Cg = (int)(g.C / g.G), OCg = (int)(g.OC / g.G), CKK = Cg * (int)(g.KH * g.KW);
     const int L = (int)(g.OH * g.OW), OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
-    const int64_t ng = blockIdx.y, n = ng / g.G, gi = ng % g.G;
+    const int64_t gi = blockIdx.y;
     for (int i = threadIdx.x; i < OCg * CKK; i += blockDim.x) ws[i] = w[gi * OCg * CKK + i];
     build_taps(g, CKK, taps);
     __syncthreads();
-    const float *xg = x + (n * g.C + gi * Cg) * (int64_t)H * W;
-    float *yg = y + (n * g.OC + gi * OCg) * (int64_t)L;
-    for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < L; l += gridDim.x * blockDim.x) {
-        int oy = l / OW, ox = l - oy * OW;
+    const int64_t total = g.N * (int64_t)L;
+    for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < total; p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = p / L;
+        const int l = (int)(p - n * L), oy = l / OW, ox = l - oy * OW;
+        const float *xg = x + (n * g.C + gi * Cg) * (int64_t)H * W;
+        float *yg = y + (n * g.OC + gi * OCg) * (int64_t)L + l;
         float in[KT];
         gather_taps<KT>(xg, taps, CKK, oy, ox, g.sh, g.sw, H, W, in);
         for (int o = 0; o < OCg; o++) {
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(256) k_conv_direct(nck_conv g, const float *__
 #pragma unroll
             for (int k = 0; k < KT; k++)
                 if (k < CKK) acc = fmaf(ws[o * CKK + k], in[k], acc);
-            yg[(int64_t)o * L + l] = acc;
+            yg[(int64_t)o * L] = acc;
         }
     }
 }
@@ -258,9 +261,10 @@ extern "C" void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *
     int64_t L = g->OH * g->OW, CKK = (g->C / g->G) * g->KH * g->KW;
     if (g->N * g->G * L <= 0) return;
     Scope sc(d, "conv_direct", 2.0 * g->N * g->OC * L * CKK, 4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L));
-    int64_t bx = (L + kThreads - 1) / kThreads;
-    if (bx > 64) bx = 64;
-    dim3 grid((unsigned)bx, (unsigned)(g->N * g->G));
+    int64_t bx = (g->N * L + kThreads - 1) / kThreads, cap = ((int64_t)d->sm_count * 8 + g->G - 1) / g->G;
+    if (bx > cap) bx = cap;
+    if (bx < 1) bx = 1;
+    dim3 grid((unsigned)bx, (unsigned)g->G);
     if (CKK <= 9) k_conv_direct<9><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
     else if (CKK <= 16) k_conv_direct<16><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
     else k_conv_direct<32><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
