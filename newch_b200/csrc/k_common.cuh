@@ -21,6 +21,26 @@ inline int grid_for(const nck_dev *d, int64_t n, int threads = kThreads, int per
     return want < 1 ? 1 : (int)want;
 }
 
+// n / d for 32-bit n < 2^31 by multiply-high with a precomputed magic number (Granlund-Montgomery):
+// l = ceil(log2 d), mul = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, mul) + n) >> l
+struct FastDiv {
+    uint32_t d, mul, shift;
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        return d == 1 ? n : (uint32_t)((__umulhi(n, mul) + n) >> shift);
+    }
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    uint32_t l = 0;
+    while (l < 32 && (1ull << l) < d) l++;
+    f.shift = l;
+    f.mul = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+    if (d <= 1) f.mul = 0, f.shift = 0, f.d = 1;
+    return f;
+}
+
 // Records a kernel-detected error (first one wins). The host reads it at its next synchronization.
 __device__ __forceinline__ void report(int *status, int code) { atomicCAS(status, 0, code); }
 

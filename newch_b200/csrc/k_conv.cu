@@ -160,11 +160,13 @@ __global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restric
         for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += sm[k];
         part[blockIdx.y * C + c] = s;
     }
-    if (last_block_done(counter)) {  // gb[c] += the splits of channel c, in order
-        for (int64_t cc = threadIdx.x; cc < C; cc += blockDim.x) {
-            float t = gb[cc];
-            for (int k = 0; k < (int)gridDim.y; k++) t += __ldcg(part + k * C + cc);
-            gb[cc] = t;
+    if (last_block_done(counter)) {  // gb[c] += the splits of channel c: 8 lanes per channel, fixed tree
+        const unsigned m = 0xFFu << (threadIdx.x & 24);
+        for (int64_t cc = threadIdx.x >> 3; cc < C; cc += blockDim.x >> 3) {
+            float t = 0.0f;
+            for (int k = threadIdx.x & 7; k < (int)gridDim.y; k += 8) t += __ldcg(part + k * C + cc);
+            for (int o = 4; o; o >>= 1) t += __shfl_xor_sync(m, t, o, 8);
+            if ((threadIdx.x & 7) == 0) gb[cc] += t;
         }
     }
 }
@@ -506,13 +508,15 @@ extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const f
 // is several times cheaper than with 64-bit operands), else int64_t.
 template <typename I>
 __global__ void k_pool_fwd(nck_conv g, const float *__restrict__ x, float *__restrict__ y, int32_t *__restrict__ arg,
-                           int is_max) {
+                           int is_max, FastDiv divOW, FastDiv divOH) {
     const I OW = (I)g.OW, OH = (I)g.OH, H = (I)g.H, W = (I)g.W, KH = (I)g.KH, KW = (I)g.KW;
     const I total = (I)(g.N * g.C) * OH * OW;
     const float inv = 1.0f / (float)(g.KH * g.KW);
     for (I t = blockIdx.x * (I)blockDim.x + threadIdx.x; t < total; t += (I)gridDim.x * blockDim.x) {
-        I r = t / OW, ox = t - r * OW;
-        I plane = r / OH, oy = r - plane * OH;
+        I r, plane;
+        if constexpr (sizeof(I) == 4) r = divOW.div(t), plane = divOH.div(r);
+        else r = t / OW, plane = r / OH;
+        I ox = t - r * OW, oy = r - plane * OH;
         const float *xp = x + (int64_t)plane * H * W;
         float best = -INFINITY, acc = 0.0f;
         int32_t bi = -1;
@@ -586,9 +590,11 @@ extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, floa
         k_maxpool2x2<<<grid_for(d, items), 256, 0, NCK_STREAM(d)>>>(x, y, arg, (uint32_t)planes, (uint32_t)g->H,
                                                                   (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW);
     } else if (small_index(g->N * g->C * g->H * g->W) && small_index(total))
-        k_pool_fwd<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
+        k_pool_fwd<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(
+            *g, x, y, arg, is_max, make_fastdiv((uint32_t)g->OW), make_fastdiv((uint32_t)g->OH));
     else
-        k_pool_fwd<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max);
+        k_pool_fwd<int64_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, y, arg, is_max, FastDiv{1, 0, 0},
+                                                                                FastDiv{1, 0, 0});
     NCK_LAUNCHED(d, 1);
 }
 
@@ -638,12 +644,12 @@ __global__ void k_pool_bwd_gather(nck_conv g, const float *__restrict__ gy, cons
 // at most one window, so it is stored once: the window's gradient where it was the maximum (max) or
 // gy / (KH*KW) (average), 0 elsewhere; the same values zero-fill plus scatter would leave.
 __global__ void k_pool_bwd_set(nck_conv g, const float *__restrict__ gy, const int32_t *__restrict__ arg,
-                               float *__restrict__ gx, int is_max) {
+                               float *__restrict__ gx, int is_max, FastDiv divW, FastDiv divH) {
     const uint32_t W = (uint32_t)g.W, H = (uint32_t)g.H, OH = (uint32_t)g.OH, OW = (uint32_t)g.OW;
     const uint32_t total = (uint32_t)(g.N * g.C) * H * W;
     const float inv = 1.0f / (float)(g.KH * g.KW);
     for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
-        const uint32_t r = t / W, ix = t - r * W, plane = r / H, iy = r - plane * H;
+        const uint32_t r = divW.div(t), ix = t - r * W, plane = divH.div(r), iy = r - plane * H;
         const uint32_t ty = iy + (uint32_t)g.ph, tx = ix + (uint32_t)g.pw;
         const uint32_t oy = ty / (uint32_t)g.sh, ox = tx / (uint32_t)g.sw;
         float v = 0.0f;
@@ -694,7 +700,8 @@ extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, con
         return;
     }
     if (!acc && g->sh >= g->KH && g->sw >= g->KW && small_index(in_total)) {
-        k_pool_bwd_set<<<grid_for(d, in_total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, arg, gx, is_max);
+        k_pool_bwd_set<<<grid_for(d, in_total), kThreads, 0, NCK_STREAM(d)>>>(
+            *g, gy, arg, gx, is_max, make_fastdiv((uint32_t)g->W), make_fastdiv((uint32_t)g->H));
         NCK_LAUNCHED(d, 1);
         return;
     }

@@ -33,26 +33,6 @@ constexpr int kMaxTaps = 1152;
 
 enum { IC_FWD = 0, IC_DX = 1, IC_DW = 2 };
 
-// n / d by multiply-high with a precomputed magic number (Granlund-Montgomery): l = ceil(log2 d),
-// mul = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, mul) + n) >> l; exact for n < 2^31
-struct FastDiv {
-    uint32_t d, mul, shift;
-    __device__ __forceinline__ uint32_t div(uint32_t n) const {
-        return d == 1 ? n : (uint32_t)((__umulhi(n, mul) + n) >> shift);
-    }
-};
-
-FastDiv make_fastdiv(uint32_t d) {
-    FastDiv f;
-    f.d = d;
-    uint32_t l = 0;
-    while (l < 32 && (1ull << l) < d) l++;
-    f.shift = l;
-    f.mul = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
-    if (d == 1) f.mul = 0, f.shift = 0;
-    return f;
-}
-
 struct IcParams {
     int mode;
     FastDiv div_pw, div_phw;  // by PW and by PH * PW
@@ -137,12 +117,11 @@ __device__ __forceinline__ void build_taps(const IcParams &p, Tap *taps) {
 // one 16-byte chunk (4 K values) of a K-major 128-byte-swizzled tile row
 __device__ __forceinline__ void put_chunk(float *tile, float *rest, int row, int q, const float (&v)[4], bool three) {
     const int idx = row * 32 + ((q ^ (row & 7)) << 2);
+    // the MMA reads the fp32 value as its TF32 head (it drops the low 13 mantissa bits)
+    *reinterpret_cast<float4 *>(tile + idx) = make_float4(v[0], v[1], v[2], v[3]);
     if (three) {
         float4 h = make_float4(tf32_hi(v[0]), tf32_hi(v[1]), tf32_hi(v[2]), tf32_hi(v[3]));
-        *reinterpret_cast<float4 *>(tile + idx) = h;
         *reinterpret_cast<float4 *>(rest + idx) = make_float4(v[0] - h.x, v[1] - h.y, v[2] - h.z, v[3] - h.w);
-    } else {
-        *reinterpret_cast<float4 *>(tile + idx) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 

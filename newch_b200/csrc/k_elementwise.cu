@@ -100,13 +100,17 @@ __global__ void k_unary_fwd(int kind, float s, const float *__restrict__ x, floa
     }
 }
 
+// nx / ny: the derivative reads x / y (a stream the derivative does not use is not loaded)
 __global__ void k_unary_bwd(int kind, float s, const float *__restrict__ x, const float *__restrict__ y,
-                            const float *__restrict__ g, float *__restrict__ gi, int64_t n, int vec, int acc) {
+                            const float *__restrict__ g, float *__restrict__ gi, int64_t n, int vec, int acc, int nx,
+                            int ny) {
     int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (vec) {
         int64_t n4 = n >> 2;
         for (int64_t i = t; i < n4; i += stride) {
-            float4 xv = ((const float4 *)x)[i], yv = ((const float4 *)y)[i], gv = ((const float4 *)g)[i];
+            const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float4 xv = nx ? __ldg((const float4 *)x + i) : z4, yv = ny ? __ldg((const float4 *)y + i) : z4;
+            float4 gv = __ldg((const float4 *)g + i);
             float4 o = acc ? ((float4 *)gi)[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             o.x = accumulate(kind, s, o.x, gv.x, unary_grad(kind, s, xv.x, yv.x, gv.x));
             o.y = accumulate(kind, s, o.y, gv.y, unary_grad(kind, s, xv.y, yv.y, gv.y));
@@ -146,9 +150,11 @@ extern "C" void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, con
     if (n <= 0) return;
     /* reads x, g and the accumulator (and y where the derivative uses it), writes the accumulator */
     int uses_y = kind == NCK_UN_EXP || kind == NCK_UN_SQRT || kind == NCK_UN_SIGMOID || kind == NCK_UN_TANH;
-    Scope sc(d, unary_name(kind, 1), 0.0, (12.0 + (acc ? 4.0 : 0.0) + (uses_y ? 4.0 : 0.0)) * n);
+    int uses_x = !uses_y && kind != NCK_UN_SCALE && kind != NCK_UN_NEG && kind != NCK_UN_ADD_SCALAR;
+    Scope sc(d, unary_name(kind, 1), 0.0, (8.0 + (acc ? 4.0 : 0.0) + (uses_x ? 4.0 : 0.0) + (uses_y ? 4.0 : 0.0)) * n);
     int vec = (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)gi) & 15) == 0;
-    k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec, acc);
+    k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec, acc, uses_x,
+                                                                                       uses_y);
     NCK_LAUNCHED(d, 1);
 }
 

@@ -453,17 +453,31 @@ struct BnFwdFin {
     int splits;
 };
 
+// Finalize work of the last block: eight lanes per channel add strided runs of the splits and a
+// three-step shuffle tree (within the eight) combines them; the order is fixed.
+__device__ __forceinline__ unsigned group8_mask() { return 0xFFu << (threadIdx.x & 24); }
+
+__device__ __forceinline__ void sum_splits8(const double *part, int splits, int64_t C, int64_t c, double &s,
+                                            double &t) {
+    s = 0.0, t = 0.0;
+    for (int k = threadIdx.x & 7; k < splits; k += 8) s += __ldcg(part + (k * C + c) * 2), t += __ldcg(part + (k * C + c) * 2 + 1);
+    const unsigned m = group8_mask();
+    for (int o = 4; o; o >>= 1) s += __shfl_xor_sync(m, s, o, 8), t += __shfl_xor_sync(m, t, o, 8);
+}
+
 __device__ void bn_fwd_finalize(const double *part, int64_t C, int64_t M, const BnFwdFin &f) {
-    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
-        double s = 0.0, ss = 0.0;
-        for (int k = 0; k < f.splits; k++) s += __ldcg(part + (k * C + c) * 2), ss += __ldcg(part + (k * C + c) * 2 + 1);
-        double mu = s / (double)M;
-        double dev = ss - s * mu; /* sum of squared deviations */
-        if (dev < 0.0) dev = 0.0;
-        f.mean[c] = (float)mu;
-        f.invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)f.eps));
-        f.rm[c] = (1.0f - f.mom) * f.rm[c] + f.mom * (float)mu;
-        f.rv[c] = (1.0f - f.mom) * f.rv[c] + f.mom * (float)(dev / (double)(M - 1));
+    for (int64_t c = threadIdx.x >> 3; c < C; c += blockDim.x >> 3) {
+        double s, ss;
+        sum_splits8(part, f.splits, C, c, s, ss);
+        if ((threadIdx.x & 7) == 0) {
+            double mu = s / (double)M;
+            double dev = ss - s * mu; /* sum of squared deviations */
+            if (dev < 0.0) dev = 0.0;
+            f.mean[c] = (float)mu;
+            f.invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)f.eps));
+            f.rm[c] = (1.0f - f.mom) * f.rm[c] + f.mom * (float)mu;
+            f.rv[c] = (1.0f - f.mom) * f.rv[c] + f.mom * (float)(dev / (double)(M - 1));
+        }
     }
 }
 
@@ -522,10 +536,16 @@ template <int V>
 __global__ void __launch_bounds__(256) k_bn_norm(const float *__restrict__ x, const float *__restrict__ w,
                                                  const float *__restrict__ b, const float *__restrict__ mean,
                                                  const float *__restrict__ invstd, float *__restrict__ y, int64_t NC,
-                                                 int64_t C, int64_t S) {
+                                                 int64_t C, int64_t S, FastDiv dsv, FastDiv dc) {
     const int64_t SV = S / V, total = NC * SV;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        int64_t c = total <= 0x7fffffff ? (int64_t)(((uint32_t)i / (uint32_t)SV) % (uint32_t)C) : (i / SV) % C;
+        int64_t c;
+        if (total <= 0x7fffffff) {
+            const uint32_t q = dsv.div((uint32_t)i);
+            c = (int64_t)(q - dc.div(q) * (uint32_t)C);
+        } else {
+            c = (i / SV) % C;
+        }
         float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
         if constexpr (V == 4) {
             float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
@@ -536,6 +556,9 @@ __global__ void __launch_bounds__(256) k_bn_norm(const float *__restrict__ x, co
         }
     }
 }
+
+// divisors of the flat element walk: by S / V (float4 items per plane) and by C
+#define BN_DIVS(S, V) make_fastdiv((uint32_t)((S) / (V)))
 
 static bool bn_vec4(int64_t S, const void *p, const void *q, const void *r) {
     return (S & 3) == 0 && (((uintptr_t)p | (uintptr_t)q | (uintptr_t)r) & 15) == 0;
@@ -571,8 +594,10 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
     if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     int64_t planes = N * C;
-    if (v4) k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
-    else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+    if (v4) k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                             BN_DIVS(S, 4), make_fastdiv((uint32_t)C));
+    else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                             BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
     NCK_LAUNCHED(d, 2);
 }
 
@@ -584,9 +609,11 @@ extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, cons
     int64_t planes = N * C;
     if (planes * S > 0) {
         if (bn_vec4(S, x, y, x))
-            k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+            k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                             BN_DIVS(S, 4), make_fastdiv((uint32_t)C));
         else
-            k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S);
+            k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                             BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
     }
     NCK_LAUNCHED(d, 2);
 }
@@ -600,13 +627,15 @@ struct BnBwdFin {
 };
 
 __device__ void bn_bwd_finalize(const double *part, int64_t C, int64_t M, const BnBwdFin &f) {
-    for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
-        double sg = 0.0, sgx = 0.0;
-        for (int k = 0; k < f.splits; k++) sg += __ldcg(part + (k * C + c) * 2), sgx += __ldcg(part + (k * C + c) * 2 + 1);
-        if (f.gw) f.gw[c] += (float)sgx;
-        if (f.gb) f.gb[c] += (float)sg;
-        f.coef[2 * c] = (float)(sg / (double)M);
-        f.coef[2 * c + 1] = (float)(sgx / (double)M);
+    for (int64_t c = threadIdx.x >> 3; c < C; c += blockDim.x >> 3) {
+        double sg, sgx;
+        sum_splits8(part, f.splits, C, c, sg, sgx);
+        if ((threadIdx.x & 7) == 0) {
+            if (f.gw) f.gw[c] += (float)sgx;
+            if (f.gb) f.gb[c] += (float)sg;
+            f.coef[2 * c] = (float)(sg / (double)M);
+            f.coef[2 * c + 1] = (float)(sgx / (double)M);
+        }
     }
 }
 
@@ -661,10 +690,16 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
                                                    const float *__restrict__ g, const float *__restrict__ mean,
                                                    const float *__restrict__ invstd, const float *__restrict__ coef,
                                                    float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
-                                                   int training, int acc) {
+                                                   int training, int acc, FastDiv dsv, FastDiv dc) {
     const int64_t SV = S / V, total = NC * SV;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        int64_t c = total <= 0x7fffffff ? (int64_t)(((uint32_t)i / (uint32_t)SV) % (uint32_t)C) : (i / SV) % C;
+        int64_t c;
+        if (total <= 0x7fffffff) {
+            const uint32_t q = dsv.div((uint32_t)i);
+            c = (int64_t)(q - dc.div(q) * (uint32_t)C);
+        } else {
+            c = (i / SV) % C;
+        }
         float mu = __ldg(mean + c), is = __ldg(invstd + c), k = __ldg(w + c) * is;
         float mg = __ldg(coef + 2 * c), mgx = __ldg(coef + 2 * c + 1);
         float xv[V], gv[V], ov[V];
@@ -704,11 +739,11 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
     if (gx) {
         int64_t planes = N * C;
         if (v4)
-            k_bn_bwd_dx<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
-                                                                                   planes, C, S, training, acc_gx);
+            k_bn_bwd_dx<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(
+                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 4), make_fastdiv((uint32_t)C));
         else
-            k_bn_bwd_dx<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, g, mean, invstd, coef, gx,
-                                                                               planes, C, S, training, acc_gx);
+            k_bn_bwd_dx<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(
+                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
         launched++;
     }
     NCK_LAUNCHED(d, launched);

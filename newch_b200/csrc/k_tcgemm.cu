@@ -14,8 +14,9 @@
 //   warp 4     TMA loader (one thread) feeding a ring of up to 8 stages, K in steps of 32 (128 B)
 //   warp 5     MMA issuer (one thread): 4 MMAs of K = 8 per stage, commits each stage back to the
 //              loader and each finished tile to the epilogue
-//   warps 6-13 3xTF32 only: split every staged fp32 tile into its TF32 head (top 19 bits) and the
-//              remainder; the MMA thread then accumulates head*head + head*rest + rest*head
+//   warps 6-13 3xTF32 only: write the remainder of every staged fp32 tile below its TF32 head (the
+//              top 19 bits, which the MMA reads from the staged tile itself); the MMA thread then
+//              accumulates head*head + head*rest + rest*head
 // Two accumulators in TMEM let the epilogue of one tile overlap the main loop of the next.
 //
 // Every mbarrier wait gives up after 2 s of device time and records an error in the status word; a
@@ -235,7 +236,9 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
             mbar_wait(&s.mma_done, 0, p.status);
         }
     } else if (THREE && warp >= kSplitWarp0) {
-        // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head -------------
+        // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head. The tensor
+        // core reads an fp32 operand as TF32 by dropping those 13 bits (truncation, checked on B200), so
+        // the staged x already serves as the head and only the rest is written ------------------------
         const int t2 = tid - kSplitWarp0 * 32;  // 0 .. kSplitThreads - 1
         const int nb = BN * TK / 4;
         int st = 0;
@@ -248,13 +251,11 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                 float4 *ah = reinterpret_cast<float4 *>(ring_a + st * kStageA), *al = reinterpret_cast<float4 *>(rest_a + st * kStageA);
                 for (int i = t2; i < TM * TK / 4; i += kSplitThreads) {
                     float4 v = ah[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                    ah[i] = h;
                     al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
                 }
                 float4 *bh = reinterpret_cast<float4 *>(ring_b + st * sbq), *bl = reinterpret_cast<float4 *>(rest_b + st * sbq);
                 for (int i = t2; i < nb; i += kSplitThreads) {
                     float4 v = bh[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                    bh[i] = h;
                     bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
