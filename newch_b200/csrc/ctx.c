@@ -373,6 +373,7 @@ nc_ctx *nc_init(const nc_config *cfg) {
     {
         const char *cv = getenv("NC_CONV");
         ctx->dev.conv_implicit = cv && !strcmp(cv, "implicit");
+        ctx->dev.conv_tap = !cv || !strcmp(cv, "tap");
     }
     cudaStream_t s;
     if (!nc__cuda_ok(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return ctx;

@@ -120,8 +120,7 @@ __device__ __forceinline__ void put_chunk(float *tile, float *rest, int row, int
     // the MMA reads the fp32 value as its TF32 head (it drops the low 13 mantissa bits)
     *reinterpret_cast<float4 *>(tile + idx) = make_float4(v[0], v[1], v[2], v[3]);
     if (three) {
-        float4 h = make_float4(tf32_hi(v[0]), tf32_hi(v[1]), tf32_hi(v[2]), tf32_hi(v[3]));
-        *reinterpret_cast<float4 *>(rest + idx) = make_float4(v[0] - h.x, v[1] - h.y, v[2] - h.z, v[3] - h.w);
+        *reinterpret_cast<float4 *>(rest + idx) = make_float4(tf32_rest(v[0]), tf32_rest(v[1]), tf32_rest(v[2]), tf32_rest(v[3]));
     }
 }
 

@@ -15,7 +15,8 @@
 //   warp 5     MMA issuer (one thread): 4 MMAs of K = 8 per stage, commits each stage back to the
 //              loader and each finished tile to the epilogue
 //   warps 6-13 3xTF32 only: write the remainder of every staged fp32 tile below its TF32 head (the
-//              top 19 bits, which the MMA reads from the staged tile itself); the MMA thread then
+//              top 19 bits, which the MMA reads from the staged tile itself), rounded to TF32; the
+//              MMA thread then
 //              accumulates head*head + head*rest + rest*head
 // Two accumulators in TMEM let the epilogue of one tile overlap the main loop of the next.
 //
@@ -55,23 +56,6 @@ struct TcParams {
     int p_bat, q_bat;      // operand has a batch coordinate (3-D tensor map)
     int *status;
 };
-
-__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
-
 
 // Barriers sit in the first KiB of dynamic shared memory; the stage buffers follow, 1 KiB aligned:
 // [P stages][Q stages] and in 3xTF32 mode [P rests][Q rests], `stages` of each.
@@ -236,9 +220,10 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
             mbar_wait(&s.mma_done, 0, p.status);
         }
     } else if (THREE && warp >= kSplitWarp0) {
-        // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head. The tensor
-        // core reads an fp32 operand as TF32 by dropping those 13 bits (truncation, checked on B200), so
-        // the staged x already serves as the head and only the rest is written ------------------------
+        // ---- 3xTF32 split: head = x with the low 13 mantissa bits cleared, rest = x - head rounded to
+        // the nearest TF32 value. The tensor core reads an fp32 operand as TF32 by dropping those 13 bits
+        // (truncation, checked on B200), so the staged x already serves as the head and only the rest is
+        // written --------------------------------------------------------------------------------------
         const int t2 = tid - kSplitWarp0 * 32;  // 0 .. kSplitThreads - 1
         const int nb = BN * TK / 4;
         int st = 0;
@@ -250,13 +235,11 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                 if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
                 float4 *ah = reinterpret_cast<float4 *>(ring_a + st * kStageA), *al = reinterpret_cast<float4 *>(rest_a + st * kStageA);
                 for (int i = t2; i < TM * TK / 4; i += kSplitThreads) {
-                    float4 v = ah[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                    al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                    al[i] = tf32_rest4(ah[i]);
                 }
                 float4 *bh = reinterpret_cast<float4 *>(ring_b + st * sbq), *bl = reinterpret_cast<float4 *>(rest_b + st * sbq);
                 for (int i = t2; i < nb; i += kSplitThreads) {
-                    float4 v = bh[i], h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                    bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                    bl[i] = tf32_rest4(bh[i]);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
                 mbar_arrive(&s.ready[st]);
@@ -347,42 +330,6 @@ __global__ void k_tc_combine(TcParams p, int64_t nout) {
 
 // ---- host side -------------------------------------------------------------------------------------
 
-typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encoder() {
-    static EncodeTiled fn = nullptr;
-    static int tried = 0;
-    if (!tried) {
-        tried = 1;
-        cudaDriverEntryPointQueryResult q;
-        void *f = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiled)f;
-        cudaGetLastError();
-    }
-    return fn;
-}
-
-// operand view: `inner` elements contiguous (ld elements between outer rows), optional batch dim
-bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
-              int64_t bstride, int box_inner, int box_outer, bool mn_major) {
-    EncodeTiled enc = encoder();
-    if (!enc) return false;
-    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
-    cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bstride * 4};
-    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
-    cuuint32_t estr[3] = {1, 1, 1};
-    cuuint32_t rank = batch > 1 ? 3 : 2;
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, (void *)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 // stages that fit: per stage a P tile (16 KiB) and a Q tile (BN * 128 B), doubled in 3xTF32 mode
 int ring_stages(int bn, bool three) {
     size_t per = (size_t)(kStageA + bn * TK) * 4 * (three ? 2 : 1);
@@ -452,11 +399,12 @@ extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
     const int64_t maxpart = (int64_t)(d->scratch_bytes / sizeof(float)) / (a->M * a->N * nout);
     int64_t splits = 1;
     if (p.reduce) {
-        // the batch sum: enough slices to occupy every SM, each slice a run of whole samples
-        splits = (sms + tiles - 1) / tiles;
+        // the batch sum: a slice per SM (no more units than SMs), each slice a run of whole samples
+        splits = sms / tiles > 1 ? sms / tiles : 1;
         if (splits > a->batch) splits = a->batch;
     } else if (tiles * nout < sms) {
-        splits = (sms + tiles * nout - 1) / (tiles * nout);
+        // no more units than SMs: one unit over the grid would run as a second wave on its own
+        splits = sms / (tiles * nout);
         int64_t cap = (a->K + 4 * TK - 1) / (4 * TK);
         if (splits > cap) splits = cap;
     }

@@ -3,6 +3,8 @@
 // split. All functions are inline; each kernel family includes this header in its own file.
 #pragma once
 
+#include <cuda.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "k_common.cuh"
@@ -110,7 +112,38 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                  : "memory");
 }
 
+// TMA tile loads into shared memory (no multicast), completing on an mbarrier
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+// The 3xTF32 remainder x - head, rounded to the nearest TF32 value (cvt.rna: ties away from zero).
+// The tensor core truncates its operands, so an unrounded remainder would lose its own low 13 bits
+// toward zero on every product, a bias that grows with the length of the reduction; a remainder that
+// is already a TF32 value passes through exactly and its rounding error has no preferred sign.
+__device__ __forceinline__ float tf32_rest(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x - tf32_hi(x)));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ float4 tf32_rest4(float4 v) {
+    return make_float4(tf32_rest(v.x), tf32_rest(v.y), tf32_rest(v.z), tf32_rest(v.w));
+}
 
 // 16 consecutive accumulator columns of this warp's 32 lanes (32x32b shape, one register per column)
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -122,9 +155,71 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// TMEM columns to allocate for two accumulators of bn columns (a power of two, at least 32)
+// TMEM columns to allocate for two accumulators of bn columns (a power of two, at least 32, at most 512)
 __host__ __device__ constexpr uint32_t tmem_cols(int bn) {
-    return bn * 2 <= 32 ? 32 : bn * 2 <= 64 ? 64 : bn * 2 <= 128 ? 128 : 256;
+    return bn * 2 <= 32 ? 32 : bn * 2 <= 64 ? 64 : bn * 2 <= 128 ? 128 : bn * 2 <= 256 ? 256 : 512;
+}
+
+// tmem_ld16 without the wait: several loads in flight, then one tmem_wait_ld
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// waits for every tcgen05.ld of this thread; r (loaded before the wait) is tied to the wait so that
+// no use of it is scheduled above it
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// ties registers loaded before an earlier tmem_wait_ld to a point after it (volatile asm keeps order)
+__device__ __forceinline__ void tmem_regs_after_wait(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+
+// ---- host side: TMA tensor maps ------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static int tried = 0;
+    if (!tried) {
+        tried = 1;
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiled)f;
+        cudaGetLastError();
+    }
+    return fn;
+}
+
+// operand view: `inner` elements contiguous (ld elements between outer rows), optional batch dim
+inline bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
+              int64_t bstride, int box_inner, int box_outer, bool mn_major) {
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bstride * 4};
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    cuuint32_t rank = batch > 1 ? 3 : 2;
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, (void *)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 }  // namespace tc

@@ -26,6 +26,7 @@ typedef struct nck_dev {
     int64_t launches;  /* kernels enqueued so far */
     int gemm_mode;     /* NCK_GEMM_* */
     int conv_implicit; /* 1: convolutions try the implicit-GEMM kernels before unfolding (NC_CONV=implicit) */
+    int conv_tap;      /* 1: stride-1 convolutions run as tap-shifted GEMMs (default; NC_CONV=unfolded|implicit: 0) */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
     unsigned *counters; /* device counters for last-block-finishes reductions; each user leaves it at 0 */
@@ -182,6 +183,27 @@ int nck_conv_implicit(nck_dev *d, int mode, const nck_conv *g, const float *in, 
                       const float *bias);
 /* whether nck_conv_implicit would take this convolution (nothing is launched) */
 int nck_conv_implicit_supported(const nck_dev *d, int mode, const nck_conv *g);
+/* Stride-1 convolutions (groups 1) as tap-shifted GEMMs on tcgen05. An activation or output gradient
+ * is packed into a zero-padded, position-major matrix: row v = n*Hp*Wp + h'*Wp + w' of the padded grid
+ * (Hp = H + 2ph, Wp = W + 2pw), channels padded to a multiple of 32 along the row. Filter tap (ki, kj)
+ * is then the row shift ki*dh*Wp + kj*dw of that matrix, so every tap is a plain TMA tile load. In
+ * 3xTF32 mode every packed buffer is followed by its TF32 remainders (planes = 2, same shape). */
+typedef struct {
+    int64_t Hp, Wp, Nv, Cp, OCp, T;
+    int planes;
+} nck_tapgeom;
+/* 1 when the convolution takes the tap-shifted path; fills *t */
+int nck_convtap_plan(const nck_dev *d, const nck_conv *g, nck_tapgeom *t);
+/* dst[v][k] (Kp columns) from src [N][C][Hs][Ws] placed at padded offset (eh, ew), zero elsewhere */
+void nck_tap_pack(nck_dev *d, const float *src, int64_t N, int64_t C, int64_t Hs, int64_t Ws, const nck_tapgeom *t,
+                  int eh, int ew, int64_t Kp, float *dst);
+/* weights for the forward, [OC][T][Cp] (tr 0), or for dX, [C][T][OCp] (tr 1) */
+void nck_tap_pack_w(nck_dev *d, const nck_conv *g, const nck_tapgeom *t, const float *w, float *dst, int tr);
+/* mode 0: y = conv(x) + bias (P = packed x, Q = forward weights); 1: gx (+)= conv-transpose(gy)
+ * (P = packed gy, Q = dX weights); 2: gw += sum over positions (P = packed x, Q = packed gy).
+ * acc: add into out (modes 1, 2) instead of storing. Returns 0 when nothing was launched. */
+int nck_convtap(nck_dev *d, int mode, const nck_conv *g, const nck_tapgeom *t, const float *P, const float *Q,
+                float *out, const float *bias, int acc);
 /* gw[oc, k] += sum over n, l of gy[n, oc, l] * x-tap k at l (same eligibility as the direct forward) */
 void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw);
 void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);

@@ -5,9 +5,12 @@
  * :318-357, pooling :375-509). The schedule is the B200 one:
  *   - depthwise (groups == C == OC) and few-input-channel convolutions run direct kernels;
  *   - 1x1 stride-1 convolutions are plain strided-batch GEMMs on the activations themselves;
- *   - other convolutions unfold a chunk of samples at once (im2col over the whole chunk, bounded
- *     to 256 MiB) and run one strided-batch GEMM per group for Y, dX and dW; dW sums over the
- *     samples inside the GEMM, so no atomics and a fixed summation order.
+ *   - other stride-1 convolutions (groups 1) pack x (and, for the backward, dY) once into a
+ *     zero-padded position-major matrix and run Y, dX and dW as tap-shifted tcgen05 GEMMs over it
+ *     (nck_convtap: every filter tap is a row shift of the packed matrix, no unfolded copy);
+ *   - the rest unfold a chunk of samples at once (im2col over the whole chunk, bounded to 256 MiB)
+ *     and run one strided-batch GEMM per group for Y, dX and dW; dW sums over the samples inside
+ *     the GEMM, so no atomics and a fixed summation order.
  */
 #include "nc_internal.h"
 
@@ -123,6 +126,14 @@ static void gemm_fwd(nc_ctx *ctx, const nck_conv *g, const float *W, const float
     }
 }
 
+/* what the forward left for the backward: x unfolded (whole batch in one chunk) or x packed for the
+ * tap-shifted path */
+enum { SAVED_COL = 1, SAVED_TAP = 2 };
+typedef struct {
+    int kind;
+    float *buf;
+} conv_saved;
+
 static nc_status conv_fwd(nc_node *n) {
     nc_tensor *x = n->in[0], *w = n->in[1], *b = n->n_in > 2 ? n->in[2] : NULL;
     nc_ctx *ctx = x->ctx;
@@ -144,6 +155,21 @@ static nc_status conv_fwd(nc_node *n) {
         gemm_fwd(ctx, &g, Wt, X, g.C * HW, HW, B, Y, g.N);
         return NC_OK;
     }
+    nck_tapgeom tg;
+    if (nck_convtap_plan(nc__k(ctx), &g, &tg)) {
+        /* x packed once; the backward's weight gradient reads the same packed copy */
+        conv_saved *sv = (conv_saved *)nc__meta_alloc(ctx, sizeof(conv_saved), 0);
+        float *xp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.Cp * tg.planes) * sizeof(float));
+        float *wp = (float *)nc__arena_alloc(ctx, (size_t)(g.OC * tg.T * tg.Cp * tg.planes) * sizeof(float));
+        if (!sv || !xp || !wp) return NC_ERR_OOM;
+        nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp);
+        nck_tap_pack_w(nc__k(ctx), &g, &tg, Wt, wp, 0);
+        if (nck_convtap(nc__k(ctx), 0, &g, &tg, xp, wp, Y, B, 0)) {
+            sv->kind = SAVED_TAP, sv->buf = xp;
+            n->saved = sv;
+            return NC_OK;
+        }
+    }
     if (nck_conv_implicit(nc__k(ctx), 0, &g, X, Wt, Y, B)) return NC_OK; /* tensor cores, no unfolded copy */
     int64_t CKKL = g.C * g.KH * g.KW * L, nbmax = chunk_samples(&g);
     float *col = (float *)nc__arena_alloc(ctx, (size_t)(nbmax * CKKL) * sizeof(float));
@@ -155,7 +181,10 @@ static nc_status conv_fwd(nc_node *n) {
     }
     /* one chunk held the whole batch: the unfolded input stays valid in the step arena until step end
      * and the weight gradient reads it instead of unfolding x again */
-    if (nbmax >= g.N) n->saved = col;
+    if (nbmax >= g.N) {
+        conv_saved *sv = (conv_saved *)nc__meta_alloc(ctx, sizeof(conv_saved), 0);
+        if (sv) sv->kind = SAVED_COL, sv->buf = col, n->saved = sv;
+    }
     return NC_OK;
 }
 
@@ -231,6 +260,31 @@ static void conv_bwd(nc_node *n) {
         gw = NULL;
         if (!gx) return;
     }
+    const conv_saved *sv = (const conv_saved *)n->saved;
+    nck_tapgeom tg;
+    if ((gw || gx) && !is_pointwise(&g) && nck_convtap_plan(nc__k(ctx), &g, &tg)) {
+        /* dY packed once on the padded grid of x; dW against the packed x the forward left, dX from
+         * the shifted dY rows */
+        float *gp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.OCp * tg.planes) * sizeof(float));
+        if (!gp) return;
+        nck_tap_pack(nc__k(ctx), G, g.N, g.OC, g.OH, g.OW, &tg, 0, 0, tg.OCp, gp);
+        if (gw) {
+            float *xp = sv && sv->kind == SAVED_TAP ? sv->buf : NULL;
+            if (!xp) {
+                xp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.Cp * tg.planes) * sizeof(float));
+                if (!xp) return;
+                nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp);
+            }
+            if (nck_convtap(nc__k(ctx), 2, &g, &tg, xp, gp, (float *)gw->data, NULL, 1)) gw = NULL;
+        }
+        if (gx) {
+            float *wp = (float *)nc__arena_alloc(ctx, (size_t)(g.C * tg.T * tg.OCp * tg.planes) * sizeof(float));
+            if (!wp) return;
+            nck_tap_pack_w(nc__k(ctx), &g, &tg, Wt, wp, 1);
+            if (nck_convtap(nc__k(ctx), 1, &g, &tg, gp, wp, (float *)gx->data, NULL, acc_gx)) gx = NULL;
+        }
+        if (!gw && !gx) return;
+    }
     if (!is_pointwise(&g)) {
         /* tensor cores straight from x and dY (dX for unit strides); what is not handled here takes
          * the unfolded path below */
@@ -245,7 +299,7 @@ static void conv_bwd(nc_node *n) {
         return;
     }
     int64_t CKKL = g.C * g.KH * g.KW * L, nbmax = chunk_samples(&g);
-    const float *fwd_col = nbmax >= g.N ? (const float *)n->saved : NULL; /* x unfolded by the forward */
+    const float *fwd_col = nbmax >= g.N && sv && sv->kind == SAVED_COL ? sv->buf : NULL; /* x unfolded by the forward */
     if (gw && fwd_col) {
         gemm_dw(ctx, &g, G, fwd_col, CKKL, L, (float *)gw->data, g.N);
         gw = NULL;

@@ -4,8 +4,12 @@ padding, dilation, non-square kernels, position counts that are not a multiple o
 tile, channel counts above one 128-wide tile, reductions split across CTAs. Unit-stride dX runs on
 the implicit path too; strided dX and the FFMA mode take the unfolded path, checked the same way.
 
-Every case runs on both convolution paths: unfolded (im2col + GEMM + col2im) and implicit
-(NC_CONV=implicit). Tolerances (normwise, max|err| / max|ref|): FFMA and 3xTF32 1e-5, TF32 2e-3."""
+Every case runs on three convolution paths: tap-shifted GEMMs over the packed padded grid (the
+default, NC_CONV=tap; strided convolutions fall through to the unfolded path), unfolded (im2col +
+GEMM + col2im, NC_CONV=unfolded) and implicit (NC_CONV=implicit). Tolerances (normwise,
+max|err| / max|ref|): FFMA 1e-5; 3xTF32 4e-5 (the tap-shifted dX sums taps x output channels, up to
+1800 products here, in one tensor-memory accumulator, whose fp32 additions are not round-to-nearest);
+TF32 2e-3. The contract for the tensor-core path is 1e-3."""
 
 from __future__ import annotations
 
@@ -15,7 +19,7 @@ import pytest
 from nchelp import Eng, rel_err, seeded
 
 pytestmark = pytest.mark.gpu
-TOL = {"ffma": 1e-5, "3xtf32": 1e-5, "tf32": 2e-3}
+TOL = {"ffma": 1e-5, "3xtf32": 4e-5, "tf32": 2e-3}
 
 # (N, C, H, W), (OC, KH, KW), stride, pad, dilation
 GEOMS = [
@@ -38,9 +42,10 @@ def mode(request, monkeypatch):
     return request.param
 
 
-@pytest.fixture(params=["unfolded", "implicit"], autouse=True)
+@pytest.fixture(params=["tap", "unfolded", "implicit"], autouse=True)
 def conv_path(request, monkeypatch):
-    """NC_CONV=implicit: tensor-core convolutions gathered straight from x / dY (no unfolded copy)."""
+    """NC_CONV=tap: tap-shifted GEMMs over packed x / dY; implicit: tensor-core convolutions gathered
+    straight from x / dY; unfolded: im2col + GEMM + col2im."""
     monkeypatch.setenv("NC_CONV", request.param)
     return request.param
 
@@ -89,7 +94,7 @@ def test_conv_grads_accumulate(mode):
 
 
 def test_conv_large_batch_against_unfolded_path(monkeypatch):
-    """cfg2's second convolution at batch 128: implicit (3xTF32) against the unfolded FFMA path."""
+    """cfg2's second convolution at batch 128: the tensor-core path (3xTF32) against FFMA."""
     xs, ws = (128, 32, 14, 14), (64, 32, 3, 3)
     X, W, B = seeded(9, xs), seeded(10, ws, 0.2), seeded(11, (64,))
     res = {}
@@ -103,4 +108,4 @@ def test_conv_large_batch_against_unfolded_path(monkeypatch):
             e.backward_with(y, G)
             res[m] = (out, e.grad(x), e.grad(w), e.grad(b))
     for a, r in zip(res["3xtf32"], res["ffma"]):
-        assert rel_err(a, r) < 1e-5
+        assert rel_err(a, r) < TOL["3xtf32"]

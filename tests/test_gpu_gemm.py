@@ -87,4 +87,7 @@ def test_conv_weight_grad_batch_reduction_large(mode):
         dw = e.grad(w)
     import ncoracle as O
     _, dw_ref, _ = O.conv2d_grads(X, W, G, pad=(1, 1))
-    assert rel_err(dw, dw_ref) < TOL[mode]
+    # a sum over 50k positions: in 3xTF32 each reduction slice adds ~1000 tensor-core products into one
+    # tensor-memory accumulator (fp32 additions that are not round-to-nearest), ~1e-5 normwise
+    tol = 4e-5 if mode == "3xtf32" else TOL[mode]
+    assert rel_err(dw, dw_ref) < tol
