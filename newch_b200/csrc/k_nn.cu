@@ -322,6 +322,80 @@ __device__ __forceinline__ ulonglong4 warp_matvec(const ulonglong4 *__restrict__
 
 __device__ __forceinline__ unsigned long long rotl64(unsigned long long x, int k) { return (x << k) | (x >> (64 - k)); }
 
+// one xoshiro256** state transition
+__device__ __forceinline__ void xo_step(unsigned long long (&s)[4]) {
+    const unsigned long long t = s[1] << 17;
+    s[2] ^= s[0];
+    s[3] ^= s[1];
+    s[1] ^= s[2];
+    s[0] ^= s[3];
+    s[2] ^= t;
+    s[3] = rotl64(s[3], 45);
+}
+
+// The thread's 64 draws from state s0 (uniform u = (r >> 40) * 2^-24, exact; kept when u >= p) into
+// its two mask words in shared memory, then the block's 8192 outputs and mask words, coalesced.
+__device__ __forceinline__ void drop_block_out(const unsigned long long (&s0)[4], const float *__restrict__ x,
+                                               float *__restrict__ y, uint32_t *__restrict__ bits, int64_t n, float p,
+                                               uint32_t *mb) {
+    const int tid = threadIdx.x;
+    unsigned long long s[4] = {s0[0], s0[1], s0[2], s0[3]};
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll 8
+    for (int i = 0; i < kDropDraws; i++) {
+        const unsigned long long r = rotl64(s[1] * 5ull, 7) * 9ull;
+        xo_step(s);
+        const float u = (float)(r >> 40) * (1.0f / 16777216.0f);
+        const uint32_t keep = u >= p ? 1u : 0u;
+        if (i < 32) w0 |= keep << i;
+        else w1 |= keep << (i - 32);
+    }
+    mb[2 * tid] = w0;
+    mb[2 * tid + 1] = w1;
+    __syncthreads();
+    const float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+    const int64_t base = (int64_t)blockIdx.x * kDropBlock;
+    for (int j = tid; j < kDropBlock; j += kDropThreads) {
+        const int64_t e = base + j;
+        if (e < n) {
+            const float m = (mb[j >> 5] >> (j & 31)) & 1u ? keepv : 0.0f;
+            y[e] = x[e] * m;
+        }
+    }
+    const int64_t words = (n + 31) / 32;
+    for (int w = tid; w < kDropBlock / 32; w += kDropThreads) {
+        const int64_t gw = (int64_t)blockIdx.x * (kDropBlock / 32) + w;
+        if (gw < words) bits[gw] = mb[w];
+    }
+}
+
+// Thread k of the grid owns draws [64 k, 64 k + 64) (the same runs as the matrix-jump kernel below).
+// Its start state is q_k(T) s0, q_k = x^(64 k) mod P (P the characteristic polynomial of the
+// transition T, q_k from the host's table), evaluated by Horner's rule: 256 transitions of a running
+// state, XORed into the result where q_k has a one. No thread waits for another before its draws.
+__global__ void __launch_bounds__(kDropThreads) k_dropout_fwd_poly(ulonglong4 s0, const ulonglong4 *__restrict__ polys,
+                                                                   const float *__restrict__ x, float *__restrict__ y,
+                                                                   uint32_t *__restrict__ bits, int64_t n, float p) {
+    __shared__ uint32_t mb[kDropBlock / 32];
+    const int64_t k = (int64_t)blockIdx.x * kDropThreads + threadIdx.x;
+    unsigned long long a[4] = {0, 0, 0, 0};
+    if (k * kDropDraws < n) {
+        const ulonglong4 q = polys[k];
+        const unsigned long long qw[4] = {q.x, q.y, q.z, q.w};
+        unsigned long long s[4] = {s0.x, s0.y, s0.z, s0.w};
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+#pragma unroll 16
+            for (int b = 0; b < 64; b++) {
+                const unsigned long long m = 0ull - ((qw[w] >> b) & 1ull);
+                a[0] ^= s[0] & m, a[1] ^= s[1] & m, a[2] ^= s[2] & m, a[3] ^= s[3] & m;
+                xo_step(s);
+            }
+        }
+    }
+    drop_block_out(a, x, y, bits, n, p, mb);
+}
+
 __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
                                                               float *__restrict__ y, uint32_t *__restrict__ bits,
                                                               int64_t n, float p) {
@@ -347,48 +421,51 @@ __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, con
         }
         __syncthreads();
     }
-    // 64 draws: uniform u = (r >> 40) * 2^-24 (exact), kept when u >= p
-    unsigned long long s[4] = {st[tid].x, st[tid].y, st[tid].z, st[tid].w};
-    uint32_t w0 = 0, w1 = 0;
-    for (int i = 0; i < kDropDraws; i++) {
-        unsigned long long r = rotl64(s[1] * 5ull, 7) * 9ull;
-        unsigned long long t = s[1] << 17;
-        s[2] ^= s[0];
-        s[3] ^= s[1];
-        s[1] ^= s[2];
-        s[0] ^= s[3];
-        s[2] ^= t;
-        s[3] = rotl64(s[3], 45);
-        float u = (float)(r >> 40) * (1.0f / 16777216.0f);
-        uint32_t keep = u >= p ? 1u : 0u;
-        if (i < 32) w0 |= keep << i;
-        else w1 |= keep << (i - 32);
+    const unsigned long long s[4] = {st[tid].x, st[tid].y, st[tid].z, st[tid].w};
+    drop_block_out(s, x, y, bits, n, p, mb);
+}
+
+// the device copy of the run polynomials x^(64 k) mod P: grown on demand, never shrunk
+struct PolyTable {
+    void *dev;
+    int64_t n;
+};
+static PolyTable g_polys[128];
+
+extern "C" const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t count) {
+    if (d->device < 0 || d->device >= 128) return nullptr;
+    PolyTable &t = g_polys[d->device];
+    if (t.n >= count) return t.dev;
+    void *dev = nullptr;
+    if (cudaMalloc(&dev, (size_t)count * 32) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
     }
-    mb[2 * tid] = w0;
-    mb[2 * tid + 1] = w1;
-    __syncthreads();
-    float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
-    int64_t base = (int64_t)blockIdx.x * kDropBlock;
-    for (int j = tid; j < kDropBlock; j += kDropThreads) {
-        int64_t e = base + j;
-        if (e < n) {
-            float m = (mb[j >> 5] >> (j & 31)) & 1u ? keepv : 0.0f;
-            y[e] = x[e] * m;
-        }
+    if (cudaMemcpy(dev, host, (size_t)count * 32, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(dev);
+        return nullptr;
     }
-    int64_t words = (n + 31) / 32;
-    for (int w = tid; w < kDropBlock / 32; w += kDropThreads) {
-        int64_t gw = (int64_t)blockIdx.x * (kDropBlock / 32) + w;
-        if (gw < words) bits[gw] = mb[w];
+    if (t.dev) {
+        // kernels in flight may still read the shorter table
+        cudaDeviceSynchronize();
+        cudaFree(t.dev);
     }
+    t.dev = dev, t.n = count;
+    return dev;
 }
 
 extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits,
-                                int64_t n, float p) {
+                                int64_t n, float p, const void *polys) {
     if (n <= 0) return;
     Scope sc(d, "dropout", 0.0, 8.0 * n + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
+    if (polys) {
+        k_dropout_fwd_poly<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(
+            s0, reinterpret_cast<const ulonglong4 *>(polys), x, y, bits, n, p);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     static int attr_done = 0;
     if (!attr_done) {
         cudaFuncSetAttribute(k_dropout_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDropSmem);

@@ -213,6 +213,8 @@ float nc__rand_normal(nc_ctx *ctx);
 /* advances the context stream by n draws without producing them */
 void nc__rng_skip(nc_ctx *ctx, uint64_t n);
 int nc__rng_device_init(nc_ctx *ctx);
+const uint64_t *nc__rng_run_polys(int64_t count);          /* x^(64 k) mod P, k < count (host) */
+const void *nc__rng_dropout_table(nc_ctx *ctx, int64_t n); /* the same on the device, or NULL */
 
 void nc__detect_cpu(nc_cpu_info *info);
 

@@ -132,8 +132,11 @@ void nck_cross_entropy_bwd(nck_dev *d, const float *prob, const int32_t *lab, co
 void nck_nll_fwd(nck_dev *d, const float *x, const int32_t *lab, float *loss, int64_t N, int64_t C, int sum);
 void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, int64_t N, int64_t C, int sum);
 /* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i */
+/* polys: the device table of run polynomials (nck_rng_polys) or NULL to jump by matrices */
 void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits, int64_t n,
-                     float p);
+                     float p, const void *polys);
+/* device copy of x^(64 k) mod P for k < count from the host table (uploaded once, grown on demand) */
+const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t count);
 void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p, int acc);
 /* one-time upload of the xoshiro256** jump tables (host-computed) */
 int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes);

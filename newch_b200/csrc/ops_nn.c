@@ -156,7 +156,8 @@ static nc_status dropout_fwd(nc_node *n) {
     int64_t words = (N + 31) / 32 + 1;
     uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
     if (!x || !bits) return NC_ERR_OOM;
-    if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0]);
+    if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0],
+                           nc__rng_dropout_table(ctx, N));
     nc__rng_skip(ctx, (uint64_t)N);
     n->saved = bits;
     return NC_OK;

@@ -10,6 +10,13 @@
  *
  * Bit matrices are stored by column: column j (4 x 64 bits) is the image of the state with only bit
  * j set. Bit j of the state is bit (j % 64) of word j / 64.
+ *
+ * Jumps by polynomial. T satisfies its characteristic polynomial P (degree 256, found once by
+ * Berlekamp-Massey on 512 output bits of the generator), so T^d = q_d(T) with q_d = x^d mod P, a
+ * 256-bit polynomial that does not depend on the state. The host keeps q_(64 k) for the runs of 64
+ * draws the dropout kernel gives each thread (grown on demand, checked against the matrix jumps),
+ * and a thread reaches its start state from the launch's state by Horner's rule: 256 generator
+ * steps with a conditional XOR, independent of every other thread.
  */
 #include "nc_internal.h"
 
@@ -118,4 +125,143 @@ int nc__rng_device_init(nc_ctx *ctx) {
         return 0;
     }
     return 1;
+}
+
+/* ---- jump polynomials --------------------------------------------------------------------------- */
+
+typedef uint64_t poly[4]; /* GF(2) polynomial of degree < 256: bit i = coefficient of x^i */
+
+static poly g_charp;                       /* P(x) - x^256 */
+static pthread_once_t g_charp_once = PTHREAD_ONCE_INIT;
+static int g_charp_ok;
+
+/* Berlekamp-Massey over GF(2) on the lowest output bit of the state's first word */
+static void find_charpoly(void) {
+    enum { NB = 512 };
+    uint8_t a[NB];
+    uint64_t s[4] = {0x9E3779B97F4A7C15ull, 0xBF58476D1CE4E5B9ull, 0x94D049BB133111EBull, 0x2545F4914F6CDD1Dull};
+    for (int k = 0; k < NB; k++) {
+        a[k] = (uint8_t)(s[0] & 1u);
+        step(s);
+    }
+    uint8_t C[NB + 1] = {1}, B[NB + 1] = {1}, Tm[NB + 1];
+    int L = 0, m = 1;
+    for (int n = 0; n < NB; n++) {
+        uint8_t dsc = a[n];
+        for (int i = 1; i <= L; i++) dsc ^= (uint8_t)(C[i] & a[n - i]);
+        if (!dsc) {
+            m++;
+        } else if (2 * L <= n) {
+            memcpy(Tm, C, sizeof C);
+            for (int i = 0; i + m <= NB; i++) C[i + m] ^= B[i];
+            L = n + 1 - L;
+            memcpy(B, Tm, sizeof B);
+            m = 1;
+        } else {
+            for (int i = 0; i + m <= NB; i++) C[i + m] ^= B[i];
+            m++;
+        }
+    }
+    if (L != 256) return;
+    /* a[k+256] = sum_j C[j] a[k+256-j]  =>  P(x) = x^256 + sum_{i<256} C[256-i] x^i */
+    memset(g_charp, 0, sizeof g_charp);
+    for (int i = 0; i < 256; i++)
+        if (C[256 - i]) g_charp[i / 64] |= 1ull << (i % 64);
+    g_charp_ok = 1;
+}
+
+/* a <- a * x mod P */
+static inline void poly_mulx(uint64_t *a) {
+    uint64_t top = a[3] >> 63;
+    a[3] = (a[3] << 1) | (a[2] >> 63);
+    a[2] = (a[2] << 1) | (a[1] >> 63);
+    a[1] = (a[1] << 1) | (a[0] >> 63);
+    a[0] <<= 1;
+    if (top) a[0] ^= g_charp[0], a[1] ^= g_charp[1], a[2] ^= g_charp[2], a[3] ^= g_charp[3];
+}
+
+/* q(T) v by Horner: the same loop a device thread runs */
+static void poly_apply(const uint64_t *q, const uint64_t *v, uint64_t *out) {
+    uint64_t s[4], acc[4] = {0, 0, 0, 0};
+    memcpy(s, v, sizeof s);
+    for (int i = 0; i < 256; i++) {
+        if ((q[i / 64] >> (i % 64)) & 1u) acc[0] ^= s[0], acc[1] ^= s[1], acc[2] ^= s[2], acc[3] ^= s[3];
+        step(s);
+    }
+    memcpy(out, acc, sizeof acc);
+}
+
+static poly *g_runs;   /* g_runs[k] = x^(64 k) mod P */
+static int64_t g_nruns, g_capruns;
+static pthread_mutex_t g_runs_mu = PTHREAD_MUTEX_INITIALIZER;
+
+/* x^(64 k) mod P for k < count (host copy, grown on demand); NULL when unavailable. The first call
+ * checks a few polynomial jumps against the matrix jumps. */
+const uint64_t *nc__rng_run_polys(int64_t count) {
+    pthread_once(&g_charp_once, find_charpoly);
+    if (!g_charp_ok || count <= 0 || !powers_ready()) return NULL;
+    pthread_mutex_lock(&g_runs_mu);
+    if (count > g_capruns || g_capruns < 8) {
+        int64_t cap = g_capruns ? g_capruns : 1024;
+        while (cap < count) cap *= 2;
+        poly *r = (poly *)realloc(g_runs, (size_t)cap * sizeof(poly));
+        if (!r) {
+            pthread_mutex_unlock(&g_runs_mu);
+            return NULL;
+        }
+        g_runs = r, g_capruns = cap;
+    }
+    int check = g_nruns == 0;
+    if (count < 8) count = 8; /* the first call's check reads entries 1 and 5 */
+    if (count > g_capruns) {
+        pthread_mutex_unlock(&g_runs_mu);
+        return NULL;
+    }
+    if (g_nruns == 0) {
+        memset(g_runs[0], 0, sizeof(poly));
+        g_runs[0][0] = 1;
+        g_nruns = 1;
+    }
+    for (; g_nruns < count; g_nruns++) {
+        memcpy(g_runs[g_nruns], g_runs[g_nruns - 1], sizeof(poly));
+        for (int i = 0; i < 64; i++) poly_mulx(g_runs[g_nruns]);
+    }
+    if (check) {
+        /* q_(64 k)(T) v must equal T^(64 k) v from the squared matrices */
+        const uint64_t v[4] = {1, 0x1234567ull, 0xFEDCBA9876543210ull, 42};
+        const int64_t ks[3] = {1, 5, count - 1};
+        for (int t = 0; t < 3; t++) {
+            uint64_t a[4], b[4], o[4];
+            poly_apply(g_runs[ks[t]], v, a);
+            memcpy(b, v, sizeof b);
+            uint64_t d = (uint64_t)ks[t] * 64u;
+            for (int i = 0; i < 64; i++) {
+                if (!((d >> i) & 1)) continue;
+                matvec(g_pow[i], b, o);
+                memcpy(b, o, sizeof b);
+            }
+            if (memcmp(a, b, sizeof a)) {
+                g_charp_ok = 0;
+                pthread_mutex_unlock(&g_runs_mu);
+                return NULL;
+            }
+        }
+    }
+    const uint64_t *out = &g_runs[0][0];
+    pthread_mutex_unlock(&g_runs_mu);
+    return out;
+}
+
+/* Device table of run polynomials covering n draws (runs of 64), uploaded once and grown on demand;
+ * NULL when n is beyond the table's cap (2^27 draws) or the table is unavailable, and the dropout
+ * kernel then jumps by matrices instead. */
+const void *nc__rng_dropout_table(nc_ctx *ctx, int64_t n) {
+    if (n <= 0 || n > ((int64_t)1 << 27)) return NULL;
+    const char *jump = getenv("NC_DROPOUT_JUMP"); /* "matrix": always the matrix-jump kernel */
+    if (jump && !strcmp(jump, "matrix")) return NULL;
+    int64_t runs = (n + 63) / 64, want = 1024;
+    while (want < runs) want *= 2;
+    const uint64_t *host = nc__rng_run_polys(want);
+    if (!host) return NULL;
+    return nck_rng_polys(nc__k(ctx), host, want);
 }

@@ -228,10 +228,13 @@ def test_int8_layer_bit_exact_against_reference():
     assert np.array_equal(outs[0][2], yo)
 
 
+@pytest.mark.parametrize("jump", ["poly", "matrix"])
 @pytest.mark.parametrize("n", [1, 31, 16384, 16385, 100000, 1 << 20])
-def test_dropout_masks_match_reference_stream(n):
+def test_dropout_masks_match_reference_stream(n, jump, monkeypatch):
     """Device jump-ahead reproduces the reference stream for any length, and the host stream
-    continues where the kernel stopped."""
+    continues where the kernel stopped. Both jump kernels: by run polynomials (the default) and by
+    jump matrices (NC_DROPOUT_JUMP=matrix; the path for tensors beyond the polynomial table)."""
+    monkeypatch.setenv("NC_DROPOUT_JUMP", jump)
     res = []
     for which in ("b200", "ref"):
         with Eng(which, seed=99) as e:
