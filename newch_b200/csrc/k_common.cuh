@@ -41,6 +41,24 @@ inline FastDiv make_fastdiv(uint32_t d) {
     return f;
 }
 
+// A block's walk over the items of one channel in an [N][C][S] tensor: planes [n0, n1) of channel c,
+// SV vector items per plane. Thread t takes items t, t + B, t + 2B, ... (B = blockDim.x) and advances
+// its (plane, item) pair by a carry instead of a division per item.
+struct ChanWalk {
+    int na, ia, dn, dr, SV;
+    int64_t cnt;
+    __device__ __forceinline__ void init(int sv, int64_t planes) {
+        SV = sv, cnt = planes;
+        na = (int)(threadIdx.x / (unsigned)sv), ia = (int)threadIdx.x - na * sv;
+        dn = (int)(blockDim.x / (unsigned)sv), dr = (int)blockDim.x - dn * sv;
+    }
+    __device__ __forceinline__ bool live() const { return na < cnt; }
+    __device__ __forceinline__ void next() {
+        ia += dr, na += dn;
+        if (ia >= SV) ia -= SV, na++;
+    }
+};
+
 // Records a kernel-detected error (first one wins). The host reads it at its next synchronization.
 __device__ __forceinline__ void report(int *status, int code) { atomicCAS(status, 0, code); }
 

@@ -126,29 +126,35 @@ __global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restric
                                                           float *__restrict__ gb, unsigned *counter) {
     __shared__ float sm[kThreads / 32];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
-    const int SV = (int)(S / V);
-    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
+    // four items in flight per thread
+    const int64_t pstride = C * S;
+    const float *xc = x + (n0 * C + c) * S;
+    ChanWalk w;
+    w.init((int)(S / V), n1 > n0 ? n1 - n0 : 0);
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-    int t = threadIdx.x;
-    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
-        const int u = t + blockDim.x, na = t / SV, nb = u / SV;
-        const float *pa = x + ((n0 + na) * C + c) * S, *pb = x + ((n0 + nb) * C + c) * S;
-        if (V == 4) {
-            float4 va = __ldg(reinterpret_cast<const float4 *>(pa) + (t - na * SV));
-            float4 vb = __ldg(reinterpret_cast<const float4 *>(pb) + (u - nb * SV));
-            a0 += va.x + va.y, a1 += va.z + va.w, a2 += vb.x + vb.y, a3 += vb.z + vb.w;
-        } else {
-            a0 += __ldg(pa + (t - na * SV)), a2 += __ldg(pb + (u - nb * SV));
+    while (w.live()) {
+        float v[4][V];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (w.live()) {
+                const float *pa = xc + w.na * pstride;
+                if constexpr (V == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(pa) + w.ia);
+                    v[j][0] = q.x, v[j][1] = q.y, v[j][2] = q.z, v[j][3] = q.w;
+                } else {
+                    v[j][0] = __ldg(pa + w.ia);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < V; k++) v[j][k] = 0.0f;
+            }
+            w.next();
         }
-    }
-    if (t < total) {
-        const int na = t / SV;
-        const float *pa = x + ((n0 + na) * C + c) * S;
-        if (V == 4) {
-            float4 va = __ldg(reinterpret_cast<const float4 *>(pa) + (t - na * SV));
-            a0 += va.x + va.y, a1 += va.z + va.w;
+        if constexpr (V == 4) {
+            a0 += v[0][0] + v[0][1], a1 += v[0][2] + v[0][3], a2 += v[1][0] + v[1][1], a3 += v[1][2] + v[1][3];
+            a0 += v[2][0] + v[2][1], a1 += v[2][2] + v[2][3], a2 += v[3][0] + v[3][1], a3 += v[3][2] + v[3][3];
         } else {
-            a0 += __ldg(pa + (t - na * SV));
+            a0 += v[0][0], a1 += v[1][0], a2 += v[2][0], a3 += v[3][0];
         }
     }
     float acc = (a0 + a1) + (a2 + a3);
@@ -578,6 +584,24 @@ __global__ void __launch_bounds__(256) k_maxpool2x2(const float *__restrict__ x,
     }
 }
 
+// the same for an even input width: one output per thread from one float2 of each window row
+__global__ void __launch_bounds__(256) k_maxpool2x2_w2(const float *__restrict__ x, float *__restrict__ y,
+                                                       int32_t *__restrict__ arg, uint32_t planes, uint32_t H,
+                                                       uint32_t W, uint32_t OH, uint32_t OW, FastDiv dow, FastDiv doh) {
+    const uint32_t total = planes * OH * OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
+        const float *r0 = x + (size_t)pl * H * W + (size_t)(2 * oy) * W + 2 * ox;
+        const float2 a = __ldg(reinterpret_cast<const float2 *>(r0));
+        const float2 b = __ldg(reinterpret_cast<const float2 *>(r0 + W));
+        float best;
+        int32_t bi;
+        max4(a.x, a.y, b.x, b.y, (int32_t)(2 * oy * W + 2 * ox), (int32_t)W, best, bi);
+        y[t] = best;
+        arg[t] = bi;
+    }
+}
+
 extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max) {
     int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
@@ -589,6 +613,11 @@ extern "C" void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, floa
         const int64_t items = planes * g->OH * ((g->OW + 1) / 2);
         k_maxpool2x2<<<grid_for(d, items), 256, 0, NCK_STREAM(d)>>>(x, y, arg, (uint32_t)planes, (uint32_t)g->H,
                                                                   (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW);
+    } else if (is_max && g->KH == 2 && g->KW == 2 && g->sh == 2 && g->sw == 2 && g->ph == 0 && g->pw == 0 &&
+               g->W % 2 == 0 && ((uintptr_t)x & 7) == 0 && small_index(planes * g->H * g->W)) {
+        k_maxpool2x2_w2<<<grid_for(d, total), 256, 0, NCK_STREAM(d)>>>(
+            x, y, arg, (uint32_t)planes, (uint32_t)g->H, (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW,
+            make_fastdiv((uint32_t)g->OW), make_fastdiv((uint32_t)g->OH));
     } else if (small_index(g->N * g->C * g->H * g->W) && small_index(total))
         k_pool_fwd<uint32_t><<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(
             *g, x, y, arg, is_max, make_fastdiv((uint32_t)g->OW), make_fastdiv((uint32_t)g->OH));
@@ -686,6 +715,26 @@ __global__ void __launch_bounds__(256) k_maxpool2x2_bwd_set(const float *__restr
     }
 }
 
+// the same for an even width: a thread stores the two inputs of one window row with one 8-byte write
+__global__ void __launch_bounds__(256) k_maxpool2x2_bwd_set_w2(const float *__restrict__ gy,
+                                                               const int32_t *__restrict__ arg, float *__restrict__ gx,
+                                                               uint32_t planes, uint32_t H, uint32_t W, uint32_t OH,
+                                                               uint32_t OW, FastDiv dhalf, FastDiv dh) {
+    const uint32_t half = W / 2, total = planes * H * half;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dhalf.div(t), q = t - r * half, pl = dh.div(r), iy = r - pl * H, oy = iy >> 1;
+        float2 v = make_float2(0.0f, 0.0f);
+        if (oy < OH) {
+            const size_t o = (size_t)pl * OH * OW + (size_t)oy * OW + q;
+            const int32_t i0 = (int32_t)(iy * W + 2 * q), a = __ldg(arg + o);
+            const float gv = __ldg(gy + o);
+            v.x = a == i0 ? gv : 0.0f;
+            v.y = a == i0 + 1 ? gv : 0.0f;
+        }
+        *reinterpret_cast<float2 *>(gx + (size_t)pl * H * W + (size_t)iy * W + 2 * q) = v;
+    }
+}
+
 extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx,
                              int is_max, int acc) {
     Scope sc(d, is_max ? "max_pool_bwd" : "avg_pool_bwd", 0.0,
@@ -696,6 +745,14 @@ extern "C" void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, con
         const int64_t items = in_total / 4;
         k_maxpool2x2_bwd_set<<<grid_for(d, items), 256, 0, NCK_STREAM(d)>>>(
             gy, arg, gx, (uint32_t)(g->N * g->C), (uint32_t)g->H, (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
+    if (!acc && is_max && g->KH == 2 && g->KW == 2 && g->sh == 2 && g->sw == 2 && g->ph == 0 && g->pw == 0 &&
+        g->W % 2 == 0 && ((uintptr_t)gx & 7) == 0 && small_index(in_total)) {
+        k_maxpool2x2_bwd_set_w2<<<grid_for(d, in_total / 2), 256, 0, NCK_STREAM(d)>>>(
+            gy, arg, gx, (uint32_t)(g->N * g->C), (uint32_t)g->H, (uint32_t)g->W, (uint32_t)g->OH, (uint32_t)g->OW,
+            make_fastdiv((uint32_t)(g->W / 2)), make_fastdiv((uint32_t)g->H));
         NCK_LAUNCHED(d, 1);
         return;
     }

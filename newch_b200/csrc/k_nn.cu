@@ -564,31 +564,30 @@ __global__ void __launch_bounds__(256) k_bn_stats(const float *__restrict__ x, d
                                                   unsigned *counter) {
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
-    const int SV = (int)(S / V);
-    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
+    // four items in flight per thread, then their double sums (two chains)
+    const int64_t pstride = C * S;
+    const float *xc = x + (n0 * C + c) * S;
+    ChanWalk w;
+    w.init((int)(S / V), n1 > n0 ? n1 - n0 : 0);
     double s0 = 0.0, q0 = 0.0, s1 = 0.0, q1 = 0.0;
-    int t = threadIdx.x;
-    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
-        int u = t + blockDim.x;
-        int na = t / SV, nb = u / SV;
-        float va[V], vb[V];
-        bn_load<V>(x + ((n0 + na) * C + c) * S, t - na * SV, va);
-        bn_load<V>(x + ((n0 + nb) * C + c) * S, u - nb * SV, vb);
+    while (w.live()) {
+        float v[4][V];
 #pragma unroll
-        for (int k = 0; k < V; k++) {
-            double a = (double)va[k], b = (double)vb[k];
-            s0 += a, q0 += a * a, s1 += b, q1 += b * b;
-        }
-    }
-    if (t < total) {
-        int na = t / SV;
-        float va[V];
-        bn_load<V>(x + ((n0 + na) * C + c) * S, t - na * SV, va);
+        for (int j = 0; j < 4; j++) {
+            if (w.live()) bn_load<V>(xc + w.na * pstride, w.ia, v[j]);
+            else
 #pragma unroll
-        for (int k = 0; k < V; k++) {
-            double a = (double)va[k];
-            s0 += a, q0 += a * a;
+                for (int k = 0; k < V; k++) v[j][k] = 0.0f;
+            w.next();
         }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int k = 0; k < V; k++) {
+                const double a = (double)v[j][k];
+                if (j & 1) s1 += a, q1 += a * a;
+                else s0 += a, q0 += a * a;
+            }
     }
     double s = s0 + s1, ss = q0 + q1;
     block_sum2(s, ss, sm);
@@ -724,33 +723,32 @@ __global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const float mu = mean[c], is = invstd[c];
-    const int SV = (int)(S / V);
-    const int total = (int)(n1 > n0 ? (n1 - n0) * SV : 0);
+    // four items of x and g in flight per thread, then float products into double sums (two chains)
+    const int64_t pstride = C * S, cbase = (n0 * C + c) * S;
+    ChanWalk w;
+    w.init((int)(S / V), n1 > n0 ? n1 - n0 : 0);
     double g0 = 0.0, h0 = 0.0, g1 = 0.0, h1 = 0.0;
-    int t = threadIdx.x;
-    for (; t + (int)blockDim.x < total; t += 2 * blockDim.x) {
-        int u = t + blockDim.x;
-        int na = t / SV, nb = u / SV;
-        int64_t oa = ((n0 + na) * C + c) * S, ob = ((n0 + nb) * C + c) * S;
-        float xa[V], ga[V], xb[V], gb[V];
-        bn_load<V>(x + oa, t - na * SV, xa);
-        bn_load<V>(g + oa, t - na * SV, ga);
-        bn_load<V>(x + ob, u - nb * SV, xb);
-        bn_load<V>(g + ob, u - nb * SV, gb);
+    while (w.live()) {
+        float xv[4][V], gv[4][V];
 #pragma unroll
-        for (int k = 0; k < V; k++) {
-            g0 += ga[k], h0 += ga[k] * (xa[k] - mu) * is;
-            g1 += gb[k], h1 += gb[k] * (xb[k] - mu) * is;
+        for (int j = 0; j < 4; j++) {
+            if (w.live()) {
+                const int64_t o = cbase + w.na * pstride;
+                bn_load<V>(x + o, w.ia, xv[j]);
+                bn_load<V>(g + o, w.ia, gv[j]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < V; k++) xv[j][k] = mu, gv[j][k] = 0.0f;
+            }
+            w.next();
         }
-    }
-    if (t < total) {
-        int na = t / SV;
-        int64_t oa = ((n0 + na) * C + c) * S;
-        float xa[V], ga[V];
-        bn_load<V>(x + oa, t - na * SV, xa);
-        bn_load<V>(g + oa, t - na * SV, ga);
 #pragma unroll
-        for (int k = 0; k < V; k++) g0 += ga[k], h0 += ga[k] * (xa[k] - mu) * is;
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int k = 0; k < V; k++) {
+                if (j & 1) g1 += gv[j][k], h1 += gv[j][k] * (xv[j][k] - mu) * is;
+                else g0 += gv[j][k], h0 += gv[j][k] * (xv[j][k] - mu) * is;
+            }
     }
     double sg = g0 + g1, sgx = h0 + h1;
     block_sum2(sg, sgx, sm);

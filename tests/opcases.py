@@ -76,6 +76,31 @@ def case_maxpool_2x2(e):
     return _pool(e, (2, 3, 8, 8), (2, 2), (2, 2), (0, 0), True, 70)
 
 
+def _pool_fresh(e, xs, seed):
+    """2x2 / stride-2 max pooling of an intermediate (scale by 1): its gradient is a fresh buffer, so the
+    backward takes the kernels that store every input gradient instead of adding."""
+    x = e.param(seeded(seed, xs))
+    h = e.check(e.L.nc_scale(x, 1.0))
+    y = e.check(e.L.nc_max_pool2d(h, 2, 2, 2, 2, 0, 0))
+    G = seeded(seed + 1, e.shape(y))
+    out = {"x": e.np(x), "y": e.np(y), "G": G}
+    e.backward_with(y, G)
+    out["dx"] = e.grad(x)
+    return out
+
+
+def case_maxpool_2x2_w4(e):
+    return _pool_fresh(e, (2, 3, 9, 12), 71)  # width a multiple of 4, odd height
+
+
+def case_maxpool_2x2_w2(e):
+    return _pool_fresh(e, (3, 4, 14, 14), 72)  # even width (cfg2's second pooling)
+
+
+def case_maxpool_2x2_odd(e):
+    return _pool_fresh(e, (2, 2, 7, 9), 73)  # odd width and height
+
+
 def case_maxpool_overlap(e):
     return _pool(e, (1, 2, 5, 6), (3, 3), (1, 1), (1, 1), True, 80)
 

@@ -26,6 +26,9 @@ EXACT = {
     "reductions": {"argmax_1", "max_0_y", "max_1_y", "max_2_y", "max_all_y", "max_0_dx", "max_1_dx", "max_2_dx",
                    "max_all_dx"},
     "maxpool_2x2": {"y"},
+    "maxpool_2x2_w4": {"y", "dx"},
+    "maxpool_2x2_w2": {"y", "dx"},
+    "maxpool_2x2_odd": {"y", "dx"},
     "maxpool_overlap": {"y"},
     "to_dtype": {"u8", "f", "u8_f32", "f_i32", "f_i8"},
     "index_select": {"y"},
