@@ -41,6 +41,20 @@ inline FastDiv make_fastdiv(uint32_t d) {
     return f;
 }
 
+// Blocks of `kernel` that fit on the whole GPU at once (its occupancy per SM times the SMs): grids of
+// split reductions are sized to one full wave, so no block runs in a second, mostly idle wave. The
+// occupancy query runs once per call site (cache it in a static).
+template <typename K>
+inline int resident_blocks(const nck_dev *d, K kernel, int threads, size_t smem = 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        per_sm = 1;
+    }
+    if (per_sm < 1) per_sm = 1;
+    return per_sm * (d->sm_count > 0 ? d->sm_count : 148);
+}
+
 // A block's walk over the items of one channel in an [N][C][S] tensor: planes [n0, n1) of channel c,
 // SV vector items per plane. Thread t takes items t, t + B, t + 2B, ... (B = blockDim.x) and advances
 // its (plane, item) pair by a carry instead of a division per item.

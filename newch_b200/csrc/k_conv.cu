@@ -180,7 +180,11 @@ __global__ void __launch_bounds__(256) k_chan_sum_partial(const float *__restric
 extern "C" void nck_conv_bias_grad(nck_dev *d, const float *g, float *gb, int64_t N, int64_t OC, int64_t L) {
     if (N * OC * L <= 0) return;
     Scope sc(d, "conv_bias_grad", 0.0, 4.0 * (N * OC * L + 2 * OC));
-    int64_t splits = ((int64_t)d->sm_count * 8 + OC - 1) / OC;
+    const bool v4 = (L & 3) == 0 && ((uintptr_t)g & 15) == 0;
+    static int res4 = 0, res1 = 0;
+    if (v4 && !res4) res4 = resident_blocks(d, k_chan_sum_partial<4>, kThreads);
+    if (!v4 && !res1) res1 = resident_blocks(d, k_chan_sum_partial<1>, kThreads);
+    int64_t splits = (v4 ? res4 : res1) / OC;  // one full wave
     int64_t need = (N * L + ((int64_t)1 << 30) - 1) >> 30; /* a block walks at most 2^30 elements */
     if (splits < need) splits = need;
     if (splits > N) splits = N;
@@ -352,7 +356,9 @@ template <int KT, int OCW>
 static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
     const int64_t OCg = g->OC / g->G, CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
     const int64_t chunks = (OCg + OCW - 1) / OCW, total = g->N * L, wsz = g->OC * CKK;
-    int64_t splits = ((int64_t)d->sm_count * 8 + g->G * chunks - 1) / (g->G * chunks);
+    static int resident = 0;  // one full wave of blocks
+    if (!resident) resident = resident_blocks(d, k_direct_dw_partial<KT, OCW>, 128);
+    int64_t splits = resident / (g->G * chunks);
     int64_t maxs = (int64_t)(d->scratch_bytes / sizeof(float)) / wsz;
     if (splits > maxs) splits = maxs;
     if (splits > (total + 127) / 128) splits = (total + 127) / 128;

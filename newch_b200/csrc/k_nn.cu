@@ -646,10 +646,11 @@ static int flat_grid(const nck_dev *d, int64_t items) {
     return want < 1 ? 1 : (int)want;
 }
 
-// runs of samples per channel: about 8 blocks per SM, and at most 2^30 elements per block (the
-// statistics kernels index a block's elements with 32-bit integers)
-static int64_t bn_splits(const nck_dev *d, int64_t N, int64_t C, int64_t S) {
-    int64_t want = ((int64_t)d->sm_count * 8 + C - 1) / C;
+// runs of samples per channel: as many blocks as fit on the GPU at once (`resident`, one full wave),
+// and at most 2^30 elements per block (the statistics kernels index a block's elements with 32-bit
+// integers)
+static int64_t bn_splits(int64_t resident, int64_t N, int64_t C, int64_t S) {
+    int64_t want = resident / C;
     int64_t need = (N * S + ((int64_t)1 << 30) - 1) >> 30;
     if (want < need) want = need;
     if (want < 1) want = 1;
@@ -661,11 +662,14 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
                                  float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
                                  float eps) {
     Scope sc(d, "bn_fwd", 0.0, 8.0 * N * C * S);
-    int64_t splits = bn_splits(d, N, C, S), per = (N + splits - 1) / splits;
+    const bool v4 = bn_vec4(S, x, y, x);
+    static int res4 = 0, res1 = 0;
+    if (v4 && !res4) res4 = resident_blocks(d, k_bn_stats<4>, kThreads);
+    if (!v4 && !res1) res1 = resident_blocks(d, k_bn_stats<1>, kThreads);
+    int64_t splits = bn_splits(v4 ? res4 : res1, N, C, S), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     dim3 g1((unsigned)C, (unsigned)splits);
-    const bool v4 = bn_vec4(S, x, y, x);
     const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits};
     if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
@@ -801,12 +805,15 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
                            const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
                            int training, int acc_gx) {
     Scope sc(d, "bn_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * N * C * S);
-    int64_t splits = bn_splits(d, N, C, S), per = (N + splits - 1) / splits;
+    const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
+    static int res4 = 0, res1 = 0;
+    if (v4 && !res4) res4 = resident_blocks(d, k_bn_bwd_sums<4>, kThreads);
+    if (!v4 && !res1) res1 = resident_blocks(d, k_bn_bwd_sums<1>, kThreads);
+    int64_t splits = bn_splits(v4 ? res4 : res1, N, C, S), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     dim3 g1((unsigned)C, (unsigned)splits);
-    const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
     const BnBwdFin fin = {gw, gb, coef, (int)splits};
     if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
     else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
