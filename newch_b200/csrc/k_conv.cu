@@ -268,6 +268,65 @@ __global__ void __launch_bounds__(256) k_conv_direct(nck_conv g, const float *__
     }
 }
 
+// ---- direct 3x3 convolution of one input channel (stride 1, dilation 1, groups 1): a thread owns one
+// output column and four consecutive output rows --------------------------------------------------------
+
+// the 6 x 3 input window of outputs (oy0 .. oy0 + 3, ox): win[kj][i] = x[oy0 - ph + i][ox - pw + kj], zero
+// outside the image
+__device__ __forceinline__ void window3x4(const float *__restrict__ xn, int H, int W, int ph, int pw, int oy0, int ox,
+                                          float (&win)[3][6]) {
+#pragma unroll
+    for (int i = 0; i < 6; i++) {
+        const int iy = oy0 - ph + i;
+        const bool rowok = iy >= 0 && iy < H;
+#pragma unroll
+        for (int kj = 0; kj < 3; kj++) {
+            const int ix = ox - pw + kj;
+            win[kj][i] = (rowok && ix >= 0 && ix < W) ? __ldg(xn + (int64_t)iy * W + ix) : 0.0f;
+        }
+    }
+}
+
+// y[n, o, oy0 + d, ox] = bias[o] + sum over taps k = (ki, kj) in order of w[o, k] * x (fused multiply-adds,
+// the order of the one-position kernel); item = (image, group of 4 rows, column)
+__global__ void __launch_bounds__(256) k_conv_direct3(nck_conv g, const float *__restrict__ x,
+                                                      const float *__restrict__ w, const float *__restrict__ b,
+                                                      float *__restrict__ y, FastDiv dow, FastDiv drg) {
+    __shared__ float ws[64 * 9];
+    const int OC = (int)g.OC, H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW;
+    const uint32_t RG = (uint32_t)(OH + 3) / 4, total = (uint32_t)g.N * RG * (uint32_t)OW;
+    for (int i = threadIdx.x; i < OC * 9; i += blockDim.x) ws[i] = w[i];
+    __syncthreads();
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * (uint32_t)OW, n = drg.div(r), oy0 = 4 * (r - n * RG);
+        float win[3][6];
+        window3x4(x + (int64_t)n * H * W, H, W, g.ph, g.pw, (int)oy0, (int)ox, win);
+        float *yo = y + ((int64_t)n * OC * OH + oy0) * OW + ox;
+        const int rows = OH - (int)oy0 < 4 ? OH - (int)oy0 : 4;
+        for (int o = 0; o < OC; o++) {
+            const float bv = b ? __ldg(b + o) : 0.0f;
+            float a[4] = {bv, bv, bv, bv};
+#pragma unroll
+            for (int ki = 0; ki < 3; ki++)
+#pragma unroll
+                for (int kj = 0; kj < 3; kj++) {
+                    const float wk = ws[o * 9 + ki * 3 + kj];
+#pragma unroll
+                    for (int d = 0; d < 4; d++) a[d] = fmaf(wk, win[kj][d + ki], a[d]);
+                }
+            float *yp = yo + (int64_t)o * OH * OW;
+#pragma unroll
+            for (int d = 0; d < 4; d++)
+                if (d < rows) yp[(int64_t)d * OW] = a[d];
+        }
+    }
+}
+
+static bool direct3_ok(const nck_conv *g) {
+    return g->G == 1 && g->C == 1 && g->KH == 3 && g->KW == 3 && g->sh == 1 && g->sw == 1 && g->dh == 1 &&
+           g->dw == 1 && g->OC <= 64 && g->N * ((g->OH + 3) / 4) * g->OW < ((int64_t)1 << 31);
+}
+
 extern "C" void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b,
                                     float *y) {
     int64_t L = g->OH * g->OW, CKK = (g->C / g->G) * g->KH * g->KW;
@@ -276,6 +335,13 @@ extern "C" void nck_conv_direct_fwd(nck_dev *d, const nck_conv *g, const float *
     int64_t bx = (g->N * L + kThreads - 1) / kThreads, cap = ((int64_t)d->sm_count * 8 + g->G - 1) / g->G;
     if (bx > cap) bx = cap;
     if (bx < 1) bx = 1;
+    if (direct3_ok(g)) {
+        const int64_t items = g->N * ((g->OH + 3) / 4) * g->OW;
+        k_conv_direct3<<<grid_for(d, items), kThreads, 0, NCK_STREAM(d)>>>(
+            *g, x, w, b, y, make_fastdiv((uint32_t)g->OW), make_fastdiv((uint32_t)((g->OH + 3) / 4)));
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     dim3 grid((unsigned)bx, (unsigned)g->G);
     if (CKK <= 9) k_conv_direct<9><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
     else if (CKK <= 16) k_conv_direct<16><<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
@@ -352,6 +418,88 @@ __global__ void k_direct_dw_combine(const float *__restrict__ part, int splits, 
     }
 }
 
+// The same weight gradient for the 3x3 one-channel case (the forward's fast-path conditions): a
+// block takes channels [o0, o0 + 4) and a slice of the (image, group of 4 rows, column) items; per
+// item the 6 x 3 window is loaded once and each channel's four dY values feed 36 fused multiply-adds
+// into its 9 accumulators. Warp shuffles and shared memory reduce to one partial per block;
+// k_direct_dw_combine adds the slices in order.
+__global__ void __launch_bounds__(256) k_direct3_dw_partial(nck_conv g, const float *__restrict__ x,
+                                                            const float *__restrict__ gy, float *__restrict__ part,
+                                                            uint32_t per_split, FastDiv dow, FastDiv drg) {
+    constexpr int OCW = 4;
+    __shared__ float red[8][OCW * 9];
+    const int OC = (int)g.OC, H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW, o0 = blockIdx.y * OCW;
+    float acc[OCW][9];
+#pragma unroll
+    for (int o = 0; o < OCW; o++)
+#pragma unroll
+        for (int k = 0; k < 9; k++) acc[o][k] = 0.0f;
+    const uint32_t RG = (uint32_t)(OH + 3) / 4, total = (uint32_t)g.N * RG * (uint32_t)OW, p0 = blockIdx.x * per_split;
+    const uint32_t p1 = p0 + per_split < total ? p0 + per_split : total;
+    for (uint32_t t = p0 + threadIdx.x; t < p1; t += blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * (uint32_t)OW, n = drg.div(r), oy0 = 4 * (r - n * RG);
+        float win[3][6];
+        window3x4(x + (int64_t)n * H * W, H, W, g.ph, g.pw, (int)oy0, (int)ox, win);
+        const int rows = OH - (int)oy0 < 4 ? OH - (int)oy0 : 4;
+        const float *gp = gy + ((int64_t)n * OC * OH + oy0) * OW + ox;
+#pragma unroll
+        for (int o = 0; o < OCW; o++) {
+            float gv[4];
+#pragma unroll
+            for (int d = 0; d < 4; d++)
+                gv[d] = (o0 + o < OC && d < rows) ? __ldg(gp + ((int64_t)(o0 + o) * OH + d) * OW) : 0.0f;
+#pragma unroll
+            for (int ki = 0; ki < 3; ki++)
+#pragma unroll
+                for (int kj = 0; kj < 3; kj++) {
+                    float a = acc[o][ki * 3 + kj];
+#pragma unroll
+                    for (int d = 0; d < 4; d++) a = fmaf(gv[d], win[kj][d + ki], a);
+                    acc[o][ki * 3 + kj] = a;
+                }
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 0; o < OCW; o++)
+#pragma unroll
+        for (int k = 0; k < 9; k++) {
+            float v = acc[o][k];
+            for (int sft = 16; sft; sft >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sft);
+            if (lane == 0) red[warp][o * 9 + k] = v;
+        }
+    __syncthreads();
+    for (int i = threadIdx.x; i < OCW * 9; i += blockDim.x) {
+        const int o = i / 9, k = i - o * 9;
+        if (o0 + o < OC) {
+            float v = red[0][i];
+            for (int wv = 1; wv < 8; wv++) v += red[wv][i];
+            part[((int64_t)blockIdx.x * OC + o0 + o) * 9 + k] = v;
+        }
+    }
+}
+
+static void direct3_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
+    const int64_t chunks = (g->OC + 3) / 4, wsz = g->OC * 9;
+    const int64_t total = g->N * ((g->OH + 3) / 4) * g->OW;
+    static int resident = 0;  // one full wave of blocks
+    if (!resident) resident = resident_blocks(d, k_direct3_dw_partial, kThreads);
+    int64_t splits = resident / chunks;
+    int64_t maxs = (int64_t)(d->scratch_bytes / sizeof(float)) / wsz;
+    if (splits > maxs) splits = maxs;
+    if (splits > (total + 255) / 256) splits = (total + 255) / 256;
+    if (splits < 1) splits = 1;
+    int64_t per = (total + splits - 1) / splits;
+    splits = (total + per - 1) / per;
+    float *part = (float *)d->scratch;
+    dim3 grid((unsigned)splits, (unsigned)chunks);
+    k_direct3_dw_partial<<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, gy, part, (uint32_t)per,
+                                                               make_fastdiv((uint32_t)g->OW),
+                                                               make_fastdiv((uint32_t)((g->OH + 3) / 4)));
+    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
+    NCK_LAUNCHED(d, 2);
+}
+
 template <int KT, int OCW>
 static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
     const int64_t OCg = g->OC / g->G, CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
@@ -377,7 +525,8 @@ extern "C" void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x
     if (g->N * L <= 0 || CKK <= 0) return;
     Scope sc(d, "conv_direct_dw", 2.0 * g->N * g->OC * L * CKK,
              4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L + 2 * g->OC * CKK));
-    if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
+    if (direct3_ok(g)) direct3_dw_launch(d, g, x, gy, gw);
+    else if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
     else if (CKK <= 16) direct_dw_launch<16, 4>(d, g, x, gy, gw);
     else direct_dw_launch<32, 2>(d, g, x, gy, gw);
 }

@@ -33,6 +33,14 @@ GEOMS = [
     ((2, 150, 5, 6), (20, 3, 3), (1, 1), (1, 1), (1, 1)),
     ((16, 32, 14, 14), (64, 3, 3), (1, 1), (1, 1), (1, 1)),
     ((5, 20, 10, 9), (12, 3, 2), (1, 2), (0, 1), (1, 1)),
+    # few taps (C * KH * KW <= 32): direct kernels, four positions per thread where the output width is
+    # a multiple of 4 and the stride 1, one position per thread otherwise
+    ((4, 1, 28, 28), (32, 3, 3), (1, 1), (1, 1), (1, 1)),
+    ((2, 1, 9, 10), (16, 3, 3), (1, 1), (1, 1), (2, 2)),
+    ((2, 1, 6, 8), (8, 1, 3), (1, 1), (0, 1), (1, 1)),
+    ((3, 1, 10, 14), (8, 3, 3), (1, 1), (2, 2), (2, 2)),
+    ((2, 1, 12, 12), (16, 3, 3), (1, 1), (0, 0), (1, 1)),
+    ((2, 3, 16, 16), (8, 3, 3), (2, 2), (1, 1), (1, 1)),
 ]
 
 
