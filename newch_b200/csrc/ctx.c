@@ -374,6 +374,8 @@ nc_ctx *nc_init(const nc_config *cfg) {
         const char *cv = getenv("NC_CONV");
         ctx->dev.conv_implicit = cv && !strcmp(cv, "implicit");
         ctx->dev.conv_tap = !cv || !strcmp(cv, "tap");
+        const char *gs = getenv("NC_GEMM_SMALL");
+        ctx->dev.gemm_small = !gs || strcmp(gs, "0") != 0;
     }
     cudaStream_t s;
     if (!nc__cuda_ok(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return ctx;

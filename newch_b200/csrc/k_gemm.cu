@@ -204,11 +204,61 @@ __global__ void k_sgemm_combine(GemmP p, int64_t nout) {
     }
 }
 
+// ---- small problems ---------------------------------------------------------------------------------
+//
+// Products with few outputs (at most 64k) and little work (at most 16M multiply-adds), where 128 x 128
+// tiles would leave most SMs idle: one thread per output when the reduction (K, times the batch when
+// it is summed) is short, else one warp per output with the lanes taking strided runs of it and a
+// fixed shuffle tree. Exact fp32 in every GEMM mode.
+
+__device__ __forceinline__ float op_a(const GemmP &p, int64_t b, int64_t m, int64_t k) {
+    return __ldg(p.A + b * p.sA + (p.ta ? k * p.lda + m : m * p.lda + k));
+}
+__device__ __forceinline__ float op_b(const GemmP &p, int64_t b, int64_t k, int64_t n) {
+    return __ldg(p.B + b * p.sB + (p.tb ? n * p.ldb + k : k * p.ldb + n));
+}
+
+// acc + the r-th product of output (ob, m, n), r over (batch when summed) x K, one fused multiply-add
+__device__ __forceinline__ float small_fma(const GemmP &p, int64_t ob, int64_t m, int64_t n, int64_t r, float acc) {
+    const int64_t b = p.reduce ? r / p.K : ob, k = p.reduce ? r - (r / p.K) * p.K : r;
+    return fmaf(op_a(p, p.sA ? b : 0, m, k), op_b(p, p.sB ? b : 0, k, n), acc);
+}
+
+__global__ void __launch_bounds__(256) k_sgemm_small_thread(GemmP p, int64_t nout) {
+    const int64_t MN = p.M * p.N, total = nout * MN, R = p.reduce ? p.batch * p.K : p.K;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t ob = t / MN, rm = t - ob * MN, m = rm / p.N, n = rm - m * p.N;
+        float acc = 0.0f;
+        for (int64_t r = 0; r < R; r++) acc = small_fma(p, ob, m, n, r, acc);
+        float *c = p.C + ob * p.sC + m * p.ldc + n;
+        *c = epi(p, acc, m, n, c);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_sgemm_small_warp(GemmP p, int64_t nout) {
+    const int lane = threadIdx.x & 31;
+    const int64_t MN = p.M * p.N, total = nout * MN, R = p.reduce ? p.batch * p.K : p.K;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; t < total; t += warps) {
+        const int64_t ob = t / MN, rm = t - ob * MN, m = rm / p.N, n = rm - m * p.N;
+        float acc = 0.0f;
+        for (int64_t r = lane; r < R; r += 32) acc = small_fma(p, ob, m, n, r, acc);
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            float *c = p.C + ob * p.sC + m * p.ldc + n;
+            *c = epi(p, acc, m, n, c);
+        }
+    }
+}
+
 }  // namespace
 
 extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (a->M <= 0 || a->N <= 0 || a->batch <= 0) return;
-    if (d->gemm_mode != NCK_GEMM_FFMA && nck_gemm_tc(d, a)) return;
+    const int64_t nout_s = a->reduce_batch && a->batch > 1 ? 1 : a->batch;
+    const bool small = d->gemm_small && a->M * a->N * nout_s <= ((int64_t)1 << 16) &&
+                       a->M * a->N * a->K * a->batch <= ((int64_t)1 << 24);
+    if (!small && d->gemm_mode != NCK_GEMM_FFMA && nck_gemm_tc(d, a)) return;
     double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
     double nC = (a->reduce_batch ? 1.0 : (double)a->batch) * (a->beta != 0.0f ? 2.0 : 1.0);
     Scope sc(d, "gemm_f32", 2.0 * a->M * a->N * a->K * a->batch,
@@ -224,6 +274,13 @@ extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     p.vecB = (a->ldb % 4 == 0) && (contB % 4 == 0) && (bstepB % 4 == 0) && (((uintptr_t)a->B & 15) == 0);
     p.vecC = a->N % 4 == 0;
 
+    if (small) {
+        const int64_t R = p.reduce ? a->batch * a->K : a->K, outs = nout_s * a->M * a->N;
+        if (R <= 64) k_sgemm_small_thread<<<grid_for(d, outs), 256, 0, NCK_STREAM(d)>>>(p, nout_s);
+        else k_sgemm_small_warp<<<grid_for(d, outs * 32), 256, 0, NCK_STREAM(d)>>>(p, nout_s);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     int64_t tiles = ((a->M + BM - 1) / BM) * ((a->N + BN - 1) / BN);
     int64_t nout = p.reduce ? 1 : a->batch;
     int64_t target = (int64_t)d->sm_count * 2;

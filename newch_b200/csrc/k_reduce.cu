@@ -225,9 +225,32 @@ __global__ void k_colsum_combine(const float *__restrict__ part, float *__restri
     }
 }
 
+// small matrices in one launch: a block of 32 warps takes 32 columns; warp w adds rows w, w + 32, ...
+// of each column, and the 32 warp sums are added in order
+__global__ void __launch_bounds__(1024) k_colsum_small(const float *__restrict__ x, float *__restrict__ gy, int64_t M,
+                                                        int64_t N) {
+    __shared__ float sm[32][33];
+    const int64_t n = blockIdx.x * 32 + threadIdx.x;
+    float acc = 0.0f;
+    if (n < N)
+        for (int64_t m = threadIdx.y; m < M; m += 32) acc += __ldg(x + m * N + n);
+    sm[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && n < N) {
+        float s = gy[n];
+        for (int k = 0; k < 32; k++) s += sm[k][threadIdx.x];
+        gy[n] = s;
+    }
+}
+
 extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return;
     Scope sc(d, "colsum");
+    if (M * N <= ((int64_t)1 << 20) && M <= ((int64_t)1 << 14)) {
+        k_colsum_small<<<(unsigned)((N + 31) / 32), dim3(32, 32), 0, NCK_STREAM(d)>>>(x, gy, M, N);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     int64_t col_blocks = (N + 31) / 32;
     int64_t want = (int64_t)d->sm_count * 4;
     int64_t splits = want / col_blocks;

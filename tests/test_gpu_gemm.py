@@ -23,6 +23,9 @@ GOLD = np.load(Path(__file__).resolve().parent / "golden" / "ops.npz")
 @pytest.fixture(params=["ffma", "tf32", "3xtf32"])
 def mode(request, monkeypatch):
     monkeypatch.setenv("NC_GEMM", request.param)
+    # small products would take the one-thread / one-warp-per-output kernels; these tests keep them on
+    # the tiled FFMA and tensor-core kernels (test_small_products covers the small path)
+    monkeypatch.setenv("NC_GEMM_SMALL", "0")
     return request.param
 
 
@@ -91,3 +94,61 @@ def test_conv_weight_grad_batch_reduction_large(mode):
     # tensor-memory accumulator (fp32 additions that are not round-to-nearest), ~1e-5 normwise
     tol = 4e-5 if mode == "3xtf32" else TOL[mode]
     assert rel_err(dw, dw_ref) < tol
+
+
+@pytest.mark.parametrize("M,N,K", [(10, 128, 512), (512, 10, 128), (512, 128, 10), (8, 8, 8192), (1, 1, 1),
+                                   (37, 19, 70), (64, 196, 288)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_small_products(mode, monkeypatch, M, N, K, ta, tb):
+    """Products with at most 64k outputs and 16M multiply-adds take the small kernels (one thread per
+    output for a reduction of at most 64, else one warp per output), exact fp32 in every mode: the
+    FFMA tolerance applies whatever NC_GEMM says. Forward and both gradients (dA, dB are small too)."""
+    monkeypatch.setenv("NC_GEMM_SMALL", "1")
+    A = seeded(M * 7 + K, (K, M) if ta else (M, K))
+    B = seeded(N * 13 + K, (N, K) if tb else (K, N))
+    G = seeded(5, (M, N))
+    with engine(mode) as e:
+        a, b = e.param(A), e.param(B)
+        at = e.check(e.L.nc_transpose(a, 0, 1)) if ta else a
+        bt = e.check(e.L.nc_transpose(b, 0, 1)) if tb else b
+        y = e.check(e.L.nc_matmul(at, bt))
+        out = e.np(y)
+        e.backward_with(y, G)
+        da, db = e.grad(a), e.grad(b)
+    A64, B64, G64 = (x.astype(np.float64) for x in (A, B, G))
+    Am, Bm = (A64.T if ta else A64), (B64.T if tb else B64)
+    assert rel_err(out, Am @ Bm) < 1e-5
+    dAm, dBm = G64 @ Bm.T, Am.T @ G64
+    assert rel_err(da, dAm.T if ta else dAm) < 1e-5
+    assert rel_err(db, dBm.T if tb else dBm) < 1e-5
+
+
+def test_small_linear_bias_and_batch_sum():
+    """The small kernels' epilogue (bias, accumulation into an existing gradient) through Linear, and the
+    batch-summed reduction through a small convolution weight gradient."""
+    import ncoracle as O
+
+    X, W, Bv = seeded(1, (64, 40)), seeded(2, (10, 40), 0.2), seeded(3, (10,))
+    with Eng("b200") as e:
+        x, w, b = e.param(X), e.param(W), e.param(Bv)
+        y = e.check(e.L.nc_linear_fn(x, w, b))
+        out = e.np(y)
+        G = seeded(4, out.shape)
+        for _ in range(2):  # the second backward adds into the gradients
+            y = e.check(e.L.nc_linear_fn(x, w, b))
+            e.backward_with(y, G)
+        dx, dw, db = e.grad(x), e.grad(w), e.grad(b)
+    X64, W64, G64 = (v.astype(np.float64) for v in (X, W, G))
+    assert rel_err(out, X64 @ W64.T + Bv) < 1e-5
+    assert rel_err(dx, 2 * G64 @ W64) < 1e-5
+    assert rel_err(dw, 2 * G64.T @ X64) < 1e-5
+    assert rel_err(db, 2 * G64.sum(0)) < 1e-5
+    Xc, Wc = seeded(5, (6, 3, 5, 5)), seeded(6, (4, 3, 1, 1), 0.3)
+    with Eng("b200") as e:
+        x, w = e.param(Xc), e.param(Wc)
+        y = e.check(e.L.nc_conv2d(x, w, None, 1, 1, 0, 0))
+        Gc = seeded(7, e.shape(y))
+        e.backward_with(y, Gc)
+        dwc = e.grad(w)
+    _, dw_ref, _ = O.conv2d_grads(Xc, Wc, Gc)
+    assert rel_err(dwc, dw_ref) < 1e-5
