@@ -406,15 +406,20 @@ __global__ void __launch_bounds__(128) k_direct_dw_partial(nck_conv g, const flo
     }
 }
 
-// one warp per weight: lanes add strided runs of the slices, then a fixed shuffle tree
-__global__ void k_direct_dw_combine(const float *__restrict__ part, int splits, int64_t n, float *__restrict__ gw) {
+// one warp per output: lanes add strided runs of the slices, then a fixed shuffle tree; outputs from n0
+// on go to the second array (the bias, when the partials carry it)
+__global__ void k_direct_dw_combine(const float *__restrict__ part, int splits, int64_t n, float *__restrict__ gw,
+                                    int64_t n0, float *__restrict__ gb) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; i < n; i += warps) {
         float s = 0.0f;
         for (int k = lane; k < splits; k += 32) s += __ldg(part + k * n + i);
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) gw[i] += s;
+        if (lane == 0) {
+            if (i < n0) gw[i] += s;
+            else if (gb) gb[i - n0] += s;
+        }
     }
 }
 
@@ -427,13 +432,13 @@ __global__ void __launch_bounds__(256) k_direct3_dw_partial(nck_conv g, const fl
                                                             const float *__restrict__ gy, float *__restrict__ part,
                                                             uint32_t per_split, FastDiv dow, FastDiv drg) {
     constexpr int OCW = 4;
-    __shared__ float red[8][OCW * 9];
+    __shared__ float red[8][OCW * 10];
     const int OC = (int)g.OC, H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW, o0 = blockIdx.y * OCW;
-    float acc[OCW][9];
+    float acc[OCW][10];  // 9 taps, then the bias (the sum of dY)
 #pragma unroll
     for (int o = 0; o < OCW; o++)
 #pragma unroll
-        for (int k = 0; k < 9; k++) acc[o][k] = 0.0f;
+        for (int k = 0; k < 10; k++) acc[o][k] = 0.0f;
     const uint32_t RG = (uint32_t)(OH + 3) / 4, total = (uint32_t)g.N * RG * (uint32_t)OW, p0 = blockIdx.x * per_split;
     const uint32_t p1 = p0 + per_split < total ? p0 + per_split : total;
     for (uint32_t t = p0 + threadIdx.x; t < p1; t += blockDim.x) {
@@ -457,30 +462,33 @@ __global__ void __launch_bounds__(256) k_direct3_dw_partial(nck_conv g, const fl
                     for (int d = 0; d < 4; d++) a = fmaf(gv[d], win[kj][d + ki], a);
                     acc[o][ki * 3 + kj] = a;
                 }
+            acc[o][9] += (gv[0] + gv[1]) + (gv[2] + gv[3]);
         }
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 0; o < OCW; o++)
 #pragma unroll
-        for (int k = 0; k < 9; k++) {
+        for (int k = 0; k < 10; k++) {
             float v = acc[o][k];
             for (int sft = 16; sft; sft >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sft);
-            if (lane == 0) red[warp][o * 9 + k] = v;
+            if (lane == 0) red[warp][o * 10 + k] = v;
         }
     __syncthreads();
-    for (int i = threadIdx.x; i < OCW * 9; i += blockDim.x) {
-        const int o = i / 9, k = i - o * 9;
+    // partials [block][OC * 9 weights | OC biases]
+    for (int i = threadIdx.x; i < OCW * 10; i += blockDim.x) {
+        const int o = i / 10, k = i - o * 10;
         if (o0 + o < OC) {
             float v = red[0][i];
             for (int wv = 1; wv < 8; wv++) v += red[wv][i];
-            part[((int64_t)blockIdx.x * OC + o0 + o) * 9 + k] = v;
+            const int64_t row = (int64_t)blockIdx.x * OC * 10;
+            part[row + (k < 9 ? (int64_t)(o0 + o) * 9 + k : (int64_t)OC * 9 + o0 + o)] = v;
         }
     }
 }
 
-static void direct3_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
-    const int64_t chunks = (g->OC + 3) / 4, wsz = g->OC * 9;
+static void direct3_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb) {
+    const int64_t chunks = (g->OC + 3) / 4, wsz = g->OC * 10;
     const int64_t total = g->N * ((g->OH + 3) / 4) * g->OW;
     static int resident = 0;  // one full wave of blocks
     if (!resident) resident = resident_blocks(d, k_direct3_dw_partial, kThreads);
@@ -496,7 +504,8 @@ static void direct3_dw_launch(nck_dev *d, const nck_conv *g, const float *x, con
     k_direct3_dw_partial<<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, gy, part, (uint32_t)per,
                                                                make_fastdiv((uint32_t)g->OW),
                                                                make_fastdiv((uint32_t)((g->OH + 3) / 4)));
-    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
+    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw,
+                                                                               g->OC * 9, gb);
     NCK_LAUNCHED(d, 2);
 }
 
@@ -516,19 +525,27 @@ static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, cons
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)splits, (unsigned)(g->G * chunks));
     k_direct_dw_partial<KT, OCW><<<grid, 128, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
-    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw);
+    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw, wsz,
+                                                                               nullptr);
     NCK_LAUNCHED(d, 2);
 }
 
-extern "C" void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
+extern "C" int nck_conv_direct3_ok(const nck_conv *g) { return direct3_ok(g); }
+
+extern "C" int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw,
+                                  float *gb) {
     int64_t CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
-    if (g->N * L <= 0 || CKK <= 0) return;
+    if (g->N * L <= 0 || CKK <= 0) return 0;
     Scope sc(d, "conv_direct_dw", 2.0 * g->N * g->OC * L * CKK,
              4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L + 2 * g->OC * CKK));
-    if (direct3_ok(g)) direct3_dw_launch(d, g, x, gy, gw);
-    else if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
+    if (direct3_ok(g)) {
+        direct3_dw_launch(d, g, x, gy, gw, gb);
+        return gb != nullptr;
+    }
+    if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
     else if (CKK <= 16) direct_dw_launch<16, 4>(d, g, x, gy, gw);
     else direct_dw_launch<32, 2>(d, g, x, gy, gw);
+    return 0;
 }
 
 // ---- depthwise (groups == C == OC) ---------------------------------------------------------------

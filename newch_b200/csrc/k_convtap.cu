@@ -340,8 +340,10 @@ __global__ void k_tap_dw_combine(const float *__restrict__ part, float *__restri
 // image coordinates are divided out once.
 __global__ void __launch_bounds__(256) k_tap_pack(const float *__restrict__ src, float *__restrict__ dst,
                                                   float *__restrict__ rest, int64_t Nv, int C, int Kp, int Hs,
-                                                  int Ws, FastDiv dimg, FastDiv drow, int eh, int ew) {
+                                                  int Ws, FastDiv dimg, FastDiv drow, int eh, int ew,
+                                                  float *__restrict__ csum) {
     __shared__ float tile[128][33];
+    __shared__ float red[8][32];
     const int64_t v0 = blockIdx.x * 128ll;
     const int k0 = blockIdx.y * 32;
     const int64_t plane = (int64_t)Hs * Ws, img = (int64_t)C * plane;
@@ -359,6 +361,20 @@ __global__ void __launch_bounds__(256) k_tap_pack(const float *__restrict__ src,
         for (int k = kb; k < 32; k += 2) tile[r][k] = (s && k0 + k < C) ? __ldg(s + (k0 + k) * plane) : 0.0f;
     }
     __syncthreads();
+    if (csum) {
+        // this block's sum of each of its 32 columns (rows in a fixed order: 16 per warp, then 8 warps)
+        const int k = threadIdx.x & 31, wv = threadIdx.x >> 5;
+        float a = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 16; r++) a += tile[wv * 16 + r][k];
+        red[wv][k] = a;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float t = red[0][threadIdx.x];
+            for (int j = 1; j < 8; j++) t += red[j][threadIdx.x];
+            csum[(int64_t)blockIdx.x * Kp + k0 + threadIdx.x] = t;
+        }
+    }
     for (int e = threadIdx.x; e < 8 * 128; e += blockDim.x) {
         const int q = e & 7, r = e >> 3;  // 16-byte quarter q of row r
         const int64_t v = v0 + r;
@@ -366,6 +382,20 @@ __global__ void __launch_bounds__(256) k_tap_pack(const float *__restrict__ src,
         const float4 x = make_float4(tile[r][4 * q], tile[r][4 * q + 1], tile[r][4 * q + 2], tile[r][4 * q + 3]);
         *reinterpret_cast<float4 *>(dst + v * Kp + k0 + 4 * q) = x;
         if (rest) *reinterpret_cast<float4 *>(rest + v * Kp + k0 + 4 * q) = tf32_rest4(x);
+    }
+}
+
+// gb[c] += the sum over pack blocks of their column-c sums: one warp per channel, lanes take strided
+// runs of the blocks, then a fixed shuffle tree
+__global__ void k_tap_colsum_combine(const float *__restrict__ csum, int64_t blocks, int Kp, int C,
+                                     float *__restrict__ gb) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t c = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; c < C; c += warps) {
+        float a = 0.0f;
+        for (int64_t b = lane; b < blocks; b += 32) a += __ldcg(csum + b * Kp + c);
+        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) gb[c] += a;
     }
 }
 
@@ -442,15 +472,27 @@ extern "C" int nck_convtap_plan(const nck_dev *d, const nck_conv *g, nck_tapgeom
 }
 
 extern "C" void nck_tap_pack(nck_dev *d, const float *src, int64_t N, int64_t C, int64_t Hs, int64_t Ws,
-                             const nck_tapgeom *t, int eh, int ew, int64_t Kp, float *dst) {
+                             const nck_tapgeom *t, int eh, int ew, int64_t Kp, float *dst, float *colsum) {
     if (t->Nv <= 0) return;
     Scope sc(d, "conv_tap_pack", 0.0, 4.0 * (N * C * Hs * Ws + (double)t->planes * t->Nv * Kp));
-    dim3 grid((unsigned)((t->Nv + 127) / 128), (unsigned)(Kp / 32));
+    const int64_t blocks = (t->Nv + 127) / 128;
+    dim3 grid((unsigned)blocks, (unsigned)(Kp / 32));
     float *rest = t->planes == 2 ? dst + t->Nv * Kp : nullptr;
+    // per-block column sums go to scratch, consumed by the combine right behind (stream order)
+    float *csum = colsum && (size_t)(blocks * Kp) * sizeof(float) <= d->scratch_bytes ? (float *)d->scratch : nullptr;
     k_tap_pack<<<grid, 256, 0, NCK_STREAM(d)>>>(src, dst, rest, t->Nv, (int)C, (int)Kp, (int)Hs, (int)Ws,
                                                  make_fastdiv((uint32_t)(t->Hp * t->Wp)),
-                                                 make_fastdiv((uint32_t)t->Wp), eh, ew);
-    NCK_LAUNCHED(d, 1);
+                                                 make_fastdiv((uint32_t)t->Wp), eh, ew, csum);
+    int n = 1;
+    if (csum) {
+        k_tap_colsum_combine<<<grid_for(d, C * 32), kThreads, 0, NCK_STREAM(d)>>>(csum, blocks, (int)Kp, (int)C, colsum);
+        n++;
+    }
+    NCK_LAUNCHED(d, n);
+}
+
+extern "C" int nck_tap_pack_colsum_ok(const nck_dev *d, const nck_tapgeom *t, int64_t Kp) {
+    return (size_t)(((t->Nv + 127) / 128) * Kp) * sizeof(float) <= d->scratch_bytes;
 }
 
 extern "C" void nck_tap_pack_w(nck_dev *d, const nck_conv *g, const nck_tapgeom *t, const float *w, float *dst,

@@ -198,9 +198,12 @@ typedef struct {
 } nck_tapgeom;
 /* 1 when the convolution takes the tap-shifted path; fills *t */
 int nck_convtap_plan(const nck_dev *d, const nck_conv *g, nck_tapgeom *t);
-/* dst[v][k] (Kp columns) from src [N][C][Hs][Ws] placed at padded offset (eh, ew), zero elsewhere */
+/* dst[v][k] (Kp columns) from src [N][C][Hs][Ws] placed at padded offset (eh, ew), zero elsewhere;
+ * colsum (optional): colsum[c] += the sum of channel c of src, computed from the same pass */
 void nck_tap_pack(nck_dev *d, const float *src, int64_t N, int64_t C, int64_t Hs, int64_t Ws, const nck_tapgeom *t,
-                  int eh, int ew, int64_t Kp, float *dst);
+                  int eh, int ew, int64_t Kp, float *dst, float *colsum);
+/* whether nck_tap_pack can add the channel sums (its per-block sums fit the scratch) */
+int nck_tap_pack_colsum_ok(const nck_dev *d, const nck_tapgeom *t, int64_t Kp);
 /* weights for the forward, [OC][T][Cp] (tr 0), or for dX, [C][T][OCp] (tr 1) */
 void nck_tap_pack_w(nck_dev *d, const nck_conv *g, const nck_tapgeom *t, const float *w, float *dst, int tr);
 /* mode 0: y = conv(x) + bias (P = packed x, Q = forward weights); 1: gx (+)= conv-transpose(gy)
@@ -209,7 +212,11 @@ void nck_tap_pack_w(nck_dev *d, const nck_conv *g, const nck_tapgeom *t, const f
 int nck_convtap(nck_dev *d, int mode, const nck_conv *g, const nck_tapgeom *t, const float *P, const float *Q,
                 float *out, const float *bias, int acc);
 /* gw[oc, k] += sum over n, l of gy[n, oc, l] * x-tap k at l (same eligibility as the direct forward) */
-void nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw);
+/* gb (optional): when the 3x3 one-channel kernel runs, gb[oc] += sum of gy[:, oc] from the same pass
+ * and 1 is returned; otherwise gb is left alone and 0 is returned */
+int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
+/* whether nck_conv_direct_dw takes the 3x3 one-channel kernel (and can add the bias gradient) */
+int nck_conv_direct3_ok(const nck_conv *g);
 void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
 void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx);
 #define NCK_DW_MAX_TAPS 25 /* nck_dw_dw handles kernels up to 5x5 */

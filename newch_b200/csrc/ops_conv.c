@@ -162,7 +162,7 @@ static nc_status conv_fwd(nc_node *n) {
         float *xp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.Cp * tg.planes) * sizeof(float));
         float *wp = (float *)nc__arena_alloc(ctx, (size_t)(g.OC * tg.T * tg.Cp * tg.planes) * sizeof(float));
         if (!sv || !xp || !wp) return NC_ERR_OOM;
-        nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp);
+        nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp, NULL);
         nck_tap_pack_w(nc__k(ctx), &g, &tg, Wt, wp, 0);
         if (nck_convtap(nc__k(ctx), 0, &g, &tg, xp, wp, Y, B, 0)) {
             sv->kind = SAVED_TAP, sv->buf = xp;
@@ -241,7 +241,15 @@ static void conv_bwd(nc_node *n) {
     nc_tensor *gb = b && nc__needs_grad(b) ? nc__grad_buf(b) : NULL;
     int64_t L = g.OH * g.OW, HW = g.H * g.W;
     if (!g.N) return;
-    if (gb) nck_conv_bias_grad(nc__k(ctx), G, (float *)gb->data, g.N, g.OC, L);
+    /* the bias gradient (channel sums of dY) rides along with a pass that reads all of dY anyway: the
+     * direct 3x3 weight gradient, or the packing of dY for the tap-shifted path; else its own pass */
+    nck_tapgeom tg;
+    const int direct_dw = gw && use_direct(&g) && !is_depthwise(&g);
+    const int tap = !is_depthwise(&g) && !is_pointwise(&g) && ((gw && !direct_dw) || gx) &&
+                    nck_convtap_plan(nc__k(ctx), &g, &tg);
+    float *gb_direct = gb && direct_dw && nck_conv_direct3_ok(&g) ? (float *)gb->data : NULL;
+    float *gb_tap = gb && !gb_direct && tap && nck_tap_pack_colsum_ok(nc__k(ctx), &tg, tg.OCp) ? (float *)gb->data : NULL;
+    if (gb && !gb_direct && !gb_tap) nck_conv_bias_grad(nc__k(ctx), G, (float *)gb->data, g.N, g.OC, L);
     if (is_depthwise(&g)) {
         if (gx) {
             zero_if_fresh(ctx, gx, &acc_gx);
@@ -256,24 +264,23 @@ static void conv_bwd(nc_node *n) {
     }
     if (gw && use_direct(&g)) {
         /* few taps per group: dW straight from x and dY, no unfolded copy */
-        nck_conv_direct_dw(nc__k(ctx), &g, X, G, (float *)gw->data);
+        nck_conv_direct_dw(nc__k(ctx), &g, X, G, (float *)gw->data, gb_direct);
         gw = NULL;
         if (!gx) return;
     }
     const conv_saved *sv = (const conv_saved *)n->saved;
-    nck_tapgeom tg;
-    if ((gw || gx) && !is_pointwise(&g) && nck_convtap_plan(nc__k(ctx), &g, &tg)) {
+    if (tap) {
         /* dY packed once on the padded grid of x; dW against the packed x the forward left, dX from
          * the shifted dY rows */
         float *gp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.OCp * tg.planes) * sizeof(float));
         if (!gp) return;
-        nck_tap_pack(nc__k(ctx), G, g.N, g.OC, g.OH, g.OW, &tg, 0, 0, tg.OCp, gp);
+        nck_tap_pack(nc__k(ctx), G, g.N, g.OC, g.OH, g.OW, &tg, 0, 0, tg.OCp, gp, gb_tap);
         if (gw) {
             float *xp = sv && sv->kind == SAVED_TAP ? sv->buf : NULL;
             if (!xp) {
                 xp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.Cp * tg.planes) * sizeof(float));
                 if (!xp) return;
-                nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp);
+                nck_tap_pack(nc__k(ctx), X, g.N, g.C, g.H, g.W, &tg, g.ph, g.pw, tg.Cp, xp, NULL);
             }
             if (nck_convtap(nc__k(ctx), 2, &g, &tg, xp, gp, (float *)gw->data, NULL, 1)) gw = NULL;
         }
