@@ -376,6 +376,8 @@ nc_ctx *nc_init(const nc_config *cfg) {
         ctx->dev.conv_tap = !cv || !strcmp(cv, "tap");
         const char *gs = getenv("NC_GEMM_SMALL");
         ctx->dev.gemm_small = !gs || strcmp(gs, "0") != 0;
+        const char *qg = getenv("NC_QGEMM");
+        ctx->dev.qgemm_tc = !qg || strcmp(qg, "dp4a") != 0;
     }
     cudaStream_t s;
     if (!nc__cuda_ok(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return ctx;

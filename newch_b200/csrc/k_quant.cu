@@ -6,7 +6,10 @@
 // compiled without FMA contraction, so the rescale rounds as newch's.
 #include <math.h>
 
+#include <string.h>
+
 #include "k_common.cuh"
+#include "k_tcgen05.cuh"
 
 using namespace nck;
 
@@ -113,10 +116,195 @@ __global__ void __launch_bounds__(256) k_qgemm(const int8_t *__restrict__ A, con
 }
 }  // namespace
 
+// ---- int8 GEMM on the tensor cores (tcgen05.mma kind::i8) ------------------------------------------------
+//
+// acc[m, n] = sum_k xq[m, k] * wq[n, k] exactly in int32 (the tensor core adds integer products without
+// rounding), then y[m, n] = (float)acc * xs[m] * ws[n] + b[n] as above. Weight rows n run on the 128
+// TMEM lanes and activation rows m along the accumulator's BN columns, so each epilogue warp store
+// writes 32 consecutive outputs of one row. Persistent CTAs, one per SM: warps 0-3 epilogue, warp 4
+// TMA loader (K in steps of 128 bytes, 128-byte swizzle, no multicast), warp 5 MMA issuer (4 MMAs of
+// K = 32 per stage); two TMEM accumulators. Every mbarrier wait is bounded and a timeout is reported
+// through the status word, after which the CTA drains its copies and MMAs and frees its TMEM.
+namespace {
+using namespace tc;
+
+constexpr int kQBN = 128, kQStageP = TM * 128, kQThreads = 6 * 32;  // stage bytes of the weight tile
+
+struct QtcParams {
+    int64_t M, N, K;
+    int64_t tiles_p, tiles_q, units;
+    int stages;
+    const float *xs, *ws, *bias;
+    float *y;
+    int32_t *acc_out;
+    int *status;
+};
+
+struct QBars {
+    uint64_t full[kMaxStages], empty[kMaxStages];
+    uint64_t tfull[2], tempty[2], mma_done;
+    uint32_t tmem;
+};
+
+__global__ void __launch_bounds__(kQThreads, 1) k_qgemm_tc(const __grid_constant__ CUtensorMap tmW,
+                                                           const __grid_constant__ CUtensorMap tmX, QtcParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                            ~(uintptr_t)1023);
+    QBars &s = *reinterpret_cast<QBars *>(base);
+    const int S = p.stages;
+    unsigned char *const ring_p = base + 1024;
+    unsigned char *const ring_q = ring_p + S * kQStageP;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t tcols = tmem_cols(kQBN), stage_bytes = (uint32_t)(TM + kQBN) * 128;
+    const int64_t ksteps = (p.K + 127) / 128;
+
+    if (tid == 0) {
+        for (int i = 0; i < S; i++) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s.tfull[i], 1);
+            mbar_init(&s.tempty[i], 4);
+        }
+        mbar_init(&s.mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem)),
+                     "r"(tcols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = s.tmem;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            int64_t it = 0;
+            int st = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                // the activation tiles of one weight tile are neighbours: the weight tile stays in L2
+                const int p0 = (int)((u / p.tiles_q) * TM), q0 = (int)((u % p.tiles_q) * kQBN);
+                for (int64_t t = 0; t < ksteps; t++, it++) {
+                    if (it >= S && !(ok = mbar_wait(&s.empty[st], ph ^ 1, p.status))) break;
+                    mbar_expect_tx(&s.full[st], stage_bytes);
+                    tma_2d(ring_p + st * kQStageP, &tmW, (int)(t * 128), p0, &s.full[st]);
+                    tma_2d(ring_q + st * (kQBN * 128), &tmX, (int)(t * 128), q0, &s.full[st]);
+                    if (++st == S) st = 0, ph ^= 1;
+                }
+            }
+            int64_t first = it > S ? it - S : 0;
+            for (int64_t j = first; j < it; j++)
+                if (!mbar_wait(&s.full[j % S], (uint32_t)((j / S) & 1), p.status)) break;
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_s8(kQBN);
+            const uint64_t dA = stage_desc(smem_u32(ring_p), 0, 0), dB = stage_desc(smem_u32(ring_q), 0, 0);
+            const uint32_t stA = (uint32_t)kQStageP >> 4, stB = (uint32_t)(kQBN * 128) >> 4;
+            int64_t local = 0;
+            int st = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, local++) {
+                const int acc = (int)(local & 1);
+                if (local >= 2 && !(ok = mbar_wait(&s.tempty[acc], (uint32_t)(((local >> 1) & 1) ^ 1), p.status)))
+                    break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t d = tmem + (uint32_t)acc * (tcols / 2);
+                for (int64_t t = 0; t < ksteps; t++) {
+                    if (!(ok = mbar_wait(&s.full[st], ph, p.status))) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint64_t a0 = dA + (uint64_t)(st * stA), b0 = dB + (uint64_t)(st * stB);
+#pragma unroll
+                    for (int k = 0; k < 4; k++)  // K = 32 bytes per MMA: 2 descriptor units
+                        mma_s8(d, a0 + (uint64_t)(k * 2), b0 + (uint64_t)(k * 2), idesc, (t > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(&s.empty[st]);
+                    if (++st == S) st = 0, ph ^= 1;
+                }
+                if (ok) mma_commit(&s.tfull[acc]);
+            }
+            mma_commit(&s.mma_done);
+            mbar_wait(&s.mma_done, 0, p.status);
+        }
+    } else if (warp < 4) {
+        int64_t local = 0;
+        for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x, local++) {
+            const int64_t p0 = (u / p.tiles_q) * TM, q0 = (u % p.tiles_q) * kQBN;
+            const int acc = (int)(local & 1);
+            if (!mbar_wait(&s.tfull[acc], (uint32_t)((local >> 1) & 1), p.status)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int64_t n = p0 + warp * 32 + lane;
+            const bool live = n < p.N;
+            const float wsn = live ? p.ws[n] : 0.0f, bn = (live && p.bias) ? p.bias[n] : 0.0f;
+            for (int c0 = 0; c0 < kQBN; c0 += 16) {
+                uint32_t r[16];
+                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)acc * (tcols / 2) + (uint32_t)c0, r);
+                if (!live) continue;
+#pragma unroll
+                for (int jj = 0; jj < 16; jj++) {
+                    const int64_t m = q0 + c0 + jj;
+                    if (m < p.M) {
+                        const int32_t a = (int32_t)r[jj];
+                        if (p.acc_out) p.acc_out[m * p.N + n] = a;
+                        p.y[m * p.N + n] = (float)a * p.xs[m] * wsn + bn;
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.tempty[acc]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
+}
+
+// 1 when launched on the tensor cores; 0 when the operands do not fit TMA (K not a multiple of 16
+// bytes, unaligned bases) or the product is tiny, and the dp4a kernel is used
+int qgemm_tc(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, const float *b,
+             float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out) {
+    if (!d->qgemm_tc || K % 16 || (((uintptr_t)xq | (uintptr_t)wq) & 15) || M * N < 4096 || M >= ((int64_t)1 << 31) ||
+        N >= ((int64_t)1 << 31) || K >= ((int64_t)1 << 31))
+        return 0;
+    CUtensorMap mw, mx;
+    if (!make_map_u8(&mw, wq, K, N, K, 128, TM) || !make_map_u8(&mx, xq, K, M, K, 128, kQBN)) return 0;
+    static int attr = 0;
+    if (!attr) {
+        if (cudaFuncSetAttribute(k_qgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        attr = 1;
+    }
+    QtcParams p;
+    memset(&p, 0, sizeof p);
+    p.M = M, p.N = N, p.K = K, p.xs = xs, p.ws = ws, p.bias = b, p.y = y, p.acc_out = acc_out, p.status = d->status;
+    p.tiles_p = (N + TM - 1) / TM, p.tiles_q = (M + kQBN - 1) / kQBN, p.units = p.tiles_p * p.tiles_q;
+    const size_t per = (size_t)(TM + kQBN) * 128;
+    size_t nst = (kSmemLimit - 2048) / per;
+    p.stages = (int)(nst > (size_t)kMaxStages ? kMaxStages : nst);
+    const size_t smem = 2048 + (size_t)p.stages * per;
+    const int64_t sms = d->sm_count > 0 ? d->sm_count : 148;
+    const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
+    k_qgemm_tc<<<grid, kQThreads, smem, NCK_STREAM(d)>>>(mw, mx, p);
+    if (cudaGetLastError() != cudaSuccess) *(volatile int *)d->status_host = NCK_ERR_LAUNCH;
+    NCK_LAUNCHED(d, 1);
+    return 1;
+}
+}  // namespace
+
 extern "C" void nck_qlinear(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
                             const float *b, float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out) {
     if (M <= 0 || N <= 0) return;
     Scope sc(d, "qgemm_i8", 2.0 * M * N * K, (double)M * K + (double)N * K + 4.0 * M * N);
+    if (qgemm_tc(d, xq, xs, wq, ws, b, y, M, N, K, acc_out)) return;
     int vec = K % 16 == 0 && (((uintptr_t)xq | (uintptr_t)wq) & 15) == 0;
     dim3 grid((unsigned)((N + QBN - 1) / QBN), (unsigned)((M + QBM - 1) / QBM));
     k_qgemm<<<grid, 256, 0, NCK_STREAM(d)>>>(xq, wq, xs, ws, b, y, acc_out, M, N, K, vec);

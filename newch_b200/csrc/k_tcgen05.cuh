@@ -184,6 +184,25 @@ __device__ __forceinline__ void tmem_regs_after_wait(uint32_t (&r)[16]) {
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
 }
 
+// instruction descriptor: D s32, A/B signed int8, K-major, M = 128, N = bn (kind::i8)
+__device__ __forceinline__ uint32_t idesc_s8(int bn) {
+    uint32_t d = 0;
+    d |= 2u << 4;   // D format S32
+    d |= 1u << 7;   // A signed 8-bit
+    d |= 1u << 10;  // B signed 8-bit
+    d |= (uint32_t)(bn >> 3) << 17;
+    d |= (uint32_t)(TM >> 4) << 24;
+    return d;
+}
+
+__device__ __forceinline__ void mma_s8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
 // ---- host side: TMA tensor maps ------------------------------------------------------------------
 
 typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -219,6 +238,21 @@ inline bool make_map(CUtensorMap *map, const float *base, int64_t inner, int64_t
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// byte matrix (int8 / uint8) view: rows of `inner` bytes, `ld` bytes apart; 128-byte swizzle
+inline bool make_map_u8(CUtensorMap *map, const void *base, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+                        int box_outer) {
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

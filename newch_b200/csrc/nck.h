@@ -28,6 +28,7 @@ typedef struct nck_dev {
     int conv_implicit; /* 1: convolutions try the implicit-GEMM kernels before unfolding (NC_CONV=implicit) */
     int conv_tap;      /* 1: stride-1 convolutions run as tap-shifted GEMMs (default; NC_CONV=unfolded|implicit: 0) */
     int gemm_small;    /* 1: small products take the one-thread / one-warp-per-output kernels (NC_GEMM_SMALL=0: off) */
+    int qgemm_tc;      /* 1: int8 GEMMs on tcgen05 kind::i8 where TMA allows (NC_QGEMM=dp4a: CUDA cores) */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
     unsigned *counters; /* device counters for last-block-finishes reductions; each user leaves it at 0 */

@@ -228,6 +228,27 @@ def test_int8_layer_bit_exact_against_reference():
     assert np.array_equal(outs[0][2], yo)
 
 
+@pytest.mark.parametrize("path", ["tc", "dp4a"])
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 1024), (300, 200, 1040), (129, 130, 256), (64, 64, 64), (40, 700, 96)])
+def test_int8_gemm_paths_bit_exact(path, M, N, K, monkeypatch):
+    """The int8 GEMM on tcgen05 (kind::i8, exact int32 accumulation; K in 128-byte steps with the TMA's
+    zero fill past K) and on dp4a: quantization, outputs and the rescale equal the reference's bit for
+    bit. Shapes: cfg5-like, ragged M / N / K tails, one partial K step."""
+    monkeypatch.setenv("NC_QGEMM", path)
+    w, x, b = seeded(30, (N, K), 0.2), seeded(31, (M, K)), seeded(32, (N,))
+    outs = []
+    for which in ("b200", "ref"):
+        with Eng(which) as e:
+            sp = capi.ptr_array([None])
+            q = e.check(e.L.nc_quantize_rows(e.t(w), sp))
+            y = e.check(e.L.nc_linear_int8(e.t(x), q, sp[0], e.t(b)))
+            outs.append((e.np(q), e.np(sp[0]), e.np(y)))
+    for a, r in zip(*outs):
+        assert np.array_equal(a, r)
+    yo, _, _, _ = O.linear_int8(x, outs[1][0], outs[1][1], b)
+    assert np.array_equal(outs[0][2], yo)
+
+
 @pytest.mark.parametrize("jump", ["poly", "matrix"])
 @pytest.mark.parametrize("n", [1, 31, 16384, 16385, 100000, 1 << 20])
 def test_dropout_masks_match_reference_stream(n, jump, monkeypatch):
