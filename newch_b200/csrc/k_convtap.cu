@@ -385,20 +385,6 @@ __global__ void __launch_bounds__(256) k_tap_pack(const float *__restrict__ src,
     }
 }
 
-// gb[c] += the sum over pack blocks of their column-c sums: one warp per channel, lanes take strided
-// runs of the blocks, then a fixed shuffle tree
-__global__ void k_tap_colsum_combine(const float *__restrict__ csum, int64_t blocks, int Kp, int C,
-                                     float *__restrict__ gb) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t c = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; c < C; c += warps) {
-        float a = 0.0f;
-        for (int64_t b = lane; b < blocks; b += 32) a += __ldcg(csum + b * Kp + c);
-        for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) gb[c] += a;
-    }
-}
-
 // forward weights dst[oc][tap][c] (tr 0, c < Cp) or dX weights dst[c][tap][oc] (tr 1, oc < OCp) from
 // w[oc][c][tap]; padding columns are zero; the remainder plane follows
 __global__ void k_tap_pack_w(const float *__restrict__ w, float *__restrict__ dst, float *__restrict__ rest, int OC,
@@ -478,17 +464,13 @@ extern "C" void nck_tap_pack(nck_dev *d, const float *src, int64_t N, int64_t C,
     const int64_t blocks = (t->Nv + 127) / 128;
     dim3 grid((unsigned)blocks, (unsigned)(Kp / 32));
     float *rest = t->planes == 2 ? dst + t->Nv * Kp : nullptr;
-    // per-block column sums go to scratch, consumed by the combine right behind (stream order)
+    // per-block column sums go to scratch, consumed by the column sum right behind (stream order)
     float *csum = colsum && (size_t)(blocks * Kp) * sizeof(float) <= d->scratch_bytes ? (float *)d->scratch : nullptr;
     k_tap_pack<<<grid, 256, 0, NCK_STREAM(d)>>>(src, dst, rest, t->Nv, (int)C, (int)Kp, (int)Hs, (int)Ws,
                                                  make_fastdiv((uint32_t)(t->Hp * t->Wp)),
                                                  make_fastdiv((uint32_t)t->Wp), eh, ew, csum);
-    int n = 1;
-    if (csum) {
-        k_tap_colsum_combine<<<grid_for(d, C * 32), kThreads, 0, NCK_STREAM(d)>>>(csum, blocks, (int)Kp, (int)C, colsum);
-        n++;
-    }
-    NCK_LAUNCHED(d, n);
+    NCK_LAUNCHED(d, 1);
+    if (csum) nck_colsum_ld(d, csum, Kp, colsum, blocks, C);  // gb[c] += the blocks' sums, in order
 }
 
 extern "C" int nck_tap_pack_colsum_ok(const nck_dev *d, const nck_tapgeom *t, int64_t Kp) {

@@ -241,8 +241,17 @@ __global__ void __launch_bounds__(256) k_sgemm_small_warp(GemmP p, int64_t nout)
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; t < total; t += warps) {
         const int64_t ob = t / MN, rm = t - ob * MN, m = rm / p.N, n = rm - m * p.N;
-        float acc = 0.0f;
-        for (int64_t r = lane; r < R; r += 32) acc = small_fma(p, ob, m, n, r, acc);
+        // four independent chains per lane, so the loads of several terms are in flight together
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int64_t r = lane;
+        for (; r + 96 < R; r += 128) {
+            a0 = small_fma(p, ob, m, n, r, a0);
+            a1 = small_fma(p, ob, m, n, r + 32, a1);
+            a2 = small_fma(p, ob, m, n, r + 64, a2);
+            a3 = small_fma(p, ob, m, n, r + 96, a3);
+        }
+        for (; r < R; r += 32) a0 = small_fma(p, ob, m, n, r, a0);
+        float acc = (a0 + a1) + (a2 + a3);
         for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) {
             float *c = p.C + ob * p.sC + m * p.ldc + n;

@@ -226,15 +226,18 @@ __global__ void k_colsum_combine(const float *__restrict__ part, float *__restri
 }
 
 // small matrices in one launch: a block of 32 warps takes 32 columns; warp w adds rows w, w + 32, ...
-// of each column, and the 32 warp sums are added in order
-__global__ void __launch_bounds__(1024) k_colsum_small(const float *__restrict__ x, float *__restrict__ gy, int64_t M,
-                                                        int64_t N) {
+// of each column (two running sums), and the 32 warp sums are added in order; rows are ld apart
+__global__ void __launch_bounds__(1024) k_colsum_small(const float *__restrict__ x, int64_t ld, float *__restrict__ gy,
+                                                        int64_t M, int64_t N) {
     __shared__ float sm[32][33];
     const int64_t n = blockIdx.x * 32 + threadIdx.x;
-    float acc = 0.0f;
-    if (n < N)
-        for (int64_t m = threadIdx.y; m < M; m += 32) acc += __ldg(x + m * N + n);
-    sm[threadIdx.y][threadIdx.x] = acc;
+    float a0 = 0.0f, a1 = 0.0f;
+    if (n < N) {
+        int64_t m = threadIdx.y;
+        for (; m + 32 < M; m += 64) a0 += __ldcg(x + m * ld + n), a1 += __ldcg(x + (m + 32) * ld + n);
+        if (m < M) a0 += __ldcg(x + m * ld + n);
+    }
+    sm[threadIdx.y][threadIdx.x] = a0 + a1;
     __syncthreads();
     if (threadIdx.y == 0 && n < N) {
         float s = gy[n];
@@ -247,7 +250,7 @@ extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M,
     if (M <= 0 || N <= 0) return;
     Scope sc(d, "colsum");
     if (M * N <= ((int64_t)1 << 20) && M <= ((int64_t)1 << 14)) {
-        k_colsum_small<<<(unsigned)((N + 31) / 32), dim3(32, 32), 0, NCK_STREAM(d)>>>(x, gy, M, N);
+        k_colsum_small<<<(unsigned)((N + 31) / 32), dim3(32, 32), 0, NCK_STREAM(d)>>>(x, N, gy, M, N);
         NCK_LAUNCHED(d, 1);
         return;
     }
@@ -298,4 +301,10 @@ extern "C" void nck_sumsq(nck_dev *d, const float *x, int64_t n, double *out, in
     else cudaMemsetAsync(part, 0, sizeof(double), NCK_STREAM(d));
     k_sumsq_combine<<<1, 1, 0, NCK_STREAM(d)>>>(part, nb, out, accumulate);
     NCK_LAUNCHED(d, 2);
+}
+
+extern "C" void nck_colsum_ld(nck_dev *d, const float *x, int64_t ld, float *gy, int64_t M, int64_t N) {
+    if (M <= 0 || N <= 0) return;
+    k_colsum_small<<<(unsigned)((N + 31) / 32), dim3(32, 32), 0, NCK_STREAM(d)>>>(x, ld, gy, M, N);
+    NCK_LAUNCHED(d, 1);
 }

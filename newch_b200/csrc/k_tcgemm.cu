@@ -318,8 +318,14 @@ __global__ void k_tc_combine(TcParams p, int64_t nout) {
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         int64_t ob = t / MN, r = t - ob * MN, m = r / p.R, n = r - m * p.R;
         const float *src = p.part + ob * p.splits * MN + r;
-        float s = 0.0f;
-        for (int k = 0; k < p.splits; k++) s += src[k * MN];
+        // slices in order over four interleaved running sums (k mod 4), added at the end
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        int k = 0;
+        for (; k + 4 <= p.splits; k += 4)
+            s0 += __ldcg(src + k * MN), s1 += __ldcg(src + (k + 1) * MN), s2 += __ldcg(src + (k + 2) * MN),
+                s3 += __ldcg(src + (k + 3) * MN);
+        for (; k < p.splits; k++) s0 += __ldcg(src + k * MN);
+        const float s = (s0 + s1) + (s2 + s3);
         float *c = p.C + ob * p.sC + m * p.ldc + n;
         float v = p.alpha * s;
         if (p.bias) v = v + (p.bias_q ? p.bias[m] : p.bias[n]);

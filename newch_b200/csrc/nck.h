@@ -115,6 +115,8 @@ void nck_reduce_sum_i32(nck_dev *d, const int32_t *x, int32_t *y, int64_t outer,
 void nck_reduce_max(nck_dev *d, const float *x, float *y, int32_t *arg, int64_t outer, int64_t R, int64_t inner);
 /* gy[n] += sum_m x[m, n] for a contiguous [M, N] matrix (bias gradients) */
 void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N);
+/* gy[n] += sum over m of x[m * ld + n], one launch (for matrices of a few million elements at most) */
+void nck_colsum_ld(nck_dev *d, const float *x, int64_t ld, float *gy, int64_t M, int64_t N);
 void nck_reduce_sum_bwd(nck_dev *d, const float *g, float *gi, int64_t outer, int64_t R, int64_t inner,
                         float scale);
 void nck_reduce_max_bwd(nck_dev *d, const float *g, const int32_t *arg, float *gi, int64_t outer, int64_t R,
