@@ -193,7 +193,7 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     tf = REPO / "profiles" / "traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(name)
-    kernels = sorted(table, key=lambda t: -t[1])[:8]
+    kernels = sorted(table, key=lambda t: -t[1])[:16]
     sec = max(per_launch_ms, 1e-9) / 1e3
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "traffic": traffic, "peak_src": peaks["src"] + " (MEASURED_PEAKS.json)",

@@ -145,12 +145,15 @@ nc_status nc_backward_ex(nc_tensor *loss, int flags, nc_tensor *const *keep, int
             n->out->grad->coh &= ~NC_COH_HOST_VALID;
         }
 
-    nc_tensor *g = nc__grad_buf(loss);
+    int seed_acc;
+    nc_tensor *g = nc__grad_buf_acc(loss, &seed_acc);
     if (!g) {
         free(kept);
         return ctx->status;
     }
-    nck_add_scalar_inplace(nc__k(ctx), (float *)g->data, 1.0f);
+    /* d loss / d loss = 1: stored into a fresh buffer, added to one that already holds a gradient */
+    if (seed_acc) nck_add_scalar_inplace(nc__k(ctx), (float *)g->data, 1.0f);
+    else nck_fill_f32(nc__k(ctx), (float *)g->data, 1.0f, nc_numel(loss));
 
     for (nc_node *n = ctx->tape; n; n = n->prev) {
         if (n->mark != ep || !n->out->grad) continue;

@@ -118,8 +118,25 @@ __device__ __forceinline__ int32_t checked_label(const int32_t *lab, int64_t i, 
     return l;
 }
 
+// the loss from the rows' terms, summed by the block that finishes last in k_loss_combine's order
+__device__ void loss_combine_block(const float *terms, int64_t n, float *out, int mean) {
+    __shared__ double sm[kThreads / 32];
+    double acc = 0.0;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) acc += (double)__ldcg(terms + i);
+    acc = warp_sum_d(acc);
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int k = 0; k < kThreads / 32; k++) s += sm[k];
+        double loss = -s;
+        *out = mean ? (n ? (float)(loss / (double)n) : NAN) : (float)loss;
+    }
+}
+
 __global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict__ lab, float *__restrict__ prob,
-                          float *__restrict__ terms, int64_t N, int64_t C, int *status) {
+                          float *__restrict__ terms, int64_t N, int64_t C, int *status, float *loss,
+                          unsigned *counter) {
     int lane = threadIdx.x & 31;
     int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t r = warp; r < N; r += nw) {
@@ -136,15 +153,22 @@ __global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict
             q[c] = expf(lp);
         }
     }
+    // loss (optional): the mean over rows, by the last block (one launch for the whole forward)
+    if (loss && last_block_done(counter)) loss_combine_block(terms, N, loss, 1);
 }
 
 extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t *lab, float *prob, float *loss,
                                       int64_t N, int64_t C) {
     Scope sc(d, "cross_entropy", 0.0, 8.0 * N * C + 4.0 * N);
     float *terms = (float *)d->scratch;
-    if (N > 0) k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status);
+    if (N > 0) {
+        k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status, loss,
+                                                                        d->counters);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     k_loss_combine<<<1, kThreads, 0, NCK_STREAM(d)>>>(terms, N, loss, 1);
-    NCK_LAUNCHED(d, 2);
+    NCK_LAUNCHED(d, 1);
 }
 
 // ---- cross entropy on caller-owned buffers, with no allocation ------------------------------------------
@@ -210,7 +234,7 @@ extern "C" NC_API int nc_ext_cross_entropy_fwd_noalloc(const float *logits, cons
     if (rows > 0) {
         int64_t want = (rows * 32 + kThreads - 1) / kThreads, cap = (int64_t)dev->sm_count * 8;
         int grid = (int)(want < cap ? want : cap);
-        k_ce_rows<<<grid, kThreads, 0, st>>>(logits, labels, prob, dev->terms, rows, classes, status);
+        k_ce_rows<<<grid, kThreads, 0, st>>>(logits, labels, prob, dev->terms, rows, classes, status, nullptr, nullptr);
     }
     k_loss_combine<<<1, kThreads, 0, st>>>(dev->terms, rows, loss, 1);
     return cudaGetLastError() == cudaSuccess ? NC_OK : NC_ERR_STATE;
@@ -333,6 +357,52 @@ __device__ __forceinline__ void xo_step(unsigned long long (&s)[4]) {
     s[3] = rotl64(s[3], 45);
 }
 
+// y = x * mask * 1/(1-p) and the mask words for the block's 8192 draws (mask bits in shared memory):
+// float4 items, all of a thread's loads issued before its stores; a scalar tail when n is not a
+// multiple of 4 or the pointers are not 16-byte aligned
+__device__ __forceinline__ void drop_block_write(const float *__restrict__ x, float *__restrict__ y,
+                                                 uint32_t *__restrict__ bits, int64_t n, float p, const uint32_t *mb) {
+    const float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+    const int64_t base = (int64_t)blockIdx.x * kDropBlock;
+    const bool vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+    constexpr int kItems = kDropBlock / 4;
+    if (vec && base + kDropBlock <= n) {
+        for (int i0 = threadIdx.x; i0 < kItems; i0 += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < kItems) v[u] = __ldcs(reinterpret_cast<const float4 *>(x + base) + i);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < kItems) {
+                    const uint32_t m4 = (mb[i >> 3] >> ((i & 7) * 4)) & 15u;
+                    v[u].x *= (m4 & 1u) ? keepv : 0.0f;
+                    v[u].y *= (m4 & 2u) ? keepv : 0.0f;
+                    v[u].z *= (m4 & 4u) ? keepv : 0.0f;
+                    v[u].w *= (m4 & 8u) ? keepv : 0.0f;
+                    __stcs(reinterpret_cast<float4 *>(y + base) + i, v[u]);
+                }
+            }
+        }
+    } else {
+        for (int jj = threadIdx.x; jj < kDropBlock; jj += blockDim.x) {
+            const int64_t e = base + jj;
+            if (e < n) {
+                const float m = (mb[jj >> 5] >> (jj & 31)) & 1u ? keepv : 0.0f;
+                y[e] = x[e] * m;
+            }
+        }
+    }
+    const int64_t words = (n + 31) / 32;
+    for (int w = threadIdx.x; w < kDropBlock / 32; w += blockDim.x) {
+        const int64_t gw = (int64_t)blockIdx.x * (kDropBlock / 32) + w;
+        if (gw < words) bits[gw] = mb[w];
+    }
+}
+
 // The thread's 64 draws from state s0 (uniform u = (r >> 40) * 2^-24, exact; kept when u >= p) into
 // its two mask words in shared memory, then the block's 8192 outputs and mask words, coalesced.
 __device__ __forceinline__ void drop_block_out(const unsigned long long (&s0)[4], const float *__restrict__ x,
@@ -353,47 +423,90 @@ __device__ __forceinline__ void drop_block_out(const unsigned long long (&s0)[4]
     mb[2 * tid] = w0;
     mb[2 * tid + 1] = w1;
     __syncthreads();
-    const float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
-    const int64_t base = (int64_t)blockIdx.x * kDropBlock;
-    for (int j = tid; j < kDropBlock; j += kDropThreads) {
-        const int64_t e = base + j;
-        if (e < n) {
-            const float m = (mb[j >> 5] >> (j & 31)) & 1u ? keepv : 0.0f;
-            y[e] = x[e] * m;
-        }
-    }
-    const int64_t words = (n + 31) / 32;
-    for (int w = tid; w < kDropBlock / 32; w += kDropThreads) {
-        const int64_t gw = (int64_t)blockIdx.x * (kDropBlock / 32) + w;
-        if (gw < words) bits[gw] = mb[w];
-    }
+    drop_block_write(x, y, bits, n, p, mb);
 }
 
-// Thread k of the grid owns draws [64 k, 64 k + 64) (the same runs as the matrix-jump kernel below).
-// Its start state is q_k(T) s0, q_k = x^(64 k) mod P (P the characteristic polynomial of the
-// transition T, q_k from the host's table), evaluated by Horner's rule: 256 transitions of a running
-// state, XORed into the result where q_k has a one. No thread waits for another before its draws.
-__global__ void __launch_bounds__(kDropThreads) k_dropout_fwd_poly(ulonglong4 s0, const ulonglong4 *__restrict__ polys,
+// Run k of the grid (draws [64 k, 64 k + 64), the same runs as the matrix-jump kernel below) is taken
+// by four consecutive lanes. Its start state is q_k(T) s0 with q_k = x^(64 k) mod P (P the
+// characteristic polynomial of the transition T, q_k from the host's table). Splitting q_k into its
+// four 64-bit words r_j gives q_k(T) s0 = sum_j r_j(T) (T^(64 j) s0): lane j evaluates its word by
+// Horner's rule from the base state T^(64 j) s0 (the host passes the four bases), 64 transitions with a
+// conditional XOR, and the four partial states are XORed across the lanes. Lane j then moves 16 j
+// further and makes draws [16 j, 16 j + 16) of the run; the 64 mask bits are gathered by shuffles.
+// The Horner sums depend on the launch's bases only, so each block tabulates them in 4-bit windows:
+// tab[j][n][v] = XOR over the set bits t of v of T^(4 n + t) b_j, and a lane's word costs 16 table
+// reads instead of 64 transitions.
+constexpr int kDropGroup = 4;                              // lanes per run
+constexpr int kDropPolyThreads = kDropThreads * kDropGroup;  // one run per lane group: 512 threads
+
+__global__ void __launch_bounds__(kDropPolyThreads) k_dropout_fwd_poly(ulonglong4 b0, ulonglong4 b1, ulonglong4 b2,
+                                                                   ulonglong4 b3, const ulonglong4 *__restrict__ polys,
                                                                    const float *__restrict__ x, float *__restrict__ y,
                                                                    uint32_t *__restrict__ bits, int64_t n, float p) {
     __shared__ uint32_t mb[kDropBlock / 32];
-    const int64_t k = (int64_t)blockIdx.x * kDropThreads + threadIdx.x;
-    unsigned long long a[4] = {0, 0, 0, 0};
-    if (k * kDropDraws < n) {
-        const ulonglong4 q = polys[k];
-        const unsigned long long qw[4] = {q.x, q.y, q.z, q.w};
-        unsigned long long s[4] = {s0.x, s0.y, s0.z, s0.w};
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-#pragma unroll 16
-            for (int b = 0; b < 64; b++) {
-                const unsigned long long m = 0ull - ((qw[w] >> b) & 1ull);
-                a[0] ^= s[0] & m, a[1] ^= s[1] & m, a[2] ^= s[2] & m, a[3] ^= s[3] & m;
-                xo_step(s);
-            }
+    __shared__ ulonglong4 vtab[4][64];      // T^i b_j
+    __shared__ ulonglong4 tab[4][16][16];   // 4-bit windows of the Horner sums
+    const int j = threadIdx.x & (kDropGroup - 1);
+    if (threadIdx.x < 4) {
+        const int jj = threadIdx.x;
+        const ulonglong4 bj = jj == 0 ? b0 : jj == 1 ? b1 : jj == 2 ? b2 : b3;
+        unsigned long long st[4] = {bj.x, bj.y, bj.z, bj.w};
+        for (int i = 0; i < 64; i++) {
+            vtab[jj][i] = make_ulonglong4(st[0], st[1], st[2], st[3]);
+            xo_step(st);
         }
     }
-    drop_block_out(a, x, y, bits, n, p, mb);
+    __syncthreads();
+    for (int e = threadIdx.x; e < 4 * 16 * 16; e += blockDim.x) {
+        const int jj = e >> 8, nn = (e >> 4) & 15, v = e & 15;
+        ulonglong4 acc = make_ulonglong4(0, 0, 0, 0);
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            if ((v >> t) & 1) {
+                const ulonglong4 q = vtab[jj][4 * nn + t];
+                acc.x ^= q.x, acc.y ^= q.y, acc.z ^= q.z, acc.w ^= q.w;
+            }
+        tab[jj][nn][v] = acc;
+    }
+    __syncthreads();
+    const int64_t base_run = (int64_t)blockIdx.x * kDropThreads;  // runs of this block: kDropThreads of them
+    {
+        const int rr = threadIdx.x / kDropGroup;  // the block's run rr, of kDropThreads
+        const int64_t k = base_run + rr;
+        const bool live = k * kDropDraws < n;
+        unsigned long long a[4] = {0, 0, 0, 0};
+        if (live) {
+            const ulonglong4 q = polys[k];
+            const unsigned long long w = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
+#pragma unroll
+            for (int nn = 0; nn < 16; nn++) {
+                const ulonglong4 t = tab[j][nn][(w >> (4 * nn)) & 15];
+                a[0] ^= t.x, a[1] ^= t.y, a[2] ^= t.z, a[3] ^= t.w;
+            }
+        }
+        // XOR of the four partial states: every lane of the group gets the run's start state
+#pragma unroll
+        for (int o = 1; o < kDropGroup; o <<= 1)
+#pragma unroll
+            for (int e = 0; e < 4; e++) a[e] ^= __shfl_xor_sync(0xffffffffu, a[e], o);
+        // lane j: draws [16 j, 16 j + 16) of the run
+        for (int t = 0; t < 16 * j; t++) xo_step(a);
+        uint32_t bits16 = 0;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const unsigned long long r = rotl64(a[1] * 5ull, 7) * 9ull;
+            xo_step(a);
+            const float u = (float)(r >> 40) * (1.0f / 16777216.0f);
+            bits16 |= (u >= p ? 1u : 0u) << i;
+        }
+        const uint32_t lo = __shfl_sync(0xffffffffu, bits16, (threadIdx.x & 31 & ~3) + 0) |
+                            (__shfl_sync(0xffffffffu, bits16, (threadIdx.x & 31 & ~3) + 1) << 16);
+        const uint32_t hi = __shfl_sync(0xffffffffu, bits16, (threadIdx.x & 31 & ~3) + 2) |
+                            (__shfl_sync(0xffffffffu, bits16, (threadIdx.x & 31 & ~3) + 3) << 16);
+        if (j == 0) mb[2 * rr] = lo, mb[2 * rr + 1] = hi;
+    }
+    __syncthreads();
+    drop_block_write(x, y, bits, n, p, mb);
 }
 
 __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
@@ -461,8 +574,19 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
     if (polys) {
-        k_dropout_fwd_poly<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(
-            s0, reinterpret_cast<const ulonglong4 *>(polys), x, y, bits, n, p);
+        // base states T^(64 j) s0, j < 4: 64, 128 and 192 transitions of the host's copy
+        uint64_t st[4] = {state[0], state[1], state[2], state[3]};
+        ulonglong4 bj[4];
+        for (int j = 0; j < 4; j++) {
+            bj[j] = make_ulonglong4(st[0], st[1], st[2], st[3]);
+            for (int t = 0; t < 64; t++) {
+                const uint64_t tt = st[1] << 17;
+                st[2] ^= st[0], st[3] ^= st[1], st[1] ^= st[2], st[0] ^= st[3], st[2] ^= tt;
+                st[3] = (st[3] << 45) | (st[3] >> 19);
+            }
+        }
+        k_dropout_fwd_poly<<<(unsigned)blocks, kDropPolyThreads, 0, NCK_STREAM(d)>>>(
+            bj[0], bj[1], bj[2], bj[3], reinterpret_cast<const ulonglong4 *>(polys), x, y, bits, n, p);
         NCK_LAUNCHED(d, 1);
         return;
     }
