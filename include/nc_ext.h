@@ -64,8 +64,11 @@ NC_API void nc_ext_timing_reset(nc_ctx *ctx);
  * The call is asynchronous. Returns NC_OK, NC_ERR_ARG (rows < 0, rows > NC_EXT_CE_NOALLOC_MAX_ROWS,
  * classes <= 0, or a NULL pointer; nothing is launched) or NC_ERR_STATE (CUDA set-up or launch
  * failure).
- * - The first call on a device (made with that device current) looks up the static array's address;
- *   make it before any stream capture begins.
+ * - The first call on a device (made with that device current) looks up the static array's address
+ *   in the current CUDA context; a later call under another context (after cudaDeviceReset, say)
+ *   looks it up again. Make such a first call before any stream capture begins.
+ * - Launch failures are taken from the launches themselves: an error the caller left pending in the
+ *   runtime's last-error slot is neither reported nor cleared.
  * - *status must start at zero; a label outside [0, classes) sets it to 2 (that row's label is
  *   read as class 0). The static array needs no initialisation.
  * - Calls on one device share the static array: calls that can run at the same time (on streams

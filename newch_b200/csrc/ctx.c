@@ -378,6 +378,10 @@ nc_ctx *nc_init(const nc_config *cfg) {
         ctx->dev.gemm_small = !gs || strcmp(gs, "0") != 0;
         const char *qg = getenv("NC_QGEMM");
         ctx->dev.qgemm_tc = !qg || strcmp(qg, "dp4a") != 0;
+        /* exp / sigmoid / tanh / erf: newch's AVX2-tier polynomials unless the reference tier's C
+         * library forms are asked for (force_reference, as newch selects its reference tier) */
+        const char *mm = getenv("NC_MATH");
+        ctx->dev.math_mode = (c.force_reference || (mm && !strcmp(mm, "libm"))) ? NCK_MATH_LIBM : NCK_MATH_POLY;
     }
     cudaStream_t s;
     if (!nc__cuda_ok(ctx, cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return ctx;

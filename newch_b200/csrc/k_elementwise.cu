@@ -8,6 +8,7 @@
 #include <math.h>
 
 #include "k_common.cuh"
+#include "k_math.cuh"
 
 using namespace nck;
 
@@ -16,15 +17,16 @@ using namespace nck;
 #define NC_SQRT_2_PI 0.79788456080286536f
 #define NC_GELU_C 0.044715f
 
+template <int M>
 __device__ __forceinline__ float unary_f(int kind, float s, float x) {
     switch (kind) {
     case NCK_UN_NEG: return -1.0f * x;
-    case NCK_UN_EXP: return expf(x);
+    case NCK_UN_EXP: return m_exp<M>(x);
     case NCK_UN_LOG: return logf(x);
     case NCK_UN_SQRT: return sqrtf(x);
     case NCK_UN_RELU: return x > 0.0f ? x : 0.0f;
-    case NCK_UN_SIGMOID: return 1.0f / (1.0f + expf(-x));
-    case NCK_UN_TANH: return tanhf(x);
+    case NCK_UN_SIGMOID: return m_sigmoid<M>(x);
+    case NCK_UN_TANH: return m_tanh<M>(x);
     case NCK_UN_SCALE: return s * x;
     case NCK_UN_ADD_SCALAR: return x + s;
     case NCK_UN_POW: return powf(x, s);
@@ -32,16 +34,17 @@ __device__ __forceinline__ float unary_f(int kind, float s, float x) {
     case NCK_UN_RELU6: return fminf(fmaxf(x, 0.0f), 6.0f);
     case NCK_UN_HARDSIGMOID: return fminf(fmaxf(x * (1.0f / 6.0f) + 0.5f, 0.0f), 1.0f);
     case NCK_UN_HARDSWISH: return x * fminf(fmaxf(x + 3.0f, 0.0f), 6.0f) * (1.0f / 6.0f);
-    case NCK_UN_SILU: return (1.0f / (1.0f + expf(-x))) * x;
-    case NCK_UN_GELU: return 0.5f * x * (1.0f + erff(NC_SQRT1_2 * x));
+    case NCK_UN_SILU: return m_sigmoid<M>(x) * x;
+    case NCK_UN_GELU: return 0.5f * x * (1.0f + m_erf<M>(NC_SQRT1_2 * x));
     case NCK_UN_GELU_TANH: {
-        float t = tanhf(NC_SQRT_2_PI * (x + NC_GELU_C * x * x * x));
+        float t = m_tanh<M>(NC_SQRT_2_PI * (x + NC_GELU_C * x * x * x));
         return 0.5f * x * (1.0f + t);
     }
     }
     return x;
 }
 
+template <int M>
 __device__ __forceinline__ float unary_grad(int kind, float s, float x, float y, float g) {
     switch (kind) {
     case NCK_UN_NEG: return -1.0f * g;
@@ -59,15 +62,15 @@ __device__ __forceinline__ float unary_grad(int kind, float s, float x, float y,
     case NCK_UN_HARDSIGMOID: return (x > -3.0f && x < 3.0f) ? g * (1.0f / 6.0f) : 0.0f;
     case NCK_UN_HARDSWISH: return x < -3.0f ? 0.0f : x <= 3.0f ? g * (x * (1.0f / 3.0f) + 0.5f) : g;
     case NCK_UN_SILU: {
-        float t = 1.0f / (1.0f + expf(-x));
+        float t = m_sigmoid<M>(x);
         return g * t * (1.0f + x * (1.0f - t));
     }
     case NCK_UN_GELU: {
-        float t = erff(NC_SQRT1_2 * x), t2 = expf(-0.5f * x * x);
+        float t = m_erf<M>(NC_SQRT1_2 * x), t2 = m_exp<M>(-0.5f * x * x);
         return g * (0.5f * (1.0f + t) + x * NC_INV_SQRT_2PI * t2);
     }
     case NCK_UN_GELU_TANH: {
-        float t = tanhf(NC_SQRT_2_PI * (x + NC_GELU_C * x * x * x));
+        float t = m_tanh<M>(NC_SQRT_2_PI * (x + NC_GELU_C * x * x * x));
         float dt = (1.0f - t * t) * NC_SQRT_2_PI * (1.0f + 3.0f * NC_GELU_C * x * x);
         return g * (0.5f * (1.0f + t) + 0.5f * x * dt);
     }
@@ -83,6 +86,7 @@ __device__ __forceinline__ float accumulate(int kind, float s, float gi, float g
     return gi + v;
 }
 
+template <int M>
 __global__ void k_unary_fwd(int kind, float s, const float *__restrict__ x, float *__restrict__ y, int64_t n,
                             int vec) {
     int64_t stride = (int64_t)gridDim.x * blockDim.x, t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -90,17 +94,18 @@ __global__ void k_unary_fwd(int kind, float s, const float *__restrict__ x, floa
         int64_t n4 = n >> 2;
         for (int64_t i = t; i < n4; i += stride) {
             float4 v = ((const float4 *)x)[i];
-            v.x = unary_f(kind, s, v.x), v.y = unary_f(kind, s, v.y), v.z = unary_f(kind, s, v.z);
-            v.w = unary_f(kind, s, v.w);
+            v.x = unary_f<M>(kind, s, v.x), v.y = unary_f<M>(kind, s, v.y), v.z = unary_f<M>(kind, s, v.z);
+            v.w = unary_f<M>(kind, s, v.w);
             ((float4 *)y)[i] = v;
         }
-        for (int64_t i = (n4 << 2) + t; i < n; i += stride) y[i] = unary_f(kind, s, x[i]);
+        for (int64_t i = (n4 << 2) + t; i < n; i += stride) y[i] = unary_f<M>(kind, s, x[i]);
     } else {
-        for (int64_t i = t; i < n; i += stride) y[i] = unary_f(kind, s, x[i]);
+        for (int64_t i = t; i < n; i += stride) y[i] = unary_f<M>(kind, s, x[i]);
     }
 }
 
 // nx / ny: the derivative reads x / y (a stream the derivative does not use is not loaded)
+template <int M>
 __global__ void k_unary_bwd(int kind, float s, const float *__restrict__ x, const float *__restrict__ y,
                             const float *__restrict__ g, float *__restrict__ gi, int64_t n, int vec, int acc, int nx,
                             int ny) {
@@ -112,17 +117,17 @@ __global__ void k_unary_bwd(int kind, float s, const float *__restrict__ x, cons
             float4 xv = nx ? __ldg((const float4 *)x + i) : z4, yv = ny ? __ldg((const float4 *)y + i) : z4;
             float4 gv = __ldg((const float4 *)g + i);
             float4 o = acc ? ((float4 *)gi)[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            o.x = accumulate(kind, s, o.x, gv.x, unary_grad(kind, s, xv.x, yv.x, gv.x));
-            o.y = accumulate(kind, s, o.y, gv.y, unary_grad(kind, s, xv.y, yv.y, gv.y));
-            o.z = accumulate(kind, s, o.z, gv.z, unary_grad(kind, s, xv.z, yv.z, gv.z));
-            o.w = accumulate(kind, s, o.w, gv.w, unary_grad(kind, s, xv.w, yv.w, gv.w));
+            o.x = accumulate(kind, s, o.x, gv.x, unary_grad<M>(kind, s, xv.x, yv.x, gv.x));
+            o.y = accumulate(kind, s, o.y, gv.y, unary_grad<M>(kind, s, xv.y, yv.y, gv.y));
+            o.z = accumulate(kind, s, o.z, gv.z, unary_grad<M>(kind, s, xv.z, yv.z, gv.z));
+            o.w = accumulate(kind, s, o.w, gv.w, unary_grad<M>(kind, s, xv.w, yv.w, gv.w));
             ((float4 *)gi)[i] = o;
         }
         for (int64_t i = (n4 << 2) + t; i < n; i += stride)
-            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad(kind, s, x[i], y[i], g[i]));
+            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad<M>(kind, s, x[i], y[i], g[i]));
     } else {
         for (int64_t i = t; i < n; i += stride)
-            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad(kind, s, x[i], y[i], g[i]));
+            gi[i] = accumulate(kind, s, acc ? gi[i] : 0.0f, g[i], unary_grad<M>(kind, s, x[i], y[i], g[i]));
     }
 }
 
@@ -141,7 +146,8 @@ extern "C" void nck_unary_fwd(nck_dev *d, int kind, float s, const float *x, flo
     if (n <= 0) return;
     Scope sc(d, unary_name(kind, 0), 0.0, 8.0 * n);
     int vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
-    k_unary_fwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, n, vec);
+    auto k = d->math_mode == MATH_LIBM ? k_unary_fwd<MATH_LIBM> : k_unary_fwd<MATH_POLY>;
+    k<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, n, vec);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -153,8 +159,9 @@ extern "C" void nck_unary_bwd(nck_dev *d, int kind, float s, const float *x, con
     int uses_x = !uses_y && kind != NCK_UN_SCALE && kind != NCK_UN_NEG && kind != NCK_UN_ADD_SCALAR;
     Scope sc(d, unary_name(kind, 1), 0.0, (8.0 + (acc ? 4.0 : 0.0) + (uses_x ? 4.0 : 0.0) + (uses_y ? 4.0 : 0.0)) * n);
     int vec = (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)gi) & 15) == 0;
-    k_unary_bwd<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec, acc, uses_x,
-                                                                                       uses_y);
+    auto k = d->math_mode == MATH_LIBM ? k_unary_bwd<MATH_LIBM> : k_unary_bwd<MATH_POLY>;
+    k<<<grid_for(d, vec ? (n + 3) / 4 : n), kThreads, 0, NCK_STREAM(d)>>>(kind, s, x, y, g, gi, n, vec, acc, uses_x,
+                                                                         uses_y);
     NCK_LAUNCHED(d, 1);
 }
 

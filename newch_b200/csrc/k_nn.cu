@@ -8,6 +8,7 @@
 #include <math.h>
 
 #include "k_common.cuh"
+#include "k_math.cuh"
 
 #include <mutex>
 
@@ -38,6 +39,7 @@ __device__ __forceinline__ float row_max(const float *p, int64_t C, int lane) {
     return warp_max(m);
 }
 
+template <int M>
 __global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t C, int logf_) {
     int lane = threadIdx.x & 31;
     int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -46,21 +48,22 @@ __global__ void k_softmax_fwd(const float *__restrict__ x, float *__restrict__ y
         float *q = y + r * C;
         float m = row_max(p, C, lane);
         float s = 0.0f;
-        for (int64_t c = lane; c < C; c += 32) s += expf(p[c] - m);
+        for (int64_t c = lane; c < C; c += 32) s += m_exp<M>(p[c] - m);
         s = warp_sum(s);
         if (logf_) {
             float ls = logf(s);
             for (int64_t c = lane; c < C; c += 32) q[c] = p[c] - m - ls;
         } else {
             float inv = 1.0f / s;
-            for (int64_t c = lane; c < C; c += 32) q[c] = inv * expf(p[c] - m);
+            for (int64_t c = lane; c < C; c += 32) q[c] = inv * m_exp<M>(p[c] - m);
         }
     }
 }
 
 extern "C" void nck_softmax_fwd(nck_dev *d, const float *x, float *y, int64_t rows, int64_t C, int log_form) {
     Scope sc(d, log_form ? "log_softmax" : "softmax", 0.0, 8.0 * rows * C);
-    k_softmax_fwd<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, rows, C, log_form);
+    auto k = d->math_mode == MATH_LIBM ? k_softmax_fwd<MATH_LIBM> : k_softmax_fwd<MATH_POLY>;
+    k<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, rows, C, log_form);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -134,6 +137,7 @@ __device__ void loss_combine_block(const float *terms, int64_t n, float *out, in
     }
 }
 
+template <int M>
 __global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict__ lab, float *__restrict__ prob,
                           float *__restrict__ terms, int64_t N, int64_t C, int *status, float *loss,
                           unsigned *counter) {
@@ -144,13 +148,13 @@ __global__ void k_ce_rows(const float *__restrict__ x, const int32_t *__restrict
         float *q = prob + r * C;
         float m = row_max(p, C, lane);
         float s = 0.0f;
-        for (int64_t c = lane; c < C; c += 32) s += expf(p[c] - m);
+        for (int64_t c = lane; c < C; c += 32) s += m_exp<M>(p[c] - m);
         float ls = logf(warp_sum(s));
         int32_t l = checked_label(lab, r, C, status);
         for (int64_t c = lane; c < C; c += 32) {
             float lp = p[c] - m - ls;
             if (c == l) terms[r] = lp;
-            q[c] = expf(lp);
+            q[c] = m_exp<M>(lp);
         }
     }
     // loss (optional): the mean over rows, by the last block (one launch for the whole forward)
@@ -162,8 +166,8 @@ extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t 
     Scope sc(d, "cross_entropy", 0.0, 8.0 * N * C + 4.0 * N);
     float *terms = (float *)d->scratch;
     if (N > 0) {
-        k_ce_rows<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status, loss,
-                                                                        d->counters);
+        auto k = d->math_mode == MATH_LIBM ? k_ce_rows<MATH_LIBM> : k_ce_rows<MATH_POLY>;
+        k<<<grid_for(d, N * 32), kThreads, 0, NCK_STREAM(d)>>>(x, lab, prob, terms, N, C, d->status, loss, d->counters);
         NCK_LAUNCHED(d, 1);
         return;
     }
@@ -185,8 +189,9 @@ extern "C" void nck_cross_entropy_fwd(nck_dev *d, const float *x, const int32_t 
 // - Size limit: rows <= NC_EXT_CE_NOALLOC_MAX_ROWS (1 MiB of float terms); larger calls are rejected
 //   with NC_ERR_ARG before anything is launched.
 // - Set-up: the first call on each device (with that device current) looks up the array's device
-//   address with cudaGetSymbolAddress and caches it with the SM count. Make that first call before
-//   any stream capture begins.
+//   address with cudaGetSymbolAddress and caches it with the SM count and the CUDA context it was
+//   taken in; a call under another context (after cudaDeviceReset, say) looks it up again. Make the
+//   first call on a device, and the first after such a change, before any stream capture begins.
 // - Nothing in the array has to start at zero: each call writes terms[0, rows) before reading them.
 //   The caller's status word must start at zero; a label outside [0, classes) sets it to 2.
 // - The array is shared by every call on a device: two calls whose kernels can overlap (different
@@ -199,27 +204,52 @@ constexpr int kMaxDevices = 64;
 struct NoAllocDevice {
     float *terms;
     int sm_count;
+    void *cu_ctx;  // the CUDA context the address belongs to
     bool ready;
 };
 NoAllocDevice g_noalloc_dev[kMaxDevices];
 std::mutex g_noalloc_mu;
 
-// Address of the static terms array and the SM count of the current device, looked up once.
-const NoAllocDevice *noalloc_device() {
+// The calling thread's current CUDA context (driver cuCtxGetCurrent, reached through the runtime's
+// entry-point table so the library needs no link against the driver library).
+void *current_cu_context() {
+    typedef int (*GetCurrent)(void **);
+    static GetCurrent fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (GetCurrent)f;
+    });
+    void *c = nullptr;
+    if (!fn || fn(&c) != 0) return nullptr;
+    return c;
+}
+
+// Address of the static terms array and the SM count of the current device. Looked up on the first
+// call on a device and again whenever the current context differs from the one the address was
+// taken in (after cudaDeviceReset the module is loaded anew, at another address).
+bool noalloc_device(NoAllocDevice *out) {
     int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+    void *cu = current_cu_context();
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     NoAllocDevice &e = g_noalloc_dev[dev];
-    if (!e.ready) {
+    if (!e.ready || e.cu_ctx != cu) {
         void *p = nullptr;
         int sms = 0;
-        if (cudaGetSymbolAddress(&p, g_ce_terms_static) != cudaSuccess || !p) return nullptr;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return nullptr;
+        if (cudaGetSymbolAddress(&p, g_ce_terms_static) != cudaSuccess || !p) return false;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return false;
+        // the symbol lookup may have created the context: take its handle after the lookup
+        e.cu_ctx = current_cu_context();
         e.terms = (float *)p;
         e.sm_count = sms;
         e.ready = true;
     }
-    return &e;
+    *out = e;
+    return true;
 }
 }  // namespace
 
@@ -228,16 +258,34 @@ extern "C" NC_API int nc_ext_cross_entropy_fwd_noalloc(const float *logits, cons
                                                        void *stream) {
     if (rows < 0 || rows > NC_EXT_CE_NOALLOC_MAX_ROWS || classes <= 0) return NC_ERR_ARG;
     if (!loss || !status || (rows > 0 && (!logits || !labels || !prob))) return NC_ERR_ARG;
-    const NoAllocDevice *dev = noalloc_device();
-    if (!dev) return NC_ERR_STATE;
-    cudaStream_t st = (cudaStream_t)stream;
-    if (rows > 0) {
-        int64_t want = (rows * 32 + kThreads - 1) / kThreads, cap = (int64_t)dev->sm_count * 8;
-        int grid = (int)(want < cap ? want : cap);
-        k_ce_rows<<<grid, kThreads, 0, st>>>(logits, labels, prob, dev->terms, rows, classes, status, nullptr, nullptr);
+    NoAllocDevice dev;
+    if (!noalloc_device(&dev)) {
+        cudaGetLastError();  // the failed lookup's error is this call's, not the caller's
+        return NC_ERR_STATE;
     }
-    k_loss_combine<<<1, kThreads, 0, st>>>(dev->terms, rows, loss, 1);
-    return cudaGetLastError() == cudaSuccess ? NC_OK : NC_ERR_STATE;
+    cudaStream_t st = (cudaStream_t)stream;
+    // each launch's own status: an error the caller left pending is neither reported here nor cleared
+    float *terms = dev.terms;
+    if (rows > 0) {
+        int64_t want = (rows * 32 + kThreads - 1) / kThreads, cap = (int64_t)dev.sm_count * 8;
+        int grid = (int)(want < cap ? want : cap);
+        unsigned *no_counter = nullptr;
+        float *no_loss = nullptr;
+        void *a[] = {(void *)&logits, (void *)&labels, (void *)&prob, (void *)&terms, (void *)&rows,
+                     (void *)&classes, (void *)&status, (void *)&no_loss, (void *)&no_counter};
+        if (cudaLaunchKernel((const void *)k_ce_rows<MATH_POLY>, dim3(grid), dim3(kThreads), a, 0, st) != cudaSuccess) {
+            cudaGetLastError();
+            return NC_ERR_STATE;
+        }
+    }
+    const float *cterms = terms;
+    int mean = 1;
+    void *b[] = {(void *)&cterms, (void *)&rows, (void *)&loss, (void *)&mean};
+    if (cudaLaunchKernel((const void *)k_loss_combine, dim3(1), dim3(kThreads), b, 0, st) != cudaSuccess) {
+        cudaGetLastError();
+        return NC_ERR_STATE;
+    }
+    return NC_OK;
 }
 
 __global__ void k_ce_bwd(const float *__restrict__ prob, const int32_t *__restrict__ lab,

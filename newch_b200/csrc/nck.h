@@ -29,6 +29,7 @@ typedef struct nck_dev {
     int conv_tap;      /* 1: stride-1 convolutions run as tap-shifted GEMMs (default; NC_CONV=unfolded|implicit: 0) */
     int gemm_small;    /* 1: small products take the one-thread / one-warp-per-output kernels (NC_GEMM_SMALL=0: off) */
     int qgemm_tc;      /* 1: int8 GEMMs on tcgen05 kind::i8 where TMA allows (NC_QGEMM=dp4a: CUDA cores) */
+    int math_mode;     /* NCK_MATH_*: how exp / sigmoid / tanh / erf are evaluated */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
     unsigned *counters; /* device counters for last-block-finishes reductions; each user leaves it at 0 */
@@ -39,6 +40,11 @@ typedef struct nck_dev {
 enum { NCK_OK = 0, NCK_ERR_INDEX = 1, NCK_ERR_LABEL = 2, NCK_ERR_PIPELINE = 3, NCK_ERR_LAUNCH = 4 };
 
 enum { NCK_GEMM_FFMA = 0, NCK_GEMM_TF32 = 1, NCK_GEMM_3XTF32 = 2 };
+
+/* NCK_MATH_POLY: newch's AVX2-tier polynomials (bit-identical to that tier; the default);
+ * NCK_MATH_LIBM: CUDA's libm functions, as newch's reference tier calls the C library
+ * (force_reference, or NC_MATH=libm). The values equal nck::MATH_POLY / MATH_LIBM (k_math.cuh). */
+enum { NCK_MATH_POLY = 0, NCK_MATH_LIBM = 1 };
 
 /* ---- timing (bench instrumentation) ------------------------------------------------------ */
 void nck_timer_enable(nck_dev *d, int on);

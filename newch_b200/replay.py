@@ -89,7 +89,10 @@ class Replayer:
     """Executes trace calls on `lib`. `seed_offset` regenerates synthetic inputs with another seed
     (per-rank data shards); `check` raises when a call's success differs from the recording."""
 
-    def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True, pinned: bool = False):
+    OPTIMIZERS = ("nc_sgd", "nc_adam", "nc_adamw", "nc_rmsprop")
+
+    def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True, pinned: bool = False,
+                 grads: bool = False, capture=()):
         self.lib = lib
         self.trace = trace
         self.check = check
@@ -97,6 +100,17 @@ class Replayer:
         self.h: dict = {}
         self.items: list = []    # (call index, value) of nc_item results
         self.outputs: list = []  # (call index, bytes) of nc_copy_to results
+        # grads=True: after every backward call, each optimizer parameter's gradient (bytes, or None
+        # when it has none) as (call index, [per parameter]); parameters in the optimizer's order
+        self.capture_grads = grads
+        self.grads: list = []
+        self._param_handles: list = []
+        # capture: names of calls whose returned tensor (and nc_quantize_rows' scale output) is copied
+        # out right after the call: self.captured lists (call index, name, argument handles, result
+        # handle) and self.tensors maps those result handles (trace numbering) to the bytes
+        self.capture = frozenset(capture)
+        self.captured: list = []
+        self.tensors: dict = {}
         self._keep: list = []
         self._blobs: dict = {}
         self.seed_offset = seed_offset
@@ -194,10 +208,31 @@ class Replayer:
                 raise ReplayMismatch(f"call {i} {name}: succeeded where the reference returned NULL")
             if out_h is not None:
                 h[out_h] = outbuf[0]
+            if name in self.capture and r and ret_h is not None:
+                self.captured.append((i, name, [v if kind == 1 else None for kind, v in conv], ret_h))
+                self.tensors[ret_h] = self._tensor_bytes(r)
+                if out_h is not None:
+                    self.tensors[out_h] = self._tensor_bytes(outbuf[0])
             if name == "nc_item":
                 self.items.append((i, r))
             elif name == "nc_copy_to" and outbuf is not None:
                 self.outputs.append((i, bytes(outbuf)))
+            elif self.capture_grads:
+                if name in self.OPTIMIZERS:
+                    self._param_handles = next((list(v) for kind, v in conv if kind == 3), [])
+                elif name in ("nc_backward", "nc_backward_ex"):
+                    self.grads.append((i, [self._grad_bytes(h[p]) for p in self._param_handles]))
+
+    def _tensor_bytes(self, t):
+        n = int(self.lib.nc_numel(t)) * {0: 4, 1: 4, 2: 2, 3: 1, 4: 1}[int(self.lib.nc_get_dtype(t))]
+        buf = (ctypes.c_char * max(n, 1))()
+        if not self.lib.nc_copy_to(t, buf, n):
+            raise ReplayMismatch(f"nc_copy_to of a captured tensor failed: {self._error()}")
+        return bytes(buf)[:n]
+
+    def _grad_bytes(self, p):
+        g = self.lib.nc_grad(p)
+        return self._tensor_bytes(g) if g else None
 
     def _error(self) -> str:
         ctx = self.h.get(1)  # nc_init is every trace's first call

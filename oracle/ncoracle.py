@@ -93,6 +93,143 @@ def _erf(x):
     return np.vectorize(lambda v: f32(math.erf(float(v))), otypes=[f32])(x)
 
 
+# newch's AVX2-tier transcendental functions (engine/src/kernels/x86/kernels_avx2.c:75-177), the ones
+# a newch build on an AVX2+FMA host evaluates for exp / sigmoid / tanh / erf. Restated elementwise in
+# float32 with each fused multiply-add rounded once (fma32), so results are bit-identical to that
+# tier's.
+
+def fma32(a, b, c) -> np.ndarray:
+    """float32 a * b + c with one rounding. a * b is exact in float64 (24-bit factors); the float64 sum
+    is made round-to-odd from its exact error (TwoSum), so the final conversion to float32 rounds the
+    exact value once."""
+    a, b, c = (np.asarray(v, dtype=f32).astype(np.float64) for v in (a, b, c))
+    p = a * b
+    t = p + c
+    bb = t - p
+    err = (p - (t - bb)) + (c - bb)  # TwoSum: t + err == p + c exactly
+    with np.errstate(invalid="ignore", over="ignore"):
+        fix = np.isfinite(t) & (err != 0)
+        # round to odd: the truncation of the exact value, with its last bit forced to 1
+        toward_zero = np.where(np.sign(err) != np.sign(t), np.nextafter(t, 0.0), t)
+        bits = toward_zero.view(np.int64)
+        odd = (bits | 1).view(np.float64)
+        t = np.where(fix, odd, t)
+    return t.astype(f32)
+
+
+_EXP_LO, _EXP_HI = f32(-87.3365448), f32(88.8)
+_EXP_P = [f32(v) for v in (1.9875691500e-4, 1.3981999507e-3, 8.3334519073e-3, 4.1665795894e-2, 1.6666665459e-1,
+                           5.0000001201e-1)]
+
+
+def poly_exp(x0: np.ndarray) -> np.ndarray:
+    """exp8 (kernels_avx2.c:96-118): range reduction by n = floor(x log2e + 1/2) with ln2 in two parts,
+    the degree-7 polynomial, 2^n from the exponent bits (n = 128 as 2^127 * 2), 0 below the input
+    window, NaN passed through."""
+    x0 = np.asarray(x0, dtype=f32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        x = np.minimum(np.maximum(np.nan_to_num(x0, nan=_EXP_LO, posinf=_EXP_HI, neginf=_EXP_LO), _EXP_LO), _EXP_HI)
+        fx = np.floor(fma32(x, f32(1.44269504088896341), f32(0.5))).astype(f32)
+        x = fma32(-fx, f32(0.693359375), x)
+        x = fma32(-fx, f32(-2.12194440e-4), x)
+        y = np.full_like(x, _EXP_P[0])
+        for c in _EXP_P[1:]:
+            y = fma32(y, x, c)
+        y = fma32(y, (x * x).astype(f32), (x + f32(1)).astype(f32))
+        n = fx.astype(np.int32)
+        big = n > 127
+        n = np.where(big, n - 1, n)
+        scale = ((n + 127).astype(np.int32) << 23).view(f32)
+        r = (y * scale).astype(f32)
+        r = (r * np.where(big, f32(2), f32(1))).astype(f32)
+        r = np.where(x0 < _EXP_LO, f32(0), r)
+        return np.where(np.isnan(x0), x0, r).astype(f32)
+
+
+def _copysign_bits(mag, sgn):
+    return ((mag.view(np.uint32) | (np.asarray(sgn, f32).view(np.uint32) & np.uint32(0x80000000)))).view(f32)
+
+
+def poly_sigmoid(x):
+    """sigmoid8 (kernels_avx2.c:120-123): 1 / (1 + exp(0 - x))."""
+    x = np.asarray(x, dtype=f32)
+    with np.errstate(over="ignore", divide="ignore"):
+        return (f32(1) / (f32(1) + poly_exp((f32(0) - x).astype(f32)))).astype(f32)
+
+
+def poly_tanh(x):
+    """tanh8 (kernels_avx2.c:125-139): odd polynomial below |x| = 1/4, else (1 - e) / (1 + e) with
+    e = exp(-2|x|) and the sign of x."""
+    x = np.asarray(x, dtype=f32)
+    ax = np.abs(x)
+    with np.errstate(invalid="ignore", over="ignore"):
+        e = poly_exp((ax * f32(-2)).astype(f32))
+        big = _copysign_bits(((f32(1) - e) / (f32(1) + e)).astype(f32), x)
+        z = (x * x).astype(f32)
+        p = fma32(f32(0.021869489), z, f32(-0.053968254))
+        p = fma32(p, z, f32(0.133333333))
+        p = fma32(p, z, f32(-0.333333333))
+        p = fma32((p * z).astype(f32), x, x)
+    return np.where(ax < f32(0.25), p, big).astype(f32)
+
+
+def poly_erf(x):
+    """erf8 (kernels_avx2.c:148-159): 1 - poly(t) t exp(-x^2), t = 1 / (1 + p|x|), sign restored."""
+    x = np.asarray(x, dtype=f32)
+    ax = np.abs(x)
+    with np.errstate(invalid="ignore", over="ignore"):
+        t = (f32(1) / fma32(ax, f32(0.3275911), f32(1))).astype(f32)
+        p = fma32(f32(1.061405429), t, f32(-1.453152027))
+        p = fma32(p, t, f32(1.421413741))
+        p = fma32(p, t, f32(-0.284496736))
+        p = fma32(p, t, f32(0.254829592))
+        e = poly_exp((f32(0) - (ax * ax).astype(f32)).astype(f32))
+        r = fma32(-(p * t).astype(f32), e, f32(1))
+    return _copysign_bits(r, x)
+
+
+def unary_avx2(kind: str, x: np.ndarray):
+    """Forward and the derivative factors of the exp / tanh / erf activations as newch evaluates them on
+    its AVX2 tier (ops_elementwise.c:229-266 with kernels_avx2.c's exp_f32 / sigmoid_f32 / tanh_f32 /
+    erf_f32). Returns (y, dfun) where dfun(g) gives the backward contribution (ops_elementwise.c:289-338)."""
+    y, d = _unary_avx2(kind, np.asarray(x, dtype=f32))
+
+    def dfun(g):
+        with np.errstate(all="ignore"):
+            return d(np.asarray(g, dtype=f32))
+    return y, dfun
+
+
+def _unary_avx2(kind: str, x: np.ndarray):
+    with np.errstate(all="ignore"):
+        if kind == "exp":
+            y = poly_exp(x)
+            return y, lambda g: (g * y).astype(f32)
+        if kind == "sigmoid":
+            y = poly_sigmoid(x)
+            return y, lambda g: (g * y * (f32(1) - y)).astype(f32)
+        if kind == "tanh":
+            y = poly_tanh(x)
+            return y, lambda g: (g * (f32(1) - y * y)).astype(f32)
+        if kind == "silu":
+            t = poly_sigmoid(x)
+            return (t * x).astype(f32), lambda g: (g * t * (f32(1) + x * (f32(1) - t))).astype(f32)
+        if kind == "gelu":
+            t = poly_erf((SQRT1_2 * x).astype(f32))
+            t2 = poly_exp((f32(-0.5) * x * x).astype(f32))
+            y = (f32(0.5) * x * (f32(1) + t)).astype(f32)
+            return y, lambda g: (g * (f32(0.5) * (f32(1) + t) + x * INV_SQRT_2PI * t2)).astype(f32)
+        if kind == "gelu_tanh":
+            t = poly_tanh((SQRT_2_PI * (x + GELU_C * x * x * x)).astype(f32))
+            y = (f32(0.5) * x * (f32(1) + t)).astype(f32)
+
+            def d(g):
+                dt = (f32(1) - t * t) * SQRT_2_PI * (f32(1) + f32(3) * GELU_C * x * x)
+                return (g * (f32(0.5) * (f32(1) + t) + f32(0.5) * x * dt)).astype(f32)
+            return y, d
+    raise ValueError(kind)
+
+
 def unary(kind: str, x: np.ndarray, s: float = 0.0) -> np.ndarray:
     """Forward of the unary ops (ops_elementwise.c:229-266)."""
     x = x.astype(f32)
@@ -469,8 +606,10 @@ def quantize_rows(w):
 
 
 def gemm_s8_nt(a, b):
-    """C[i, j] = sum_k a[i, k] b[j, k] in exact integer arithmetic (kernels_ref.c:117-128)."""
-    return (a.astype(np.int64) @ b.astype(np.int64).T).astype(np.int32)
+    """C[i, j] = sum_k a[i, k] b[j, k] in exact integer arithmetic (kernels_ref.c:117-128). Evaluated as a
+    float64 product: every partial sum is an integer below 127 * 127 * K < 2^53, so the result is
+    exact in any summation order."""
+    return np.rint(a.astype(np.float64) @ b.astype(np.float64).T).astype(np.int64).astype(np.int32)
 
 
 def linear_int8(x, wq, ws, bias=None):

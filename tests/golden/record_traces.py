@@ -8,12 +8,14 @@ arguments, tensor pointers are replaced by handle numbers, host buffers by blobs
 inputs by their generator spec instead of their bytes), and scalar results (losses from
 ``nc_item``) and copied-out buffers are kept as golden values.
 
-Run here, where the reference package and its engine are available:
+Test-fixture tooling: run it on a machine where a newch checkout (its Python package and the
+engine built from its sources) is available:
 
-    make -C oracle
-    python newch_b200/workloads/record_traces.py --ref /root/reference --lib oracle/_ref/libnc_ref.so
+    make -C oracle REF=<newch checkout>
+    python tests/golden/record_traces.py --ref <newch checkout> [--lib oracle/_ref/libnc_ref.so] [names...]
 
-Output: ``newch_b200/workloads/<name>.json.gz`` (workload definitions for bench.py and the tests).
+Output: ``newch_b200/workloads/<name>.json.gz`` (the workload definitions bench.py, smoke() and the
+tests replay).
 """
 
 from __future__ import annotations
@@ -34,7 +36,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, str(HERE.parent.parent))
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
 
 from newch_b200 import synth  # noqa: E402
 
@@ -391,7 +394,7 @@ def cfg5_int8_mlp(nc, nn, F, rec, *, rows=8192, steps=2, seed=5, dims=(1024, 409
 
 
 CONFIGS = {
-    # full sizes
+    # full sizes (the five benchmark configurations)
     "cfg1": (cfg1_small_cnn, {}),
     "cfg2": (cfg2_two_block_cnn, {}),
     "cfg3": (cfg3_depthwise, {}),
@@ -433,9 +436,9 @@ def record(name: str, ref: Path, libpath: Path, out_dir: Path) -> Path:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
-    ap.add_argument("--lib", default=str(HERE.parent.parent / "oracle" / "_ref" / "libnc_ref.so"))
-    ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--ref", required=True, help="newch source checkout (its Python package is imported)")
+    ap.add_argument("--lib", default=str(REPO / "oracle" / "_ref" / "libnc_ref.so"))
+    ap.add_argument("--out", default=str(REPO / "newch_b200" / "workloads"))
     ap.add_argument("names", nargs="*", default=list(CONFIGS))
     args = ap.parse_args()
     import subprocess

@@ -261,6 +261,34 @@ def case_unary(e):
     return out
 
 
+TRANSCENDENTAL = ["sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh"]
+
+
+def case_transcendental(e):
+    """The activations built on exp / tanh / erf over their whole range: a dense sweep of [-12, 12],
+    both sides of every branch and clamp of newch's polynomial forms (|x| = 1/4 for tanh, the exp
+    input window [-87.34, 88.8] and the 2^128 scale step near ln(FLT_MAX)), denormal and signed
+    zero inputs, +-inf and NaN."""
+    sweep = np.linspace(-12.0, 12.0, 1201, dtype=np.float32)
+    edges = np.array([0.0, -0.0, 1e-40, -1e-40, 1e-30, -1e-30, 0.25, -0.25, np.nextafter(np.float32(0.25), 0),
+                      -np.nextafter(np.float32(0.25), 0), 0.2500001, 88.0, 88.37, 88.5, 88.72, 88.73, 88.8, 88.81,
+                      89.0, 100.0, -87.0, -87.33, -87.3365448, -87.34, -87.5, -88.0, -103.0, -104.0, -150.0,
+                      np.inf, -np.inf, np.nan, 1e30, -1e30, 44.0, -44.0, 9.0, -9.0, 13.2, -13.2, 3.0, -3.0],
+                     dtype=np.float32)
+    base = np.concatenate([sweep, edges]).astype(np.float32)
+    out = {"x": base}
+    G = seeded(172, base.shape)
+    out["G"] = G
+    for kind in TRANSCENDENTAL:
+        x = e.param(base)
+        y = e.check(_unary_call(e, kind, x))
+        out[f"{kind}_y"] = e.np(y)
+        e.backward_with(y, G)
+        out[f"{kind}_dx"] = e.grad(x)
+        e.step_end()
+    return out
+
+
 def case_binary_broadcast(e):
     out = {}
     A, B = seeded(180, (3, 1, 4)), np.abs(seeded(181, (5, 1))) + 0.5
@@ -412,8 +440,8 @@ def case_adamw(e):
 CASES = {name[5:]: fn for name, fn in globals().items() if name.startswith("case_")}
 
 
-def run_case(which: str, name: str) -> dict:
-    with Eng(which, seed=1) as e:
+def run_case(which: str, name: str, force_reference: bool = False) -> dict:
+    with Eng(which, seed=1, force_reference=int(force_reference)) as e:
         out = CASES[name](e)
         assert e.ok(), e.err()
         return {k: np.asarray(v) for k, v in out.items() if v is not None}

@@ -1,10 +1,11 @@
 """Op parity on the B200: every case of tests/opcases.py through the C ABI against the reference
 engine's golden vectors (tests/golden/ops.npz).
 
-Tolerances: normwise max|got - ref| / max|ref| <= 1e-5 for float results (the FP32 FFMA GEMM mode,
-ulp-level differences from summation order and from the reference's polynomial exp/tanh/erf), and
-bit-exact equality for integer results, argmax indices, the RNG stream, dropout masks, int8
-quantization and accumulators, and pure data movement."""
+Tolerances: normwise max|got - ref| / max|ref| <= 1e-5 for float results (ulp-level differences from
+summation order), and bit-exact equality for integer results, argmax indices, the RNG stream, dropout
+masks, int8 quantization and accumulators, pure data movement, and the activations built on exp /
+tanh / erf (the engine evaluates newch's own AVX2-tier polynomials, which is what the reference
+engine runs on an AVX2+FMA host such as the one the golden vectors came from)."""
 
 from __future__ import annotations
 
@@ -38,7 +39,10 @@ EXACT = {
     "binary_broadcast": {"add_y", "sub_y", "mul_y", "div_y"},
     "unary": {"relu_y", "neg_y", "scale_y", "add_scalar_y", "leaky_relu_y", "relu6_y", "hardsigmoid_y",
               "hardswish_y", "relu_dx", "neg_dx", "scale_dx", "add_scalar_dx", "leaky_relu_dx", "relu6_dx",
-              "hardsigmoid_dx", "hardswish_dx"},
+              "hardsigmoid_dx", "hardswish_dx"}
+    | {f"{k}_{o}" for k in ("sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh") for o in ("y", "dx")},
+    "transcendental": {f"{k}_{o}" for k in ("sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh")
+                       for o in ("y", "dx")},
 }
 TOL = 1e-5
 
@@ -57,3 +61,20 @@ def test_op_matches_reference(case):
         else:
             err = rel_err(got, ref)
             assert err <= TOL, f"{case}/{k}: rel err {err:.3g}"
+
+
+@pytest.mark.parametrize("how", ["env", "force_reference"])
+def test_libm_math_mode(how, monkeypatch):
+    """NC_MATH=libm (or force_reference, as newch selects its reference tier) evaluates exp / tanh / erf
+    with CUDA's libm, as newch's reference tier calls the C library: within 1e-5 of the AVX2-tier
+    goldens on the sweep, and the same special values (+-inf, NaN, 0) at the edges."""
+    if how == "env":
+        monkeypatch.setenv("NC_MATH", "libm")
+    out = run_case("b200", "transcendental", force_reference=(how == "force_reference"))
+    x = GOLD["transcendental/x"]
+    finite = np.isfinite(x) & (np.abs(x) < 80)
+    for k in [k for k in out if k.endswith("_y") or k.endswith("_dx")]:
+        ref, got = GOLD[f"transcendental/{k}"], out[k]
+        assert rel_err(got[finite], ref[finite]) <= TOL, k
+        special = ~finite & np.isfinite(ref)
+        assert np.allclose(got[special], ref[special], rtol=1e-5, atol=1e-30), k

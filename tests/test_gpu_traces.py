@@ -1,16 +1,25 @@
 """End-to-end parity of the five benchmark configurations: the recorded newch call sequences replayed
 on the B200 engine and on the reference engine (CPU), step by step.
 
-Checked: every nc_item result (the per-step losses, BatchNorm's num_batches_tracked), and the copied-out
-results after training (final parameters, or the int8 model's logits). Losses must agree to 1e-5
-relative on the CUDA-core GEMM path (NC_GEMM=ffma) and to 1e-3 relative on the tensor-core paths
-(3xTF32, the default, and TF32), whose contractions round differently from the reference's loops;
-in TF32 mode only the first loss (identical weights) is held to 1e-3, later ones to 1e-2.
-Final parameters after Adam are compared normwise against the reference with a
-tolerance for Adam's normalisation: for a parameter whose true gradient is zero (a conv bias in front
-of BatchNorm, the key bias of attention), the update lr * m / sqrt(v) is the sign of rounding noise and
-can differ by up to 2 * lr per step between any two correct implementations; every other parameter
-must agree to 1e-3 relative after the three recorded steps.
+Checked, per configuration and GEMM mode:
+- every nc_item result (the per-step losses, BatchNorm's num_batches_tracked);
+- every parameter's gradient after every backward pass;
+- every parameter after the recorded optimizer steps;
+- for the int8 model (config 5): every layer's output, the quantized weights and their scales, the
+  GELU outputs and the logits bit for bit, and each layer's int32 accumulators against the oracle's
+  exact integer product of the same quantized operands.
+
+Tolerances (normwise per tensor, max|got - ref| / max|ref|): the CUDA-core GEMM path (NC_GEMM=ffma)
+1e-5; the default tensor-core path (3xTF32) 1e-3 (it measures ~1e-6). The plain TF32 mode
+(NC_GEMM=tf32) is an opt-in speed mode whose GEMMs round to 10-bit mantissas: its gradients and
+parameters are held to 2e-2, its first loss to 1e-3 and later losses to 1e-2.
+
+Adam normalises each gradient element by its own magnitude, so an element whose true gradient is zero
+is moved by lr * sign(rounding noise), which two correct implementations need not share. Such elements
+are exempt by name: the bias of a convolution followed by BatchNorm (BatchNorm removes any per-channel
+shift, so the bias gets no gradient) and the key third of attention's packed input-projection bias
+(softmax is invariant to the per-row shift q . b_k). The test asserts that their reference gradients
+are indeed at rounding level before exempting them.
 """
 
 from __future__ import annotations
@@ -18,24 +27,17 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from nchelp import REF_LIB, capi, rel_err
+from nchelp import REF_LIB, capi
 from newch_b200 import replay
+import ncoracle as O
 
 pytestmark = pytest.mark.gpu
-LR = {"cfg1": 1e-3, "cfg2": 1e-3, "cfg2_stream": 1e-3, "cfg3": 1e-3, "cfg4": 3e-4}
-
-
-def run(lib, name):
-    t = replay.Trace(name)
-    r = replay.Replayer(lib, t)
-    r.run_all()
-    return t, r
-
 
 LOSS_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 1e-3}
-# TF32 rounding (rel ~1e-3 per GEMM) moves the weights after the first update; on these short,
-# high-learning-rate runs over random labels the losses that follow drift apart by up to ~0.5%.
-TF32_DRIFT = 1e-2
+TF32_DRIFT = 1e-2  # later TF32 losses come from weights that already differ by TF32 updates
+TENSOR_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 2e-2}
+NOISE = 1e-5  # a reference gradient below this fraction of the step's largest gradient is rounding noise
+INT8_CALLS = ("nc_from_data", "nc_quantize_rows", "nc_add_scalar", "nc_linear_int8", "nc_gelu")
 
 
 @pytest.fixture(params=["ffma", "3xtf32", "tf32"])
@@ -44,33 +46,141 @@ def mode(request, monkeypatch):
     return request.param
 
 
-def compare(name, mode="ffma"):
-    ref = capi.load(REF_LIB)
-    gpu = capi.load_b200()
-    t, rg = run(gpu, name)
-    _, rr = run(ref, name)
-    assert gpu.nc_ok(rg.ctx), gpu.nc_error(rg.ctx)
-    gi, ri = [v for _, v in rg.items], [v for _, v in rr.items]
+def run(lib, t, **kw):
+    r = replay.Replayer(lib, t, **kw)
+    r.run_all()
+    return r
+
+
+def param_shapes(r):
+    lib = r.lib
+    out = []
+    for p in r._param_handles:
+        h = r.h[p]
+        nd = lib.nc_ndim(h)
+        shp = lib.nc_shape(h)
+        out.append(tuple(int(shp[k]) for k in range(nd)))
+    return out
+
+
+def zero_gradient_elements(shapes):
+    """{parameter index: (description, element slice)} of the parameters named in the module docstring,
+    found from the parameter list's structure: a 1-D convolution bias (after a 4-D weight) followed by a
+    BatchNorm weight of the same length; attention's packed [3E] input-projection bias between its
+    [3E, E] weight and the [E, E] output projection, of which elements [E, 2E) are the key bias."""
+    out = {}
+    for i, s in enumerate(shapes):
+        if len(s) != 1 or i == 0:
+            continue
+        prev = shapes[i - 1]
+        if len(prev) == 4 and prev[0] == s[0] and i + 1 < len(shapes) and shapes[i + 1] == s:
+            out[i] = ("conv bias in front of BatchNorm", slice(0, s[0]))
+        elif (len(prev) == 2 and prev[0] == s[0] == 3 * prev[1] and i + 1 < len(shapes)
+              and shapes[i + 1] == (prev[1], prev[1])):
+            E = prev[1]
+            out[i] = ("attention key bias", slice(E, 2 * E))
+    return out
+
+
+def normwise(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30)) if b.size else 0.0
+
+
+def check_losses(mode, gi, ri):
     assert len(gi) == len(ri)
     first_loss = next((k for k, b in enumerate(ri) if b != round(b)), len(ri))
     for k, (a, b) in enumerate(zip(gi, ri)):
-        tol = LOSS_TOL[mode]
-        if mode == "tf32" and k > first_loss:
-            tol = TF32_DRIFT  # later losses come from weights that already differ by TF32 updates
+        tol = TF32_DRIFT if (mode == "tf32" and k > first_loss) else LOSS_TOL[mode]
         assert a == pytest.approx(b, rel=tol, abs=1e-6), (mode, k, gi, ri)
-    assert len(rg.outputs) == len(rr.outputs)
-    base = name.replace("_small", "")
-    steps = len(t.steps())
-    for (_, a), (_, b) in zip(rg.outputs, rr.outputs):
+
+
+def check_gradients(name, mode, rg, rr, exempt):
+    tol = TENSOR_TOL[mode]
+    assert len(rg.grads) == len(rr.grads) and rg.grads, "backward passes differ in number"
+    worst = 0.0
+    for step, ((_, gs), (_, rs)) in enumerate(zip(rg.grads, rr.grads)):
+        scale = max((float(np.max(np.abs(np.frombuffer(b, np.float32)))) for b in rs if b), default=0.0)
+        for k, (a, b) in enumerate(zip(gs, rs)):
+            assert (a is None) == (b is None), f"{name} step {step}: parameter {k} gradient presence differs"
+            if a is None:
+                continue
+            x, y = np.frombuffer(a, np.float32), np.frombuffer(b, np.float32)
+            if k in exempt:
+                sl = exempt[k][1]
+                assert float(np.max(np.abs(y[sl]))) <= NOISE * scale, f"{name}: exempt {exempt[k][0]} has a gradient"
+                keep = np.ones(y.size, bool)
+                keep[sl] = False
+                x, y = x[keep], y[keep]
+                if y.size == 0:
+                    continue
+            err = normwise(x, y)
+            worst = max(worst, err)
+            assert err <= tol, f"{name} ({mode}) step {step}: gradient of parameter {k} differs by {err:.3g}"
+    return worst
+
+
+def check_parameters(name, mode, got, ref, exempt, lr, steps):
+    tol = TENSOR_TOL[mode]
+    worst = 0.0
+    for k, ((_, a), (_, b)) in enumerate(zip(got, ref)):
         x, y = np.frombuffer(a, np.float32), np.frombuffer(b, np.float32)
-        if base == "cfg5":
-            assert rel_err(x, y) < 2e-2  # GELU between int8 layers re-quantizes: see test_gpu_engine int8
+        if k in exempt:
+            sl = exempt[k][1]
+            # the exempt elements move by at most lr per step in either implementation
+            assert np.all(np.abs(x[sl].astype(np.float64) - y[sl]) <= 2.0 * lr * steps + 1e-6)
+            keep = np.ones(y.size, bool)
+            keep[sl] = False
+            x, y = x[keep], y[keep]
+            if y.size == 0:
+                continue
+        err = normwise(x, y)
+        worst = max(worst, err)
+        assert err <= tol, f"{name} ({mode}): parameter {k} after training differs by {err:.3g}"
+    return worst
+
+
+def check_int8_chain(rg, rr, logits_g, logits_r):
+    assert len(rg.captured) == len(rr.captured)
+    for (ig, ng, ag, hg), (ir, nr, ar, hr) in zip(rg.captured, rr.captured):
+        assert (ig, ng, hg) == (ir, nr, hr)
+        assert rg.tensors[hg] == rr.tensors[hr], f"call {ig} {ng}: output differs from the reference"
+    for a, b in zip(logits_g, logits_r):
+        assert a == b, "logits differ from the reference"
+    # int32 accumulators: the oracle's exact product of the reference's quantized operands, rescaled,
+    # reproduces the engine's layer outputs bit for bit
+    T = rg.tensors
+    for i, name, args, ret in rg.captured:
+        if name != "nc_linear_int8":
             continue
-        err = np.abs(x.astype(np.float64) - y)
-        ok = err <= 1e-3 * np.max(np.abs(y)) + 2.0 * LR[base] * steps
-        assert ok.all(), f"{name}: parameter differs beyond Adam noise: {err.max():.3g}"
-        if mode == "ffma":  # tensor-core gradients (rel 1e-6..1e-3) flip near-zero-gradient Adam updates
-            assert rel_err(x, y) < 0.1
+        wq = np.frombuffer(T[args[1]], np.int8)
+        ws = np.frombuffer(T[args[2]], np.float32)
+        out = np.frombuffer(T[ret], np.float32).reshape(-1, ws.size)
+        x = np.frombuffer(T[args[0]], np.float32).reshape(out.shape[0], -1)
+        b = np.frombuffer(T[args[3]], np.float32) if args[3] is not None else None
+        y, acc, _, _ = O.linear_int8(x, wq.reshape(ws.size, -1), ws, b)
+        assert np.array_equal(y, out), f"call {i}: the layer output is not the rescaled exact accumulator"
+
+
+def compare(name, mode="ffma"):
+    ref = capi.load(REF_LIB)
+    gpu = capi.load_b200()
+    t = replay.Trace(name)
+    base = name.replace("_small", "")
+    int8 = base == "cfg5"
+    kw = {"capture": INT8_CALLS} if int8 else {"grads": True}
+    rg = run(gpu, t, **kw)
+    rr = run(ref, t, **kw)
+    assert gpu.nc_ok(rg.ctx), gpu.nc_error(rg.ctx)
+    check_losses(mode, [v for _, v in rg.items], [v for _, v in rr.items])
+    assert len(rg.outputs) == len(rr.outputs)
+    if int8:
+        check_int8_chain(rg, rr, [b for _, b in rg.outputs], [b for _, b in rr.outputs])
+    else:
+        exempt = zero_gradient_elements(param_shapes(rr))
+        check_gradients(name, mode, rg, rr, exempt)
+        lr = {"cfg4": 3e-4}.get(base.split("_")[0], 1e-3)
+        check_parameters(name, mode, rg.outputs, rr.outputs, exempt, lr, len(t.steps()))
     gpu.nc_free_ctx(rg.ctx)
     ref.nc_free_ctx(rr.ctx)
 
@@ -89,7 +199,8 @@ def test_full_size_against_recorded_losses(monkeypatch):
     """The B200 replay of config 2 reproduces the losses newch itself logged when the trace was made."""
     monkeypatch.setenv("NC_GEMM", "ffma")
     gpu = capi.load_b200()
-    t, r = run(gpu, "cfg2")
+    t = replay.Trace("cfg2")
+    r = run(gpu, t)
     got = [v for _, v in r.items]
     assert got == pytest.approx(t.golden_items(), rel=1e-5, abs=1e-6)
     gpu.nc_free_ctx(r.ctx)

@@ -172,3 +172,15 @@ def test_known_answers_from_reference_tests():
                                           np.zeros(1, np.float32), np.ones(1, np.float32), 1.0, 0.0)
     assert abs(rm[0] - 3.0) < 1e-6 and abs(rv[0] - 14.0 / 3.0) < 1e-5
     assert abs(yb[3, 0] - 3.0 / np.sqrt(3.5)) < 1e-5
+
+
+@pytest.mark.parametrize("kind", ["sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh"])
+@pytest.mark.parametrize("case", ["unary", "transcendental"])
+def test_avx2_transcendentals_bit_exact(case, kind):
+    """The restated AVX2-tier exp / sigmoid / tanh / erf forms reproduce the reference engine's outputs
+    and gradients bit for bit, over the dense sweep and the edge values (clamps, overflow, denormals,
+    signed zeros, infinities, NaN)."""
+    x = g(case, "x")
+    y, d = O.unary_avx2(kind, x)
+    assert np.array_equal(y, g(case, f"{kind}_y"), equal_nan=True)
+    assert np.array_equal(d(g(case, "G")), g(case, f"{kind}_dx"), equal_nan=True)
