@@ -2,17 +2,24 @@
 """Training-step throughput of the B200 newch engine (train samples/sec), with its roofline and the
 reference engine's multithreaded CPU path timed on the same host.
 
-The workload is a recorded nc.h call sequence of the unchanged newch Python package (see
-newch_b200/workloads/record_traces.py): by default configuration 2 of the baseline, the two-block
-CNN trained through compile/fit with AdamW at batch 512 per GPU. One timed step replays exactly the
-calls newch's fit() makes for one batch (forward, cross entropy, zero_grad, backward, optimizer step,
-loss.item(), step_end) through the C ABI.
+The workload is a recorded nc.h call sequence of the unchanged newch Python package (recorded by
+tests/golden/record_traces.py): by default configuration 2, the two-block CNN trained through
+compile/fit with AdamW at batch 512 per GPU. One timed step replays exactly the calls newch's fit()
+makes for one batch (forward, cross entropy, zero_grad, backward, optimizer step, loss.item(),
+step_end) through the C ABI.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config cfg2]
+                  [--extra cfg1,cfg3,cfg4,cfg5 | --extra none]
+
+The JSON line's headline (value, e2e, roofline, cpu_baseline) is the --config workload. Under
+"configs" the same line carries shorter measurements of the other configurations (--extra): their
+samples/s (rows/s for the int8 inference of config 5), host wall-clock end-to-end rate, dominant
+kernel against its roof and, at N=1, the reference engine's CPU rate on a bounded sample.
 
 Multi-GPU: launched by torch.distributed.run, one process per GPU; each rank trains on its own data
 shard and the engine all-reduces the flat gradient buffer over NCCL before every update (weak
-scaling). Rank 0 prints one JSON line.
+scaling; config 5 is batch-sharded inference, config 1 runs at N=1 only). Rank 0 prints one JSON
+line.
 """
 
 from __future__ import annotations
@@ -47,6 +54,20 @@ DESC = {
     "cfg5": "int8 quantize_ MLP inference, 8192 rows",
 }
 E2E_TRACE = {"cfg2": "cfg2_stream"}
+UNIT = {"cfg4": "sequences/s", "cfg5": "rows/s"}
+DATA = {"cfg1": "synthetic (seeded uint8 images [B,1,28,28], 10 uniform labels)",
+        "cfg2": "synthetic (seeded, MNIST-shaped)", "cfg3": "synthetic (seeded N(0,1) [B,3,64,64], 100 labels)",
+        "cfg4": "synthetic (seeded token ids uniform in [0,96), T=128)",
+        "cfg5": "synthetic (seeded N(0,1) activations [8192,1024])"}
+SETUP_DRIVER = "recorded newch call sequence replayed through the nc.h C ABI"
+L2_NOTE = "flushed between timed steps (256 MiB write, outside the timed events)"
+
+
+def config_dict(cfg: str, world: int) -> dict:
+    """The workload description both arms report (identical keys and values)."""
+    b = BATCH.get(cfg, 1)
+    return {"workload": f"{cfg}: {DESC.get(cfg, cfg)}", "global_batch": b * world, "per_gpu_batch": b,
+            "parallelism": f"dp{world}"}
 
 
 def dist_env():
@@ -168,6 +189,23 @@ def timed_steps(run: Run, k: int, stream, flush):
     return sum(a.elapsed_time(b) for a, b in evs) / 1e3
 
 
+def wall_steps(run: Run, k: int, stream, flush):
+    """Host wall-clock time of k steps through the public calls, each step timed from its first call to
+    the device finishing its work (the step's loss read waits for it; a final synchronize covers calls
+    after it), the L2 flush between steps outside the timed spans."""
+    import torch
+    total = 0.0
+    for _ in range(k):
+        t0 = time.perf_counter()
+        run.one()
+        run.lib.nc_ext_synchronize(run.ctx)
+        total += time.perf_counter() - t0
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        torch.cuda.synchronize()
+    return total
+
+
 def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     lib, ctx = run.lib, run.ctx
     lib.nc_ext_timing(ctx, 1)
@@ -206,7 +244,8 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
 
 
 def cpu_reference(trace_name: str, budget_s: float, max_steps: int, warmup: int = 1):
-    """The reference engine (its multithreaded AVX2 tier, all host cores) replaying the same trace."""
+    """The reference engine (its multithreaded AVX2 tier, all host cores) replaying the same trace;
+    returns the step times, the thread count and the kernel tier, and frees its context."""
     lib = capi.load(REF_LIB)
     tr = replay.Trace(trace_name)
     rep = replay.Replayer(lib, tr)
@@ -224,7 +263,82 @@ def cpu_reference(trace_name: str, budget_s: float, max_steps: int, warmup: int 
     ctx = rep.ctx
     cores = lib.nc_num_threads(ctx)
     backend = lib.nc_kernel_backend(ctx).decode()
+    lib.nc_free_ctx(ctx)
     return times, cores, backend
+
+
+def max_over_ranks(pg, secs: float) -> float:
+    if not pg:
+        return secs
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([secs], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+    return float(t[0])
+
+
+def measure(lib, cfg: str, rank: int, world: int, pg, local: int, steps: int, warmup: int, flush, *,
+            extras: bool = True, cpu_budget_s: float = 20.0, cpu_steps: int = 30, clocks=None) -> dict:
+    """One workload on this rank's GPU: device-timed steps (max over ranks), then the wall-clock
+    end-to-end rate, the dominant kernel against its roof and (rank 0 at N=1) the CPU reference."""
+    import torch
+    import torch.distributed as dist
+    batch = BATCH.get(cfg, 1)
+    run = Run(lib, cfg, rank, world, pg)
+    stream = torch.cuda.ExternalStream(lib.nc_ext_stream(run.ctx), device=torch.device("cuda", local))
+    for _ in range(warmup):
+        run.one()
+    lib.nc_ext_synchronize(run.ctx)
+    if pg:
+        dist.barrier(pg)
+    torch.cuda.synchronize()
+    l0 = lib.nc_ext_launch_count(run.ctx)
+    if clocks is not None:  # nvidia-smi samples span the timed steps only
+        with clocks:
+            secs = timed_steps(run, steps, stream, flush)
+    else:
+        secs = timed_steps(run, steps, stream, flush)
+    launches = (lib.nc_ext_launch_count(run.ctx) - l0) // max(steps, 1)
+    if pg:
+        dist.barrier(pg)
+    secs = max_over_ranks(pg, secs)
+    if not lib.nc_ok(run.ctx):
+        raise SystemExit(f"{cfg}: engine error: {lib.nc_error(run.ctx).decode()}")
+    res = {"value": round(batch * world * steps / secs, 3), "unit": UNIT.get(cfg, "samples/s"),
+           "ms_per_step": round(1e3 * secs / steps, 4), "steps": steps, "warmup": warmup,
+           "gpu_launches": int(launches), "gemm": lib.nc_ext_gemm_mode(run.ctx).decode(),
+           "config": config_dict(cfg, world)}
+    if extras:
+        et = E2E_TRACE.get(cfg, cfg)
+        erun = run if et == cfg else Run(lib, et, rank, world, pg, pinned=True)
+        estream = torch.cuda.ExternalStream(lib.nc_ext_stream(erun.ctx), device=torch.device("cuda", local))
+        for _ in range(max(warmup, 3)):
+            erun.one()
+        ek = max(10, min(steps, 200))
+        if pg:
+            dist.barrier(pg)
+        ewall = max_over_ranks(pg, wall_steps(erun, ek, estream, flush))
+        edev = max_over_ranks(pg, timed_steps(erun, ek, estream, flush))
+        h2d, d2h = step_io_bytes(erun.trace, *erun.step)
+        res["e2e"] = {"value": round(batch * world * ek / ewall, 3), "unit": res["unit"], "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h, "trace": et, "steps": ek,
+                      "timing": "host wall clock around each step's public calls, to the device finishing",
+                      "value_device_events": round(batch * world * ek / edev, 3)}
+        if erun is not run:
+            lib.nc_free_ctx(erun.ctx)
+        # every rank steps (each step all-reduces gradients); rank 0 reports its kernel table
+        res["roofline"] = roofline(run, load_peaks())
+        res["cpu_baseline"] = None
+        if rank == 0 and world == 1 and REF_LIB.exists():
+            times, cores, backend = cpu_reference(cfg, budget_s=cpu_budget_s, max_steps=cpu_steps)
+            res["cpu_baseline"] = {
+                "value": round(batch * len(times) / sum(times), 3), "unit": res["unit"], "cores": cores,
+                "kind": "reference",
+                "sample": f"{len(times)} steps of {cfg} (median {1e3 * statistics.median(times):.1f} ms), "
+                          f"newch engine {backend} tier built from its sources, same recorded calls"}
+    lib.nc_ext_synchronize(run.ctx)
+    lib.nc_free_ctx(run.ctx)
+    return res
 
 
 def main() -> int:
@@ -234,11 +348,16 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg2")
-    ap.add_argument("--no-extras", action="store_true", help="skip e2e, roofline and CPU baseline")
+    ap.add_argument("--extra", default="cfg1,cfg3,cfg4,cfg5",
+                    help="other configurations measured briefly into the line's 'configs' ('none': skip)")
+    ap.add_argument("--no-extras", action="store_true", help="skip e2e, roofline, CPU baseline and --extra")
     args = ap.parse_args()
     rank, world, local = dist_env()
     cfg = args.config
     batch = BATCH.get(cfg, 1)
+    extra = [] if args.no_extras or args.extra == "none" else [c for c in args.extra.split(",") if c and c != cfg]
+    if world > 1:
+        extra = [c for c in extra if c != "cfg1"]  # config 1 is a single-GPU configuration
 
     if args.impl == "reference":
         if rank != 0:
@@ -250,15 +369,16 @@ def main() -> int:
                                                warmup=max(args.warmup, 1))
         t = sum(times)
         value = batch * len(times) / t
-        out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "samples/s", "n_gpus": 0,
-               "steps": len(times), "warmup": args.warmup, "ms_per_step": round(1e3 * t / len(times), 3),
+        out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT.get(cfg, "samples/s"),
+               "n_gpus": world, "steps": len(times), "warmup": args.warmup, "ms_per_step": round(1e3 * t / len(times), 3),
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-               "data": "synthetic (seeded, MNIST-shaped)",
-               "config": {"workload": f"{cfg}: {DESC.get(cfg, cfg)}", "global_batch": batch, "per_gpu_batch": batch},
-               "cpu_baseline": {"value": round(value, 3), "unit": "samples/s", "cores": cores, "kind": "reference",
-                                "sample": f"{len(times)} {cfg} steps, newch engine ({backend} tier) built from its "
-                                          f"sources, same recorded calls"},
-               "e2e": {"value": round(value, 3), "unit": "samples/s", "h2d_bytes_per_step": 0,
+               "data": DATA.get(cfg, "synthetic"), "config": config_dict(cfg, world),
+               "setup": {"driver": SETUP_DRIVER, "engine": f"newch reference engine, {backend} tier, {cores} threads"},
+               "cpu_baseline": {"value": round(value, 3), "unit": UNIT.get(cfg, "samples/s"), "cores": cores,
+                                "kind": "reference",
+                                "sample": f"{len(times)} {cfg} steps of {batch} samples on one host process, newch "
+                                          f"engine ({backend} tier) built from its sources, same recorded calls"},
+               "e2e": {"value": round(value, 3), "unit": UNIT.get(cfg, "samples/s"), "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
         return 0
@@ -275,74 +395,29 @@ def main() -> int:
     lib = capi.load_b200()
     if lib.nc_ext_device_count() < 1:
         raise SystemExit("no CUDA device")
-
-    run = Run(lib, cfg, rank, world, pg)
-    stream = torch.cuda.ExternalStream(lib.nc_ext_stream(run.ctx), device=torch.device("cuda", local))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
-    for _ in range(args.warmup):
-        run.one()
-    lib.nc_ext_synchronize(run.ctx)
-    if pg:
-        dist.barrier(pg)
-    torch.cuda.synchronize()
-    l0 = lib.nc_ext_launch_count(run.ctx)
-    with Clocks(local) as clk:
-        secs = timed_steps(run, args.steps, stream, flush)
-    launches = (lib.nc_ext_launch_count(run.ctx) - l0) // max(args.steps, 1)
-    if pg:
-        dist.barrier(pg)
-        t = torch.tensor([secs], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
-        secs = float(t[0])
-    if not lib.nc_ok(run.ctx):
-        raise SystemExit(f"engine error: {lib.nc_error(run.ctx).decode()}")
-    value = batch * world * args.steps / secs
 
-    e2e = None
-    rl = None
-    cpu = None
-    if not args.no_extras:
-        et = E2E_TRACE.get(cfg, cfg)
-        erun = Run(lib, et, rank, world, pg, pinned=True)
-        estream = torch.cuda.ExternalStream(lib.nc_ext_stream(erun.ctx), device=torch.device("cuda", local))
-        for _ in range(max(args.warmup, 3)):
-            erun.one()
-        ek = max(10, min(args.steps, 200))
-        if pg:
-            dist.barrier(pg)
-        esecs = timed_steps(erun, ek, estream, flush)
-        if pg:
-            t = torch.tensor([esecs], dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
-            esecs = float(t[0])
-        h2d, d2h = step_io_bytes(erun.trace, *erun.step)
-        e2e = {"value": round(batch * world * ek / esecs, 3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "trace": et, "steps": ek}
-        # every rank steps (each step all-reduces gradients); rank 0 reports its kernel table
-        rl = roofline(run, load_peaks())
-        if rank == 0:
-            if world == 1 and REF_LIB.exists():
-                times, cores, backend = cpu_reference(cfg, budget_s=20.0, max_steps=30)
-                cpu = {"value": round(batch * len(times) / sum(times), 3), "unit": "samples/s", "cores": cores,
-                       "kind": "reference",
-                       "sample": f"{len(times)} steps of {cfg} (median {1e3 * statistics.median(times):.1f} ms), "
-                                 f"newch engine {backend} tier built from its sources, same recorded calls"}
+    clk = Clocks(local)
+    head = measure(lib, cfg, rank, world, pg, local, args.steps, args.warmup, flush, extras=not args.no_extras,
+                   clocks=clk)
+    others = {}
+    for c in extra:
+        k = max(3, min(args.steps, {"cfg1": 50, "cfg5": 10}.get(c, 10)))
+        others[c] = measure(lib, c, rank, world, pg, local, k, max(3, min(args.warmup, 5)), flush,
+                            cpu_budget_s={"cfg1": 5.0}.get(c, 12.0), cpu_steps={"cfg1": 30}.get(c, 3))
     if rank == 0:
-        out = {"metric": METRIC, "value": round(value, 3), "unit": "samples/s", "n_gpus": world, "steps": args.steps,
-               "warmup": args.warmup, "ms_per_step": round(1e3 * secs / args.steps, 4), "higher_is_better": True,
-               "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, MNIST-shaped)",
-               "config": {"workload": f"{cfg}: {DESC.get(cfg, cfg)}", "global_batch": batch * world,
-                          "per_gpu_batch": batch, "parallelism": f"dp{world}",
-                          "gemm": lib.nc_ext_gemm_mode(run.ctx).decode(),
-                          "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
-                          "driver": "recorded newch fit() call sequence replayed through the nc.h C ABI"},
-               "gpu_launches": int(launches), "clocks": clk.summary(), "e2e": e2e, "roofline": rl,
-               "cpu_baseline": cpu}
+        out = {"metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA.get(cfg, "synthetic"),
+               "config": config_dict(cfg, world),
+               "setup": {"gemm": head["gemm"], "l2": L2_NOTE, "driver": SETUP_DRIVER},
+               "gpu_launches": head["gpu_launches"], "clocks": clk.summary(), "e2e": head.get("e2e"),
+               "roofline": head.get("roofline"), "cpu_baseline": head.get("cpu_baseline"), "configs": others}
         print(json.dumps(out), flush=True)
     if pg:
         dist.barrier(pg)
         dist.destroy_process_group()
-    os._exit(0)  # engine contexts go with the process
+    return 0
 
 
 if __name__ == "__main__":

@@ -36,6 +36,15 @@ NC_API int nc_ext_nccl_unique_id(void *buf, int cap);
  * Returns NC_OK or an error status. */
 NC_API int nc_ext_dp_init(nc_ctx *ctx, int rank, int world, const void *id, int id_len);
 NC_API int nc_ext_dp_world(const nc_ctx *ctx);
+/* Dropout streams of a data-parallel group that reproduce newch's gradient accumulation over the
+ * ranks' batches (rank r's step draws what newch draws for the r-th micro-batch of an accumulated
+ * step): every step of every rank takes at most `draws_per_step` random numbers, rank r starts r
+ * strides into each step's span of world * draws_per_step draws, and nc_step_end moves it to its
+ * place in the next span. Call after nc_ext_dp_init, at the point training starts. 0 turns the
+ * interleaving off. Returns NC_OK or NC_ERR_ARG. */
+NC_API int nc_ext_dp_rng_stride(nc_ctx *ctx, int64_t draws_per_step);
+/* Random numbers taken from the context's stream since it was seeded. */
+NC_API int64_t nc_ext_rng_position(const nc_ctx *ctx);
 
 /* The cudaStream_t every kernel of this context runs on. */
 NC_API void *nc_ext_stream(nc_ctx *ctx);

@@ -165,6 +165,8 @@ EXT_SIGNATURES: dict = {
     "nc_ext_nccl_unique_id": (c_int, [c_void_p, c_int]),
     "nc_ext_dp_init": (c_int, [P, c_int, c_int, c_void_p, c_int]),
     "nc_ext_dp_world": (c_int, [P]),
+    "nc_ext_dp_rng_stride": (c_int, [P, c_int64]),
+    "nc_ext_rng_position": (c_int64, [P]),
     "nc_ext_stream": (c_void_p, [P]),
     "nc_ext_timing": (c_int, [P, c_int]),
     "nc_ext_kernel_time": (c_int, [P, c_char_p, POINTER(ctypes.c_double), POINTER(c_int64)]),

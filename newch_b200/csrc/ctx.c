@@ -36,6 +36,7 @@ int nc__cuda_ok(nc_ctx *ctx, int err, const char *what) {
 
 int nc__sync(nc_ctx *ctx) {
     if (!ctx->device_ok) return 0;
+    nc__dp_join(ctx); /* gradient reduces on the communication stream finish first */
     cudaError_t e = cudaStreamSynchronize((cudaStream_t)ctx->dev.stream);
     if (!nc__cuda_ok(ctx, e, "stream synchronize")) return 0;
     int code = *(volatile int *)ctx->dev.status_host;
@@ -424,6 +425,7 @@ nc_ctx *nc_init(const nc_config *cfg) {
 void nc_manual_seed(nc_ctx *ctx, uint64_t seed) {
     uint64_t s = seed ? seed : 0x6E63u;
     for (int i = 0; i < 4; i++) ctx->rng[i] = splitmix64(&s);
+    ctx->rng_count = ctx->rng_step_start = 0;
 }
 
 void nc__dp_free(nc_ctx *ctx); /* dp.c */
@@ -463,6 +465,8 @@ void nc_free_ctx(nc_ctx *ctx) {
 }
 
 void nc_step_end(nc_ctx *ctx) {
+    if (ctx->bn_n) nc__dp_bn_flush(ctx, 0); /* statistics staged in a step no optimizer step closed */
+    nc__dp_rng_step_end(ctx);
     for (int i = 0; i < ctx->n_dchunks; i++) ctx->dchunks[i].used = 0;
     ctx->cur_dchunk = 0;
     ctx->n_dfree = 0;

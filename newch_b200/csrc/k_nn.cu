@@ -695,11 +695,14 @@ __device__ __forceinline__ void bn_load(const float *p, int64_t i, float (&v)[V]
     }
 }
 
-// per-channel statistics -> mean, invstd and running statistics (unbiased variance), splits in order
+// per-channel statistics -> mean, invstd and running statistics (unbiased variance), splits in order.
+// stage != 0 (data-parallel runs): rm / rv receive this batch's mean and unbiased variance instead,
+// for the running-statistic updates applied later in rank order (nck_bn_running_apply).
 struct BnFwdFin {
     float *mean, *invstd, *rm, *rv;
     float mom, eps;
     int splits;
+    int stage;
 };
 
 // Finalize work of the last block: eight lanes per channel add strided runs of the splits and a
@@ -724,8 +727,13 @@ __device__ void bn_fwd_finalize(const double *part, int64_t C, int64_t M, const 
             if (dev < 0.0) dev = 0.0;
             f.mean[c] = (float)mu;
             f.invstd[c] = (float)(1.0 / sqrt(dev / (double)M + (double)f.eps));
-            f.rm[c] = (1.0f - f.mom) * f.rm[c] + f.mom * (float)mu;
-            f.rv[c] = (1.0f - f.mom) * f.rv[c] + f.mom * (float)(dev / (double)(M - 1));
+            if (f.stage) {
+                f.rm[c] = (float)mu;
+                f.rv[c] = (float)(dev / (double)(M - 1));
+            } else {
+                f.rm[c] = (1.0f - f.mom) * f.rm[c] + f.mom * (float)mu;
+                f.rv[c] = (1.0f - f.mom) * f.rv[c] + f.mom * (float)(dev / (double)(M - 1));
+            }
         }
     }
 }
@@ -832,7 +840,7 @@ static int64_t bn_splits(int64_t resident, int64_t N, int64_t C, int64_t S) {
 
 extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                                  float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
-                                 float eps) {
+                                 float eps, int stage) {
     Scope sc(d, "bn_fwd", 0.0, 8.0 * N * C * S);
     const bool v4 = bn_vec4(S, x, y, x);
     static int res4 = 0, res1 = 0;
@@ -842,7 +850,7 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     dim3 g1((unsigned)C, (unsigned)splits);
-    const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits};
+    const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits, stage};
     if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     int64_t planes = N * C;
@@ -851,6 +859,35 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
     else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
                                                                              BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
     NCK_LAUNCHED(d, 2);
+}
+
+// Running statistics of data-parallel BatchNorm: group g (one running_mean / running_var pair) takes
+// the momentum updates of its staged forwards, rank by rank and, within a rank, in recording order,
+// which is the order newch applies them when it runs the ranks' batches one after another
+// (engine/src/ops/ops_nn.c:291-292, the same two-product update as bn_fwd_finalize).
+__global__ void k_bn_running(const nck_bn_group *__restrict__ groups, const nck_bn_staged *__restrict__ staged,
+                             const float *__restrict__ gathered, int64_t rank_stride, int ranks) {
+    const nck_bn_group gr = groups[blockIdx.x];
+    for (int64_t c = threadIdx.x; c < gr.C; c += blockDim.x) {
+        float m = gr.rm[c], v = gr.rv[c];
+        for (int r = 0; r < ranks; r++)
+            for (int e = gr.e0; e < gr.e1; e++) {
+                const float *g = gathered + r * rank_stride + staged[e].off;
+                const float mom = staged[e].mom;
+                m = (1.0f - mom) * m + mom * g[c];
+                v = (1.0f - mom) * v + mom * g[gr.C + c];
+            }
+        gr.rm[c] = m;
+        gr.rv[c] = v;
+    }
+}
+
+extern "C" void nck_bn_running_apply(nck_dev *d, const nck_bn_group *groups, int ngroups, const nck_bn_staged *staged,
+                                     const float *gathered, int64_t rank_stride, int ranks) {
+    if (ngroups <= 0) return;
+    Scope sc(d, "bn_running");
+    k_bn_running<<<ngroups, 256, 0, NCK_STREAM(d)>>>(groups, staged, gathered, rank_stride, ranks);
+    NCK_LAUNCHED(d, 1);
 }
 
 extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,

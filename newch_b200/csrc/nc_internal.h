@@ -60,6 +60,12 @@ struct nc_tensor {
     void *host;        /* host mirror of the whole allocation (NULL until needed) */
     uint32_t coh;
     int host_pinned;   /* mirror came from cudaMallocHost */
+    /* leaves during a backward pass: writers of this tensor's gradient still to run */
+    uint32_t bw_epoch;
+    int32_t bw_pending;
+    /* parameters registered with an optimizer: the optimizer and the parameter's index in it */
+    struct nc_optim *optim;
+    int32_t optim_slot;
 };
 
 /* ---- op registry ------------------------------------------------------------------------------ */
@@ -88,8 +94,9 @@ struct nc_node {
     nc_tensor *out;
     nc_op_params p;
     void *saved;       /* op-private host record (host arena); may point at device scratch */
-    nc_node *prev;
-    uint32_t mark;
+    nc_node *prev;     /* the step's record log, newest first */
+    uint64_t seq;      /* recording order within the context */
+    uint32_t mark;     /* backward epoch in which the node was found live */
     int released;
 };
 
@@ -165,6 +172,7 @@ struct nc_ctx {
     int bwd_logging;
     int grad_alloc;
     uint32_t mark_epoch;
+    uint64_t node_seq;
 
     int persistent_depth;
     int grad_enabled;
@@ -174,6 +182,9 @@ struct nc_ctx {
     char err[256];
 
     uint64_t rng[4];
+    uint64_t rng_count;       /* draws taken from the stream since it was seeded */
+    uint64_t rng_step_start;  /* rng_count at the start of the current step */
+    int64_t dp_rng_stride;    /* data parallel: draws of one micro-batch step (0: streams not interleaved) */
     nc_cpu_info cpu;
     int n_threads;
     int force_reference;
@@ -187,6 +198,19 @@ struct nc_ctx {
     /* data parallel */
     int dp_rank, dp_world;
     void *nccl_comm;
+    void *comm_stream;   /* cudaStream_t of the gradient all-reduces (created with the communicator) */
+    void *ev_main;       /* cudaEvent_t: main-stream point a reduce waits for */
+    void *ev_comm;       /* cudaEvent_t: comm-stream point the main stream waits for */
+    int comm_pending;    /* reduces enqueued on comm_stream since the last join */
+    struct nc_optim *optims; /* optimizers of this context (intrusive list) */
+    /* data parallel BatchNorm: each training forward stages its batch (mean, unbiased variance) here;
+     * nc__dp_bn_flush gathers every rank's and applies the running-statistic updates in rank order */
+    float *bn_stage, *bn_gather;
+    int64_t bn_stage_cap, bn_stage_used;
+    struct nc_bn_pending *bn_pending;
+    int bn_n, bn_cap;
+    void *bn_table_dev;
+    int bn_table_cap;
 
     /* scratch double accumulators etc. */
     double *dscratch;
@@ -266,7 +290,27 @@ void nc__gemm(nc_ctx *ctx, int ta, int tb, int64_t M, int64_t N, int64_t K, floa
               int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc);
 void nc__gemm_batched(nc_ctx *ctx, const nck_gemm_args *a);
 
-/* data parallel: all-reduce of a device float buffer, averaged over ranks */
+/* data parallel: all-reduce of a device float buffer, averaged over ranks (on the main stream) */
 int nc__dp_allreduce_mean(nc_ctx *ctx, float *buf, int64_t n);
+/* dst = mean over ranks of src, enqueued on the communication stream after the main stream's work so
+ * far; nc__dp_join makes the main stream wait for every such reduce */
+int nc__dp_reduce_async(nc_ctx *ctx, const float *src, float *dst, int64_t n);
+/* elementwise maximum over ranks of a byte buffer, in place, on the communication stream */
+int nc__dp_max_bytes_async(nc_ctx *ctx, unsigned char *buf, int64_t n);
+void nc__dp_join(nc_ctx *ctx);
+/* data-parallel BatchNorm running statistics (dp.c): staging of one training forward's statistics
+ * (returns the device address for 2 * C floats: means, then unbiased variances), and the flush */
+float *nc__dp_bn_stage(nc_ctx *ctx, float *running_mean, float *running_var, int64_t C, float momentum);
+int nc__dp_bn_flush(nc_ctx *ctx, int on_comm_stream);
+/* data-parallel dropout streams at a step boundary (dp.c) */
+void nc__dp_rng_step_end(nc_ctx *ctx);
+
+/* Backward-pass gradient readiness of optimizer parameters (optim.c). A backward pass announces each
+ * leaf whose gradient it will write (nc__grad_expect, once per leaf per pass) and reports it final
+ * after its last writer has been enqueued (nc__grad_final); nc__grad_pass_begin opens a pass. They
+ * let data-parallel runs all-reduce gradient buckets while the rest of the pass is still running. */
+void nc__grad_pass_begin(nc_ctx *ctx);
+void nc__grad_expect(nc_tensor *leaf);
+void nc__grad_final(nc_tensor *leaf);
 
 #endif /* NC_INTERNAL_H */

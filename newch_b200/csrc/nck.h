@@ -153,7 +153,22 @@ int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes);
 
 /* batch norm over x [N, C, S] */
 void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
-                      float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom, float eps);
+                      float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom, float eps,
+                      int stage);
+/* data-parallel BatchNorm: a forward's staged statistics at off (means, then C unbiased variances) */
+typedef struct {
+    int64_t off;
+    float mom;
+    int32_t pad;
+} nck_bn_staged;
+/* one running-statistics pair and its staged forwards [e0, e1) */
+typedef struct {
+    float *rm, *rv;
+    int64_t C;
+    int32_t e0, e1;
+} nck_bn_group;
+void nck_bn_running_apply(nck_dev *d, const nck_bn_group *groups, int ngroups, const nck_bn_staged *staged,
+                          const float *gathered, int64_t rank_stride, int ranks);
 void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                      float *invstd, const float *rm, const float *rv, int64_t N, int64_t C, int64_t S, float eps);
 void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean, const float *invstd,
@@ -262,15 +277,29 @@ typedef struct {
     const float *g;
     float *m, *v;
     int64_t n;
+    int32_t param; /* index into the presence bytes */
+    int32_t pad;
 } nck_param_seg;
+/* one block's work: elements [off, off + len) of segment seg (off a multiple of 4) */
+typedef struct {
+    int32_t seg;
+    int32_t len;
+    int64_t off;
+} nck_opt_chunk;
 enum { NCK_OPT_SGD, NCK_OPT_ADAM, NCK_OPT_ADAMW, NCK_OPT_RMSPROP };
 typedef struct {
     int kind;
     float lr, momentum, weight_decay, beta1, beta2, eps, gs, bc1, bc2;
     int eps_inside_sqrt;
 } nck_opt_hyper;
-/* one launch for all parameter segments; segs is a host array, copied into the launch */
-void nck_optim_step(nck_dev *d, const nck_opt_hyper *h, const nck_param_seg *segs, int nseg);
+#define NCK_OPT_CHUNK 4096 /* elements per block */
+/* fills chunks (when not NULL) for the segments; returns how many there are */
+int nck_optim_chunks(const nck_param_seg *segs, int nseg, nck_opt_chunk *chunks);
+/* One launch over device-resident tables: dsegs[nseg], dchunks[nchunk]; total = elements in all
+ * segments (for the timer's byte count). present (device, may be NULL): a segment whose
+ * present[param] is 0 is left as it is. */
+void nck_optim_step(nck_dev *d, const nck_opt_hyper *h, const nck_param_seg *dsegs, const nck_opt_chunk *dchunks,
+                    int nchunk, int64_t total, const unsigned char *present);
 
 /* ---- int8 quantization -------------------------------------------------------------------------- */
 void nck_quantize_rows(nck_dev *d, const float *x, int8_t *q, float *scale, int64_t rows, int64_t cols);

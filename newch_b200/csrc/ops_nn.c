@@ -241,9 +241,20 @@ static nc_status bn_fwd(nc_node *n) {
     if (n->p.i[0]) {
         nc__dev_write(rm);
         nc__dev_write(rv);
-        nck_bn_fwd_train(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd, (float *)nc__dev(rm),
-                         (float *)nc__dev(rv), N, C, S, n->p.f[0], n->p.f[1]);
+        float *rmd = (float *)nc__dev(rm), *rvd = (float *)nc__dev(rv);
+        if (ctx->dp_world > 1) {
+            /* data parallel: this rank's batch statistics are staged; the running statistics take all
+             * ranks' updates in rank order when the step's statistics are gathered */
+            float *st = nc__dp_bn_stage(ctx, rmd, rvd, C, n->p.f[0]);
+            if (!st) return ctx->status;
+            nck_bn_fwd_train(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd, st, st + C, N, C, S,
+                             n->p.f[0], n->p.f[1], 1);
+        } else {
+            nck_bn_fwd_train(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd, rmd, rvd, N, C, S,
+                             n->p.f[0], n->p.f[1], 0);
+        }
     } else {
+        if (ctx->bn_n && !nc__dp_bn_flush(ctx, 0)) return ctx->status; /* pending updates reach rm / rv first */
         nck_bn_fwd_eval(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd,
                         (const float *)nc__dev(rm), (const float *)nc__dev(rv), N, C, S, n->p.f[1]);
     }

@@ -4,11 +4,19 @@
  * Update rules, defaults, the accumulation gate and the state-slot layout are newch's
  * (engine/src/optim/optim.c: struct :15-27, create :29-67, defaults :81-104, accumulation :106-130,
  * state access :132-158, step :161-213, clip_grad_norm :216-233). What is B200-specific:
- *   - the optimizer owns one flat gradient buffer; every parameter's grad becomes a view into it,
- *     so data-parallel ranks all-reduce a single buffer (one NCCL call) before the update;
- *   - Adam's m and v are flat buffers too; one multi-segment kernel updates every parameter;
+ *   - the optimizer owns one flat gradient buffer; every parameter's grad becomes a view into it;
+ *   - Adam's m and v are flat buffers too; one launch updates every parameter, each block one
+ *     chunk of one parameter (a table built once and kept on the device);
  *   - nc_optim_state hands out a host mirror of the flat state, uploaded again before the next step
- *     (newch/optim.py reads and writes it with ctypes.string_at / memmove).
+ *     (newch/optim.py reads and writes it with ctypes.string_at / memmove);
+ *   - data parallelism: the flat buffer is cut into buckets of consecutive parameters (about 1 MiB,
+ *     filled from the last parameter, whose gradient a backward pass finishes first). When a
+ *     backward pass has enqueued the last writer of every parameter of a bucket, the bucket's mean
+ *     over ranks is enqueued on the communication stream into a second flat buffer, so the
+ *     all-reduces overlap the rest of the pass; the step reduces what is left, joins, and updates
+ *     from the reduced buffer. A parameter with no gradient on any rank (a presence byte per
+ *     parameter, maximum over ranks) is skipped as a single-GPU run skips it; one absent on some
+ *     ranks only counts as zero there.
  */
 #include "nc_internal.h"
 
@@ -18,8 +26,19 @@
 
 enum { OPT_SGD = NCK_OPT_SGD, OPT_ADAM = NCK_OPT_ADAM, OPT_ADAMW = NCK_OPT_ADAMW, OPT_RMSPROP = NCK_OPT_RMSPROP };
 
+typedef struct {
+    int p0, p1;      /* parameters [p0, p1) */
+    int64_t e0, e1;  /* their elements in the flat buffers */
+    int expect;      /* parameters of the bucket the running backward pass has still to finish */
+    int touched;     /* the running pass writes at least one of them */
+    int fresh;       /* gred holds the mean over ranks of the bucket's current gradients */
+} grad_bucket;
+
+#define NC_BUCKET_FLOATS ((int64_t)1 << 18) /* 1 MiB */
+
 struct nc_optim {
     nc_ctx *ctx;
+    nc_optim *next_in_ctx;
     int kind;
     int n;
     nc_tensor **params;
@@ -33,7 +52,16 @@ struct nc_optim {
     int64_t t;
     int accum_steps, accum_count;
     int eps_inside_sqrt;
-    nck_param_seg *segs;
+    /* update launch: segments and chunks on the host (last built) and on the device */
+    nck_param_seg *segs, *dsegs;
+    nck_opt_chunk *chunks, *dchunks;
+    int nseg, nchunk, cap_chunk;
+    /* data parallel */
+    float *gred;             /* device: gradients averaged over ranks */
+    grad_bucket *bk;
+    int nbk;
+    int *bucket_of;          /* bucket of each parameter */
+    unsigned char *pres_h, *pres_d; /* presence bytes (host staging / device, max over ranks) */
 };
 
 /* The parameter's grad becomes a view into the flat buffer (keeping any gradient it holds). */
@@ -62,6 +90,8 @@ static int adopt_grad(nc_optim *opt, int i) {
         p->flags |= NC_TF_GRAD_CLEARED; /* absent until a backward reaches it */
     }
     p->grad = g;
+    p->optim = opt;
+    p->optim_slot = i;
     return 1;
 }
 
@@ -87,7 +117,8 @@ static nc_optim *create(nc_ctx *ctx, int kind, nc_tensor **params, int n, nc_opt
     opt->accum_steps = 1;
     opt->params = (nc_tensor **)calloc((size_t)(n ? n : 1), sizeof(nc_tensor *));
     opt->off = (int64_t *)calloc((size_t)(n ? n : 1), sizeof(int64_t));
-    opt->segs = (nck_param_seg *)calloc((size_t)(n ? n : 1), sizeof(nck_param_seg));
+    opt->segs = (nck_param_seg *)calloc((size_t)(n ? 2 * n : 2), sizeof(nck_param_seg)); /* built | scratch */
+    opt->nseg = -1; /* no table built yet */
     if (!opt->params || !opt->off || !opt->segs) goto fail;
     memcpy(opt->params, params, sizeof(nc_tensor *) * (size_t)n);
     for (int i = 0; i < n; i++) {
@@ -108,6 +139,8 @@ static nc_optim *create(nc_ctx *ctx, int kind, nc_tensor **params, int n, nc_opt
     for (int i = 0; i < n; i++)
         if (!adopt_grad(opt, i)) goto fail;
     opt->state_host_valid = 0;
+    opt->next_in_ctx = ctx->optims;
+    ctx->optims = opt;
     return opt;
 fail:
     nc__error(ctx, NC_ERR_OOM, "optimizer: out of memory");
@@ -121,15 +154,118 @@ fail:
 void nc_optim_free(nc_optim *o) {
     if (!o) return;
     nc_ctx *ctx = o->ctx;
+    for (nc_optim **link = &ctx->optims; *link; link = &(*link)->next_in_ctx)
+        if (*link == o) {
+            *link = o->next_in_ctx;
+            break;
+        }
+    nc__dp_join(ctx);
+    if (ctx->device_ok) cudaStreamSynchronize((cudaStream_t)ctx->dev.stream);
     size_t bytes = (size_t)(o->total ? o->total : 1) * sizeof(float);
     if (o->s1) nc__persistent_free(ctx, o->s1, bytes);
     if (o->s2) nc__persistent_free(ctx, o->s2, bytes);
+    if (o->gred) nc__persistent_free(ctx, o->gred, bytes);
+    if (o->dsegs) nc__persistent_free(ctx, o->dsegs, sizeof(nck_param_seg) * (size_t)(o->n ? o->n : 1));
+    if (o->dchunks) nc__persistent_free(ctx, o->dchunks, sizeof(nck_opt_chunk) * (size_t)o->cap_chunk);
+    if (o->pres_d) nc__persistent_free(ctx, o->pres_d, (size_t)(o->n ? o->n : 1));
     if (o->h1) cudaFreeHost(o->h1);
     if (o->h2) cudaFreeHost(o->h2);
     free(o->params);
     free(o->off);
     free(o->segs);
+    free(o->chunks);
+    free(o->bk);
+    free(o->bucket_of);
+    free(o->pres_h);
     free(o);
+}
+
+/* ---- data-parallel gradient buckets ------------------------------------------------------------- */
+
+/* o when it is still one of its context's optimizers (a parameter can outlive its optimizer) */
+static nc_optim *live_optim(nc_tensor *p) {
+    nc_optim *o = p->optim;
+    if (!o) return NULL;
+    for (nc_optim *q = p->ctx->optims; q; q = q->next_in_ctx)
+        if (q == o) return (p->optim_slot >= 0 && p->optim_slot < o->n && o->params[p->optim_slot] == p) ? o : NULL;
+    return NULL;
+}
+
+/* Buckets, the reduced buffer and the presence bytes, made when the context first runs data
+ * parallel. Returns 1 when the optimizer all-reduces. */
+static int dp_ready(nc_optim *o) {
+    nc_ctx *ctx = o->ctx;
+    if (ctx->dp_world <= 1) return 0;
+    if (o->bk) return 1;
+    size_t bytes = (size_t)(o->total ? o->total : 1) * sizeof(float);
+    o->gred = (float *)nc__persistent_alloc(ctx, bytes);
+    o->bk = (grad_bucket *)calloc((size_t)(o->n ? o->n : 1), sizeof(grad_bucket));
+    o->bucket_of = (int *)calloc((size_t)(o->n ? o->n : 1), sizeof(int));
+    o->pres_h = (unsigned char *)calloc((size_t)(o->n ? o->n : 1), 1);
+    o->pres_d = (unsigned char *)nc__persistent_alloc(ctx, (size_t)(o->n ? o->n : 1));
+    if (!o->gred || !o->bk || !o->bucket_of || !o->pres_h || !o->pres_d) {
+        nc__error(ctx, NC_ERR_OOM, "optimizer: out of memory for data-parallel buffers");
+        return 0;
+    }
+    /* from the last parameter backwards: a bucket closes once it holds NC_BUCKET_FLOATS */
+    int nb = 0;
+    for (int hi = o->n; hi > 0;) {
+        int lo = hi;
+        int64_t sz = 0;
+        while (lo > 0 && (sz == 0 || sz + (o->off[lo] - o->off[lo - 1]) <= NC_BUCKET_FLOATS)) {
+            lo--;
+            sz = o->off[hi - 1] + ((nc_numel(o->params[hi - 1]) + 3) & ~(int64_t)3) - o->off[lo];
+        }
+        grad_bucket *b = &o->bk[nb];
+        b->p0 = lo, b->p1 = hi;
+        b->e0 = o->off[lo];
+        b->e1 = o->off[hi - 1] + ((nc_numel(o->params[hi - 1]) + 3) & ~(int64_t)3);
+        for (int i = lo; i < hi; i++) o->bucket_of[i] = nb;
+        nb++;
+        hi = lo;
+    }
+    o->nbk = nb;
+    return 1;
+}
+
+/* Enqueues the bucket's all-reduce. Parameters whose gradient was cleared (set_to_none) and not
+ * written since hold last cycle's values in their slots: they count as zero. */
+static void launch_bucket(nc_optim *o, grad_bucket *b) {
+    nc_ctx *ctx = o->ctx;
+    cudaStream_t s = (cudaStream_t)ctx->dev.stream;
+    for (int i = b->p0; i < b->p1; i++) {
+        nc_tensor *p = o->params[i];
+        if (!nc_grad(p) && p->grad) cudaMemsetAsync(p->grad->data, 0, p->grad->bytes, s);
+        else if (p->grad) nc__dev(p->grad); /* host writes to a gradient reach the device first */
+    }
+    if (nc__dp_reduce_async(ctx, o->gflat + b->e0, o->gred + b->e0, b->e1 - b->e0)) b->fresh = 1;
+}
+
+void nc__grad_pass_begin(nc_ctx *ctx) {
+    if (!ctx->optims) return;
+    nc__dp_join(ctx); /* reduces still reading the gradients this pass is about to write */
+    for (nc_optim *o = ctx->optims; o; o = o->next_in_ctx)
+        for (int b = 0; b < o->nbk; b++) o->bk[b].expect = o->bk[b].touched = 0;
+}
+
+void nc__grad_expect(nc_tensor *leaf) {
+    nc_optim *o = live_optim(leaf);
+    if (!o || !dp_ready(o)) return;
+    grad_bucket *b = &o->bk[o->bucket_of[leaf->optim_slot]];
+    b->expect++;
+    b->touched = 1;
+    b->fresh = 0;
+}
+
+void nc__grad_final(nc_tensor *leaf) {
+    nc_optim *o = live_optim(leaf);
+    if (!o || !o->bk) return;
+    grad_bucket *b = &o->bk[o->bucket_of[leaf->optim_slot]];
+    if (b->expect > 0 && --b->expect == 0 && o->accum_steps == 1) launch_bucket(o, b);
+}
+
+static void mark_stale(nc_optim *o) {
+    for (int b = 0; b < o->nbk; b++) o->bk[b].fresh = 0;
 }
 
 nc_optim *nc_sgd(nc_ctx *ctx, nc_tensor **params, int n, nc_optim_opts opts) {
@@ -171,11 +307,14 @@ void nc_optim_set_accumulation(nc_optim *o, int steps) {
 
 void nc_optim_zero_grad(nc_optim *o) {
     if (!o || o->accum_count != 0) return;
+    nc__dp_join(o->ctx);
+    mark_stale(o);
     for (int i = 0; i < o->n; i++) nc_zero_grad(o->params[i]);
 }
 
 void nc_optim_clear_grad(nc_optim *o) {
     if (!o || o->accum_count != 0) return;
+    mark_stale(o);
     for (int i = 0; i < o->n; i++) nc_clear_grad(o->params[i]);
 }
 
@@ -233,6 +372,48 @@ void nc_optim_set_opts(nc_optim *o, nc_optim_opts opts) {
     o->o = opts;
 }
 
+/* The update launch's tables on the device, rebuilt and uploaded only when the list of segments
+ * differs from the one uploaded last (normally once, at the first step). */
+static int upload_tables(nc_optim *o, const nck_param_seg *segs, int nseg) {
+    nc_ctx *ctx = o->ctx;
+    if (o->nseg == nseg && o->dsegs && !memcmp(o->segs, segs, sizeof(nck_param_seg) * (size_t)nseg)) return 1;
+    if (!o->dsegs && !(o->dsegs = (nck_param_seg *)nc__persistent_alloc(ctx, sizeof(nck_param_seg) *
+                                                                                (size_t)(o->n ? o->n : 1))))
+        return 0;
+    int nchunk = nck_optim_chunks(segs, nseg, NULL);
+    if (nchunk > o->cap_chunk) {
+        if (o->dchunks) nc__persistent_free(ctx, o->dchunks, sizeof(nck_opt_chunk) * (size_t)o->cap_chunk);
+        free(o->chunks);
+        o->cap_chunk = 0;
+        o->chunks = (nck_opt_chunk *)malloc(sizeof(nck_opt_chunk) * (size_t)nchunk);
+        o->dchunks = (nck_opt_chunk *)nc__persistent_alloc(ctx, sizeof(nck_opt_chunk) * (size_t)nchunk);
+        if (!o->chunks || !o->dchunks) return 0;
+        o->cap_chunk = nchunk;
+    }
+    nck_optim_chunks(segs, nseg, o->chunks);
+    if (segs != o->segs) memcpy(o->segs, segs, sizeof(nck_param_seg) * (size_t)nseg);
+    nc__upload(ctx, o->dsegs, o->segs, sizeof(nck_param_seg) * (size_t)nseg);
+    nc__upload(ctx, o->dchunks, o->chunks, sizeof(nck_opt_chunk) * (size_t)nchunk);
+    o->nseg = nseg;
+    o->nchunk = nchunk;
+    return ctx->status == NC_OK;
+}
+
+/* Data parallel: every bucket not reduced since its last write is reduced now (the same calls on
+ * every rank, which all run the same graph), then the presence bytes, then the main stream waits. */
+static int dp_finish_reduce(nc_optim *o) {
+    nc_ctx *ctx = o->ctx;
+    for (int b = 0; b < o->nbk; b++)
+        if (!o->bk[b].fresh) launch_bucket(o, &o->bk[b]);
+    if (ctx->bn_n && !nc__dp_bn_flush(ctx, 1)) return 0;
+    for (int i = 0; i < o->n; i++) o->pres_h[i] = nc_grad(o->params[i]) ? 1 : 0;
+    nc__upload(ctx, o->pres_d, o->pres_h, (size_t)o->n);
+    if (!nc__dp_max_bytes_async(ctx, o->pres_d, o->n)) return 0;
+    nc__dp_join(ctx);
+    for (int b = 0; b < o->nbk; b++) o->bk[b].fresh = 0; /* the next cycle writes new gradients */
+    return ctx->status == NC_OK;
+}
+
 void nc_optim_step(nc_optim *o) {
     if (!o || !nc_ok(o->ctx)) return;
     if (o->accum_steps > 1 && ++o->accum_count < o->accum_steps) return;
@@ -253,31 +434,31 @@ void nc_optim_step(nc_optim *o) {
         h.bc2 = 1.0f - powf(c->beta2, (float)o->t);
     }
     state_upload_if_dirty(o);
-    if (ctx->dp_world > 1) {
-        /* absent gradients count as zero in the sum over ranks */
-        for (int i = 0; i < o->n; i++)
-            if (!nc_grad(o->params[i]) && o->params[i]->grad)
-                cudaMemsetAsync(o->params[i]->grad->data, 0, o->params[i]->grad->bytes, (cudaStream_t)ctx->dev.stream);
-        for (int i = 0; i < o->n; i++)
-            if (o->params[i]->grad) nc__dev(o->params[i]->grad);
-        if (!nc__dp_allreduce_mean(ctx, o->gflat, o->total)) return;
-    }
+    const int dp = dp_ready(o);
+    if (ctx->status != NC_OK || (dp && !dp_finish_reduce(o))) return;
+    /* segments: parameters with a gradient here; under data parallelism every parameter, gated on
+     * the device by whether any rank had its gradient */
+    nck_param_seg *segs = o->segs + o->n; /* scratch half of the array */
     int nseg = 0;
+    int64_t total = 0;
     for (int i = 0; i < o->n; i++) {
         nc_tensor *p = o->params[i];
         nc_tensor *gt = nc_grad(p);
-        if (!gt && ctx->dp_world <= 1) continue;
-        if (!gt && !p->grad) continue;
-        if (!gt) gt = p->grad;
+        if (!gt && !dp) continue;
+        if (gt) nc__dev(gt);
         nc__dev_write(p);
-        nck_param_seg *sg = &o->segs[nseg++];
+        nck_param_seg *sg = &segs[nseg++];
+        memset(sg, 0, sizeof *sg);
         sg->w = (float *)nc__dev(p);
-        sg->g = (const float *)nc__dev(gt);
+        sg->g = (dp ? o->gred : o->gflat) + o->off[i];
         sg->m = o->s1 ? o->s1 + o->off[i] : NULL;
         sg->v = o->s2 ? o->s2 + o->off[i] : NULL;
         sg->n = nc_numel(p);
+        sg->param = i;
+        total += sg->n;
     }
-    if (nseg) nck_optim_step(nc__k(ctx), &h, o->segs, nseg);
+    if (nseg && upload_tables(o, segs, nseg))
+        nck_optim_step(nc__k(ctx), &h, o->dsegs, o->dchunks, o->nchunk, total, dp ? o->pres_d : NULL);
     o->state_host_valid = 0;
 }
 

@@ -40,6 +40,7 @@ uint64_t nc__rng_next(nc_ctx *ctx) {
     uint64_t *s = ctx->rng;
     uint64_t r = rotl64(s[1] * 5, 7) * 9;
     step(s);
+    ctx->rng_count++;
     return r;
 }
 
@@ -96,6 +97,7 @@ static int powers_ready(void) {
 
 void nc__rng_skip(nc_ctx *ctx, uint64_t n) {
     if (!n) return;
+    ctx->rng_count += n;
     if (n < 64 || !powers_ready()) {
         for (uint64_t i = 0; i < n; i++) step(ctx->rng);
         return;

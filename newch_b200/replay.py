@@ -92,7 +92,7 @@ class Replayer:
     OPTIMIZERS = ("nc_sgd", "nc_adam", "nc_adamw", "nc_rmsprop")
 
     def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True, pinned: bool = False,
-                 grads: bool = False, capture=()):
+                 grads: bool = False, capture=(), force_reference: int | None = None):
         self.lib = lib
         self.trace = trace
         self.check = check
@@ -114,6 +114,7 @@ class Replayer:
         self._keep: list = []
         self._blobs: dict = {}
         self.seed_offset = seed_offset
+        self.force_reference = force_reference  # overrides nc_init's config field when not None
         self._fns = {name: getattr(lib, name) for name in {c[0] for c in trace.calls}}
         self._prepared = [self._prepare(i, c) for i, c in enumerate(trace.calls)]
 
@@ -159,6 +160,8 @@ class Replayer:
                     if st_t is None and t is not None and hasattr(t, "_type_"):
                         st_t = t._type_
                     obj = st_t(*a["st"])
+                    if name == "nc_init" and self.force_reference is not None:
+                        obj.force_reference = int(self.force_reference)
                     self._keep.append(obj)
                     conv.append((0, ctypes.byref(obj) if name == "nc_init" else obj))
                 elif "str" in a:

@@ -25,7 +25,9 @@ def test_reference_arm_json_line():
               "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert k in line, k
     assert line["impl"] == "reference" and line["value"] > 0 and line["higher_is_better"] is True
-    assert "workload" in line["config"]
+    # the B200 arm's line carries the same config dict (bench.config_dict), so the two arms compare
+    assert line["config"] == {"workload": line["config"]["workload"], "global_batch": 512, "per_gpu_batch": 512,
+                              "parallelism": "dp1"}
     assert {"value", "unit", "cores", "kind", "sample"} <= set(line["cpu_baseline"])
     assert line["cpu_baseline"]["kind"] == "reference"
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,

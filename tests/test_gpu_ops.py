@@ -41,8 +41,8 @@ EXACT = {
               "hardswish_y", "relu_dx", "neg_dx", "scale_dx", "add_scalar_dx", "leaky_relu_dx", "relu6_dx",
               "hardsigmoid_dx", "hardswish_dx"}
     | {f"{k}_{o}" for k in ("sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh") for o in ("y", "dx")},
-    "transcendental": {f"{k}_{o}" for k in ("sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh")
-                       for o in ("y", "dx")},
+    "transcendental": {"x", "G"} | {f"{k}_{o}" for k in ("sigmoid", "tanh", "exp", "silu", "gelu", "gelu_tanh")
+                                    for o in ("y", "dx")},
 }
 TOL = 1e-5
 

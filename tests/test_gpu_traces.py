@@ -10,9 +10,15 @@ Checked, per configuration and GEMM mode:
   exact integer product of the same quantized operands.
 
 Tolerances (normwise per tensor, max|got - ref| / max|ref|): the CUDA-core GEMM path (NC_GEMM=ffma)
-1e-5; the default tensor-core path (3xTF32) 1e-3 (it measures ~1e-6). The plain TF32 mode
-(NC_GEMM=tf32) is an opt-in speed mode whose GEMMs round to 10-bit mantissas: its gradients and
-parameters are held to 2e-2, its first loss to 1e-3 and later losses to 1e-2.
+1e-5; the default tensor-core path (3xTF32) 1e-3. The plain TF32 mode (NC_GEMM=tf32) is an opt-in
+speed mode whose GEMMs round operands to 10-bit mantissas: its gradients and parameters are held to
+5e-2, its first loss to 1e-3 and later losses to 1e-2.
+
+Each tolerance has a floor: twice the distance between the reference engine's own two kernel tiers
+(AVX2 and scalar, tests/golden/trace_spread.json) on the same tensor. Both tiers are correct fp32
+arithmetic in different summation orders; where a gradient is a long sum with heavy cancellation (a
+convolution weight feeding BatchNorm: ~4e5 products per element at batch 512, summing to a result far
+below its terms) they lie up to ~6e-3 apart, and no fp32 implementation can be held closer than that.
 
 Adam normalises each gradient element by its own magnitude, so an element whose true gradient is zero
 is moved by lr * sign(rounding noise), which two correct implementations need not share. Such elements
@@ -27,6 +33,10 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+import json
+import os
+from pathlib import Path
+
 from nchelp import REF_LIB, capi
 from newch_b200 import replay
 import ncoracle as O
@@ -35,7 +45,17 @@ pytestmark = pytest.mark.gpu
 
 LOSS_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 1e-3}
 TF32_DRIFT = 1e-2  # later TF32 losses come from weights that already differ by TF32 updates
-TENSOR_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 2e-2}
+TENSOR_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 5e-2}
+SPREAD = json.loads((Path(__file__).resolve().parent / "golden" / "trace_spread.json").read_text())
+SPREAD_FACTOR = 2.0
+# NC_PARITY_REPORT=<file>: every measured error (and its tolerance) is appended there as JSON lines
+REPORT = os.environ.get("NC_PARITY_REPORT")
+
+
+def report(**kw):
+    if REPORT:
+        with open(REPORT, "a") as f:
+            f.write(json.dumps(kw) + "\n")
 NOISE = 1e-5  # a reference gradient below this fraction of the step's largest gradient is rounding noise
 INT8_CALLS = ("nc_from_data", "nc_quantize_rows", "nc_add_scalar", "nc_linear_int8", "nc_gelu")
 
@@ -95,8 +115,12 @@ def check_losses(mode, gi, ri):
         assert a == pytest.approx(b, rel=tol, abs=1e-6), (mode, k, gi, ri)
 
 
-def check_gradients(name, mode, rg, rr, exempt):
-    tol = TENSOR_TOL[mode]
+def floor_tol(mode, spread):
+    return max(TENSOR_TOL[mode], SPREAD_FACTOR * spread)
+
+
+def check_gradients(name, mode, rg, rr, exempt, failures):
+    spread = SPREAD[name]["grads"]
     assert len(rg.grads) == len(rr.grads) and rg.grads, "backward passes differ in number"
     worst = 0.0
     for step, ((_, gs), (_, rs)) in enumerate(zip(rg.grads, rr.grads)):
@@ -116,12 +140,15 @@ def check_gradients(name, mode, rg, rr, exempt):
                     continue
             err = normwise(x, y)
             worst = max(worst, err)
-            assert err <= tol, f"{name} ({mode}) step {step}: gradient of parameter {k} differs by {err:.3g}"
+            tol = floor_tol(mode, spread[step][k])
+            report(trace=name, mode=mode, what="grad", step=step, param=k, err=err, tol=tol)
+            if err > tol:
+                failures.append(f"{name} ({mode}) step {step}: gradient of parameter {k} differs by {err:.3g} > {tol:.3g}")
     return worst
 
 
-def check_parameters(name, mode, got, ref, exempt, lr, steps):
-    tol = TENSOR_TOL[mode]
+def check_parameters(name, mode, got, ref, exempt, lr, steps, failures):
+    spread = SPREAD[name]["params"]
     worst = 0.0
     for k, ((_, a), (_, b)) in enumerate(zip(got, ref)):
         x, y = np.frombuffer(a, np.float32), np.frombuffer(b, np.float32)
@@ -136,7 +163,11 @@ def check_parameters(name, mode, got, ref, exempt, lr, steps):
                 continue
         err = normwise(x, y)
         worst = max(worst, err)
-        assert err <= tol, f"{name} ({mode}): parameter {k} after training differs by {err:.3g}"
+        tol = floor_tol(mode, spread[k])
+        report(trace=name, mode=mode, what="param", param=k, err=err, tol=tol,
+               frob=float(np.linalg.norm(x.astype(np.float64) - y) / max(np.linalg.norm(y.astype(np.float64)), 1e-30)))
+        if err > tol:
+            failures.append(f"{name} ({mode}): parameter {k} after training differs by {err:.3g} > {tol:.3g}")
     return worst
 
 
@@ -178,9 +209,11 @@ def compare(name, mode="ffma"):
         check_int8_chain(rg, rr, [b for _, b in rg.outputs], [b for _, b in rr.outputs])
     else:
         exempt = zero_gradient_elements(param_shapes(rr))
-        check_gradients(name, mode, rg, rr, exempt)
+        failures = []  # every tensor is measured (and reported) before the test fails on any
+        check_gradients(name, mode, rg, rr, exempt, failures)
         lr = {"cfg4": 3e-4}.get(base.split("_")[0], 1e-3)
-        check_parameters(name, mode, rg.outputs, rr.outputs, exempt, lr, len(t.steps()))
+        check_parameters(name, mode, rg.outputs, rr.outputs, exempt, lr, len(t.steps()), failures)
+        assert not failures, "\n".join(failures)
     gpu.nc_free_ctx(rg.ctx)
     ref.nc_free_ctx(rr.ctx)
 
