@@ -549,134 +549,312 @@ extern "C" int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x,
 }
 
 // ---- depthwise (groups == C == OC) ---------------------------------------------------------------
+//
+// One block works on a tile of consecutive rows (full width) of one (sample, channel) plane. The
+// input rows the tile needs, padding included, are staged in shared memory with coalesced row loads;
+// the out-of-image padding is stored as zeros, so the tap loops need no bounds tests (a zero term
+// leaves a sum unchanged). Sums run in newch's order (engine/src/ops/ops_conv.c dw_fwd_range :192,
+// dw_dx_range :222): the forward starts from the bias and adds taps (ki, kj) row-major; the input
+// gradient adds, for each element, its taps in the order newch's row passes reach it (ki from the
+// last kernel row up, kj ascending). With unit column stride newch adds through its fused
+// multiply-add axpy, otherwise with a product and a sum; the kernels do the same, so both are
+// bit-identical to newch's AVX2 tier.
 
-// y = bias + sum over (ki, kj) in order of w * x, fused multiply-adds as newch's axpy rows
-__global__ void k_dw_fwd(nck_conv g, const float *__restrict__ x, const float *__restrict__ w,
-                         const float *__restrict__ b, float *__restrict__ y) {
-    int64_t total = g.N * g.C * g.OH * g.OW;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ox = t % g.OW, r = t / g.OW;
-        int64_t oy = r % g.OH, plane = r / g.OH;
-        int64_t c = plane % g.C;
-        const float *xp = x + plane * g.H * g.W, *wk = w + c * g.KH * g.KW;
-        float acc = b ? b[c] : 0.0f;
-        for (int64_t ki = 0; ki < g.KH; ki++) {
-            int64_t iy = oy * g.sh - g.ph + ki * g.dh;
-            if (iy < 0 || iy >= g.H) continue;
-            for (int64_t kj = 0; kj < g.KW; kj++) {
-                int64_t ix = ox * g.sw - g.pw + kj * g.dw;
-                if (ix < 0 || ix >= g.W) continue;
-                acc = fmaf(wk[ki * g.KW + kj], xp[iy * g.W + ix], acc);
+namespace {
+
+constexpr int kDwThreads = 256;
+constexpr int kDwTileOut = 2048; // outputs per block (8 per thread)
+
+struct DwPlan {
+    int rows;     // output rows per tile (input-gradient rows for dx)
+    int tiles;    // tiles per plane
+    int srows;    // staged rows
+    int scols;    // staged row width
+};
+
+// Stages rows [r0, r0 + nr) x columns [c0, c0 + SW) of a plane (H x W) in shared memory, zero outside.
+__device__ __forceinline__ void dw_stage(const float *__restrict__ src, int H, int W, int r0, int nr, int c0, int SW,
+                                         float *__restrict__ sm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int r = warp; r < nr; r += nw) {
+        const int iy = r0 + r;
+        const bool row_ok = iy >= 0 && iy < H;
+        const float *row = src + (int64_t)iy * W;
+        for (int cc = lane; cc < SW; cc += 32) {
+            const int ix = c0 + cc;
+            sm[r * SW + cc] = (row_ok && ix >= 0 && ix < W) ? __ldg(row + ix) : 0.0f;
+        }
+    }
+}
+
+// KH_T, KW_T: the kernel size when fixed at compile time (3 x 3), 0 for any size
+template <bool FMA, int KH_T, int KW_T>
+__global__ void __launch_bounds__(kDwThreads) k_dw_fwd(nck_conv g, const float *__restrict__ x,
+                                                       const float *__restrict__ w, const float *__restrict__ b,
+                                                       float *__restrict__ y, DwPlan pl, FastDiv div_ow) {
+    extern __shared__ float sm[];
+    float *wk = sm;              // the channel's taps
+    float *sx = sm + NCK_DW_MAX_TAPS;
+    const int64_t plane = blockIdx.x / pl.tiles;
+    const int tile = (int)(blockIdx.x - plane * pl.tiles);
+    const int c = (int)(plane % g.C);
+    const int H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW;
+    const int KH = KH_T ? KH_T : (int)g.KH, KW = KW_T ? KW_T : (int)g.KW;
+    const int oy0 = tile * pl.rows, oy1 = min(OH, oy0 + pl.rows);
+    const int KK = KH * KW;
+    if (threadIdx.x < KK) wk[threadIdx.x] = __ldg(w + (int64_t)c * KK + threadIdx.x);
+    dw_stage(x + plane * (int64_t)H * W, H, W, oy0 * g.sh - g.ph, pl.srows, -g.pw, pl.scols, sx);
+    __syncthreads();
+    const float bias = b ? __ldg(b + c) : 0.0f;
+    float *yp = y + plane * (int64_t)OH * OW + (int64_t)oy0 * OW;
+    const int n = (oy1 - oy0) * OW;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int oy = (int)div_ow.div((uint32_t)t), ox = t - oy * OW;
+        const float *base = sx + oy * g.sh * pl.scols + ox * g.sw;
+        float acc = bias;
+#pragma unroll
+        for (int ki = 0; ki < KH; ki++) {
+            const float *rowp = base + ki * g.dh * pl.scols;
+#pragma unroll
+            for (int kj = 0; kj < KW; kj++) {
+                const float wv = wk[ki * KW + kj], xv = rowp[kj * g.dw];
+                acc = FMA ? fmaf(wv, xv, acc) : acc + wv * xv;
             }
         }
-        y[t] = acc;
+        yp[t] = acc;
     }
+}
+
+// dx rows [iy0, iy1) of a plane; the gy rows they draw on are staged (zero outside the output).
+template <bool FMA, bool UNIT, int KH_T, int KW_T>
+__global__ void __launch_bounds__(kDwThreads) k_dw_dx(nck_conv g, const float *__restrict__ gy,
+                                                      const float *__restrict__ w, float *__restrict__ gx, int acc_in,
+                                                      DwPlan pl, FastDiv div_w) {
+    extern __shared__ float sm[];
+    float *wk = sm;
+    float *sg = sm + NCK_DW_MAX_TAPS;
+    const int64_t plane = blockIdx.x / pl.tiles;
+    const int tile = (int)(blockIdx.x - plane * pl.tiles);
+    const int c = (int)(plane % g.C);
+    const int H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW;
+    const int KH = KH_T ? KH_T : (int)g.KH, KW = KW_T ? KW_T : (int)g.KW;
+    const int iy0 = tile * pl.rows, iy1 = min(H, iy0 + pl.rows);
+    const int KK = KH * KW;
+    if (threadIdx.x < KK) wk[threadIdx.x] = __ldg(w + (int64_t)c * KK + threadIdx.x);
+    // output rows that reach this tile: oy in [oy_lo, oy_lo + srows), staged from column -cpad
+    const int span = (KH - 1) * g.dh;
+    const int oy_lo = UNIT ? iy0 + g.ph - span : (iy0 + g.ph - span >= 0 ? (iy0 + g.ph - span) / g.sh : -((g.sh - 1 - (iy0 + g.ph - span)) / g.sh));
+    const int cpad = UNIT ? (KW - 1) * g.dw - g.pw : 0;
+    dw_stage(gy + plane * (int64_t)OH * OW, OH, OW, oy_lo, pl.srows, -cpad, pl.scols, sg);
+    __syncthreads();
+    float *xp = gx + plane * (int64_t)H * W + (int64_t)iy0 * W;
+    const int n = (iy1 - iy0) * W;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int r = (int)div_w.div((uint32_t)t), ix = t - r * W, iy = iy0 + r;
+        float acc = acc_in ? xp[t] : 0.0f;
+#pragma unroll
+        for (int ki = KH - 1; ki >= 0; ki--) {
+            const int ty = iy + g.ph - ki * g.dh;
+            int oy;
+            if (UNIT) {
+                oy = ty;
+            } else {
+                if (ty < 0 || ty % g.sh) continue;
+                oy = ty / g.sh;
+                if (oy >= OH) continue;
+            }
+            const float *rowp = sg + (oy - oy_lo) * pl.scols;
+#pragma unroll
+            for (int kj = 0; kj < KW; kj++) {
+                const int tx = ix + g.pw - kj * g.dw;
+                float gv;
+                if (UNIT) {
+                    gv = rowp[tx + cpad];
+                } else {
+                    if (tx < 0 || tx % g.sw) continue;
+                    const int ox = tx / g.sw;
+                    if (ox >= OW) continue;
+                    gv = rowp[ox];
+                }
+                const float wv = wk[ki * KW + kj];
+                acc = FMA ? fmaf(wv, gv, acc) : acc + wv * gv;
+            }
+        }
+        xp[t] = acc;
+    }
+}
+
+// Weight and bias gradients: block (c, split) walks the (plane, row tile) items of its samples; a
+// thread keeps one running sum per tap (and one for the bias) over its output positions; the block
+// then adds the threads' sums in a fixed tree, and a combine kernel adds the splits in order.
+template <int KH_T, int KW_T>
+__global__ void __launch_bounds__(kDwThreads) k_dw_dw_partial(nck_conv g, const float *__restrict__ x,
+                                                              const float *__restrict__ gy, float *__restrict__ part,
+                                                              int64_t per_split, DwPlan pl, FastDiv div_ow) {
+    extern __shared__ float sm[];
+    __shared__ float red[kDwThreads / 32][NCK_DW_MAX_TAPS + 1];
+    const int c = blockIdx.x;
+    const int64_t n0 = blockIdx.y * per_split, n1 = min(g.N, n0 + per_split);
+    const int H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW;
+    const int KH = KH_T ? KH_T : (int)g.KH, KW = KW_T ? KW_T : (int)g.KW;
+    const int KK = KH * KW;
+    constexpr int NA = (KH_T && KW_T) ? KH_T * KW_T : NCK_DW_MAX_TAPS; // tap sums; the bias sum is separate
+    float acc[NA];
+    float bsum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NA; k++) acc[k] = 0.0f;
+    for (int64_t nn = n0; nn < n1; nn++) {
+        const int64_t plane = nn * g.C + c;
+        const float *xp = x + plane * (int64_t)H * W, *gp = gy + plane * (int64_t)OH * OW;
+        for (int tile = 0; tile < pl.tiles; tile++) {
+            const int oy0 = tile * pl.rows, oy1 = min(OH, oy0 + pl.rows);
+            __syncthreads(); // the previous item's readers are done with the staged rows
+            dw_stage(xp, H, W, oy0 * g.sh - g.ph, pl.srows, -g.pw, pl.scols, sm);
+            __syncthreads();
+            const int n = (oy1 - oy0) * OW;
+            const float *gt = gp + (int64_t)oy0 * OW;
+            for (int t = threadIdx.x; t < n; t += blockDim.x) {
+                const int oy = (int)div_ow.div((uint32_t)t), ox = t - oy * OW;
+                const float gv = __ldg(gt + t);
+                const float *base = sm + oy * g.sh * pl.scols + ox * g.sw;
+#pragma unroll
+                for (int ki = 0; ki < KH; ki++)
+#pragma unroll
+                    for (int kj = 0; kj < KW; kj++) {
+                        const int k = ki * KW + kj;
+                        acc[k] = fmaf(base[ki * g.dh * pl.scols + kj * g.dw], gv, acc[k]);
+                    }
+                bsum += gv;
+            }
+        }
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int k = 0; k <= NA; k++) {
+        if (k < NA && k >= KK) continue;
+        float v = k < NA ? acc[k] : bsum;
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[wid][k < NA ? k : NCK_DW_MAX_TAPS] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x <= NCK_DW_MAX_TAPS && (threadIdx.x < KK || threadIdx.x == NCK_DW_MAX_TAPS)) {
+        float s = 0.0f;
+        for (int q = 0; q < (int)(blockDim.x >> 5); q++) s += red[q][threadIdx.x];
+        part[((int64_t)blockIdx.y * g.C + c) * (NCK_DW_MAX_TAPS + 1) + threadIdx.x] = s;
+    }
+}
+
+__global__ void k_dw_dw_combine(const float *__restrict__ part, int splits, int64_t C, int KK, float *__restrict__ gw,
+                                float *__restrict__ gb) {
+    const int64_t per = NCK_DW_MAX_TAPS + 1, total = C * (KK + 1);
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = t / (KK + 1);
+        const int k = (int)(t - c * (KK + 1));
+        const int slot = k < KK ? k : NCK_DW_MAX_TAPS;
+        if (k == KK && !gb) continue;
+        float s = 0.0f;
+        for (int q = 0; q < splits; q++) s += part[(q * C + c) * per + slot];
+        if (k < KK) gw[c * KK + k] += s;
+        else gb[c] += s;
+    }
+}
+
+// rows per tile so that a tile has about kDwTileOut outputs; staged rows and width for it
+DwPlan dw_plan_out(const nck_conv *g) {
+    DwPlan p;
+    const int64_t OW = g->OW > 0 ? g->OW : 1;
+    int rows = (int)(kDwTileOut / OW);
+    if (rows < 1) rows = 1;
+    if (rows > g->OH) rows = (int)g->OH;
+    p.rows = rows > 0 ? rows : 1;
+    p.tiles = (int)((g->OH + p.rows - 1) / p.rows);
+    p.srows = (p.rows - 1) * g->sh + (int)(g->KH - 1) * g->dh + 1;
+    p.scols = (int)((g->OW - 1) * g->sw + (g->KW - 1) * g->dw + 1);
+    return p;
+}
+
+size_t dw_smem(const DwPlan &p) { return sizeof(float) * ((size_t)NCK_DW_MAX_TAPS + (size_t)p.srows * p.scols); }
+
+} // namespace
+
+// Plans whose staged rows fit in shared memory take the tiled kernels (every practical depthwise
+// layer: a 3x3 over a 4096-wide row needs ~50 KB).
+static bool dw_fits(const DwPlan &p) { return dw_smem(p) <= (size_t)200 * 1024; }
+
+extern "C" int nck_dw_ok(const nck_conv *g) {
+    if (g->KH * g->KW > NCK_DW_MAX_TAPS || g->H * g->W >= ((int64_t)1 << 31) || g->OH * g->OW >= ((int64_t)1 << 31))
+        return 0;
+    DwPlan a = dw_plan_out(g);
+    nck_conv t = *g;
+    t.OH = g->H, t.OW = g->W; /* the input-gradient tiling, sized on the input plane */
+    DwPlan b = dw_plan_out(&t);
+    b.srows = (b.rows - 1 + (int)(g->KH - 1) * g->dh) / g->sh + 2;
+    b.scols = (int)(g->sh == 1 && g->sw == 1 ? g->W + (g->KW - 1) * g->dw : g->OW);
+    return dw_fits(a) && dw_fits(b);
 }
 
 extern "C" void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y) {
-    int64_t total = g->N * g->C * g->OH * g->OW;
+    const int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
     Scope sc(d, "dw_fwd", 2.0 * total * g->KH * g->KW, 4.0 * (g->N * g->C * g->H * g->W + total));
-    k_dw_fwd<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, x, w, b, y);
+    const DwPlan pl = dw_plan_out(g);
+    const size_t smem = dw_smem(pl);
+    const int64_t blocks = g->N * g->C * pl.tiles;
+    const bool k3 = g->KH == 3 && g->KW == 3;
+    auto k = g->sw == 1 ? (k3 ? k_dw_fwd<true, 3, 3> : k_dw_fwd<true, 0, 0>)
+                        : (k3 ? k_dw_fwd<false, 3, 3> : k_dw_fwd<false, 0, 0>);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<(unsigned)blocks, kDwThreads, smem, NCK_STREAM(d)>>>(*g, x, w, b, y, pl, make_fastdiv((uint32_t)g->OW));
     NCK_LAUNCHED(d, 1);
 }
 
-// dx[n, c, iy, ix] += sum over taps reaching it of w * gy
-__global__ void k_dw_dx(nck_conv g, const float *__restrict__ gy, const float *__restrict__ w, float *__restrict__ gx) {
-    int64_t total = g.N * g.C * g.H * g.W;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        int64_t ix = t % g.W, r = t / g.W;
-        int64_t iy = r % g.H, plane = r / g.H;
-        int64_t c = plane % g.C;
-        const float *gp = gy + plane * g.OH * g.OW, *wk = w + c * g.KH * g.KW;
-        float acc = gx[t];
-        for (int64_t ki = 0; ki < g.KH; ki++) {
-            int64_t ty = iy + g.ph - ki * g.dh;
-            if (ty < 0 || ty % g.sh) continue;
-            int64_t oy = ty / g.sh;
-            if (oy >= g.OH) continue;
-            for (int64_t kj = 0; kj < g.KW; kj++) {
-                int64_t tx = ix + g.pw - kj * g.dw;
-                if (tx < 0 || tx % g.sw) continue;
-                int64_t ox = tx / g.sw;
-                if (ox >= g.OW) continue;
-                acc = fmaf(wk[ki * g.KW + kj], gp[oy * g.OW + ox], acc);
-            }
-        }
-        gx[t] = acc;
-    }
-}
-
-extern "C" void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx) {
-    int64_t total = g->N * g->C * g->H * g->W;
+extern "C" void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx, int acc) {
+    const int64_t total = g->N * g->C * g->H * g->W;
     if (total <= 0) return;
     Scope sc(d, "dw_dx", 2.0 * g->N * g->C * g->OH * g->OW * g->KH * g->KW,
-             4.0 * (g->N * g->C * g->OH * g->OW + 2 * total));
-    k_dw_dx<<<grid_for(d, total), kThreads, 0, NCK_STREAM(d)>>>(*g, gy, w, gx);
+             4.0 * (g->N * g->C * g->OH * g->OW + (acc ? 2 : 1) * total));
+    nck_conv t = *g;
+    t.OH = g->H, t.OW = g->W;
+    DwPlan pl = dw_plan_out(&t); /* rows of the input plane per tile */
+    const bool unit = g->sh == 1 && g->sw == 1;
+    /* staged gy rows: those reached from the tile's rows, plus one for the rounding of the first */
+    pl.srows = unit ? pl.rows + (int)(g->KH - 1) * g->dh : (pl.rows - 1 + (int)(g->KH - 1) * g->dh) / g->sh + 2;
+    pl.scols = (int)(unit ? g->W + (g->KW - 1) * g->dw : g->OW);
+    const size_t smem = dw_smem(pl);
+    const int64_t blocks = g->N * g->C * pl.tiles;
+    const bool k3 = g->KH == 3 && g->KW == 3;
+    /* unit strides: newch's axpy rows (fused multiply-adds) */
+    auto k = unit ? (k3 ? k_dw_dx<true, true, 3, 3> : k_dw_dx<true, true, 0, 0>)
+                  : (g->sw == 1 ? (k3 ? k_dw_dx<true, false, 3, 3> : k_dw_dx<true, false, 0, 0>)
+                                : (k3 ? k_dw_dx<false, false, 3, 3> : k_dw_dx<false, false, 0, 0>));
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<(unsigned)blocks, kDwThreads, smem, NCK_STREAM(d)>>>(*g, gy, w, gx, acc, pl, make_fastdiv((uint32_t)g->W));
     NCK_LAUNCHED(d, 1);
-}
-
-// weight grads: per channel, per tap, the sum over samples and output positions of x * gy;
-// grid (C, splits over N), at most NCK_DW_MAX_TAPS taps, partials combined in order
-__global__ void k_dw_dw_partial(nck_conv g, const float *__restrict__ x, const float *__restrict__ gy,
-                                float *__restrict__ part, int64_t per_split) {
-    __shared__ float sm[kThreads / 32][NCK_DW_MAX_TAPS];
-    int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < g.N ? n0 + per_split : g.N;
-    int KK = (int)(g.KH * g.KW);
-    float acc[NCK_DW_MAX_TAPS];
-    for (int k = 0; k < NCK_DW_MAX_TAPS; k++) acc[k] = 0.0f;
-    int64_t L = g.OH * g.OW;
-    for (int64_t n = n0; n < n1; n++) {
-        const float *xp = x + (n * g.C + c) * g.H * g.W, *gp = gy + (n * g.C + c) * L;
-        for (int64_t l = threadIdx.x; l < L; l += blockDim.x) {
-            int64_t oy = l / g.OW, ox = l - oy * g.OW;
-            float gv = gp[l];
-            for (int k = 0; k < KK; k++) {
-                int64_t ki = k / g.KW, kj = k - ki * g.KW;
-                int64_t iy = oy * g.sh - g.ph + ki * g.dh, ix = ox * g.sw - g.pw + kj * g.dw;
-                if (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W) acc[k] = fmaf(xp[iy * g.W + ix], gv, acc[k]);
-            }
-        }
-    }
-    int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int k = 0; k < KK; k++) {
-        float v = acc[k];
-        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) sm[wid][k] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < KK) {
-        float s = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += sm[w][threadIdx.x];
-        part[(blockIdx.y * g.C + c) * KK + threadIdx.x] = s;
-    }
-}
-
-__global__ void k_dw_dw_combine(const float *__restrict__ part, int splits, int64_t C, int KK, float *__restrict__ gw) {
-    int64_t total = C * KK;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        float s = gw[t];
-        for (int k = 0; k < splits; k++) s += part[k * total + t];
-        gw[t] = s;
-    }
 }
 
 extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb) {
-    (void)gb; /* the bias gradient goes through nck_conv_bias_grad */
-    int KK = (int)(g->KH * g->KW);
-    if (g->N * g->C <= 0 || KK <= 0) return;
-    if (KK > NCK_DW_MAX_TAPS) return; /* the caller takes the im2col path for larger kernels */
+    const int KK = (int)(g->KH * g->KW);
+    if (g->N * g->C <= 0 || KK <= 0 || KK > NCK_DW_MAX_TAPS) return;
     Scope sc(d, "dw_dw", 2.0 * g->N * g->C * g->OH * g->OW * KK,
              4.0 * (g->N * g->C * (g->H * g->W + g->OH * g->OW)));
-    int64_t splits = ((int64_t)d->sm_count * 4 + g->C - 1) / g->C;
+    const DwPlan pl = dw_plan_out(g);
+    const size_t smem = sizeof(float) * (size_t)pl.srows * pl.scols;
+    const bool k3 = g->KH == 3 && g->KW == 3;
+    auto kp = k3 ? k_dw_dw_partial<3, 3> : k_dw_dw_partial<0, 0>;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kp, kDwThreads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 2;
+    cudaGetLastError();
+    int64_t splits = ((int64_t)d->sm_count * per_sm + g->C - 1) / g->C;
     if (splits > g->N) splits = g->N;
     if (splits < 1) splits = 1;
-    int64_t per = (g->N + splits - 1) / splits;
+    const int64_t per = (g->N + splits - 1) / splits;
     splits = (g->N + per - 1) / per;
     float *part = (float *)d->scratch;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid((unsigned)g->C, (unsigned)splits);
-    k_dw_dw_partial<<<grid, kThreads, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
-    k_dw_dw_combine<<<grid_for(d, g->C * KK), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, g->C, KK, gw);
+    kp<<<grid, kDwThreads, smem, NCK_STREAM(d)>>>(*g, x, gy, part, per, pl, make_fastdiv((uint32_t)g->OW));
+    k_dw_dw_combine<<<grid_for(d, g->C * (KK + 1)), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, g->C, KK, gw, gb);
     NCK_LAUNCHED(d, 2);
 }
 

@@ -32,35 +32,49 @@ extern "C" void nck_index_select(nck_dev *d, const void *x, const int32_t *idx, 
     NCK_LAUNCHED(d, 1);
 }
 
-// gx[n, j] += sum over b with idx[b] == n of g[b, j], rows b visited in order (no atomics):
-// one thread per (n, j); for a small table (an embedding of 96 rows) every thread scans the indices
-__global__ void k_index_select_bwd(const float *__restrict__ g, const int32_t *__restrict__ idx, float *__restrict__ gx,
-                                   int64_t B, int64_t N, int64_t row) {
-    extern __shared__ int32_t sidx[];
-    int64_t total = N * row;
-    for (int64_t t0 = blockIdx.x * (int64_t)blockDim.x; t0 < total; t0 += (int64_t)gridDim.x * blockDim.x) {
-        int64_t t = t0 + threadIdx.x;
-        int64_t n = t / row, j = t - n * row;
-        float acc = t < total ? gx[t] : 0.0f;
-        for (int64_t b0 = 0; b0 < B; b0 += 2048) {
-            int64_t nb = B - b0 < 2048 ? B - b0 : 2048;
+// gx[n, j] += sum over b with idx[b] == n of g[b, j], rows b added in ascending order (newch adds
+// them in that order; no atomics). Block (n, column chunk): the block scans the indices 256 at a
+// time, compacts the positions that point at row n (a warp ballot, then a prefix over the warps keeps
+// them in order) and every thread adds those rows' values in its column. The indices are read once
+// per destination row from L2; the gradient rows once in all.
+__global__ void __launch_bounds__(256) k_index_select_bwd(const float *__restrict__ g, const int32_t *__restrict__ idx,
+                                                          float *__restrict__ gx, int64_t B, int64_t N, int64_t row) {
+    __shared__ int32_t hits[256];
+    __shared__ int warp_base[9];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t j = blockIdx.y * (int64_t)blockDim.x + threadIdx.x;
+    for (int64_t n = blockIdx.x; n < N; n += gridDim.x) {
+        float acc = j < row ? gx[n * row + j] : 0.0f;
+        for (int64_t b0 = 0; b0 < B; b0 += blockDim.x) {
+            const int64_t b = b0 + threadIdx.x;
+            const bool hit = b < B && __ldg(idx + b) == (int32_t)n;
+            const unsigned mask = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) warp_base[warp + 1] = __popc(mask);
             __syncthreads();
-            for (int64_t k = threadIdx.x; k < nb; k += blockDim.x) sidx[k] = idx[b0 + k];
+            if (threadIdx.x == 0) {
+                warp_base[0] = 0;
+                for (int w = 1; w <= (int)(blockDim.x >> 5); w++) warp_base[w] += warp_base[w - 1];
+            }
             __syncthreads();
-            if (t < total)
-                for (int64_t k = 0; k < nb; k++)
-                    if (sidx[k] == n) acc += g[(b0 + k) * row + j];
+            if (hit) hits[warp_base[warp] + __popc(mask & ((1u << lane) - 1u))] = (int32_t)(b - b0);
+            __syncthreads();
+            const int count = warp_base[blockDim.x >> 5];
+            if (j < row)
+                for (int k = 0; k < count; k++) acc += __ldg(g + (b0 + hits[k]) * row + j);
+            __syncthreads(); // hits and warp_base are rewritten by the next chunk
         }
-        if (t < total) gx[t] = acc;
+        if (j < row) gx[n * row + j] = acc;
     }
 }
 
 extern "C" void nck_index_select_bwd(nck_dev *d, const float *g, const int32_t *idx, float *gx, int64_t B, int64_t N,
                                      int64_t row) {
     if (B <= 0 || N * row <= 0) return;
-    Scope sc(d, "index_select_bwd");
-    k_index_select_bwd<<<grid_for(d, N * row), kThreads, 2048 * sizeof(int32_t), NCK_STREAM(d)>>>(g, idx, gx, B, N,
-                                                                                                   row);
+    Scope sc(d, "index_select_bwd", 0.0, 4.0 * (B * row + 2 * N * row) + 4.0 * B);
+    const int64_t chunks = (row + 255) / 256;
+    int64_t rows = N < 65535 ? N : 65535;
+    dim3 grid((unsigned)rows, (unsigned)chunks);
+    k_index_select_bwd<<<grid, 256, 0, NCK_STREAM(d)>>>(g, idx, gx, B, N, row);
     NCK_LAUNCHED(d, 1);
 }
 

@@ -224,11 +224,24 @@ extern "C" void nck_axpy(nck_dev *d, int64_t n, float a, const float *x, float *
 }
 
 // ---- strided copies ------------------------------------------------------------------------------
+//
+// A strided view is walked in row-major order of its shape: element i of the contiguous side maps to
+// offset(i) on the strided side. Dims laid out back to back are merged first. When the innermost
+// merged dim is contiguous on both sides with a length and outer strides that keep 16-byte
+// alignment, each thread moves a float4 and divides only for the outer dims; index arithmetic is
+// 32-bit with precomputed multiply-shift divisors whenever the view's offsets fit.
 
 struct Strided {
     int nd;
     int64_t shape[NCK_MAXD];
     int64_t stride[NCK_MAXD];
+};
+
+struct Strided32 {
+    int nd;
+    uint32_t shape[NCK_MAXD];
+    uint32_t stride[NCK_MAXD];
+    FastDiv div[NCK_MAXD];
 };
 
 // element offset of linear (row-major) index i in a strided view
@@ -242,10 +255,55 @@ __device__ __forceinline__ int64_t strided_offset(const Strided &v, int64_t i) {
     return off;
 }
 
-template <typename T>
-__global__ void k_copy_strided(Strided v, const T *__restrict__ src, T *__restrict__ dst, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        dst[i] = src[strided_offset(v, i)];
+__device__ __forceinline__ uint32_t strided_offset32(const Strided32 &v, uint32_t i) {
+    uint32_t off = 0;
+#pragma unroll
+    for (int k = NCK_MAXD - 1; k >= 0; k--) {
+        if (k >= v.nd) continue;
+        const uint32_t q = v.div[k].div(i);
+        off += (i - q * v.shape[k]) * v.stride[k];
+        i = q;
+    }
+    return off;
+}
+
+// MODE 0: dst[i] = src[off(i)] (gather); 1: dst[off(i)] += src[i]; 2: dst[off(i)] = src[i]
+template <typename T, int MODE>
+__global__ void k_strided64(Strided v, const T *__restrict__ src, T *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = strided_offset(v, i);
+        if (MODE == 0) dst[i] = src[o];
+        else if (MODE == 1) dst[o] += src[i];
+        else dst[o] = src[i];
+    }
+}
+
+template <typename T, int MODE>
+__global__ void k_strided32(Strided32 v, const T *__restrict__ src, T *__restrict__ dst, uint32_t n) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const uint32_t o = strided_offset32(v, i);
+        if (MODE == 0) dst[i] = src[o];
+        else if (MODE == 1) dst[o] += src[i];
+        else dst[o] = src[i];
+    }
+}
+
+// float4 items: v describes the view in items of 4 floats (the innermost dim divided by 4)
+template <int MODE>
+__global__ void k_strided32_v4(Strided32 v, const float4 *__restrict__ src, float4 *__restrict__ dst, uint32_t n4) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const uint32_t o = strided_offset32(v, i);
+        if (MODE == 0) {
+            dst[i] = __ldg(src + o);
+        } else if (MODE == 1) {
+            float4 a = dst[o];
+            const float4 b = __ldg(src + i);
+            a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+            dst[o] = a;
+        } else {
+            dst[o] = __ldg(src + i);
+        }
+    }
 }
 
 // merges dims that are laid out back to back (fewer divisions per element)
@@ -271,45 +329,87 @@ static Strided simplify(int ndim, const int64_t *shape, const int64_t *stride) {
     return v;
 }
 
+// the 32-bit form of v when every index and offset fits (strides >= 0); `unit` elements per item
+static bool to32(const Strided &v, int64_t n, int unit, Strided32 *o) {
+    if (n >= ((int64_t)1 << 31)) return false;
+    int64_t span = 0;
+    o->nd = v.nd;
+    for (int k = 0; k < v.nd; k++) {
+        int64_t sh = v.shape[k], st = v.stride[k];
+        if (k == v.nd - 1 && unit > 1) sh /= unit, st = 1;
+        else if (unit > 1) st /= unit;
+        if (st < 0) return false;
+        span += (sh - 1) * st;
+        o->shape[k] = (uint32_t)sh;
+        o->stride[k] = (uint32_t)st;
+        o->div[k] = make_fastdiv((uint32_t)sh);
+    }
+    return span < ((int64_t)1 << 31);
+}
+
+// float4 items possible: contiguous innermost dim of a multiple of 4, outer strides multiples of 4,
+// both base pointers 16-byte aligned
+static bool vec4_ok(const Strided &v, const void *a, const void *b) {
+    if (v.stride[v.nd - 1] != 1 || (v.shape[v.nd - 1] & 3) || (((uintptr_t)a | (uintptr_t)b) & 15)) return false;
+    for (int k = 0; k < v.nd - 1; k++)
+        if (v.stride[k] & 3) return false;
+    return true;
+}
+
+template <int MODE>
+static void strided_launch(nck_dev *d, int es, const Strided &v, int64_t n, const void *src, void *dst) {
+    cudaStream_t st = NCK_STREAM(d);
+    Strided32 v32;
+    if (es == 4 && vec4_ok(v, src, dst) && to32(v, n / 4, 4, &v32)) {
+        k_strided32_v4<MODE><<<grid_for(d, n / 4), kThreads, 0, st>>>(v32, (const float4 *)src, (float4 *)dst,
+                                                                     (uint32_t)(n / 4));
+    } else if (to32(v, n, 1, &v32)) {
+        if (es == 4) k_strided32<int32_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v32, (const int32_t *)src, (int32_t *)dst, (uint32_t)n);
+        else if (es == 2) k_strided32<int16_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v32, (const int16_t *)src, (int16_t *)dst, (uint32_t)n);
+        else k_strided32<int8_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v32, (const int8_t *)src, (int8_t *)dst, (uint32_t)n);
+    } else {
+        if (es == 4) k_strided64<int32_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v, (const int32_t *)src, (int32_t *)dst, n);
+        else if (es == 2) k_strided64<int16_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v, (const int16_t *)src, (int16_t *)dst, n);
+        else k_strided64<int8_t, MODE><<<grid_for(d, n), kThreads, 0, st>>>(v, (const int8_t *)src, (int8_t *)dst, n);
+    }
+    NCK_LAUNCHED(d, 1);
+}
+
 extern "C" void nck_copy_strided(nck_dev *d, int es, int ndim, const int64_t *shape, const int64_t *stride,
                                  const void *src, void *dst) {
     int64_t n = 1;
     for (int k = 0; k < ndim; k++) n *= shape[k];
     if (n <= 0) return;
     Strided v = simplify(ndim, shape, stride);
-    Scope s(d, "copy_strided");
-    cudaStream_t st = NCK_STREAM(d);
+    Scope s(d, "copy_strided", 0.0, 2.0 * es * n);
     if (v.nd == 1 && v.stride[0] == 1) {
-        cudaMemcpyAsync(dst, src, (size_t)n * es, cudaMemcpyDeviceToDevice, st);
+        cudaMemcpyAsync(dst, src, (size_t)n * es, cudaMemcpyDeviceToDevice, NCK_STREAM(d));
         return;
     }
-    int g = grid_for(d, n);
-    if (es == 4) k_copy_strided<int32_t><<<g, kThreads, 0, st>>>(v, (const int32_t *)src, (int32_t *)dst, n);
-    else if (es == 2) k_copy_strided<int16_t><<<g, kThreads, 0, st>>>(v, (const int16_t *)src, (int16_t *)dst, n);
-    else k_copy_strided<int8_t><<<g, kThreads, 0, st>>>(v, (const int8_t *)src, (int8_t *)dst, n);
-    NCK_LAUNCHED(d, 1);
+    if (es == 4) {
+        /* integers and floats move alike; the float4 path reads them as floats */
+        strided_launch<0>(d, 4, v, n, src, dst);
+    } else {
+        strided_launch<0>(d, es, v, n, src, dst);
+    }
 }
 
-// dst[view(i)] += src[i]. Every destination element is hit at most once (views of a permutation or
-// a slice), so there is no write conflict.
-__global__ void k_acc_strided(Strided v, const float *__restrict__ src, float *__restrict__ dst, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        dst[strided_offset(v, i)] += src[i];
-}
-
+// dst[view(i)] (+)= src[i]. Every destination element is hit at most once (views of a permutation
+// or a slice), so there is no write conflict.
 extern "C" void nck_acc_strided(nck_dev *d, int ndim, const int64_t *shape, const int64_t *dst_stride,
-                                const float *src, float *dst) {
+                                const float *src, float *dst, int acc) {
     int64_t n = 1;
     for (int k = 0; k < ndim; k++) n *= shape[k];
     if (n <= 0) return;
     Strided v = simplify(ndim, shape, dst_stride);
-    Scope s(d, "acc_strided");
+    Scope s(d, "acc_strided", 0.0, (acc ? 12.0 : 8.0) * n);
     if (v.nd == 1 && v.stride[0] == 1) {
-        nck_axpy(d, n, 1.0f, src, dst);
+        if (acc) nck_axpy(d, n, 1.0f, src, dst);
+        else cudaMemcpyAsync(dst, src, (size_t)n * 4, cudaMemcpyDeviceToDevice, NCK_STREAM(d));
         return;
     }
-    k_acc_strided<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(v, src, dst, n);
-    NCK_LAUNCHED(d, 1);
+    if (acc) strided_launch<1>(d, 4, v, n, src, dst);
+    else strided_launch<2>(d, 4, v, n, src, dst);
 }
 
 // ---- dtype conversion (newch ops_shape.c:463-504: truncation toward zero, saturation, NaN -> 0) -------

@@ -73,7 +73,7 @@ void nck_copy_strided(nck_dev *d, int es, int ndim, const int64_t *shape, const 
                       void *dst);
 /* dst viewed through shape/dst_stride += src (contiguous): backward of a strided view */
 void nck_acc_strided(nck_dev *d, int ndim, const int64_t *shape, const int64_t *dst_stride, const float *src,
-                     float *dst);
+                     float *dst, int acc); /* acc 0: every strided element is stored, not added */
 /* dtype conversion (reference dtype codes: 0 f32, 1 i32, 3 i8, 4 u8); saturating, NaN -> 0 */
 void nck_convert(nck_dev *d, int from, int to, const void *src, void *dst, int64_t n);
 
@@ -241,9 +241,14 @@ int nck_convtap(nck_dev *d, int mode, const nck_conv *g, const nck_tapgeom *t, c
 int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
 /* whether nck_conv_direct_dw takes the 3x3 one-channel kernel (and can add the bias gradient) */
 int nck_conv_direct3_ok(const nck_conv *g);
+/* depthwise (groups == C == OC): shared-memory plane tiles; nck_dw_ok says whether a geometry fits
+ * them (at most NCK_DW_MAX_TAPS taps, tiles within shared memory) */
+#define NCK_DW_MAX_TAPS 25
+int nck_dw_ok(const nck_conv *g);
 void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const float *w, const float *b, float *y);
-void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx);
-#define NCK_DW_MAX_TAPS 25 /* nck_dw_dw handles kernels up to 5x5 */
+/* gx = (acc ? gx : 0) + input gradient */
+void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const float *w, float *gx, int acc);
+/* gw += weight gradient; gb (may be NULL) += bias gradient */
 void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
 void nck_pool_fwd(nck_dev *d, const nck_conv *g, const float *x, float *y, int32_t *arg, int is_max);
 void nck_pool_bwd(nck_dev *d, const nck_conv *g, const float *gy, const int32_t *arg, float *gx, int is_max, int acc);

@@ -94,7 +94,8 @@ static nc_status conv_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape) {
     return NC_OK;
 }
 
-static int is_depthwise(const nck_conv *g) { return g->G == g->C && g->OC == g->C; }
+/* depthwise layers the shared-memory plane kernels take (others go through the grouped paths) */
+static int is_depthwise(const nck_conv *g) { return g->G == g->C && g->OC == g->C && nck_dw_ok(g); }
 static int is_pointwise(const nck_conv *g) {
     return g->KH == 1 && g->KW == 1 && g->sh == 1 && g->sw == 1 && g->ph == 0 && g->pw == 0;
 }
@@ -249,18 +250,13 @@ static void conv_bwd(nc_node *n) {
                     nck_convtap_plan(nc__k(ctx), &g, &tg);
     float *gb_direct = gb && direct_dw && nck_conv_direct3_ok(&g) ? (float *)gb->data : NULL;
     float *gb_tap = gb && !gb_direct && tap && nck_tap_pack_colsum_ok(nc__k(ctx), &tg, tg.OCp) ? (float *)gb->data : NULL;
-    if (gb && !gb_direct && !gb_tap) nck_conv_bias_grad(nc__k(ctx), G, (float *)gb->data, g.N, g.OC, L);
+    /* depthwise: the weight-gradient pass also sums the bias gradient */
+    float *gb_dw = gb && gw && is_depthwise(&g) ? (float *)gb->data : NULL;
+    if (gb && !gb_direct && !gb_tap && !gb_dw) nck_conv_bias_grad(nc__k(ctx), G, (float *)gb->data, g.N, g.OC, L);
     if (is_depthwise(&g)) {
-        if (gx) {
-            zero_if_fresh(ctx, gx, &acc_gx);
-            nck_dw_dx(nc__k(ctx), &g, G, Wt, (float *)gx->data);
-        }
-        if (!gw) return;
-        if (g.KH * g.KW <= NCK_DW_MAX_TAPS) {
-            nck_dw_dw(nc__k(ctx), &g, X, G, (float *)gw->data, NULL);
-            return;
-        }
-        gx = NULL; /* larger depthwise kernels: dW through the grouped im2col path below */
+        if (gx) nck_dw_dx(nc__k(ctx), &g, G, Wt, (float *)gx->data, acc_gx);
+        if (gw) nck_dw_dw(nc__k(ctx), &g, X, G, (float *)gw->data, gb_dw);
+        return;
     }
     if (gw && use_direct(&g)) {
         /* few taps per group: dW straight from x and dY, no unfolded copy */

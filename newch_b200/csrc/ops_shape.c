@@ -42,14 +42,17 @@ static nc_status gather_by_map(nc_node *n, layout_map map) {
     return NC_OK;
 }
 
-static void scatter_grad_by_map(nc_node *n, layout_map map) {
+/* covers_all: the map reaches every element of x (a permutation), so a fresh gradient buffer is
+ * stored whole instead of zero-filled and added to */
+static void scatter_grad_by_map(nc_node *n, layout_map map, int covers_all) {
     nc_tensor *x = n->in[0], *o = n->out;
-    nc_tensor *gx = nc__grad_buf(x);
+    int acc = 1;
+    nc_tensor *gx = covers_all ? nc__grad_buf_acc(x, &acc) : nc__grad_buf(x);
     if (!gx || nc_numel(o) == 0) return;
     int64_t cst[NC_MAX_DIMS], st[NC_MAX_DIMS], off = 0;
     nc__contig_strides(x->ndim, x->shape, cst);
     map(n, cst, st, &off);
-    nck_acc_strided(nc__k(x->ctx), o->ndim, o->shape, st, (const float *)o->grad->data, (float *)gx->data + off);
+    nck_acc_strided(nc__k(x->ctx), o->ndim, o->shape, st, (const float *)o->grad->data, (float *)gx->data + off, acc);
 }
 
 /* gradient of an op whose output is x's elements in x's row-major order */
@@ -192,7 +195,7 @@ static int transpose_map(const nc_node *n, const int64_t *xst, int64_t *st, int6
 
 static int transpose_view(nc_node *n, int nd, const int64_t *shape) { return as_alias(n, nd, shape, transpose_map); }
 static nc_status transpose_fwd(nc_node *n) { return gather_by_map(n, transpose_map); }
-static void transpose_bwd(nc_node *n) { scatter_grad_by_map(n, transpose_map); }
+static void transpose_bwd(nc_node *n) { scatter_grad_by_map(n, transpose_map, 1); }
 
 const nc_op_def nc_op_transpose = {"transpose", NC_OPF_VIEW, 0, transpose_infer, transpose_view, transpose_fwd,
                                    transpose_bwd};
@@ -237,7 +240,7 @@ static int slice_map(const nc_node *n, const int64_t *xst, int64_t *st, int64_t 
 
 static int slice_view(nc_node *n, int nd, const int64_t *shape) { return as_alias(n, nd, shape, slice_map); }
 static nc_status slice_fwd(nc_node *n) { return gather_by_map(n, slice_map); }
-static void slice_bwd(nc_node *n) { scatter_grad_by_map(n, slice_map); }
+static void slice_bwd(nc_node *n) { scatter_grad_by_map(n, slice_map, 0); }
 
 const nc_op_def nc_op_slice = {"slice", NC_OPF_VIEW, 0, slice_infer, slice_view, slice_fwd, slice_bwd};
 

@@ -92,7 +92,8 @@ class Replayer:
     OPTIMIZERS = ("nc_sgd", "nc_adam", "nc_adamw", "nc_rmsprop")
 
     def __init__(self, lib, trace: Trace, seed_offset: int = 0, check: bool = True, pinned: bool = False,
-                 grads: bool = False, capture=(), force_reference: int | None = None):
+                 grads: bool = False, capture=(), force_reference: int | None = None, capture_params: bool = False,
+                 set_params=None):
         self.lib = lib
         self.trace = trace
         self.check = check
@@ -115,6 +116,13 @@ class Replayer:
         self._blobs: dict = {}
         self.seed_offset = seed_offset
         self.force_reference = force_reference  # overrides nc_init's config field when not None
+        # capture_params: each optimizer parameter's bytes after every optimizer step, in
+        # self.params_after (one list per step); set_params: such a list of lists, written into the
+        # parameters after each step instead (the step's update is replaced by the given values)
+        self.capture_params = capture_params
+        self.set_params = set_params
+        self.params_after: list = []
+        self._steps_done = 0
         self._fns = {name: getattr(lib, name) for name in {c[0] for c in trace.calls}}
         self._prepared = [self._prepare(i, c) for i, c in enumerate(trace.calls)]
 
@@ -220,11 +228,26 @@ class Replayer:
                 self.items.append((i, r))
             elif name == "nc_copy_to" and outbuf is not None:
                 self.outputs.append((i, bytes(outbuf)))
-            elif self.capture_grads:
+            if name in self.OPTIMIZERS:
+                self._param_handles = next((list(v) for kind, v in conv if kind == 3), [])
+            elif name == "nc_optim_step" and (self.capture_params or self.set_params is not None):
+                self._after_step()
+            if self.capture_grads:
                 if name in self.OPTIMIZERS:
                     self._param_handles = next((list(v) for kind, v in conv if kind == 3), [])
                 elif name in ("nc_backward", "nc_backward_ex"):
                     self.grads.append((i, [self._grad_bytes(h[p]) for p in self._param_handles]))
+
+    def _after_step(self):
+        k = self._steps_done
+        self._steps_done += 1
+        if self.set_params is not None and k < len(self.set_params):
+            for p, data in zip(self._param_handles, self.set_params[k]):
+                buf = (ctypes.c_char * len(data)).from_buffer_copy(data)
+                if not self.lib.nc_copy_from(self.h[p], buf, len(data)):
+                    raise ReplayMismatch(f"nc_copy_from of a parameter failed: {self._error()}")
+        if self.capture_params:
+            self.params_after.append([self._tensor_bytes(self.h[p]) for p in self._param_handles])
 
     def _tensor_bytes(self, t):
         n = int(self.lib.nc_numel(t)) * {0: 4, 1: 4, 2: 2, 3: 1, 4: 1}[int(self.lib.nc_get_dtype(t))]

@@ -1,6 +1,8 @@
 """Generates tests/golden/trace_spread.json: how far the reference engine's two CPU kernel tiers (its
 AVX2+FMA tier and its scalar reference tier, selected by nc_config.force_reference) lie apart on each
-workload trace, per backward pass and parameter (gradients) and per parameter (after training).
+workload trace: per backward pass and parameter, the gradients computed from the same parameters
+(the scalar-tier run is given the AVX2 run's parameters after every step), and per parameter, the
+parameters after the whole run (each tier on its own trajectory), max-norm and Frobenius.
 
 Both tiers are newch's own correct fp32 arithmetic; they differ only in summation order. Where a
 gradient is a long sum with heavy cancellation (a convolution weight whose output feeds BatchNorm
@@ -36,24 +38,29 @@ def normwise(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30)) if b.size else 0.0
 
 
+def frobenius(a: np.ndarray, b: np.ndarray) -> float:
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / max(float(np.linalg.norm(b)), 1e-30)) if b.size else 0.0
+
+
 def spread(name: str) -> dict:
     lib = capi.load(REF_LIB)
     t = replay.Trace(name)
-    runs = []
-    for force in (0, 1):
-        r = replay.Replayer(lib, t, grads=True, force_reference=force)
-        r.run_all()
-        runs.append(r)
-    a, b = runs
+    a = replay.Replayer(lib, t, grads=True, capture_params=True)
+    a.run_all()
+    synced = replay.Replayer(lib, t, grads=True, force_reference=1, set_params=a.params_after)
+    synced.run_all()
+    free = replay.Replayer(lib, t, force_reference=1)
+    free.run_all()
     grads = []
-    for (_, ga), (_, gb) in zip(a.grads, b.grads):
-        grads.append([normwise(np.frombuffer(x, np.float32), np.frombuffer(y, np.float32))
-                      if x is not None and y is not None else 0.0 for x, y in zip(gb, ga)])
-    params = [normwise(np.frombuffer(y, np.float32), np.frombuffer(x, np.float32))
-              for (_, x), (_, y) in zip(a.outputs, b.outputs)]
-    for r in runs:
+    for (_, ga), (_, gb) in zip(a.grads, synced.grads):
+        grads.append([normwise(np.frombuffer(y, np.float32), np.frombuffer(x, np.float32))
+                      if x is not None and y is not None else 0.0 for x, y in zip(ga, gb)])
+    pa = [(np.frombuffer(x, np.float32), np.frombuffer(y, np.float32)) for (_, x), (_, y) in zip(a.outputs, free.outputs)]
+    out = {"grads": grads, "params": [normwise(y, x) for x, y in pa], "params_frob": [frobenius(y, x) for x, y in pa]}
+    for r in (a, synced, free):
         lib.nc_free_ctx(r.ctx)
-    return {"grads": grads, "params": params}
+    return out
 
 
 def main() -> int:

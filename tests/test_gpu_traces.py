@@ -2,30 +2,34 @@
 on the B200 engine and on the reference engine (CPU), step by step.
 
 Checked, per configuration and GEMM mode:
-- every nc_item result (the per-step losses, BatchNorm's num_batches_tracked);
-- every parameter's gradient after every backward pass;
-- every parameter after the recorded optimizer steps;
+- the per-step losses and every parameter's gradient after every backward pass, with the engine's
+  parameters set to the reference's after each optimizer step (so every step starts from the same
+  weights and the comparison measures that step's arithmetic, not a drift of the trajectory);
+- every parameter after the recorded optimizer steps, each engine on its own trajectory;
 - for the int8 model (config 5): every layer's output, the quantized weights and their scales, the
   GELU outputs and the logits bit for bit, and each layer's int32 accumulators against the oracle's
   exact integer product of the same quantized operands.
 
-Tolerances (normwise per tensor, max|got - ref| / max|ref|): the CUDA-core GEMM path (NC_GEMM=ffma)
-1e-5; the default tensor-core path (3xTF32) 1e-3. The plain TF32 mode (NC_GEMM=tf32) is an opt-in
-speed mode whose GEMMs round operands to 10-bit mantissas: its gradients and parameters are held to
-5e-2, its first loss to 1e-3 and later losses to 1e-2.
+Tolerances (normwise per tensor, max|got - ref| / max|ref|, for losses relative): the CUDA-core GEMM
+path (NC_GEMM=ffma) 1e-5; the default tensor-core path (3xTF32) 1e-3. Each has a floor: twice the
+distance between the reference engine's own two kernel tiers (AVX2 and scalar) on the same tensor,
+measured the same way (tests/golden/trace_spread.json). Both tiers are correct fp32 arithmetic in
+different summation orders; where a gradient is a long sum with heavy cancellation (a convolution
+weight feeding BatchNorm: ~4e5 products per element at batch 512, summing to a result far below its
+terms) they lie up to ~6e-3 apart, and no fp32 implementation can be held closer than that.
+Parameters after training are compared in the Frobenius norm (relative), with the same floor from the
+reference tiers' own trajectories, and elementwise within 1e-3 of max|w| plus 2 * lr * steps: Adam
+normalises each gradient element by its own magnitude, so an element whose gradient is at rounding
+level moves by lr * sign(noise) per step, which two correct implementations need not share.
 
-Each tolerance has a floor: twice the distance between the reference engine's own two kernel tiers
-(AVX2 and scalar, tests/golden/trace_spread.json) on the same tensor. Both tiers are correct fp32
-arithmetic in different summation orders; where a gradient is a long sum with heavy cancellation (a
-convolution weight feeding BatchNorm: ~4e5 products per element at batch 512, summing to a result far
-below its terms) they lie up to ~6e-3 apart, and no fp32 implementation can be held closer than that.
+The plain TF32 mode (NC_GEMM=tf32) is an opt-in speed mode whose GEMMs round operands to 10-bit
+mantissas: losses within 2e-3 and gradients within 3e-2 (same parameters each step); its
+trajectories leave the reference's after the first update, so final parameters are not compared.
 
-Adam normalises each gradient element by its own magnitude, so an element whose true gradient is zero
-is moved by lr * sign(rounding noise), which two correct implementations need not share. Such elements
-are exempt by name: the bias of a convolution followed by BatchNorm (BatchNorm removes any per-channel
-shift, so the bias gets no gradient) and the key third of attention's packed input-projection bias
-(softmax is invariant to the per-row shift q . b_k). The test asserts that their reference gradients
-are indeed at rounding level before exempting them.
+Elements with no gradient by construction are exempt by name: the bias of a convolution followed by
+BatchNorm (BatchNorm removes any per-channel shift) and the key third of attention's packed
+input-projection bias (softmax is invariant to the per-row shift q . b_k). The test asserts that
+their reference gradients are indeed at rounding level before exempting them.
 """
 
 from __future__ import annotations
@@ -43,9 +47,8 @@ import ncoracle as O
 
 pytestmark = pytest.mark.gpu
 
-LOSS_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 1e-3}
-TF32_DRIFT = 1e-2  # later TF32 losses come from weights that already differ by TF32 updates
-TENSOR_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 5e-2}
+LOSS_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 2e-3}
+TENSOR_TOL = {"ffma": 1e-5, "3xtf32": 1e-3, "tf32": 3e-2}
 SPREAD = json.loads((Path(__file__).resolve().parent / "golden" / "trace_spread.json").read_text())
 SPREAD_FACTOR = 2.0
 # NC_PARITY_REPORT=<file>: every measured error (and its tolerance) is appended there as JSON lines
@@ -102,6 +105,11 @@ def zero_gradient_elements(shapes):
     return out
 
 
+def frobenius(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(np.linalg.norm(a - b) / max(float(np.linalg.norm(b)), 1e-30)) if b.size else 0.0
+
+
 def normwise(a, b):
     a, b = a.astype(np.float64), b.astype(np.float64)
     return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30)) if b.size else 0.0
@@ -109,10 +117,8 @@ def normwise(a, b):
 
 def check_losses(mode, gi, ri):
     assert len(gi) == len(ri)
-    first_loss = next((k for k, b in enumerate(ri) if b != round(b)), len(ri))
     for k, (a, b) in enumerate(zip(gi, ri)):
-        tol = TF32_DRIFT if (mode == "tf32" and k > first_loss) else LOSS_TOL[mode]
-        assert a == pytest.approx(b, rel=tol, abs=1e-6), (mode, k, gi, ri)
+        assert a == pytest.approx(b, rel=LOSS_TOL[mode], abs=1e-6), (mode, k, gi, ri)
 
 
 def floor_tol(mode, spread):
@@ -148,7 +154,7 @@ def check_gradients(name, mode, rg, rr, exempt, failures):
 
 
 def check_parameters(name, mode, got, ref, exempt, lr, steps, failures):
-    spread = SPREAD[name]["params"]
+    spread = SPREAD[name]["params_frob"]
     worst = 0.0
     for k, ((_, a), (_, b)) in enumerate(zip(got, ref)):
         x, y = np.frombuffer(a, np.float32), np.frombuffer(b, np.float32)
@@ -161,13 +167,16 @@ def check_parameters(name, mode, got, ref, exempt, lr, steps, failures):
             x, y = x[keep], y[keep]
             if y.size == 0:
                 continue
-        err = normwise(x, y)
+        err = frobenius(x, y)
         worst = max(worst, err)
         tol = floor_tol(mode, spread[k])
-        report(trace=name, mode=mode, what="param", param=k, err=err, tol=tol,
-               frob=float(np.linalg.norm(x.astype(np.float64) - y) / max(np.linalg.norm(y.astype(np.float64)), 1e-30)))
+        bound = TENSOR_TOL[mode] * float(np.max(np.abs(y))) + 2.0 * lr * steps
+        elem = float(np.max(np.abs(x.astype(np.float64) - y)))
+        report(trace=name, mode=mode, what="param", param=k, err=err, tol=tol, max_abs=elem, bound=bound)
         if err > tol:
             failures.append(f"{name} ({mode}): parameter {k} after training differs by {err:.3g} > {tol:.3g}")
+        if elem > bound:
+            failures.append(f"{name} ({mode}): parameter {k} has an element off by {elem:.3g} > {bound:.3g}")
     return worst
 
 
@@ -198,24 +207,32 @@ def compare(name, mode="ffma"):
     gpu = capi.load_b200()
     t = replay.Trace(name)
     base = name.replace("_small", "")
-    int8 = base == "cfg5"
-    kw = {"capture": INT8_CALLS} if int8 else {"grads": True}
-    rg = run(gpu, t, **kw)
-    rr = run(ref, t, **kw)
-    assert gpu.nc_ok(rg.ctx), gpu.nc_error(rg.ctx)
-    check_losses(mode, [v for _, v in rg.items], [v for _, v in rr.items])
-    assert len(rg.outputs) == len(rr.outputs)
-    if int8:
+    if base == "cfg5":
+        rg = run(gpu, t, capture=INT8_CALLS)
+        rr = run(ref, t, capture=INT8_CALLS)
+        assert gpu.nc_ok(rg.ctx), gpu.nc_error(rg.ctx)
+        check_losses(mode, [v for _, v in rg.items], [v for _, v in rr.items])
         check_int8_chain(rg, rr, [b for _, b in rg.outputs], [b for _, b in rr.outputs])
-    else:
-        exempt = zero_gradient_elements(param_shapes(rr))
-        failures = []  # every tensor is measured (and reported) before the test fails on any
-        check_gradients(name, mode, rg, rr, exempt, failures)
+        gpu.nc_free_ctx(rg.ctx)
+        ref.nc_free_ctx(rr.ctx)
+        return
+    rr = run(ref, t, grads=True, capture_params=True)
+    synced = run(gpu, t, grads=True, set_params=rr.params_after)
+    assert gpu.nc_ok(synced.ctx), gpu.nc_error(synced.ctx)
+    check_losses(mode, [v for _, v in synced.items], [v for _, v in rr.items])
+    exempt = zero_gradient_elements(param_shapes(rr))
+    failures = []  # every tensor is measured (and reported) before the test fails on any
+    check_gradients(name, mode, synced, rr, exempt, failures)
+    gpu.nc_free_ctx(synced.ctx)
+    if mode != "tf32":
+        free = run(gpu, t)
+        assert gpu.nc_ok(free.ctx), gpu.nc_error(free.ctx)
+        assert len(free.outputs) == len(rr.outputs)
         lr = {"cfg4": 3e-4}.get(base.split("_")[0], 1e-3)
-        check_parameters(name, mode, rg.outputs, rr.outputs, exempt, lr, len(t.steps()), failures)
-        assert not failures, "\n".join(failures)
-    gpu.nc_free_ctx(rg.ctx)
+        check_parameters(name, mode, free.outputs, rr.outputs, exempt, lr, len(t.steps()), failures)
+        gpu.nc_free_ctx(free.ctx)
     ref.nc_free_ctx(rr.ctx)
+    assert not failures, "\n".join(failures)
 
 
 @pytest.mark.parametrize("name", ["cfg1_small", "cfg2_small", "cfg3_small", "cfg4_small", "cfg5_small"])
