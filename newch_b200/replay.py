@@ -122,6 +122,7 @@ class Replayer:
         self.capture_params = capture_params
         self.set_params = set_params
         self.params_after: list = []
+        self.param_shapes: list = []  # shapes of the optimizer's parameters, taken when it is created
         self._steps_done = 0
         self._fns = {name: getattr(lib, name) for name in {c[0] for c in trace.calls}}
         self._prepared = [self._prepare(i, c) for i, c in enumerate(trace.calls)]
@@ -230,6 +231,7 @@ class Replayer:
                 self.outputs.append((i, bytes(outbuf)))
             if name in self.OPTIMIZERS:
                 self._param_handles = next((list(v) for kind, v in conv if kind == 3), [])
+                self.param_shapes = [self._shape(h[p]) for p in self._param_handles]
             elif name == "nc_optim_step" and (self.capture_params or self.set_params is not None):
                 self._after_step()
             if self.capture_grads:
@@ -237,6 +239,11 @@ class Replayer:
                     self._param_handles = next((list(v) for kind, v in conv if kind == 3), [])
                 elif name in ("nc_backward", "nc_backward_ex"):
                     self.grads.append((i, [self._grad_bytes(h[p]) for p in self._param_handles]))
+
+    def _shape(self, t):
+        nd = int(self.lib.nc_ndim(t))
+        s = self.lib.nc_shape(t)
+        return tuple(int(s[k]) for k in range(nd))
 
     def _after_step(self):
         k = self._steps_done

@@ -76,14 +76,9 @@ def run(lib, t, **kw):
 
 
 def param_shapes(r):
-    lib = r.lib
-    out = []
-    for p in r._param_handles:
-        h = r.h[p]
-        nd = lib.nc_ndim(h)
-        shp = lib.nc_shape(h)
-        out.append(tuple(int(shp[k]) for k in range(nd)))
-    return out
+    """The optimizer's parameter shapes, recorded by the replay while the parameters were alive (a
+    trace ends by releasing them)."""
+    return r.param_shapes
 
 
 def zero_gradient_elements(shapes):
