@@ -100,12 +100,16 @@ nc_tensor *nc__apply(const nc_op_def *op, nc_tensor **in, int n_in, const nc_op_
     const int on_tape = wants_node(ctx, op, in, n_in, persistent);
     const int viewed = op->view && !persistent && op->view(n, nd, shape);
     if (!viewed) {
-        for (int i = 0; i < n_in; i++) nc__dev(in[i]); /* host-side writes reach the device first */
+        for (int i = 0; i < n_in; i++) /* host-side writes reach the device first */
+            if (!(op->flags & NC_OPF_RECIPE) || !nc__deferred_of(in[i])) nc__dev(in[i]);
         n->out = nc__tensor_new(ctx, dt, nd, shape, persistent);
         if (!n->out) return NULL;
         scratch_scope sc;
         scratch_open(ctx, &sc, !on_tape && !persistent);
+        const int was = ctx->fwd_on_tape;
+        ctx->fwd_on_tape = on_tape;
         nc_status st = op->forward(n);
+        ctx->fwd_on_tape = was;
         scratch_close(ctx, &sc, n);
         if (st != NC_OK) return NULL;
     }
@@ -218,6 +222,8 @@ static int plan_collect(nc_ctx *ctx, nc_tensor *loss, bw_plan *pl) {
         }
         for (int i = 0; i < n->n_in; i++) {
             nc_tensor *x = n->in[i];
+            if (x->use_epoch != ep) x->use_epoch = ep, x->uses = 0;
+            x->uses++; /* consumers of x in this pass (a fused chain needs x to have one) */
             if (!nc__needs_grad(x)) continue;
             if (x->node) {
                 if (x->node->mark != ep) {
@@ -253,10 +259,13 @@ static void plan_release_node(nc_ctx *ctx, nc_node *n, nc_tensor *loss, const bw
     for (int i = 0; i < ctx->bwd_tmp_n; i++) nc__arena_free(ctx, ctx->bwd_tmp[i], ctx->bwd_tmp_size[i]);
     ctx->bwd_tmp_n = 0;
     nc_tensor *o = n->out;
-    nc__arena_free(ctx, o->grad->data, o->grad->bytes);
-    o->grad = NULL;
+    if (o->grad) { /* a node run inside a fused chain never formed its output gradient */
+        nc__arena_free(ctx, o->grad->data, o->grad->bytes);
+        o->grad = NULL;
+    }
     if (!free_graph || o == loss || !(o->flags & NC_TF_OWNS_DATA) || (o->flags & NC_TF_PERSISTENT)) return;
     if (ptr_set_has(&pl->keep, o->data)) return;
+    nc__deferred_release(o); /* recipes reading o are computed first; o's own is dropped */
     nc__arena_free(ctx, o->data, o->bytes);
     o->data = NULL;
     n->released = 1;
@@ -320,10 +329,18 @@ nc_status nc_backward_ex(nc_tensor *loss, int flags, nc_tensor *const *keep, int
 
     for (int k = 0; k < pl.order.n; k++) {
         nc_node *n = pl.order.v[k];
+        if (n->fused == pl.epoch) { /* its backward ran inside a fused chain */
+            if (!retain) plan_release_node(ctx, n, loss, &pl, free_graph);
+            plan_node_done(n);
+            continue;
+        }
         if (n->out->grad) { /* else nothing flowed into this node */
             ctx->bwd_logging = !retain;
             ctx->bwd_tmp_n = 0;
-            n->op->backward(n);
+            nc_node *chain[2];
+            const int nc = nc__fused_backward(ctx, n, chain);
+            for (int c = 0; c < nc; c++) chain[c]->fused = pl.epoch;
+            if (!nc) n->op->backward(n);
             ctx->bwd_logging = 0;
             if (!retain) plan_release_node(ctx, n, loss, &pl, free_graph);
         }
@@ -351,6 +368,7 @@ void nc_clear_grad(nc_tensor *t) {
 void nc_release_temp(nc_tensor *t) {
     if (!t || (t->flags & (NC_TF_PERSISTENT | NC_TF_ON_TAPE)) || !(t->flags & NC_TF_OWNS_DATA) || !t->data) return;
     nc_ctx *ctx = t->ctx;
+    nc__deferred_release(t);
     nc__arena_free(ctx, t->data, t->bytes);
     t->data = NULL;
     t->coh = 0;

@@ -381,6 +381,8 @@ nc_ctx *nc_init(const nc_config *cfg) {
         ctx->dev.qgemm_tc = !qg || strcmp(qg, "dp4a") != 0;
         /* exp / sigmoid / tanh / erf: newch's AVX2-tier polynomials unless the reference tier's C
          * library forms are asked for (force_reference, as newch selects its reference tier) */
+        const char *fz = getenv("NC_FUSE");
+        ctx->fuse = !fz || strcmp(fz, "0") != 0;
         const char *mm = getenv("NC_MATH");
         ctx->dev.math_mode = (c.force_reference || (mm && !strcmp(mm, "libm"))) ? NCK_MATH_LIBM : NCK_MATH_POLY;
     }
@@ -465,6 +467,7 @@ void nc_free_ctx(nc_ctx *ctx) {
 }
 
 void nc_step_end(nc_ctx *ctx) {
+    nc__deferred_reset(ctx);
     if (ctx->bn_n) nc__dp_bn_flush(ctx, 0); /* statistics staged in a step no optimizer step closed */
     nc__dp_rng_step_end(ctx);
     for (int i = 0; i < ctx->n_dchunks; i++) ctx->dchunks[i].used = 0;

@@ -7,6 +7,7 @@
 // newch's C loops do. Reductions run as fixed-shape trees and splits combined in a fixed order.
 #include <math.h>
 
+#include "k_act.cuh"
 #include "k_common.cuh"
 #include "k_math.cuh"
 
@@ -786,13 +787,14 @@ __global__ void k_bn_eval_stats(const float *__restrict__ rm, const float *__res
     }
 }
 
-// y = x * a + d per channel, a = w * invstd, d = b - mean * a; flat over all elements (V = 4: float4
-// items, planes of a multiple of 4 floats)
+// y = act(x * a + d) per channel, a = w * invstd, d = b - mean * a (act < 0: none); flat over all
+// elements (V = 4: float4 items, planes of a multiple of 4 floats)
 template <int V>
 __global__ void __launch_bounds__(256) k_bn_norm(const float *__restrict__ x, const float *__restrict__ w,
                                                  const float *__restrict__ b, const float *__restrict__ mean,
                                                  const float *__restrict__ invstd, float *__restrict__ y, int64_t NC,
-                                                 int64_t C, int64_t S, FastDiv dsv, FastDiv dc) {
+                                                 int64_t C, int64_t S, FastDiv dsv, FastDiv dc, int act = -1,
+                                                 float act_s = 0.0f) {
     const int64_t SV = S / V, total = NC * SV;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t c;
@@ -805,10 +807,11 @@ __global__ void __launch_bounds__(256) k_bn_norm(const float *__restrict__ x, co
         float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
         if constexpr (V == 4) {
             float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
-            v.x = v.x * a + dd, v.y = v.y * a + dd, v.z = v.z * a + dd, v.w = v.w * a + dd;
+            v.x = epi_fwd(act, act_s, v.x * a + dd), v.y = epi_fwd(act, act_s, v.y * a + dd);
+            v.z = epi_fwd(act, act_s, v.z * a + dd), v.w = epi_fwd(act, act_s, v.w * a + dd);
             reinterpret_cast<float4 *>(y)[i] = v;
         } else {
-            y[i] = __ldg(x + i) * a + dd;
+            y[i] = epi_fwd(act, act_s, __ldg(x + i) * a + dd);
         }
     }
 }
@@ -838,11 +841,10 @@ static int64_t bn_splits(int64_t resident, int64_t N, int64_t C, int64_t S) {
 }
 
 
-extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
-                                 float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
-                                 float eps, int stage) {
-    Scope sc(d, "bn_fwd", 0.0, 8.0 * N * C * S);
-    const bool v4 = bn_vec4(S, x, y, x);
+extern "C" void nck_bn_stats_train(nck_dev *d, const float *x, float *mean, float *invstd, float *rm, float *rv,
+                                   int64_t N, int64_t C, int64_t S, float mom, float eps, int stage) {
+    Scope sc(d, "bn_fwd", 0.0, 4.0 * N * C * S);
+    const bool v4 = bn_vec4(S, x, x, x);
     static int res4 = 0, res1 = 0;
     if (v4 && !res4) res4 = resident_blocks(d, k_bn_stats<4>, kThreads);
     if (!v4 && !res1) res1 = resident_blocks(d, k_bn_stats<1>, kThreads);
@@ -853,12 +855,80 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
     const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits, stage};
     if (v4) k_bn_stats<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
     else k_bn_stats<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, part, N, C, S, per, fin, d->counters);
-    int64_t planes = N * C;
-    if (v4) k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
-                                                                             BN_DIVS(S, 4), make_fastdiv((uint32_t)C));
-    else k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
-                                                                             BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
-    NCK_LAUNCHED(d, 2);
+    NCK_LAUNCHED(d, 1);
+}
+
+extern "C" void nck_bn_apply(nck_dev *d, const float *x, const float *w, const float *b, const float *mean,
+                             const float *invstd, float *y, int64_t N, int64_t C, int64_t S, int act, float act_s) {
+    const int64_t planes = N * C;
+    if (planes * S <= 0) return;
+    Scope sc(d, act < 0 ? "bn_fwd" : "bn_act_fwd", 0.0, 8.0 * planes * S);
+    if (bn_vec4(S, x, y, x))
+        k_bn_norm<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                         BN_DIVS(S, 4), make_fastdiv((uint32_t)C), act,
+                                                                         act_s);
+    else
+        k_bn_norm<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(x, w, b, mean, invstd, y, planes, C, S,
+                                                                         BN_DIVS(S, 1), make_fastdiv((uint32_t)C), act,
+                                                                         act_s);
+    NCK_LAUNCHED(d, 1);
+}
+
+extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
+                                 float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom,
+                                 float eps, int stage) {
+    nck_bn_stats_train(d, x, mean, invstd, rm, rv, N, C, S, mom, eps, stage);
+    nck_bn_apply(d, x, w, b, mean, invstd, y, N, C, S, -1, 0.0f);
+}
+
+// ---- BatchNorm + activation + 2 x 2 / stride 2 max pooling, fused ---------------------------------------
+//
+// The pooled output and its first-max argmax (index in the input plane, as the pooling kernels
+// store it) straight from the BatchNorm input: each element of a window is normalised and activated
+// in registers (the same arithmetic as k_bn_norm), so the full-size normalised and activated tensors
+// are never written. Even H and W (every window whole).
+__global__ void __launch_bounds__(256) k_bn_act_pool2x2(const float *__restrict__ x, const float *__restrict__ w,
+                                                        const float *__restrict__ b, const float *__restrict__ mean,
+                                                        const float *__restrict__ invstd, int act, float act_s,
+                                                        float *__restrict__ y, int32_t *__restrict__ arg,
+                                                        uint32_t planes, uint32_t C, uint32_t W, uint32_t OH,
+                                                        uint32_t OW, FastDiv dow, FastDiv doh, FastDiv dc) {
+    const uint32_t total = planes * OH * OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
+        const uint32_t c = pl - dc.div(pl) * C;
+        const float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
+        const uint32_t H = 2 * OH;
+        const float *r0 = x + (size_t)pl * H * W + (size_t)(2 * oy) * W + 2 * ox;
+        const float2 p = __ldg(reinterpret_cast<const float2 *>(r0));
+        const float2 q = __ldg(reinterpret_cast<const float2 *>(r0 + W));
+        const float v0 = epi_fwd(act, act_s, p.x * a + dd), v1 = epi_fwd(act, act_s, p.y * a + dd);
+        const float v2 = epi_fwd(act, act_s, q.x * a + dd), v3 = epi_fwd(act, act_s, q.y * a + dd);
+        const int32_t i0 = (int32_t)(2 * oy * W + 2 * ox);
+        float best = v0;
+        int32_t bi = i0;
+        if (v1 > best) best = v1, bi = i0 + 1;
+        if (v2 > best) best = v2, bi = i0 + (int32_t)W;
+        if (v3 > best) best = v3, bi = i0 + (int32_t)W + 1;
+        y[t] = best;
+        arg[t] = bi;
+    }
+}
+
+extern "C" int nck_bn_pool2x2_ok(int64_t N, int64_t C, int64_t H, int64_t W) {
+    return H % 2 == 0 && W % 2 == 0 && N * C * H * W < ((int64_t)1 << 31) && H > 0 && W > 0;
+}
+
+extern "C" void nck_bn_act_pool2x2(nck_dev *d, const float *x, const float *w, const float *b, const float *mean,
+                                   const float *invstd, int act, float act_s, float *y, int32_t *arg, int64_t N,
+                                   int64_t C, int64_t H, int64_t W) {
+    const int64_t planes = N * C, OH = H / 2, OW = W / 2, total = planes * OH * OW;
+    if (total <= 0) return;
+    Scope sc(d, "bn_act_pool", 0.0, 4.0 * planes * H * W + 8.0 * total);
+    k_bn_act_pool2x2<<<grid_for(d, total), 256, 0, NCK_STREAM(d)>>>(
+        x, w, b, mean, invstd, act, act_s, y, arg, (uint32_t)planes, (uint32_t)C, (uint32_t)W, (uint32_t)OH,
+        (uint32_t)OW, make_fastdiv((uint32_t)OW), make_fastdiv((uint32_t)OH), make_fastdiv((uint32_t)C));
+    NCK_LAUNCHED(d, 1);
 }
 
 // Running statistics of data-parallel BatchNorm: group g (one running_mean / running_var pair) takes
@@ -928,14 +998,20 @@ __device__ void bn_bwd_finalize(const double *part, int64_t C, int64_t M, const 
     }
 }
 
+// act >= 0: g is the gradient of act(BatchNorm output); the BatchNorm output's own gradient is formed
+// on the fly from x (the activation's backward fused in)
 template <int V>
 __global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x, const float *__restrict__ g,
                                                      const float *__restrict__ mean, const float *__restrict__ invstd,
                                                      double *__restrict__ part, int64_t N, int64_t C, int64_t S,
-                                                     int64_t per_split, BnBwdFin fin, unsigned *counter) {
+                                                     int64_t per_split, BnBwdFin fin, unsigned *counter,
+                                                     const float *__restrict__ wt = nullptr,
+                                                     const float *__restrict__ bs = nullptr, int act = -1,
+                                                     float act_s = 0.0f) {
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const float mu = mean[c], is = invstd[c];
+    const float ea = act >= 0 ? wt[c] * is : 0.0f, ed = act >= 0 ? bs[c] - mu * ea : 0.0f;
     // four items of x and g in flight per thread, then float products into double sums (two chains)
     const int64_t pstride = C * S, cbase = (n0 * C + c) * S;
     ChanWalk w;
@@ -955,6 +1031,11 @@ __global__ void __launch_bounds__(256) k_bn_bwd_sums(const float *__restrict__ x
             }
             w.next();
         }
+        if (act >= 0)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int k = 0; k < V; k++) gv[j][k] = epi_grad(act, act_s, xv[j][k] * ea + ed, gv[j][k]);
 #pragma unroll
         for (int j = 0; j < 4; j++)
 #pragma unroll
@@ -978,7 +1059,9 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
                                                    const float *__restrict__ g, const float *__restrict__ mean,
                                                    const float *__restrict__ invstd, const float *__restrict__ coef,
                                                    float *__restrict__ gx, int64_t NC, int64_t C, int64_t S,
-                                                   int training, int acc, FastDiv dsv, FastDiv dc) {
+                                                   int training, int acc, FastDiv dsv, FastDiv dc,
+                                                   const float *__restrict__ b = nullptr, int act = -1,
+                                                   float act_s = 0.0f) {
     const int64_t SV = S / V, total = NC * SV;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t c;
@@ -993,6 +1076,11 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
         float xv[V], gv[V], ov[V];
         bn_load<V>(x, i, xv);
         bn_load<V>(g, i, gv);
+        if (act >= 0) {
+            const float ea = __ldg(w + c) * is, ed = __ldg(b + c) - mu * ea;
+#pragma unroll
+            for (int e = 0; e < V; e++) gv[e] = epi_grad(act, act_s, xv[e] * ea + ed, gv[e]);
+        }
         if (!acc) {
 #pragma unroll
             for (int e = 0; e < V; e++) ov[e] = 0.0f;
@@ -1010,10 +1098,10 @@ __global__ void __launch_bounds__(256) k_bn_bwd_dx(const float *__restrict__ x, 
     }
 }
 
-extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean,
-                           const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
-                           int training, int acc_gx) {
-    Scope sc(d, "bn_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * N * C * S);
+extern "C" void nck_bn_bwd_ex(nck_dev *d, const float *x, const float *w, const float *b, const float *g,
+                              const float *mean, const float *invstd, float *gx, float *gw, float *gb, int64_t N,
+                              int64_t C, int64_t S, int training, int acc_gx, int act, float act_s) {
+    Scope sc(d, act < 0 ? "bn_bwd" : "bn_act_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * N * C * S);
     const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
     static int res4 = 0, res1 = 0;
     if (v4 && !res4) res4 = resident_blocks(d, k_bn_bwd_sums<4>, kThreads);
@@ -1024,17 +1112,127 @@ extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const flo
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     dim3 g1((unsigned)C, (unsigned)splits);
     const BnBwdFin fin = {gw, gb, coef, (int)splits};
-    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
-    else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters);
+    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters, w, b, act, act_s);
+    else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters, w,
+                                                               b, act, act_s);
     int launched = 1;
     if (gx) {
         int64_t planes = N * C;
         if (v4)
             k_bn_bwd_dx<4><<<flat_grid(d, planes * S / 4), 256, 0, NCK_STREAM(d)>>>(
-                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 4), make_fastdiv((uint32_t)C));
+                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 4), make_fastdiv((uint32_t)C), b, act,
+                act_s);
         else
             k_bn_bwd_dx<1><<<flat_grid(d, planes * S), 256, 0, NCK_STREAM(d)>>>(
-                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 1), make_fastdiv((uint32_t)C));
+                x, w, g, mean, invstd, coef, gx, planes, C, S, training, acc_gx, BN_DIVS(S, 1), make_fastdiv((uint32_t)C), b, act,
+                act_s);
+        launched++;
+    }
+    NCK_LAUNCHED(d, launched);
+}
+
+extern "C" void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *mean,
+                           const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S,
+                           int training, int acc_gx) {
+    nck_bn_bwd_ex(d, x, w, nullptr, g, mean, invstd, gx, gw, gb, N, C, S, training, acc_gx, -1, 0.0f);
+}
+
+// ---- backward of BatchNorm + activation + 2 x 2 max pooling, fused -----------------------------------
+//
+// The BatchNorm output's gradient is nonzero only at each window's argmax, where it is the pooled
+// gradient through the activation (evaluated at the recomputed BatchNorm output): the sums walk the
+// pooled elements only; the input gradient is written window by window, with the dense formula at
+// every element (the same arithmetic as k_bn_bwd_dx given that sparse gradient).
+__global__ void __launch_bounds__(256) k_bn_pool_bwd_sums(const float *__restrict__ x, const float *__restrict__ gp,
+                                                          const int32_t *__restrict__ arg,
+                                                          const float *__restrict__ w, const float *__restrict__ b,
+                                                          const float *__restrict__ mean,
+                                                          const float *__restrict__ invstd, int act, float act_s,
+                                                          double *__restrict__ part, int64_t N, int64_t C, int64_t HW,
+                                                          int64_t L, int64_t per_split, BnBwdFin fin,
+                                                          unsigned *counter) {
+    __shared__ double sm[64];
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const float mu = mean[c], is = invstd[c], ea = w[c] * is, ed = b[c] - mu * ea;
+    double g0 = 0.0, h0 = 0.0;
+    const int64_t items = (n1 > n0 ? n1 - n0 : 0) * L;
+    for (int64_t t = threadIdx.x; t < items; t += blockDim.x) {
+        const int64_t nn = n0 + t / L, l = t - (t / L) * L, pl = nn * C + c;
+        const float xv = __ldg(x + pl * HW + __ldg(arg + pl * L + l));
+        const float g = epi_grad(act, act_s, xv * ea + ed, __ldg(gp + pl * L + l));
+        g0 += g, h0 += g * (xv - mu) * is;
+    }
+    block_sum2(g0, h0, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = g0;
+        part[(blockIdx.y * C + c) * 2 + 1] = h0;
+    }
+    if (last_block_done(counter)) bn_bwd_finalize(part, C, N * HW, fin);
+}
+
+__global__ void __launch_bounds__(256) k_bn_pool_bwd_dx(const float *__restrict__ x, const float *__restrict__ gp,
+                                                        const int32_t *__restrict__ arg, const float *__restrict__ w,
+                                                        const float *__restrict__ b, const float *__restrict__ mean,
+                                                        const float *__restrict__ invstd,
+                                                        const float *__restrict__ coef, int act, float act_s,
+                                                        float *__restrict__ gx, int acc, uint32_t planes, uint32_t C,
+                                                        uint32_t W, uint32_t OH, uint32_t OW, FastDiv dow,
+                                                        FastDiv doh, FastDiv dc) {
+    const uint32_t total = planes * OH * OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
+        const uint32_t c = pl - dc.div(pl) * C;
+        const float mu = __ldg(mean + c), is = __ldg(invstd + c), k = __ldg(w + c) * is;
+        const float ea = k, ed = __ldg(b + c) - mu * ea;
+        const float mg = __ldg(coef + 2 * c), mgx = __ldg(coef + 2 * c + 1);
+        const size_t base = (size_t)pl * (2 * OH) * W + (size_t)(2 * oy) * W + 2 * ox;
+        const float2 p = __ldg(reinterpret_cast<const float2 *>(x + base));
+        const float2 q = __ldg(reinterpret_cast<const float2 *>(x + base + W));
+        const int32_t a = __ldg(arg + t) - (int32_t)(2 * oy * W + 2 * ox); // 0, 1, W or W + 1
+        const float xs[4] = {p.x, p.y, q.x, q.y};
+        const int32_t at[4] = {0, 1, (int32_t)W, (int32_t)W + 1};
+        const float gval = __ldg(gp + t);
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float ge = at[e] == a ? epi_grad(act, act_s, xs[e] * ea + ed, gval) : 0.0f;
+            o[e] = k * (ge - mg - (xs[e] - mu) * is * mgx);
+        }
+        float2 *d0 = reinterpret_cast<float2 *>(gx + base), *d1 = reinterpret_cast<float2 *>(gx + base + W);
+        if (acc) {
+            const float2 u = *d0, v = *d1;
+            o[0] = u.x + o[0], o[1] = u.y + o[1], o[2] = v.x + o[2], o[3] = v.y + o[3];
+        } else {
+            o[0] = 0.0f + o[0], o[1] = 0.0f + o[1], o[2] = 0.0f + o[2], o[3] = 0.0f + o[3];
+        }
+        *d0 = make_float2(o[0], o[1]);
+        *d1 = make_float2(o[2], o[3]);
+    }
+}
+
+extern "C" void nck_bn_pool_bwd(nck_dev *d, const float *x, const float *w, const float *b, const float *gpool,
+                                const int32_t *arg, const float *mean, const float *invstd, float *gx, float *gw,
+                                float *gb, int64_t N, int64_t C, int64_t H, int64_t W, int acc_gx, int act,
+                                float act_s) {
+    const int64_t HW = H * W, OH = H / 2, OW = W / 2, L = OH * OW;
+    Scope sc(d, "bn_pool_bwd", 0.0, 4.0 * N * C * (HW + 2 * L) + (gx ? (acc_gx ? 8.0 : 4.0) * N * C * HW : 0.0));
+    static int res = 0;
+    if (!res) res = resident_blocks(d, k_bn_pool_bwd_sums, kThreads);
+    int64_t splits = bn_splits(res, N, C, L), per = (N + splits - 1) / splits;
+    splits = (N + per - 1) / per;
+    double *part = (double *)d->scratch;
+    float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
+    const BnBwdFin fin = {gw, gb, coef, (int)splits};
+    dim3 g1((unsigned)C, (unsigned)splits);
+    k_bn_pool_bwd_sums<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, gpool, arg, w, b, mean, invstd, act, act_s, part, N, C, HW,
+                                                          L, per, fin, d->counters);
+    int launched = 1;
+    if (gx) {
+        const int64_t total = N * C * L;
+        k_bn_pool_bwd_dx<<<grid_for(d, total), 256, 0, NCK_STREAM(d)>>>(
+            x, gpool, arg, w, b, mean, invstd, coef, act, act_s, gx, acc_gx, (uint32_t)(N * C), (uint32_t)C,
+            (uint32_t)W, (uint32_t)OH, (uint32_t)OW, make_fastdiv((uint32_t)OW), make_fastdiv((uint32_t)OH),
+            make_fastdiv((uint32_t)C));
         launched++;
     }
     NCK_LAUNCHED(d, launched);

@@ -66,11 +66,24 @@ struct nc_tensor {
     /* parameters registered with an optimizer: the optimizer and the parameter's index in it */
     struct nc_optim *optim;
     int32_t optim_slot;
+    /* owners whose values are still a pending epilogue (not written yet; fusion.c) */
+    struct nc_deferred *deferred;
+    /* live consumers of this tensor in the current backward pass */
+    uint32_t use_epoch;
+    int32_t uses;
 };
 
 /* ---- op registry ------------------------------------------------------------------------------ */
 
-enum { NC_OPF_ELEMENTWISE = 1u << 0, NC_OPF_REDUCTION = 1u << 1, NC_OPF_VIEW = 1u << 2, NC_OPF_NONDIFF = 1u << 3 };
+/* NC_OPF_RECIPE: the op's forward takes a pending recipe as input itself (fusion.c) instead of having
+ * nc__apply materialise it first */
+enum {
+    NC_OPF_ELEMENTWISE = 1u << 0,
+    NC_OPF_REDUCTION = 1u << 1,
+    NC_OPF_VIEW = 1u << 2,
+    NC_OPF_NONDIFF = 1u << 3,
+    NC_OPF_RECIPE = 1u << 4
+};
 
 typedef struct {
     int64_t i[NC_MAX_DIMS + 2];
@@ -97,6 +110,7 @@ struct nc_node {
     nc_node *prev;     /* the step's record log, newest first */
     uint64_t seq;      /* recording order within the context */
     uint32_t mark;     /* backward epoch in which the node was found live */
+    uint32_t fused;    /* backward epoch in which a fused chain already ran this node's backward */
     int released;
 };
 
@@ -177,6 +191,9 @@ struct nc_ctx {
     int persistent_depth;
     int grad_enabled;
     nc_node *tape;
+    int fwd_on_tape;   /* the op whose forward is running will be recorded */
+    int fuse;          /* deferred epilogues and fused backward chains (NC_FUSE=0: off) */
+    struct nc_deferred *deferred_head;
 
     nc_status status;
     char err[256];
@@ -304,6 +321,40 @@ float *nc__dp_bn_stage(nc_ctx *ctx, float *running_mean, float *running_var, int
 int nc__dp_bn_flush(nc_ctx *ctx, int on_comm_stream);
 /* data-parallel dropout streams at a step boundary (dp.c) */
 void nc__dp_rng_step_end(nc_ctx *ctx);
+
+/* ---- deferred epilogues (fusion.c) -------------------------------------------------------------
+ * A BatchNorm output in training, and an activation of it, can be left unwritten: the tensor holds a
+ * recipe (act(BatchNorm(x)) with the batch statistics) until something reads it. A 2 x 2 max pool
+ * reads the recipe and pools straight from x; anything else that touches the data materialises it
+ * first (nc__dev and the host paths call nc__materialize). In backward, a pool or activation over
+ * such a chain runs the whole chain's backward in one fused BatchNorm backward. */
+typedef struct nc_deferred {
+    nc_tensor *owner;              /* the tensor whose values are pending */
+    nc_tensor *src;                /* the BatchNorm input's owner: its data feeds the recipe */
+    const float *x, *w, *b, *mean, *invstd;
+    int64_t N, C, S;
+    int act;                       /* NCK_UN_* kind applied after the normalisation, -1: none */
+    float act_s;
+    struct nc_deferred *next;
+} nc_deferred;
+
+void nc__defer_bn(nc_ctx *ctx, nc_tensor *out, nc_tensor *x, const float *X, const float *w, const float *b,
+                  const float *mean, const float *invstd, int64_t N, int64_t C, int64_t S);
+/* the pending recipe of t when t is the whole (owner) tensor, else NULL */
+const nc_deferred *nc__deferred_of(const nc_tensor *t);
+/* out (a fresh tensor of t's shape) := act(t) as a recipe when t is pending and act fuses */
+int nc__defer_act(nc_tensor *out, nc_tensor *t, int act, float act_s);
+void nc__materialize(nc_tensor *owner);
+/* owner's data is about to be freed or overwritten: recipes reading it are materialised first, its
+ * own recipe (if any) is dropped */
+void nc__deferred_release(nc_tensor *owner);
+void nc__deferred_flush(nc_ctx *ctx);  /* materialise every pending recipe */
+void nc__deferred_reset(nc_ctx *ctx);  /* step end: forget every recipe (their storage is reset) */
+/* Runs the fused backward of the chain that ends at node n when there is one: fills consumed with the
+ * chain's other nodes (whose own backward must not run) and returns their count, else 0. */
+int nc__fused_backward(nc_ctx *ctx, nc_node *n, nc_node **consumed);
+/* the NCK_UN_* kind of a unary activation op, -1 for any other op (ops_elementwise.c) */
+int nc__unary_kind(const nc_op_def *op);
 
 /* Backward-pass gradient readiness of optimizer parameters (optim.c). A backward pass announces each
  * leaf whose gradient it will write (nc__grad_expect, once per leaf per pass) and reports it final

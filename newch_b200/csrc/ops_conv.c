@@ -360,18 +360,32 @@ static nc_status pool_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape) {
     return NC_OK;
 }
 
+/* 2 x 2 / stride 2 max pooling straight from the pending recipe of its input (BatchNorm and maybe
+ * an activation, fusion.c): returns 1 when it did the pooling */
+static int pool_from_recipe(nc_node *n, int32_t *arg) {
+    nc_tensor *x = n->in[0];
+    const nc_deferred *d = nc__deferred_of(x);
+    const int64_t *p = n->p.i;
+    if (!d || x->ndim != 4 || p[0] != 2 || p[1] != 2 || p[2] != 0 || p[3] != 0 || p[4] != 2 || p[5] != 2) return 0;
+    if (!nck_bn_pool2x2_ok(x->shape[0], x->shape[1], x->shape[2], x->shape[3])) return 0;
+    nck_bn_act_pool2x2(nc__k(x->ctx), d->x, d->w, d->b, d->mean, d->invstd, d->act, d->act_s, (float *)n->out->data,
+                       arg, x->shape[0], x->shape[1], x->shape[2], x->shape[3]);
+    return 1;
+}
+
 static nc_status pool_fwd(nc_node *n) {
     nc_tensor *x = n->in[0];
     nck_conv g = geom(n, n->p.i[4], n->p.i[5], 0);
-    const float *X = nc__contig_f32(x);
     int is_max = n->op->kind == POOL_MAX;
     int32_t *arg = NULL;
-    if (!X) return NC_ERR_OOM;
     if (is_max) {
         arg = (int32_t *)nc__arena_alloc(x->ctx, (size_t)nc_numel(n->out) * sizeof(int32_t));
         if (!arg) return NC_ERR_OOM;
         n->saved = arg;
+        if (nc_numel(n->out) && pool_from_recipe(n, arg)) return NC_OK;
     }
+    const float *X = nc__contig_f32(x);
+    if (!X) return NC_ERR_OOM;
     if (nc_numel(n->out)) nck_pool_fwd(nc__k(x->ctx), &g, X, (float *)n->out->data, arg, is_max);
     return NC_OK;
 }
@@ -389,7 +403,7 @@ static void pool_bwd(nc_node *n) {
         zero_if_fresh(x->ctx, gt, &acc);
 }
 
-const nc_op_def nc_op_max_pool2d = {"max_pool2d", 0, POOL_MAX, pool_infer, NULL, pool_fwd, pool_bwd};
+const nc_op_def nc_op_max_pool2d = {"max_pool2d", NC_OPF_RECIPE, POOL_MAX, pool_infer, NULL, pool_fwd, pool_bwd};
 const nc_op_def nc_op_avg_pool2d = {"avg_pool2d", 0, POOL_AVG, pool_infer, NULL, pool_fwd, pool_bwd};
 
 static nc_tensor *pool(const nc_op_def *op, nc_tensor *x, int kh, int kw, int sh, int sw, int ph, int pw) {

@@ -107,6 +107,9 @@ static nc_status unary_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape) 
 }
 
 static nc_status unary_fwd(nc_node *n) {
+    /* an activation of a pending BatchNorm output extends its recipe (nothing is computed yet) */
+    if (n->out->ctx->fuse && n->out->ctx->fwd_on_tape && nc__defer_act(n->out, n->in[0], n->op->kind, n->p.f[0]))
+        return NC_OK;
     const float *x = nc__contig_f32(n->in[0]);
     if (!x) return NC_ERR_OOM;
     nck_unary_fwd(nc__k(n->out->ctx), n->op->kind, n->p.f[0], x, (float *)n->out->data, nc_numel(n->out));
@@ -123,8 +126,11 @@ static void unary_bwd(nc_node *n) {
                   (const float *)n->out->grad->data, (float *)gt->data, acc, nc_numel(in));
 }
 
+int nc__unary_kind(const nc_op_def *op) { return op && op->forward == unary_fwd ? op->kind : -1; }
+
 #define UNARY_OP(nm, KIND) \
-    const nc_op_def nc_op_##nm = {#nm, NC_OPF_ELEMENTWISE, KIND, unary_infer, NULL, unary_fwd, unary_bwd};
+    const nc_op_def nc_op_##nm = {#nm, NC_OPF_ELEMENTWISE | NC_OPF_RECIPE, KIND, unary_infer, NULL, unary_fwd, \
+                                  unary_bwd};
 UNARY_OP(neg, NCK_UN_NEG)
 UNARY_OP(exp, NCK_UN_EXP)
 UNARY_OP(log, NCK_UN_LOG)

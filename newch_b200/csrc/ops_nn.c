@@ -242,17 +242,19 @@ static nc_status bn_fwd(nc_node *n) {
         nc__dev_write(rm);
         nc__dev_write(rv);
         float *rmd = (float *)nc__dev(rm), *rvd = (float *)nc__dev(rv);
-        if (ctx->dp_world > 1) {
+        const int dp = ctx->dp_world > 1;
+        if (dp) {
             /* data parallel: this rank's batch statistics are staged; the running statistics take all
              * ranks' updates in rank order when the step's statistics are gathered */
             float *st = nc__dp_bn_stage(ctx, rmd, rvd, C, n->p.f[0]);
             if (!st) return ctx->status;
-            nck_bn_fwd_train(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd, st, st + C, N, C, S,
-                             n->p.f[0], n->p.f[1], 1);
-        } else {
-            nck_bn_fwd_train(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd, rmd, rvd, N, C, S,
-                             n->p.f[0], n->p.f[1], 0);
+            rmd = st, rvd = st + C;
         }
+        nck_bn_stats_train(nc__k(ctx), X, sv->mean, sv->invstd, rmd, rvd, N, C, S, n->p.f[0], n->p.f[1], dp);
+        if (ctx->fuse && ctx->fwd_on_tape && nc_is_contiguous(x))
+            nc__defer_bn(ctx, n->out, x, X, w, b, sv->mean, sv->invstd, N, C, S); /* output left as a recipe */
+        else
+            nck_bn_apply(nc__k(ctx), X, w, b, sv->mean, sv->invstd, (float *)n->out->data, N, C, S, -1, 0.0f);
     } else {
         if (ctx->bn_n && !nc__dp_bn_flush(ctx, 0)) return ctx->status; /* pending updates reach rm / rv first */
         nck_bn_fwd_eval(nc__k(ctx), X, w, b, (float *)n->out->data, sv->mean, sv->invstd,

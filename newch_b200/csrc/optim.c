@@ -416,6 +416,7 @@ static int dp_finish_reduce(nc_optim *o) {
 
 void nc_optim_step(nc_optim *o) {
     if (!o || !nc_ok(o->ctx)) return;
+    nc__deferred_flush(o->ctx); /* pending recipes read the parameters this step changes */
     if (o->accum_steps > 1 && ++o->accum_count < o->accum_steps) return;
     o->accum_count = 0;
     nc_ctx *ctx = o->ctx;

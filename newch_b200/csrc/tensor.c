@@ -124,6 +124,7 @@ static void mirror_free(nc_tensor *o) {
 
 /* makes the owner's mirror hold the device data; returns it */
 static void *mirror_refresh(nc_tensor *o) {
+    if (o->deferred) nc__materialize(o);
     void *h = mirror_of(o);
     if (!h) return NULL;
     if (!(o->coh & NC_COH_HOST_VALID)) {
@@ -136,6 +137,7 @@ static void *mirror_refresh(nc_tensor *o) {
 
 void *nc__dev(nc_tensor *t) {
     nc_tensor *o = nc__owner(t);
+    if (o->deferred) nc__materialize(o);
     if (o->coh & NC_COH_HOST_DIRTY) {
         nc__upload(o->ctx, o->data, o->host, o->bytes);
         o->coh &= ~NC_COH_HOST_DIRTY;
@@ -145,13 +147,14 @@ void *nc__dev(nc_tensor *t) {
 
 void nc__dev_write(nc_tensor *t) {
     nc_tensor *o = nc__owner(t);
+    if (o->deferred) nc__materialize(o);
     if (o->coh & NC_COH_HOST_DIRTY) nc__dev(o);
     o->coh &= ~NC_COH_HOST_VALID;
 }
 
 const void *nc__host_view(nc_tensor *t) {
     nc_tensor *o = nc__owner(t);
-    if (!(o->coh & NC_COH_HOST_VALID) || !o->host || !nc_is_contiguous(t)) return NULL;
+    if (o->deferred || !(o->coh & NC_COH_HOST_VALID) || !o->host || !nc_is_contiguous(t)) return NULL;
     return (const char *)o->host + ((const char *)t->data - (const char *)o->data);
 }
 

@@ -126,6 +126,54 @@ def case_batch_norm_train(e):
     return out
 
 
+def _bn_chain(e, seed, shape, act, pool, reuse=False):
+    """BatchNorm (training) -> activation -> (2 x 2 max pool): the chain the B200 engine runs as a
+    deferred epilogue and one fused backward. reuse: the BatchNorm output is read a second time (added
+    to the result), which forces the unfused paths."""
+    x = e.param(seeded(seed, shape, 2.0) + 0.5)
+    C = shape[1]
+    w = e.param(seeded(seed + 1, (C,)))
+    b = e.param(seeded(seed + 2, (C,)))
+    e.L.nc_persistent_begin(e.ctx)
+    rm = e.t(np.zeros(C, np.float32))
+    rv = e.t(np.ones(C, np.float32))
+    e.L.nc_persistent_end(e.ctx)
+    y = e.check(e.L.nc_batch_norm(x, w, b, rm, rv, 1, 0.1, 1e-5))
+    z = e.check(_unary_call(e, act, y) if act != "none" else y)
+    if reuse:
+        z = e.check(e.L.nc_add(z, y))
+    out = e.check(e.L.nc_max_pool2d(z, 2, 2, 2, 2, 0, 0)) if pool else z
+    G = seeded(seed + 3, e.shape(out))
+    res = {"x": e.np(x), "w": e.np(w), "b": e.np(b), "y": e.np(out), "G": G}
+    e.backward_with(out, G)
+    res.update(dx=e.grad(x), dw=e.grad(w), db=e.grad(b), rm=e.np(rm), rv=e.np(rv))
+    return res
+
+
+def case_bn_relu_pool(e):
+    return _bn_chain(e, 700, (4, 6, 10, 12), "relu", True)
+
+
+def case_bn_pool(e):
+    return _bn_chain(e, 710, (3, 5, 8, 8), "none", True)
+
+
+def case_bn_hardswish(e):
+    return _bn_chain(e, 720, (4, 6, 7, 9), "hardswish", False)
+
+
+def case_bn_relu6_pool(e):
+    return _bn_chain(e, 730, (2, 4, 6, 10), "relu6", True)
+
+
+def case_bn_relu_reused(e):
+    return _bn_chain(e, 740, (3, 4, 8, 8), "relu", True, reuse=True)
+
+
+def case_bn_relu_pool_odd(e):
+    return _bn_chain(e, 750, (2, 3, 9, 7), "relu", True)
+
+
 def case_batch_norm_eval(e):
     x = e.param(seeded(110, (3, 4, 6)))
     w = e.param(seeded(111, (4,)))

@@ -78,3 +78,15 @@ def test_libm_math_mode(how, monkeypatch):
         assert rel_err(got[finite], ref[finite]) <= TOL, k
         special = ~finite & np.isfinite(ref)
         assert np.allclose(got[special], ref[special], rtol=1e-5, atol=1e-30), k
+
+
+@pytest.mark.parametrize("case", ["bn_relu_pool", "bn_pool", "bn_hardswish", "bn_relu6_pool", "bn_relu_reused",
+                                  "bn_relu_pool_odd"])
+def test_bn_chains_unfused(case, monkeypatch):
+    """NC_FUSE=0: the BatchNorm chains through the unfused kernels (every intermediate written), held
+    to the same goldens as the fused default (test_op_matches_reference)."""
+    monkeypatch.setenv("NC_FUSE", "0")
+    out = run_case("b200", case)
+    for k in out:
+        ref = GOLD[f"{case}/{k}"]
+        assert rel_err(out[k], ref) <= TOL, (case, k)
