@@ -337,10 +337,13 @@ nc_status nc_backward_ex(nc_tensor *loss, int flags, nc_tensor *const *keep, int
         if (n->out->grad) { /* else nothing flowed into this node */
             ctx->bwd_logging = !retain;
             ctx->bwd_tmp_n = 0;
-            nc_node *chain[2];
+            nc_node *chain[NC_CHAIN_MAX];
             const int nc = nc__fused_backward(ctx, n, chain);
             for (int c = 0; c < nc; c++) chain[c]->fused = pl.epoch;
-            if (!nc) n->op->backward(n);
+            if (!nc) {
+                nc__backward_inputs(n); /* an unfused backward reads real values */
+                n->op->backward(n);
+            }
             ctx->bwd_logging = 0;
             if (!retain) plan_release_node(ctx, n, loss, &pl, free_graph);
         }

@@ -388,6 +388,59 @@ __global__ void k_masked_fill(nck_bcast bc, const float *__restrict__ x, const i
     }
 }
 
+// The common layout (an attention mask over the last dims, repeated over the leading ones, on a
+// contiguous tensor): the mask index is i mod Mn. float4 items when both sizes and the pointers allow.
+// bwd: gx (+)= mask ? 0 : g; forward: o = mask ? v : x.
+template <int V, int BWD>
+__global__ void __launch_bounds__(256) k_masked_fill_tail(const float *__restrict__ x, const int32_t *__restrict__ m,
+                                                          float v, float *__restrict__ o, uint32_t n, uint32_t Mn,
+                                                          FastDiv dmn, int acc) {
+    const uint32_t items = n / V;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < items; i += gridDim.x * blockDim.x) {
+        const uint32_t e = i * V, mi = e - dmn.div(e) * Mn;
+        if constexpr (V == 4) {
+            const float4 xv = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            const int4 mv = __ldg(reinterpret_cast<const int4 *>(m + mi));
+            float4 r;
+            if (BWD) {
+                float4 base = acc ? reinterpret_cast<float4 *>(o)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                r.x = mv.x ? base.x : base.x + xv.x, r.y = mv.y ? base.y : base.y + xv.y;
+                r.z = mv.z ? base.z : base.z + xv.z, r.w = mv.w ? base.w : base.w + xv.w;
+            } else {
+                r.x = mv.x ? v : xv.x, r.y = mv.y ? v : xv.y, r.z = mv.z ? v : xv.z, r.w = mv.w ? v : xv.w;
+            }
+            reinterpret_cast<float4 *>(o)[i] = r;
+        } else {
+            const int32_t mk = __ldg(m + mi);
+            if (BWD) {
+                const float base = acc ? o[e] : 0.0f;
+                o[e] = mk ? base : base + __ldg(x + e);
+            } else {
+                o[e] = mk ? v : __ldg(x + e);
+            }
+        }
+    }
+}
+
+extern "C" int nck_masked_fill_tail(nck_dev *d, int bwd, const float *x, const int32_t *m, float v, float *o,
+                                    int64_t n, int64_t Mn, int acc) {
+    if (n <= 0) return 1;
+    if (Mn <= 0 || n % Mn || n >= ((int64_t)1 << 31)) return 0;
+    Scope sc(d, bwd ? "masked_fill_bwd" : "masked_fill", 0.0, (bwd && acc ? 12.0 : 8.0) * n + 4.0 * Mn);
+    const bool v4 = Mn % 4 == 0 && (((uintptr_t)x | (uintptr_t)m | (uintptr_t)o) & 15) == 0;
+    const FastDiv dmn = make_fastdiv((uint32_t)Mn);
+    const int g = grid_for(d, v4 ? n / 4 : n);
+    if (bwd) {
+        if (v4) k_masked_fill_tail<4, 1><<<g, 256, 0, NCK_STREAM(d)>>>(x, m, v, o, (uint32_t)n, (uint32_t)Mn, dmn, acc);
+        else k_masked_fill_tail<1, 1><<<g, 256, 0, NCK_STREAM(d)>>>(x, m, v, o, (uint32_t)n, (uint32_t)Mn, dmn, acc);
+    } else {
+        if (v4) k_masked_fill_tail<4, 0><<<g, 256, 0, NCK_STREAM(d)>>>(x, m, v, o, (uint32_t)n, (uint32_t)Mn, dmn, acc);
+        else k_masked_fill_tail<1, 0><<<g, 256, 0, NCK_STREAM(d)>>>(x, m, v, o, (uint32_t)n, (uint32_t)Mn, dmn, acc);
+    }
+    NCK_LAUNCHED(d, 1);
+    return 1;
+}
+
 extern "C" void nck_masked_fill_fwd(nck_dev *d, const nck_bcast *bc, const float *x, const int32_t *m, float v,
                                     float *o) {
     int64_t n = bc_numel(bc);

@@ -408,14 +408,16 @@ __device__ __forceinline__ void xo_step(unsigned long long (&s)[4]) {
 
 // y = x * mask * 1/(1-p) and the mask words for the block's 8192 draws (mask bits in shared memory):
 // float4 items, all of a thread's loads issued before its stores; a scalar tail when n is not a
-// multiple of 4 or the pointers are not 16-byte aligned
+// multiple of 4 or the pointers are not 16-byte aligned. y == NULL: the mask words only.
 __device__ __forceinline__ void drop_block_write(const float *__restrict__ x, float *__restrict__ y,
                                                  uint32_t *__restrict__ bits, int64_t n, float p, const uint32_t *mb) {
     const float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
     const int64_t base = (int64_t)blockIdx.x * kDropBlock;
     const bool vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
     constexpr int kItems = kDropBlock / 4;
-    if (vec && base + kDropBlock <= n) {
+    if (!y) {
+        // the mask only (a fused consumer applies it)
+    } else if (vec && base + kDropBlock <= n) {
         for (int i0 = threadIdx.x; i0 < kItems; i0 += 4 * blockDim.x) {
             float4 v[4];
 #pragma unroll
@@ -488,14 +490,11 @@ __device__ __forceinline__ void drop_block_out(const unsigned long long (&s0)[4]
 constexpr int kDropGroup = 4;                              // lanes per run
 constexpr int kDropPolyThreads = kDropThreads * kDropGroup;  // one run per lane group: 512 threads
 
-__global__ void __launch_bounds__(kDropPolyThreads) k_dropout_fwd_poly(ulonglong4 b0, ulonglong4 b1, ulonglong4 b2,
-                                                                   ulonglong4 b3, const ulonglong4 *__restrict__ polys,
-                                                                   const float *__restrict__ x, float *__restrict__ y,
-                                                                   uint32_t *__restrict__ bits, int64_t n, float p) {
-    __shared__ uint32_t mb[kDropBlock / 32];
-    __shared__ ulonglong4 vtab[4][64];      // T^i b_j
-    __shared__ ulonglong4 tab[4][16][16];   // 4-bit windows of the Horner sums
-    const int j = threadIdx.x & (kDropGroup - 1);
+// The launch's Horner tables (they depend on the four base states only), built once per launch by one
+// block and read by every block of the main kernel.
+__global__ void __launch_bounds__(256) k_dropout_tables(ulonglong4 b0, ulonglong4 b1, ulonglong4 b2, ulonglong4 b3,
+                                                        ulonglong4 *__restrict__ gtab) {
+    __shared__ ulonglong4 vtab[4][64];  // T^i b_j
     if (threadIdx.x < 4) {
         const int jj = threadIdx.x;
         const ulonglong4 bj = jj == 0 ? b0 : jj == 1 ? b1 : jj == 2 ? b2 : b3;
@@ -515,8 +514,18 @@ __global__ void __launch_bounds__(kDropPolyThreads) k_dropout_fwd_poly(ulonglong
                 const ulonglong4 q = vtab[jj][4 * nn + t];
                 acc.x ^= q.x, acc.y ^= q.y, acc.z ^= q.z, acc.w ^= q.w;
             }
-        tab[jj][nn][v] = acc;
+        gtab[e] = acc;
     }
+}
+
+__global__ void __launch_bounds__(kDropPolyThreads) k_dropout_fwd_poly(const ulonglong4 *__restrict__ gtab,
+                                                                   const ulonglong4 *__restrict__ polys,
+                                                                   const float *__restrict__ x, float *__restrict__ y,
+                                                                   uint32_t *__restrict__ bits, int64_t n, float p) {
+    __shared__ uint32_t mb[kDropBlock / 32];
+    __shared__ ulonglong4 tab[4][16][16];   // 4-bit windows of the Horner sums
+    const int j = threadIdx.x & (kDropGroup - 1);
+    for (int e = threadIdx.x; e < 4 * 16 * 16; e += blockDim.x) (&tab[0][0][0])[e] = gtab[e];
     __syncthreads();
     const int64_t base_run = (int64_t)blockIdx.x * kDropThreads;  // runs of this block: kDropThreads of them
     {
@@ -619,7 +628,7 @@ extern "C" const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t c
 extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits,
                                 int64_t n, float p, const void *polys) {
     if (n <= 0) return;
-    Scope sc(d, "dropout", 0.0, 8.0 * n + n / 8.0);
+    Scope sc(d, y ? "dropout" : "dropout_mask", 0.0, (y ? 8.0 * n : 0.0) + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
     if (polys) {
@@ -634,9 +643,12 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
                 st[3] = (st[3] << 45) | (st[3] >> 19);
             }
         }
+        /* the tables live past the split-reduction area of the scratch buffer */
+        ulonglong4 *tabs = reinterpret_cast<ulonglong4 *>((char *)d->scratch + d->scratch_bytes - 4 * 16 * 16 * 32);
+        k_dropout_tables<<<1, 256, 0, NCK_STREAM(d)>>>(bj[0], bj[1], bj[2], bj[3], tabs);
         k_dropout_fwd_poly<<<(unsigned)blocks, kDropPolyThreads, 0, NCK_STREAM(d)>>>(
-            bj[0], bj[1], bj[2], bj[3], reinterpret_cast<const ulonglong4 *>(polys), x, y, bits, n, p);
-        NCK_LAUNCHED(d, 1);
+            tabs, reinterpret_cast<const ulonglong4 *>(polys), x, y, bits, n, p);
+        NCK_LAUNCHED(d, 2);
         return;
     }
     static int attr_done = 0;
@@ -1154,18 +1166,37 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_sums(const float *__restric
     __shared__ double sm[64];
     const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
     const float mu = mean[c], is = invstd[c], ea = w[c] * is, ed = b[c] - mu * ea;
-    double g0 = 0.0, h0 = 0.0;
-    const int64_t items = (n1 > n0 ? n1 - n0 : 0) * L;
-    for (int64_t t = threadIdx.x; t < items; t += blockDim.x) {
-        const int64_t nn = n0 + t / L, l = t - (t / L) * L, pl = nn * C + c;
-        const float xv = __ldg(x + pl * HW + __ldg(arg + pl * L + l));
-        const float g = epi_grad(act, act_s, xv * ea + ed, __ldg(gp + pl * L + l));
-        g0 += g, h0 += g * (xv - mu) * is;
+    // the channel's pooled elements plane by plane (a plane's L elements are contiguous): four items
+    // in flight per thread, the argmax gathers from x issued together, two double chains
+    double g0 = 0.0, h0 = 0.0, g1 = 0.0, h1 = 0.0;
+    ChanWalk wk;
+    wk.init((int)L, n1 > n0 ? n1 - n0 : 0);
+    const int64_t pbase = n0 * C + c;
+    while (wk.live()) {
+        float gv[4], xv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            gv[j] = 0.0f, xv[j] = mu;
+            if (wk.live()) {
+                const int64_t pl = pbase + (int64_t)wk.na * C;
+                const int32_t a = __ldg(arg + pl * L + wk.ia);
+                gv[j] = __ldg(gp + pl * L + wk.ia);
+                xv[j] = __ldg(x + pl * HW + a);
+            }
+            wk.next();
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float g = epi_grad(act, act_s, xv[j] * ea + ed, gv[j]);
+            if (j & 1) g1 += g, h1 += g * (xv[j] - mu) * is;
+            else g0 += g, h0 += g * (xv[j] - mu) * is;
+        }
     }
-    block_sum2(g0, h0, sm);
+    double sg = g0 + g1, sgx = h0 + h1;
+    block_sum2(sg, sgx, sm);
     if (threadIdx.x == 0) {
-        part[(blockIdx.y * C + c) * 2] = g0;
-        part[(blockIdx.y * C + c) * 2 + 1] = h0;
+        part[(blockIdx.y * C + c) * 2] = sg;
+        part[(blockIdx.y * C + c) * 2 + 1] = sgx;
     }
     if (last_block_done(counter)) bn_bwd_finalize(part, C, N * HW, fin);
 }
@@ -1267,10 +1298,138 @@ __global__ void k_ln_fwd(const float *__restrict__ x, const float *__restrict__ 
     }
 }
 
+// Rows of D = 128 NV floats kept in registers (one warp per row, NV float4 per lane): one read of x
+// for the statistics and the output; the same arithmetic as k_ln_fwd.
+template <int NV>
+__global__ void __launch_bounds__(256) k_ln_fwd_reg(const float *__restrict__ x, const float *__restrict__ w,
+                                                    const float *__restrict__ b, float *__restrict__ y,
+                                                    float *__restrict__ stats, int64_t R, float eps) {
+    constexpr int D = 128 * NV;
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < R; r += nw) {
+        const float4 *p = reinterpret_cast<const float4 *>(x + r * D);
+        float4 v[NV];
+        double s = 0.0;
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            v[k] = __ldg(p + lane + 32 * k);
+            s += (double)v[k].x, s += (double)v[k].y, s += (double)v[k].z, s += (double)v[k].w;
+        }
+        s = warp_sum_d(s);
+        const double mean = s / (double)D;
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const double a = (double)v[k].x - mean, bb = (double)v[k].y - mean, c = (double)v[k].z - mean,
+                         e = (double)v[k].w - mean;
+            ss += a * a, ss += bb * bb, ss += c * c, ss += e * e;
+        }
+        ss = warp_sum_d(ss);
+        const float rstd = (float)(1.0 / sqrt(ss / (double)D + (double)eps));
+        const float fm = (float)mean;
+        if (lane == 0) stats[2 * r] = fm, stats[2 * r + 1] = rstd;
+        float4 *q = reinterpret_cast<float4 *>(y + r * D);
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const int i = lane + 32 * k;
+            const float4 wv = w ? __ldg(reinterpret_cast<const float4 *>(w) + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 bv = b ? __ldg(reinterpret_cast<const float4 *>(b) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 o;
+            o.x = (w ? ((v[k].x - fm) * rstd) * wv.x : (v[k].x - fm) * rstd) + bv.x;
+            o.y = (w ? ((v[k].y - fm) * rstd) * wv.y : (v[k].y - fm) * rstd) + bv.y;
+            o.z = (w ? ((v[k].z - fm) * rstd) * wv.z : (v[k].z - fm) * rstd) + bv.z;
+            o.w = (w ? ((v[k].w - fm) * rstd) * wv.w : (v[k].w - fm) * rstd) + bv.w;
+            q[i] = o;
+        }
+    }
+}
+
+// Backward with the row in registers: dx in one read of x and g, and the weight / bias column sums
+// of the block's rows (lane-private running sums, then a fixed tree over the block's warps) as one
+// partial per block, combined in order by k_ln_bwd_wb_combine.
+template <int NV>
+__global__ void __launch_bounds__(256) k_ln_bwd_reg(const float *__restrict__ x, const float *__restrict__ w,
+                                                    const float *__restrict__ g, const float *__restrict__ stats,
+                                                    float *__restrict__ gx, float *__restrict__ part, int64_t R,
+                                                    int want_wb) {
+    constexpr int D = 128 * NV;
+    __shared__ float red[8][128];  // one 128-column slice at a time
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    float4 aw[NV], ab[NV];
+#pragma unroll
+    for (int k = 0; k < NV; k++) aw[k] = ab[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t r = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; r < R; r += nw) {
+        const float4 *p = reinterpret_cast<const float4 *>(x + r * D), *q = reinterpret_cast<const float4 *>(g + r * D);
+        const float mean = __ldg(stats + 2 * r), rstd = __ldg(stats + 2 * r + 1);
+        float4 xh[NV], gi[NV], gr[NV];
+        double sg = 0.0, sgx = 0.0;
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const int i = lane + 32 * k;
+            const float4 xv = __ldg(p + i);
+            gr[k] = __ldg(q + i);
+            const float4 wv = w ? __ldg(reinterpret_cast<const float4 *>(w) + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+            xh[k] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
+            gi[k] = w ? make_float4(gr[k].x * wv.x, gr[k].y * wv.y, gr[k].z * wv.z, gr[k].w * wv.w) : gr[k];
+            sg += gi[k].x, sg += gi[k].y, sg += gi[k].z, sg += gi[k].w;
+            sgx += gi[k].x * xh[k].x, sgx += gi[k].y * xh[k].y, sgx += gi[k].z * xh[k].z, sgx += gi[k].w * xh[k].w;
+            if (want_wb) {
+                aw[k].x += gr[k].x * xh[k].x, aw[k].y += gr[k].y * xh[k].y;
+                aw[k].z += gr[k].z * xh[k].z, aw[k].w += gr[k].w * xh[k].w;
+                ab[k].x += gr[k].x, ab[k].y += gr[k].y, ab[k].z += gr[k].z, ab[k].w += gr[k].w;
+            }
+        }
+        sg = warp_sum_d(sg);
+        sgx = warp_sum_d(sgx);
+        if (gx) {
+            const float mg = (float)(sg / (double)D), mgx = (float)(sgx / (double)D);
+            float4 *o = reinterpret_cast<float4 *>(gx + r * D);
+#pragma unroll
+            for (int k = 0; k < NV; k++) {
+                const int i = lane + 32 * k;
+                float4 a = o[i];
+                a.x += rstd * (gi[k].x - mg - xh[k].x * mgx), a.y += rstd * (gi[k].y - mg - xh[k].y * mgx);
+                a.z += rstd * (gi[k].z - mg - xh[k].z * mgx), a.w += rstd * (gi[k].w - mg - xh[k].w * mgx);
+                o[i] = a;
+            }
+        }
+    }
+    if (!want_wb) return;
+    // block partials: column c of the weight sums (then the bias sums at D + c), warps added in order
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+        __syncthreads();
+        const int c = 4 * lane; // columns of float4 slice k: 4 * (lane + 32 k) .. + 3, staged as 4 * lane
+        red[warp][c] = aw[k].x, red[warp][c + 1] = aw[k].y, red[warp][c + 2] = aw[k].z, red[warp][c + 3] = aw[k].w;
+        __syncthreads();
+        if (threadIdx.x < 128) {
+            float t = 0.0f;
+            for (int q = 0; q < (int)(blockDim.x >> 5); q++) t += red[q][threadIdx.x];
+            part[(int64_t)blockIdx.x * 2 * D + 128 * k + threadIdx.x] = t;
+        }
+        __syncthreads();
+        red[warp][c] = ab[k].x, red[warp][c + 1] = ab[k].y, red[warp][c + 2] = ab[k].z, red[warp][c + 3] = ab[k].w;
+        __syncthreads();
+        if (threadIdx.x < 128) {
+            float t = 0.0f;
+            for (int q = 0; q < (int)(blockDim.x >> 5); q++) t += red[q][threadIdx.x];
+            part[(int64_t)blockIdx.x * 2 * D + D + 128 * k + threadIdx.x] = t;
+        }
+    }
+}
+
 extern "C" void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats,
                            int64_t R, int64_t D, float eps) {
     Scope sc(d, "ln_fwd", 0.0, 8.0 * R * D);
-    k_ln_fwd<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, D, eps);
+    const bool vec = D % 128 == 0 && D <= 1024 && (((uintptr_t)x | (uintptr_t)y | (uintptr_t)w | (uintptr_t)b) & 15) == 0;
+    const int g = grid_for(d, R * 32);
+    if (vec && D == 128) k_ln_fwd_reg<1><<<g, 256, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, eps);
+    else if (vec && D == 256) k_ln_fwd_reg<2><<<g, 256, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, eps);
+    else if (vec && D == 512) k_ln_fwd_reg<4><<<g, 256, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, eps);
+    else if (vec && D == 1024) k_ln_fwd_reg<8><<<g, 256, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, eps);
+    else k_ln_fwd<<<g, kThreads, 0, NCK_STREAM(d)>>>(x, w, b, y, stats, R, D, eps);
     NCK_LAUNCHED(d, 1);
 }
 
@@ -1335,6 +1494,30 @@ extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const flo
                            float *gw, float *gb, int64_t R, int64_t D) {
     Scope sc(d, "ln_bwd", 0.0, (gx ? 16.0 : 8.0) * R * D);
     int launched = 0;
+    const bool vec = (D == 128 || D == 256 || D == 512 || D == 1024) &&
+                     (((uintptr_t)x | (uintptr_t)g | (uintptr_t)gx | (uintptr_t)w) & 15) == 0;
+    if (vec) {
+        static int resident = 0;
+        if (!resident) resident = resident_blocks(d, k_ln_bwd_reg<2>, 256);
+        int64_t blocks = (R + 7) / 8;
+        if (blocks > resident) blocks = resident;
+        if ((gw || gb) && blocks * 2 * D * (int64_t)sizeof(float) > (int64_t)d->scratch_bytes)
+            blocks = (int64_t)d->scratch_bytes / (2 * D * (int64_t)sizeof(float));
+        if (blocks < 1) blocks = 1;
+        float *part = (float *)d->scratch;
+        const int want = gw || gb;
+        if (D == 128) k_ln_bwd_reg<1><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
+        else if (D == 256) k_ln_bwd_reg<2><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
+        else if (D == 512) k_ln_bwd_reg<4><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
+        else k_ln_bwd_reg<8><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
+        launched = 1;
+        if (want) {
+            k_ln_bwd_wb_combine<<<grid_for(d, D), kThreads, 0, NCK_STREAM(d)>>>(part, (int)blocks, D, gw, gb);
+            launched++;
+        }
+        NCK_LAUNCHED(d, launched);
+        return;
+    }
     if (gx) {
         k_ln_bwd_dx<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, R, D);
         launched++;

@@ -249,7 +249,8 @@ __global__ void __launch_bounds__(1024) k_colsum_small(const float *__restrict__
 extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return;
     Scope sc(d, "colsum");
-    if (M * N <= ((int64_t)1 << 20) && M <= ((int64_t)1 << 14)) {
+    // one block per 32 columns only when that fills the GPU or the columns are short
+    if (M * N <= ((int64_t)1 << 20) && (M <= 1024 || (N + 31) / 32 >= d->sm_count)) {
         k_colsum_small<<<(unsigned)((N + 31) / 32), dim3(32, 32), 0, NCK_STREAM(d)>>>(x, N, gy, M, N);
         NCK_LAUNCHED(d, 1);
         return;

@@ -284,6 +284,10 @@ nc_tensor *nc__grad_buf(nc_tensor *t);
  * *acc = 1 (the writer adds). Persistent tensors always get a zero-filled buffer and *acc = 1. */
 nc_tensor *nc__grad_buf_acc(nc_tensor *t, int *acc);
 static inline int nc__needs_grad(const nc_tensor *t) { return (t->flags & NC_TF_REQUIRES_GRAD) != 0; }
+/* A backward whose input gradient is its output gradient element for element in row-major order (a
+ * reshape, a contiguous copy) passes the buffer on instead of copying it, when the input has no
+ * gradient yet and is a temporary and the pass frees gradients as it goes. Returns 1 when done. */
+int nc__grad_handoff(nc_tensor *in, nc_tensor *out);
 
 /* device pointer to t's element 0 after pushing any host writes to the device */
 void *nc__dev(nc_tensor *t);
@@ -328,13 +332,18 @@ void nc__dp_rng_step_end(nc_ctx *ctx);
  * reads the recipe and pools straight from x; anything else that touches the data materialises it
  * first (nc__dev and the host paths call nc__materialize). In backward, a pool or activation over
  * such a chain runs the whole chain's backward in one fused BatchNorm backward. */
+enum { NC_DEF_BN = 0, NC_DEF_ATTN = 1 };
 typedef struct nc_deferred {
     nc_tensor *owner;              /* the tensor whose values are pending */
-    nc_tensor *src;                /* the BatchNorm input's owner: its data feeds the recipe */
+    nc_tensor *src[3];             /* owners whose data feeds the recipe (NULL: unused) */
+    int kind;                      /* NC_DEF_* */
+    /* NC_DEF_BN: act(BatchNorm(x)) */
     const float *x, *w, *b, *mean, *invstd;
     int64_t N, C, S;
     int act;                       /* NCK_UN_* kind applied after the normalisation, -1: none */
     float act_s;
+    /* NC_DEF_ATTN: a tensor of the scores -> mask -> softmax -> dropout chain (at.stage says which) */
+    nck_attn at;
     struct nc_deferred *next;
 } nc_deferred;
 
@@ -350,9 +359,22 @@ void nc__materialize(nc_tensor *owner);
 void nc__deferred_release(nc_tensor *owner);
 void nc__deferred_flush(nc_ctx *ctx);  /* materialise every pending recipe */
 void nc__deferred_reset(nc_ctx *ctx);  /* step end: forget every recipe (their storage is reset) */
-/* Runs the fused backward of the chain that ends at node n when there is one: fills consumed with the
- * chain's other nodes (whose own backward must not run) and returns their count, else 0. */
+/* Attention chains (fusion.c). Each returns 1 when it took the op (out is a recipe, or was computed
+ * by the fused kernel), 0 when the op runs its own kernels. */
+int nc__attn_bmm(nc_node *n);                       /* scores q @ k^T, or probabilities @ v */
+int nc__attn_mask(nc_node *n);                      /* masked_fill of the scores */
+int nc__attn_softmax(nc_node *n);                   /* softmax of the (masked) scores */
+int nc__attn_scale(nc_node *n, float s);            /* scale of the scores */
+/* dropout of the probabilities: bits holds the keep mask (the caller drew it from the stream) */
+int nc__attn_dropout_ok(const nc_tensor *x); /* x is probabilities a dropout can extend */
+int nc__attn_dropout(nc_node *n, const uint32_t *bits);
+/* Runs the fused backward of the chain that ends at node n when there is one: fills consumed (room
+ * for NC_CHAIN_MAX) with the chain's other nodes (whose own backward must not run) and returns their
+ * count, else 0. */
+#define NC_CHAIN_MAX 6
 int nc__fused_backward(nc_ctx *ctx, nc_node *n, nc_node **consumed);
+/* the values of n's output and inputs, for a backward that reads them: pending recipes computed */
+void nc__backward_inputs(nc_node *n);
 /* the NCK_UN_* kind of a unary activation op, -1 for any other op (ops_elementwise.c) */
 int nc__unary_kind(const nc_op_def *op);
 

@@ -110,6 +110,11 @@ void nck_binary_bwd(nck_dev *d, int kind, int which, const nck_bcast *bc, const 
 void nck_compare(nck_dev *d, int op, const nck_bcast *bc, const void *a, int a_i32, const void *b, int b_i32,
                  int32_t *o);
 /* out = mask ? v : x with mask i32 broadcast (strides in bc->sb), x strides in bc->sa, out contiguous */
+/* masked_fill when x and the output are contiguous and the mask covers the last dims (Mn elements)
+ * repeated over the leading ones: bwd 0: o = mask ? v : x; bwd 1: o (+ when acc)= mask ? 0 : x.
+ * Returns 0 (nothing launched) when the sizes do not fit it. */
+int nck_masked_fill_tail(nck_dev *d, int bwd, const float *x, const int32_t *m, float v, float *o, int64_t n,
+                         int64_t Mn, int acc);
 void nck_masked_fill_fwd(nck_dev *d, const nck_bcast *bc, const float *x, const int32_t *m, float v, float *o);
 void nck_masked_fill_bwd(nck_dev *d, const nck_bcast *bc, const float *g, const int32_t *m, float *gx);
 
@@ -141,13 +146,45 @@ void nck_cross_entropy_bwd(nck_dev *d, const float *prob, const int32_t *lab, co
                            int64_t N, int64_t C);
 void nck_nll_fwd(nck_dev *d, const float *x, const int32_t *lab, float *loss, int64_t N, int64_t C, int sum);
 void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, int64_t N, int64_t C, int sum);
-/* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i */
+/* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i;
+ * x = y = NULL draws the keep mask only */
 /* polys: the device table of run polynomials (nck_rng_polys) or NULL to jump by matrices */
 void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits, int64_t n,
                      float p, const void *polys);
 /* device copy of x^(64 k) mod P for k < count from the host table (uploaded once, grown on demand) */
 const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t count);
 void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p, int acc);
+
+/* Attention over B independent heads: scores S = Q K^T (FFMA, d in order), masked_fill where the mask is
+ * nonzero, row softmax, inverted dropout, and the product with V. Operands are strided views, element
+ * (b, r, c) at p[b * s[0] + r * s[1] + c * s[2]]; the mask is broadcast by zero strides. stage says how
+ * far along the chain the probabilities are: a materialisation writes that tensor, and the products
+ * use it as their left operand. */
+enum { NCK_ATT_SCORES = 0, NCK_ATT_MASKED = 1, NCK_ATT_SOFTMAX = 2, NCK_ATT_DROPOUT = 3 };
+typedef struct {
+    const float *q, *k, *v;   /* q (b, i, d), k (b, j, d), v (b, j, e) */
+    int64_t qs[3], ks[3], vs[3];
+    const int32_t *mask;      /* (b, i, j): nonzero -> fill; NULL = no mask */
+    int64_t ms[3];
+    float fill;
+    const uint32_t *bits;     /* dropout keep bits of element (b * L + i) * S + j */
+    float p;
+    float scale;              /* scaled: the scores are multiplied by scale before the mask */
+    int scaled;
+    int64_t B, L, S, D, Dv;
+    int stage;
+} nck_attn;
+/* shapes the fused kernels take: L, S <= 128, D, Dv <= 32 */
+int nck_attn_ok(int64_t L, int64_t S, int64_t D, int64_t Dv);
+/* o [B, L, Dv] = probs(stage) @ V */
+void nck_attn_fwd(nck_dev *d, const nck_attn *a, float *o);
+/* out [B, L, S] = the chain's tensor at a->stage */
+void nck_attn_probs(nck_dev *d, const nck_attn *a, float *out);
+/* Gradients of o = probs @ V given dO [B, L, Dv] (contiguous): dq [B, L, D], dkt [B, D, S] (K^T's
+ * layout), dv [B, S, Dv], each contiguous, NULL when not wanted, added to when its acc flag is set.
+ * The probabilities are recomputed, so they equal the forward's. */
+void nck_attn_bwd(nck_dev *d, const nck_attn *a, const float *dout, float *dq, int acc_q, float *dkt, int acc_k,
+                  float *dv, int acc_v);
 /* one-time upload of the xoshiro256** jump tables (host-computed) */
 int nck_rng_tables_upload(nck_dev *d, const uint64_t *tables, size_t bytes);
 

@@ -110,6 +110,8 @@ static nc_status unary_fwd(nc_node *n) {
     /* an activation of a pending BatchNorm output extends its recipe (nothing is computed yet) */
     if (n->out->ctx->fuse && n->out->ctx->fwd_on_tape && nc__defer_act(n->out, n->in[0], n->op->kind, n->p.f[0]))
         return NC_OK;
+    /* a scale of pending attention scores joins the chain */
+    if (n->op->kind == NCK_UN_SCALE && nc__attn_scale(n, n->p.f[0])) return NC_OK;
     const float *x = nc__contig_f32(n->in[0]);
     if (!x) return NC_ERR_OOM;
     nck_unary_fwd(nc__k(n->out->ctx), n->op->kind, n->p.f[0], x, (float *)n->out->data, nc_numel(n->out));

@@ -241,6 +241,7 @@ static void bmm_geometry(const nc_node *n, bmm_dims *d) {
 }
 
 static nc_status bmm_fwd(nc_node *n) {
+    if (nc__attn_bmm(n)) return NC_OK; /* attention scores (a recipe) or probabilities @ v (fused) */
     nc_tensor *a = n->in[0], *b = n->in[1], *o = n->out;
     bmm_dims d;
     bmm_geometry(n, &d);
@@ -286,7 +287,7 @@ static void bmm_bwd(nc_node *n) {
     }
 }
 
-const nc_op_def nc_op_bmm = {"bmm", 0, 0, bmm_infer, NULL, bmm_fwd, bmm_bwd};
+const nc_op_def nc_op_bmm = {"bmm", NC_OPF_RECIPE, 0, bmm_infer, NULL, bmm_fwd, bmm_bwd};
 
 nc_tensor *nc_matmul(nc_tensor *a, nc_tensor *b) {
     nc_tensor *in[2] = {a, b};

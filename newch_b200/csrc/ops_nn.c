@@ -8,6 +8,8 @@
  */
 #include "nc_internal.h"
 
+#include <cuda_runtime_api.h>
+
 #include <math.h>
 
 enum { SM_LOG, SM_PLAIN };
@@ -26,6 +28,7 @@ static nc_status softmax_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape
 }
 
 static nc_status softmax_fwd(nc_node *n) {
+    if (n->op->kind == SM_PLAIN && nc__attn_softmax(n)) return NC_OK; /* attention probabilities: a recipe */
     const float *x = nc__contig_f32(n->in[0]);
     if (!x) return NC_ERR_OOM;
     int64_t C = n->out->shape[n->out->ndim - 1];
@@ -45,7 +48,7 @@ static void softmax_bwd(nc_node *n) {
 }
 
 const nc_op_def nc_op_log_softmax = {"log_softmax", 0, SM_LOG, softmax_infer, NULL, softmax_fwd, softmax_bwd};
-const nc_op_def nc_op_softmax = {"softmax", 0, SM_PLAIN, softmax_infer, NULL, softmax_fwd, softmax_bwd};
+const nc_op_def nc_op_softmax = {"softmax", NC_OPF_RECIPE, SM_PLAIN, softmax_infer, NULL, softmax_fwd, softmax_bwd};
 
 nc_tensor *nc_log_softmax(nc_tensor *x) { return nc__apply(&nc_op_log_softmax, &x, 1, NULL); }
 nc_tensor *nc_softmax(nc_tensor *x) { return nc__apply(&nc_op_softmax, &x, 1, NULL); }
@@ -151,9 +154,19 @@ static nc_status dropout_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape
  * its own copy of the state past them. The mask is kept as bits (N/8 bytes) for backward. */
 static nc_status dropout_fwd(nc_node *n) {
     nc_ctx *ctx = n->out->ctx;
-    const float *x = nc__contig_f32(n->in[0]);
     int64_t N = nc_numel(n->out);
     int64_t words = (N + 31) / 32 + 1;
+    if (nc__attn_dropout_ok(n->in[0])) { /* attention probabilities: draw the mask only, extend the recipe */
+        uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
+        if (!bits) return NC_ERR_OOM;
+        if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, NULL, NULL, bits, N, n->p.f[0], nc__rng_dropout_table(ctx, N));
+        nc__rng_skip(ctx, (uint64_t)N);
+        n->saved = bits;
+        if (nc__attn_dropout(n, bits)) return NC_OK;
+        nc__error(ctx, NC_ERR_OOM, "dropout: out of host memory");
+        return NC_ERR_OOM;
+    }
+    const float *x = nc__contig_f32(n->in[0]);
     uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
     if (!x || !bits) return NC_ERR_OOM;
     if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0],
@@ -173,7 +186,8 @@ static void dropout_bwd(nc_node *n) {
                         (float *)gt->data, N, n->p.f[0], acc);
 }
 
-const nc_op_def nc_op_dropout = {"dropout", NC_OPF_ELEMENTWISE, 0, dropout_infer, NULL, dropout_fwd, dropout_bwd};
+const nc_op_def nc_op_dropout = {"dropout", NC_OPF_ELEMENTWISE | NC_OPF_RECIPE, 0, dropout_infer, NULL, dropout_fwd,
+                                  dropout_bwd};
 
 nc_tensor *nc_dropout(nc_tensor *x, float p) {
     nc_op_params prm;
@@ -453,7 +467,34 @@ static void mf_bcast(const nc_node *n, nck_bcast *bc, int grad) {
     nc__contig_strides(o->ndim, o->shape, bc->so);
 }
 
+/* Elements of the mask's repeating block when the mask is contiguous over the output's last dims and
+ * broadcast over the leading ones (an attention mask), else 0. */
+static int64_t mask_tail(const nc_node *n) {
+    const nc_tensor *m = n->in[1], *o = n->out;
+    if (!nc_is_contiguous(m)) return 0;
+    int64_t sb[NC_MAX_DIMS];
+    nc__bcast_strides(m, o->ndim, o->shape, sb);
+    for (int k = 0; k <= o->ndim; k++) { /* the block is dims k.. of the output */
+        int ok = 1;
+        for (int i = 0; i < k && ok; i++) ok = sb[i] == 0 || o->shape[i] == 1;
+        int64_t step = 1;
+        for (int i = o->ndim - 1; i >= k && ok; i--) {
+            ok = o->shape[i] == 1 || sb[i] == step;
+            step *= o->shape[i];
+        }
+        if (ok) return step == nc_numel(m) ? step : 0;
+    }
+    return 0;
+}
+
 static nc_status masked_fill_fwd(nc_node *n) {
+    if (nc__attn_mask(n)) return NC_OK; /* masked attention scores: a recipe */
+    nc_tensor *x = n->in[0];
+    nc__dev(x);
+    const int64_t tail = nc_is_contiguous(x) ? mask_tail(n) : 0;
+    if (tail && nck_masked_fill_tail(nc__k(n->out->ctx), 0, (const float *)x->data, (const int32_t *)n->in[1]->data,
+                                     n->p.f[0], (float *)n->out->data, nc_numel(n->out), tail, 0))
+        return NC_OK;
     nck_bcast bc;
     mf_bcast(n, &bc, 0);
     nck_masked_fill_fwd(nc__k(n->out->ctx), &bc, (const float *)n->in[0]->data, (const int32_t *)n->in[1]->data,
@@ -462,6 +503,17 @@ static nc_status masked_fill_fwd(nc_node *n) {
 }
 
 static void masked_fill_bwd(nc_node *n) {
+    const int64_t tail = mask_tail(n);
+    if (tail) {
+        int acc;
+        nc_tensor *g = nc__grad_buf_acc(n->in[0], &acc);
+        if (g && nck_masked_fill_tail(nc__k(g->ctx), 1, (const float *)n->out->grad->data,
+                                      (const int32_t *)n->in[1]->data, 0.0f, (float *)g->data, nc_numel(n->out), tail,
+                                      acc))
+            return;
+        if (g && !acc) nc__cuda_ok(g->ctx, cudaMemsetAsync(g->data, 0, g->bytes, (cudaStream_t)g->ctx->dev.stream),
+                                   "memset");
+    }
     nc_tensor *gx = nc__grad_buf(n->in[0]);
     if (!gx) return;
     nck_bcast bc;
@@ -470,7 +522,8 @@ static void masked_fill_bwd(nc_node *n) {
                         (float *)gx->data);
 }
 
-const nc_op_def nc_op_masked_fill = {"masked_fill", 0, 0, masked_fill_infer, NULL, masked_fill_fwd, masked_fill_bwd};
+const nc_op_def nc_op_masked_fill = {"masked_fill", NC_OPF_RECIPE, 0, masked_fill_infer, NULL, masked_fill_fwd,
+                                      masked_fill_bwd};
 
 nc_tensor *nc_masked_fill(nc_tensor *x, nc_tensor *mask, float value) {
     if (mask && mask->dtype != NC_I32) mask = nc_to_dtype(mask, NC_I32);

@@ -57,6 +57,7 @@ static void scatter_grad_by_map(nc_node *n, layout_map map, int covers_all) {
 
 /* gradient of an op whose output is x's elements in x's row-major order */
 static void flat_grad(nc_node *n) {
+    if (nc__grad_handoff(n->in[0], n->out)) return; /* x takes dY's buffer as its gradient */
     int acc;
     nc_tensor *gx = nc__grad_buf_acc(n->in[0], &acc);
     if (!gx) return;

@@ -506,6 +506,22 @@ nc_tensor *nc__grad_buf(nc_tensor *t) {
     return t->grad;
 }
 
+int nc__grad_handoff(nc_tensor *in, nc_tensor *out) {
+    nc_tensor *g = out->grad;
+    nc_ctx *ctx = in->ctx;
+    if (!ctx->bwd_logging || !g || in->grad || (in->flags & NC_TF_PERSISTENT) || (g->flags & NC_TF_PERSISTENT) ||
+        !(g->flags & NC_TF_OWNS_DATA) || in->dtype != NC_F32 || nc_numel(in) != nc_numel(g))
+        return 0;
+    nc__dev_write(g);
+    g->ndim = in->ndim;
+    memcpy(g->shape, in->shape, sizeof(int64_t) * (size_t)in->ndim);
+    nc__contig_strides(in->ndim, g->shape, g->stride);
+    in->grad = g;
+    in->flags &= ~NC_TF_GRAD_CLEARED;
+    out->grad = NULL;
+    return 1;
+}
+
 nc_tensor *nc__grad_buf_acc(nc_tensor *t, int *acc) {
     *acc = 1;
     if (t->flags & NC_TF_PERSISTENT) return nc__grad_buf(t);

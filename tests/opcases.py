@@ -237,6 +237,77 @@ def case_bmm_broadcast(e):
     return out
 
 
+def _attention(e, seed, BH, L, S, D, Dv, p, mask="random", scale=None, layout="plain", read_probs=False):
+    """scores = q @ k^T (k through a transposed view) -> [scale] -> masked_fill(-inf) -> softmax ->
+    [dropout] -> @ v: newch's multi-head attention chain, which the B200 engine keeps as recipes and
+    runs as one fused forward and one fused backward. layout "mha": q, k, v are the [T, BH, Dh] ->
+    [BH, T, Dh] transposed views nn.MultiheadAttention makes (q scaled first, as it does).
+    read_probs: the softmax output is read back, which forces the unfused paths."""
+    e.L.nc_manual_seed(e.ctx, seed)
+    res = {}
+    if layout == "mha":
+        qb, kb, vb = (e.param(seeded(seed + i, (L, BH, D if i < 2 else Dv))) for i in range(3))
+        q = e.check(e.L.nc_scale(e.check(e.L.nc_transpose(qb, 0, 1)), 1.0 / np.sqrt(D)))
+        k = e.check(e.L.nc_transpose(kb, 0, 1))
+        v = e.check(e.L.nc_transpose(vb, 0, 1))
+        leaves = {"q": qb, "k": kb, "v": vb}
+    else:
+        q = e.param(seeded(seed, (BH, L, D)))
+        k = e.param(seeded(seed + 1, (BH, S, D)))
+        v = e.param(seeded(seed + 2, (BH, S, Dv)))
+        leaves = {"q": q, "k": k, "v": v}
+    for n, t in leaves.items():
+        res[n] = e.np(t)
+    s = e.check(e.L.nc_matmul(q, e.check(e.L.nc_transpose(k, 1, 2))))
+    if scale is not None:
+        s = e.check(e.L.nc_scale(s, scale))
+    if mask == "causal":
+        m = (np.arange(S)[None, :] > np.arange(L)[:, None]).astype(np.int32)
+    elif mask == "random":
+        m = (np.random.default_rng(seed + 3).random((L, S)) > 0.6).astype(np.int32)
+        m[:, 0] = 0  # no row fully masked
+    else:
+        m = None
+    if m is not None:
+        res["mask"] = m
+        s = e.check(e.L.nc_masked_fill(s, e.t(m), -np.inf))
+    pr = e.check(e.L.nc_softmax(s))
+    if read_probs:
+        res["probs"] = e.np(pr)
+    pd = e.check(e.L.nc_dropout(pr, p)) if p > 0 else pr
+    y = e.check(e.L.nc_matmul(pd, v))
+    G = seeded(seed + 4, e.shape(y))
+    res.update(y=e.np(y), G=G)
+    e.backward_with(y, G)
+    for n, t in leaves.items():
+        res["d" + n] = e.grad(t)
+    return res
+
+
+def case_attention_chain(e):
+    return _attention(e, 800, 6, 10, 12, 8, 6, 0.2)
+
+
+def case_attention_mha(e):
+    return _attention(e, 810, 6, 20, 20, 8, 8, 0.1, mask="causal", layout="mha")
+
+
+def case_attention_mha_128(e):
+    return _attention(e, 820, 4, 128, 128, 32, 32, 0.1, mask="causal", layout="mha")
+
+
+def case_attention_sdpa(e):
+    return _attention(e, 830, 5, 33, 40, 16, 12, 0.0, mask="random", scale=0.25)
+
+
+def case_attention_unmasked(e):
+    return _attention(e, 840, 3, 7, 9, 5, 3, 0.3, mask=None)
+
+
+def case_attention_probs_read(e):
+    return _attention(e, 850, 4, 12, 12, 8, 8, 0.2, mask="causal", read_probs=True)
+
+
 def case_softmax(e):
     x = e.param(seeded(150, (5, 9), 3.0))
     y = e.check(e.L.nc_softmax(x))

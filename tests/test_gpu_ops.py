@@ -81,10 +81,11 @@ def test_libm_math_mode(how, monkeypatch):
 
 
 @pytest.mark.parametrize("case", ["bn_relu_pool", "bn_pool", "bn_hardswish", "bn_relu6_pool", "bn_relu_reused",
-                                  "bn_relu_pool_odd"])
-def test_bn_chains_unfused(case, monkeypatch):
-    """NC_FUSE=0: the BatchNorm chains through the unfused kernels (every intermediate written), held
-    to the same goldens as the fused default (test_op_matches_reference)."""
+                                  "bn_relu_pool_odd", "attention_chain", "attention_mha", "attention_mha_128",
+                                  "attention_sdpa", "attention_unmasked", "attention_probs_read"])
+def test_chains_unfused(case, monkeypatch):
+    """NC_FUSE=0: the BatchNorm and attention chains through the unfused kernels (every intermediate
+    written), held to the same goldens as the fused default (test_op_matches_reference)."""
     monkeypatch.setenv("NC_FUSE", "0")
     out = run_case("b200", case)
     for k in out:
