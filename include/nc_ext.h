@@ -61,6 +61,12 @@ NC_API int nc_ext_kernel_entry(nc_ctx *ctx, int i, const char **name, double *ms
 /* Clears the accumulated timings (timing stays on). */
 NC_API void nc_ext_timing_reset(nc_ctx *ctx);
 
+/* Failure-reporting probe: launches one kernel whose tensor-core pipeline wait (an mbarrier that
+ * never completes) gives up after its 2 s bound, as every tcgen05 kernel's waits do, then
+ * synchronizes. Returns the context status: NC_ERR_STATE with "pipeline wait timed out" in
+ * nc_error. The device stays usable: nc_clear_error and continue. */
+NC_API int nc_ext_pipeline_wait_probe(nc_ctx *ctx);
+
 /* Cross-entropy forward on caller-owned device buffers that allocates nothing. It has no
  * counterpart in newch; the arithmetic is the engine's nc_cross_entropy (newch
  * engine/src/ops/ops_nn.c:107-149): prob[rows, classes] = softmax(logits) and

@@ -160,6 +160,7 @@ EXT_SIGNATURES: dict = {
     "nc_ext_device_count": (c_int, []),
     "nc_ext_device_name": (c_char_p, [P]),
     "nc_ext_synchronize": (c_int, [P]),
+    "nc_ext_pipeline_wait_probe": (c_int, [P]),
     "nc_ext_launch_count": (c_int64, [P]),
     "nc_ext_gemm_mode": (c_char_p, [P]),
     "nc_ext_nccl_unique_id": (c_int, [c_void_p, c_int]),

@@ -554,6 +554,13 @@ int nc_ext_synchronize(nc_ctx *ctx) {
     return ctx->status;
 }
 
+int nc_ext_pipeline_wait_probe(nc_ctx *ctx) {
+    if (!ctx->device_ok) return ctx->status;
+    nck_pipeline_wait_probe(nc__k(ctx));
+    nc__sync(ctx);
+    return ctx->status;
+}
+
 int64_t nc_ext_launch_count(const nc_ctx *ctx) { return ctx->dev.launches; }
 
 const char *nc_ext_gemm_mode(const nc_ctx *ctx) {

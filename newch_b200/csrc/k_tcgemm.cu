@@ -457,3 +457,18 @@ extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
     NCK_LAUNCHED(d, launched);
     return 1;
 }
+
+// A pipeline wait that nothing completes: an mbarrier expecting one arrival that never comes. The
+// bounded wait gives up after kWaitNs and reports kErrPipeline, the path every tcgen05 kernel takes
+// when a TMA transfer or an MMA commit does not arrive; it exercises that reporting end to end.
+__global__ void k_wait_probe(int *status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, status);
+}
+
+extern "C" void nck_pipeline_wait_probe(nck_dev *d) {
+    k_wait_probe<<<1, 32, 0, NCK_STREAM(d)>>>(d->status);
+    NCK_LAUNCHED(d, 1);
+}

@@ -337,6 +337,9 @@ void nck_gemm(nck_dev *d, const nck_gemm_args *a);
 /* tensor-core path (tcgen05 kind::tf32 via TMA); returns 0 when the operands do not meet its
  * alignment rules, leaving the GEMM to the caller */
 int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a);
+/* one kernel whose pipeline wait never completes: it gives up after its bound and sets
+ * NCK_ERR_PIPELINE (tests the failure reporting of the tcgen05 kernels' bounded waits) */
+void nck_pipeline_wait_probe(nck_dev *d);
 
 /* ---- optimizers -------------------------------------------------------------------------------- */
 typedef struct {

@@ -650,3 +650,44 @@ def sgd_step(w, g, buf, lr, momentum=0.0, weight_decay=0.0, gs=1.0):
     if buf is not None:
         gj = buf = (f32(momentum) * buf + gj).astype(f32)
     return (w - f32(lr) * gj).astype(f32), buf
+
+
+def rmsprop_step(w, g, v, buf, lr, alpha, eps, momentum=0.0, weight_decay=0.0, eps_inside=False, gs=1.0):
+    """optim.c:187-197: v = a v + (1 - a) g^2, step = g / den, optional momentum buffer."""
+    lr, a, eps, mom, wd, gs = (f32(t) for t in (lr, alpha, eps, momentum, weight_decay, gs))
+    gj = (gs * g.astype(f32) + wd * w).astype(f32)
+    v = (a * v + (f32(1) - a) * gj * gj).astype(f32)
+    den = np.sqrt(v + eps).astype(f32) if eps_inside else (np.sqrt(v).astype(f32) + eps).astype(f32)
+    step = (gj / den).astype(f32)
+    if buf is not None:
+        step = buf = (mom * buf + step).astype(f32)
+    return (w - lr * step).astype(f32), v, buf
+
+
+def attention(q, k, v, mask, p, rng, G, fill=-np.inf, scale=None):
+    """newch's attention chain (net/__init__.py:811-820) for q [B, L, D], k [B, S, D], v [B, S, Dv],
+    mask [L, S] (nonzero = masked) or None, dropout p drawn from rng, upstream gradient G: returns
+    y and the gradients of q, k and v (ops_linalg.c bmm, ops_nn.c masked_fill / softmax / dropout)."""
+    q, k, v = (t.astype(np.float64) for t in (q, k, v))
+    s = np.matmul(q, k.transpose(0, 2, 1)).astype(f32)
+    if scale is not None:
+        s = (f32(scale) * s).astype(f32)
+    m = np.zeros(s.shape[1:], bool) if mask is None else mask.astype(bool)
+    s = np.where(m, f32(fill), s).astype(f32)
+    y = softmax(s)
+    if p > 0:
+        pd, keep = dropout(y, p, rng)
+    else:
+        pd, keep = y, np.ones_like(y)
+    out = np.matmul(pd.astype(np.float64), v).astype(f32)
+    G = G.astype(np.float64)
+    gpd = np.matmul(G, v.transpose(0, 2, 1)).astype(f32)
+    gy = (gpd * keep).astype(f32)
+    gs = np.where(m, f32(0), softmax_grad(y, gy, False)).astype(f32)
+    if scale is not None:
+        gs = (f32(scale) * gs).astype(f32)
+    gs = gs.astype(np.float64)
+    dq = np.matmul(gs, k).astype(f32)
+    dk = np.matmul(gs.transpose(0, 2, 1), q).astype(f32)
+    dv = np.matmul(pd.astype(np.float64).transpose(0, 2, 1), G).astype(f32)
+    return out, dq, dk, dv

@@ -548,6 +548,43 @@ def _adam(e, decoupled, seed):
     return out
 
 
+def _optim(e, make, opts, seed, steps=4):
+    """Several update steps of one optimizer on a seeded weight vector with seeded gradients."""
+    w0 = seeded(seed, (50,))
+    w = e.param(w0)
+    opt = e.check(make(capi.ptr_array([w]), opts))
+    out = {"w0": w0}
+    for k in range(steps):
+        G = seeded(seed + 1 + k, (50,))
+        e.L.nc_optim_clear_grad(opt)
+        wt = e.check(e.L.nc_mul(w, e.t(G)))
+        assert e.L.nc_backward(e.check(e.L.nc_sum(wt, ALL, 0))) == 0
+        e.L.nc_optim_step(opt)
+        out[f"G{k}"] = G
+        out[f"w{k + 1}"] = e.np(w)
+        e.step_end()
+    e.L.nc_optim_free(opt)
+    return out
+
+
+def case_sgd(e):
+    return _optim(e, lambda a, o: e.L.nc_sgd(e.ctx, a, 1, o), capi.OptimOpts(0.1, 0.0, 0.01, 0.9, 0.999, 1e-8), 270)
+
+
+def case_sgd_momentum(e):
+    return _optim(e, lambda a, o: e.L.nc_sgd(e.ctx, a, 1, o), capi.OptimOpts(0.05, 0.9, 0.02, 0.9, 0.999, 1e-8), 280)
+
+
+def case_rmsprop(e):
+    return _optim(e, lambda a, o: e.L.nc_rmsprop(e.ctx, a, 1, o, 0),
+                  capi.OptimOpts(1e-2, 0.0, 0.01, 0.9, 0.99, 1e-8), 290)
+
+
+def case_rmsprop_momentum_eps_inside(e):
+    return _optim(e, lambda a, o: e.L.nc_rmsprop(e.ctx, a, 1, o, 1),
+                  capi.OptimOpts(1e-2, 0.8, 0.0, 0.9, 0.95, 1e-6), 300)
+
+
 def case_adam(e):
     return _adam(e, False, 260)
 

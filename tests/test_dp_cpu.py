@@ -128,3 +128,40 @@ def test_rank_average_equals_full_batch_gradient():
         full = np.concatenate([e.grad(w).ravel(), e.grad(b).ravel()])
     for _, avg in res:
         np.testing.assert_allclose(avg, full, rtol=1e-5, atol=1e-7)
+
+
+def _exit_worker(rank, world, port, q):
+    """Rank 0 leaves right after the group forms (between steps: nothing in flight); rank 1's set-up
+    exchange must end with an error, not wait for good."""
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO))
+    from newch_b200 import dist as dh
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 0:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()  # the item is delivered before the process vanishes
+        os._exit(0)
+    t0 = time.time()
+    try:
+        dh.join_engine_group(_FakeLib(), None, dist.group.WORLD, rank, world)
+        q.put((rank, "joined", time.time() - t0))
+    except Exception as ex:  # the broadcast from the departed rank fails
+        q.put((rank, f"error {type(ex).__name__}", time.time() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_departed_rank_ends_the_exchange_with_an_error():
+    res = _run(_exit_worker, 2)
+    assert res[0][1] == "left"
+    status, secs = res[1][1], res[1][2]
+    assert status.startswith("error"), status
+    assert secs < 60.0, secs

@@ -137,6 +137,90 @@ def test_save_load_round_trip():
         assert raw[:4] == b"NCW1"
 
 
+def _ncw1_items():
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    from make_ncw1 import OUT, ncw1_tensors
+
+    return OUT, ncw1_tensors()
+
+
+def test_ncw1_written_by_the_reference_loads():
+    """tests/golden/ref_state.ncw was written by the reference engine's nc_save (make_ncw1.py)."""
+    path, items = _ncw1_items()
+    with Eng() as e:
+        ts = [e.t(np.zeros_like(a), persistent=True) for _, a in items]
+        names = (ctypes.c_char_p * len(items))(*[n.encode() for n, _ in items])
+        assert e.L.nc_load(e.ctx, str(path).encode(), len(items), names, capi.ptr_array(ts)) == 0, e.err()
+        for (n, a), t in zip(items, ts):
+            assert np.array_equal(e.np(t), a), n
+
+
+def test_ncw1_written_here_matches_the_reference_bytes():
+    path, items = _ncw1_items()
+    with Eng() as e:
+        ts = [e.t(a, persistent=True) for _, a in items]
+        names = (ctypes.c_char_p * len(items))(*[n.encode() for n, _ in items])
+        out = os.path.join(tempfile.mkdtemp(), "b200.ncw")
+        assert e.L.nc_save(e.ctx, out.encode(), len(items), names, capi.ptr_array(ts)) == 0, e.err()
+    assert open(out, "rb").read() == path.read_bytes()
+
+
+def _resume_model(e, W1, B1, W2):
+    ps = [e.param(W1), e.param(B1), e.param(W2)]
+    opt = e.check(e.L.nc_adamw(e.ctx, capi.ptr_array(ps), 3, capi.OptimOpts(1e-2, 0.0, 0.01, 0.9, 0.999, 1e-8)))
+    return ps, opt
+
+
+def _resume_step(e, ps, opt, X, Y):
+    e.L.nc_optim_clear_grad(opt)
+    h = e.check(e.L.nc_relu(e.check(e.L.nc_linear_fn(e.t(X), ps[0], ps[1]))))
+    loss = e.check(e.L.nc_cross_entropy(e.check(e.L.nc_linear_fn(h, ps[2], None)), e.t(Y)))
+    assert e.L.nc_backward(loss) == 0, e.err()
+    e.L.nc_optim_step(opt)
+    e.step_end()
+
+
+def test_bit_exact_resume_from_checkpoint():
+    """Train 3 steps, checkpoint the parameters (NCW1) and the optimizer state (state pointers and
+    step count, as newch's Optimizer.state_dict does), then 3 more steps; a fresh context restored
+    from the checkpoint takes the same 3 steps to bit-identical parameters (newch
+    tests/test_checkpoint.py:57-73)."""
+    rng = np.random.default_rng(5)
+    W1, B1, W2 = (rng.standard_normal(s).astype(np.float32) * 0.3 for s in ((16, 12), (16,), (5, 16)))
+    batches = [(rng.standard_normal((32, 12)).astype(np.float32), rng.integers(0, 5, 32).astype(np.int32))
+               for _ in range(6)]
+    path = os.path.join(tempfile.mkdtemp(), "ckpt.ncw")
+    names = (ctypes.c_char_p * 3)(b"w1", b"b1", b"w2")
+    with Eng() as e:
+        ps, opt = _resume_model(e, W1, B1, W2)
+        for X, Y in batches[:3]:
+            _resume_step(e, ps, opt, X, Y)
+        assert e.L.nc_save(e.ctx, path.encode(), 3, names, capi.ptr_array(ps)) == 0
+        state = [[np.frombuffer(ctypes.string_at(e.L.nc_optim_state(opt, i, s), 4 * W.size), np.float32).copy()
+                  for s in (0, 1)] for i, W in enumerate((W1, B1, W2))]
+        step = e.L.nc_optim_get_step(opt)
+        for X, Y in batches[3:]:
+            _resume_step(e, ps, opt, X, Y)
+        straight = [e.np(p) for p in ps]
+        e.L.nc_optim_free(opt)
+    with Eng() as e:
+        ps, opt = _resume_model(e, np.zeros_like(W1), np.zeros_like(B1), np.zeros_like(W2))
+        assert e.L.nc_load(e.ctx, path.encode(), 3, names, capi.ptr_array(ps)) == 0, e.err()
+        for i, st in enumerate(state):
+            for s, arr in enumerate(st):
+                ctypes.memmove(e.L.nc_optim_state(opt, i, s), arr.ctypes.data, arr.nbytes)
+        e.L.nc_optim_set_step(opt, step)
+        for X, Y in batches[3:]:
+            _resume_step(e, ps, opt, X, Y)
+        resumed = [e.np(p) for p in ps]
+        e.L.nc_optim_free(opt)
+    for a, b in zip(straight, resumed):
+        assert np.array_equal(a, b)
+
+
 def test_optimizer_state_pointer_round_trip():
     """newch/optim.py reads the state with ctypes.string_at and writes it with memmove."""
     with Eng() as e:

@@ -160,6 +160,46 @@ def test_adam(case, decoupled):
         assert rel_err(w, g(case, f"w{k + 1}")) < 1e-6
 
 
+@pytest.mark.parametrize("case,momentum,wd,lr", [("sgd", 0.0, 0.01, 0.1), ("sgd_momentum", 0.9, 0.02, 0.05)])
+def test_sgd(case, momentum, wd, lr):
+    w = g(case, "w0")
+    buf = np.zeros_like(w) if momentum else None
+    for k in range(4):
+        w, buf = O.sgd_step(w, g(case, f"G{k}"), buf, lr, momentum=momentum, weight_decay=wd)
+        assert rel_err(w, g(case, f"w{k + 1}")) < 1e-6
+
+
+@pytest.mark.parametrize("case,mom,wd,alpha,eps,inside", [("rmsprop", 0.0, 0.01, 0.99, 1e-8, False),
+                                                          ("rmsprop_momentum_eps_inside", 0.8, 0.0, 0.95, 1e-6, True)])
+def test_rmsprop(case, mom, wd, alpha, eps, inside):
+    w = g(case, "w0")
+    v = np.zeros_like(w)
+    buf = np.zeros_like(w) if mom else None
+    for k in range(4):
+        w, v, buf = O.rmsprop_step(w, g(case, f"G{k}"), v, buf, 1e-2, alpha, eps, momentum=mom, weight_decay=wd,
+                                   eps_inside=inside)
+        assert rel_err(w, g(case, f"w{k + 1}")) < 1e-6
+
+
+@pytest.mark.parametrize("case,seed,p,scale,mha", [("attention_chain", 800, 0.2, None, False),
+                                                   ("attention_mha", 810, 0.1, None, True),
+                                                   ("attention_sdpa", 830, 0.0, 0.25, False),
+                                                   ("attention_unmasked", 840, 0.3, None, False)])
+def test_attention_chain(case, seed, p, scale, mha):
+    q, k, v = g(case, "q"), g(case, "k"), g(case, "v")
+    if mha:  # [T, BH, Dh] leaves seen through transposes, q scaled by 1 / sqrt(Dh)
+        q = (np.float32(1.0 / np.sqrt(q.shape[-1])) * q.transpose(1, 0, 2)).astype(np.float32)
+        k, v = k.transpose(1, 0, 2), v.transpose(1, 0, 2)
+    mask = g(case, "mask") if f"{case}/mask" in GOLD.files else None
+    y, dq, dk, dv = O.attention(q, k, v, mask, p, O.Rng(seed), g(case, "G"), scale=scale)
+    if mha:
+        s = np.float32(1.0 / np.sqrt(q.shape[-1]))
+        dq = (s * dq).transpose(1, 0, 2)
+        dk, dv = dk.transpose(1, 0, 2), dv.transpose(1, 0, 2)
+    for name, got in (("y", y), ("dq", dq), ("dk", dk), ("dv", dv)):
+        assert rel_err(got, g(case, name)) < 1e-5, (case, name, rel_err(got, g(case, name)))
+
+
 def test_known_answers_from_reference_tests():
     """Known values of newch's C tests (test_main.c:937-942, :1011-1021)."""
     x = np.arange(1, 10, dtype=np.float32).reshape(1, 1, 3, 3)
