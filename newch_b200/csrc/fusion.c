@@ -329,9 +329,9 @@ static int fuse_pool_chain(nc_ctx *ctx, nc_node *np, nc_node **consumed) {
     float *gx, *gw, *gb;
     int acc;
     bn_grads(nb, &gx, &acc, &gw, &gb);
-    nck_bn_pool_bwd(nc__k(ctx), X, w, b, (const float *)np->out->grad->data, (const int32_t *)np->saved, sv->mean,
-                    sv->invstd, gx, gw, gb, x->shape[0], x->shape[1], x->shape[2], x->shape[3], acc, rz->act,
-                    rz->act_s);
+    nck_bn_pool_bwd(nc__k(ctx), X, w, b, (const float *)np->out->grad->data, (const int32_t *)np->saved,
+                    nc__pool_xarg(np), sv->mean, sv->invstd, gx, gw, gb, x->shape[0], x->shape[1], x->shape[2],
+                    x->shape[3], acc, rz->act, rz->act_s);
     int k = 0;
     if (na) consumed[k++] = na;
     consumed[k++] = nb;

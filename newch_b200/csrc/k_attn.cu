@@ -12,10 +12,12 @@
 // per-lane column walk, same warp trees, same exp), so fused and unfused probabilities agree bit for
 // bit given the same scores. The products are fp32 FFMA chains over the contraction index in order.
 //
-// Geometry: 256 threads, warp w owns rows 16 w .. 16 w + 15 of a [128 x 128] score tile and lane l its
-// columns l, l + 32, l + 64, l + 96 (the unfused softmax's column walk); L, S <= 128 and D, Dv <= 32,
-// zero-padded in shared memory. Tiles of Q / K / V / dO have a row pitch of 36 floats (float4 rows,
-// conflict-free float4 reads across a quarter warp); the probability tiles 132.
+// Geometry: 512 threads (16 warps, four per scheduler), warp w owns rows 8 w .. 8 w + 7 of a
+// [128 x 128] score tile and lane l its columns l, l + 32, l + 64, l + 96 (the unfused softmax's
+// column walk); L, S <= 128 and D, Dv <= 32, zero-padded in shared memory. Tiles of Q / K / V / dO
+// have a row pitch of 36 floats (float4 rows, conflict-free float4 reads across a quarter warp); the
+// probability tiles 132. The transposed products of the backward (dV, dK) give each of 8 warps 16
+// output rows, the two products running side by side on the two halves of the block.
 #include <math.h>
 
 #include "k_common.cuh"
@@ -25,7 +27,8 @@ using namespace nck;
 
 namespace {
 
-constexpr int kAT = 256;       // threads per head
+constexpr int kAT = 512;       // threads per head
+constexpr int kRW = 8;         // score rows per warp
 constexpr int kR = 128;        // max rows L and columns S
 constexpr int kDm = 32;        // max D and Dv
 constexpr int kLd = kDm + 4;   // pitch of the [128 x 32] operand tiles
@@ -73,12 +76,13 @@ __device__ __forceinline__ void load_tile(float *__restrict__ dst, const float *
     }
 }
 
-// acc[r][c] = sum_d A[16 w + r][d] * Bt[lane + 32 c][d], d ascending (FFMA chains); D4 = D rounded up to 4
+// acc[r][c] = sum_d A[row0 + r][d] * Bt[lane + 32 c][d], d ascending (FFMA chains); D4 = D rounded up to 4
+template <int NR>
 __device__ __forceinline__ void rows_by_cols(const float *__restrict__ A, const float *__restrict__ Bt, int D4,
-                                             float (&acc)[16][4]) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+                                             int row0, float (&acc)[NR][4]) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int r = 0; r < 16; r++)
+    for (int r = 0; r < NR; r++)
 #pragma unroll
         for (int c = 0; c < 4; c++) acc[r][c] = 0.0f;
     for (int d = 0; d < D4; d += 4) {
@@ -86,8 +90,8 @@ __device__ __forceinline__ void rows_by_cols(const float *__restrict__ A, const 
 #pragma unroll
         for (int c = 0; c < 4; c++) bv[c] = *reinterpret_cast<const float4 *>(Bt + (lane + 32 * c) * kLd + d);
 #pragma unroll
-        for (int r = 0; r < 16; r++) {
-            const float4 av = *reinterpret_cast<const float4 *>(A + (16 * w + r) * kLd + d);
+        for (int r = 0; r < NR; r++) {
+            const float4 av = *reinterpret_cast<const float4 *>(A + (row0 + r) * kLd + d);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 acc[r][c] = fmaf(av.x, bv[c].x, acc[r][c]);
@@ -99,29 +103,58 @@ __device__ __forceinline__ void rows_by_cols(const float *__restrict__ A, const 
     }
 }
 
-// scores -> (scale) -> masked -> softmax -> dropout, in place, up to `stage`; columns >= S hold 0
-// after the softmax (and are skipped by its reductions), rows >= L are left as they are
-template <int M>
-__device__ __forceinline__ void chain_forward(const nck_attn &a, int64_t b, int stage, float (&v)[16][4]) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+// the dropout keep bits of columns lane + 32 c of row i (bit c of the result)
+__device__ __forceinline__ uint32_t keep_bits(const nck_attn &a, int64_t b, int i) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (b * a.L + i) * a.S;
+    uint32_t k = 0;
+    if ((a.S & 127) == 0 && ((uintptr_t)a.bits & 15) == 0) {  // the row's first four words, one load
+        const uint4 w4 = __ldg(reinterpret_cast<const uint4 *>(a.bits + (row >> 5)));
+        k = ((w4.x >> lane) & 1u) | (((w4.y >> lane) & 1u) << 1) | (((w4.z >> lane) & 1u) << 2) |
+            (((w4.w >> lane) & 1u) << 3);
+        return k;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const int64_t e = row + lane + 32 * c;
+        if (lane + 32 * c < a.S) k |= ((__ldg(a.bits + (e >> 5)) >> (e & 31)) & 1u) << c;
+    }
+    return k;
+}
+
+// the mask of columns lane + 32 c of row i (bit c set: masked)
+__device__ __forceinline__ uint32_t mask_bits(const nck_attn &a, int64_t b, int i) {
+    const int lane = threadIdx.x & 31;
+    const int32_t *mr = a.mask + b * a.ms[0] + i * a.ms[1];
+    uint32_t m = 0;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const int j = lane + 32 * c;
+        if (j < a.S && __ldg(mr + j * a.ms[2]) != 0) m |= 1u << c;
+    }
+    return m;
+}
+
+// scores -> (scale) -> masked -> softmax -> dropout, in place, up to `stage`, for rows row0 ..
+// row0 + NR - 1; columns >= S hold 0 after the softmax (and are skipped by its reductions), rows >= L
+// are left as they are
+template <int M, int NR>
+__device__ __forceinline__ void chain_forward(const nck_attn &a, int64_t b, int stage, int row0, float (&v)[NR][4]) {
+    const int lane = threadIdx.x & 31;
     const int L = (int)a.L, S = (int)a.S;
     if (stage >= NCK_ATT_MASKED && a.mask) {
-        const int32_t *mb = a.mask + b * a.ms[0];
 #pragma unroll
-        for (int r = 0; r < 16; r++) {
-            const int i = 16 * w + r;
-            if (i >= L) continue;
+        for (int r = 0; r < NR; r++) {
+            if (row0 + r >= L) continue;
+            const uint32_t m = mask_bits(a, b, row0 + r);
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int j = lane + 32 * c;
-                if (j < S && __ldg(mb + i * a.ms[1] + j * a.ms[2]) != 0) v[r][c] = a.fill;
-            }
+            for (int c = 0; c < 4; c++)
+                if ((m >> c) & 1u) v[r][c] = a.fill;
         }
     }
     if (stage < NCK_ATT_SOFTMAX) return;
-    const float keepv = a.p < 1.0f ? 1.0f / (1.0f - a.p) : 0.0f;
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
+    for (int r = 0; r < NR; r++) {
         float m = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; c++)
@@ -140,44 +173,42 @@ __device__ __forceinline__ void chain_forward(const nck_attn &a, int64_t b, int 
         for (int c = 0; c < 4; c++) v[r][c] = lane + 32 * c < S ? inv * v[r][c] : 0.0f;
     }
     if (stage < NCK_ATT_DROPOUT || !a.bits) return;
+    const float keepv = a.p < 1.0f ? 1.0f / (1.0f - a.p) : 0.0f;
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const int i = 16 * w + r;
-        if (i >= L) continue;
-        const int64_t row = (b * a.L + i) * a.S;
+    for (int r = 0; r < NR; r++) {
+        if (row0 + r >= L) continue;
+        const uint32_t k = keep_bits(a, b, row0 + r);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int j = lane + 32 * c;
-            if (j < S) {
-                const int64_t e = row + j;
-                v[r][c] *= (__ldg(a.bits + (e >> 5)) >> (e & 31)) & 1u ? keepv : 0.0f;
-            }
-        }
+        for (int c = 0; c < 4; c++)
+            if (lane + 32 * c < S) v[r][c] *= (k >> c) & 1u ? keepv : 0.0f;
     }
 }
 
-// the scores of head b (scaled when the chain scales them) into v; Q and K already staged
-__device__ __forceinline__ void scores(const nck_attn &a, const float *Qs, const float *Ks, float (&v)[16][4]) {
-    rows_by_cols(Qs, Ks, ((int)a.D + 3) & ~3, v);
+// the scores of rows row0 .. into v (scaled when the chain scales them); Q and K already staged
+template <int NR>
+__device__ __forceinline__ void scores(const nck_attn &a, const float *Qs, const float *Ks, int row0,
+                                       float (&v)[NR][4]) {
+    rows_by_cols<NR>(Qs, Ks, ((int)a.D + 3) & ~3, row0, v);
     if (a.scaled)
 #pragma unroll
-        for (int r = 0; r < 16; r++)
+        for (int r = 0; r < NR; r++)
 #pragma unroll
             for (int c = 0; c < 4; c++) v[r][c] = a.scale * v[r][c];
 }
 
-// out[16 w + r][lane] = sum_j P[16 w + r][j] X[j][lane], j ascending (P pitch kLp, X pitch kLd)
+// acc[r] = sum_j P[row0 + r][j] X[j][lane], j ascending (P pitch kLp, X pitch kLd)
+template <int NR>
 __device__ __forceinline__ void rows_times_tile(const float *__restrict__ P, const float *__restrict__ X, int S4,
-                                                float (&acc)[16]) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+                                                int row0, float (&acc)[NR]) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int r = 0; r < 16; r++) acc[r] = 0.0f;
+    for (int r = 0; r < NR; r++) acc[r] = 0.0f;
     for (int j = 0; j < S4; j += 4) {
         const float x0 = X[(j + 0) * kLd + lane], x1 = X[(j + 1) * kLd + lane];
         const float x2 = X[(j + 2) * kLd + lane], x3 = X[(j + 3) * kLd + lane];
 #pragma unroll
-        for (int r = 0; r < 16; r++) {
-            const float4 pv = *reinterpret_cast<const float4 *>(P + (16 * w + r) * kLp + j);
+        for (int r = 0; r < NR; r++) {
+            const float4 pv = *reinterpret_cast<const float4 *>(P + (row0 + r) * kLp + j);
             acc[r] = fmaf(pv.x, x0, acc[r]);
             acc[r] = fmaf(pv.y, x1, acc[r]);
             acc[r] = fmaf(pv.z, x2, acc[r]);
@@ -186,17 +217,18 @@ __device__ __forceinline__ void rows_times_tile(const float *__restrict__ P, con
     }
 }
 
-// out[16 w + r][lane] = sum_i P[i][16 w + r] X[i][lane], i ascending: the transposed product
+// acc[r] = sum_i P[i][col0 + r] X[i][lane], i ascending: the transposed product
+template <int NR>
 __device__ __forceinline__ void cols_times_tile(const float *__restrict__ P, const float *__restrict__ X, int L,
-                                                float (&acc)[16]) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+                                                int col0, float (&acc)[NR]) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int r = 0; r < 16; r++) acc[r] = 0.0f;
+    for (int r = 0; r < NR; r++) acc[r] = 0.0f;
     for (int i = 0; i < L; i++) {
         const float x = X[i * kLd + lane];
-        const float4 *pr = reinterpret_cast<const float4 *>(P + i * kLp + 16 * w);
+        const float4 *pr = reinterpret_cast<const float4 *>(P + i * kLp + col0);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
+        for (int q = 0; q < NR / 4; q++) {
             const float4 pv = pr[q];
             acc[4 * q + 0] = fmaf(pv.x, x, acc[4 * q + 0]);
             acc[4 * q + 1] = fmaf(pv.y, x, acc[4 * q + 1]);
@@ -206,42 +238,31 @@ __device__ __forceinline__ void cols_times_tile(const float *__restrict__ P, con
     }
 }
 
-// the rows of v into a [128 x 128] tile (columns >= S as 0)
-__device__ __forceinline__ void store_rows(float *__restrict__ P, const float (&v)[16][4], int S) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-    for (int r = 0; r < 16; r++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int j = lane + 32 * c;
-            P[(16 * w + r) * kLp + j] = j < S ? v[r][c] : 0.0f;
-        }
-}
-
 template <int M>
 __global__ void __launch_bounds__(kAT, 1) k_attn_fwd(const nck_attn a, float *__restrict__ o) {
     extern __shared__ float4 smem4[];
     float *Qs = reinterpret_cast<float *>(smem4), *Ks = Qs + kTile, *Vs = Ks + kTile, *Ps = Vs + kTile;
     const int64_t b = blockIdx.x;
     const int L = (int)a.L, S = (int)a.S;
+    const int lane = threadIdx.x & 31, row0 = kRW * (threadIdx.x >> 5);
     load_tile(Qs, a.q, a.qs, b, L, (int)a.D);
     load_tile(Ks, a.k, a.ks, b, S, (int)a.D);
     load_tile(Vs, a.v, a.vs, b, S, (int)a.Dv);
     __syncthreads();
-    float v[16][4];
-    scores(a, Qs, Ks, v);
-    chain_forward<M>(a, b, a.stage, v);
-    store_rows(Ps, v, S);
-    __syncthreads();
-    float acc[16];
-    rows_times_tile(Ps, Vs, (S + 3) & ~3, acc);
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float v[kRW][4];
+    scores<kRW>(a, Qs, Ks, row0, v);
+    chain_forward<M, kRW>(a, b, a.stage, row0, v);
+#pragma unroll
+    for (int r = 0; r < kRW; r++)  // the warp's own rows: only it reads them back
+#pragma unroll
+        for (int c = 0; c < 4; c++) Ps[(row0 + r) * kLp + lane + 32 * c] = lane + 32 * c < S ? v[r][c] : 0.0f;
+    __syncwarp();
+    float acc[kRW];
+    rows_times_tile<kRW>(Ps, Vs, (S + 3) & ~3, row0, acc);
     if (lane < a.Dv)
 #pragma unroll
-        for (int r = 0; r < 16; r++) {
-            const int i = 16 * w + r;
-            if (i < L) o[(b * a.L + i) * a.Dv + lane] = acc[r];
-        }
+        for (int r = 0; r < kRW; r++)
+            if (row0 + r < L) o[(b * a.L + row0 + r) * a.Dv + lane] = acc[r];
 }
 
 template <int M>
@@ -250,21 +271,20 @@ __global__ void __launch_bounds__(kAT, 1) k_attn_probs(const nck_attn a, float *
     float *Qs = reinterpret_cast<float *>(smem4), *Ks = Qs + kTile;
     const int64_t b = blockIdx.x;
     const int L = (int)a.L, S = (int)a.S;
+    const int lane = threadIdx.x & 31, row0 = kRW * (threadIdx.x >> 5);
     load_tile(Qs, a.q, a.qs, b, L, (int)a.D);
     load_tile(Ks, a.k, a.ks, b, S, (int)a.D);
     __syncthreads();
-    float v[16][4];
-    scores(a, Qs, Ks, v);
-    chain_forward<M>(a, b, a.stage, v);
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float v[kRW][4];
+    scores<kRW>(a, Qs, Ks, row0, v);
+    chain_forward<M, kRW>(a, b, a.stage, row0, v);
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const int i = 16 * w + r;
-        if (i >= L) continue;
+    for (int r = 0; r < kRW; r++) {
+        if (row0 + r >= L) continue;
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             const int j = lane + 32 * c;
-            if (j < S) out[(b * a.L + i) * a.S + j] = v[r][c];
+            if (j < S) out[(b * a.L + row0 + r) * a.S + j] = v[r][c];
         }
     }
 }
@@ -280,7 +300,7 @@ __global__ void __launch_bounds__(kAT, 1) k_attn_bwd(const nck_attn a, const flo
     float *Ps = Gs + kTile, *Ds = Ps + kPTile;
     const int64_t b = blockIdx.x;
     const int L = (int)a.L, S = (int)a.S, D = (int)a.D, Dv = (int)a.Dv;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, row0 = kRW * w;
     const int64_t gs[3] = {a.L * a.Dv, a.Dv, 1};
     load_tile(Qs, a.q, a.qs, b, L, D);
     load_tile(Ks, a.k, a.ks, b, S, D);
@@ -288,73 +308,77 @@ __global__ void __launch_bounds__(kAT, 1) k_attn_bwd(const nck_attn a, const flo
     load_tile(Gs, dout, gs, b, L, Dv);
     __syncthreads();
 
-    // probabilities y (after the softmax) and the gradient reaching them through the dropout
-    float y[16][4], g[16][4];
-    scores(a, Qs, Ks, y);
-    chain_forward<M>(a, b, NCK_ATT_SOFTMAX, y);
-    rows_by_cols(Gs, Vs, (Dv + 3) & ~3, g);  // dO V^T: the gradient of the dropped probabilities
-    const bool drop = a.stage >= NCK_ATT_DROPOUT && a.bits;
-    const float keepv = a.p < 1.0f ? 1.0f / (1.0f - a.p) : 0.0f;
+    {  // probabilities y (after the softmax), the gradient reaching them through the dropout, dS
+        float y[kRW][4], g[kRW][4];
+        scores<kRW>(a, Qs, Ks, row0, y);
+        chain_forward<M, kRW>(a, b, NCK_ATT_SOFTMAX, row0, y);
+        rows_by_cols<kRW>(Gs, Vs, (Dv + 3) & ~3, row0, g);  // dO V^T: the gradient of the dropped probabilities
+        const bool drop = a.stage >= NCK_ATT_DROPOUT && a.bits;
+        const float keepv = a.p < 1.0f ? 1.0f / (1.0f - a.p) : 0.0f;
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const int i = 16 * w + r;
-        const int64_t row = (b * a.L + i) * a.S;
-        float dot = 0.0f;
+        for (int r = 0; r < kRW; r++) {
+            const int i = row0 + r;
+            const uint32_t kb = drop && i < L ? keep_bits(a, b, i) : 0xFu;
+            const uint32_t mb = a.mask && i < L ? mask_bits(a, b, i) : 0u;
+            float dot = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int j = lane + 32 * c;
-            float pd = y[r][c];
-            if (drop && i < L && j < S) {
-                const int64_t e = row + j;
-                const float mk = (__ldg(a.bits + (e >> 5)) >> (e & 31)) & 1u ? keepv : 0.0f;
-                pd = y[r][c] * mk;
-                g[r][c] = 0.0f + g[r][c] * mk;  // dropout backward into a fresh gradient
+            for (int c = 0; c < 4; c++) {
+                const int j = lane + 32 * c;
+                float pd = y[r][c];
+                if (drop) {
+                    const float mk = (kb >> c) & 1u ? keepv : 0.0f;
+                    pd = y[r][c] * mk;
+                    g[r][c] = 0.0f + g[r][c] * mk;  // dropout backward into a fresh gradient
+                }
+                Ps[i * kLp + j] = j < S && i < L ? pd : 0.0f;
+                if (j < S) dot += g[r][c] * y[r][c];
             }
-            Ps[i * kLp + j] = j < S && i < L ? pd : 0.0f;
-            if (j < S) dot += g[r][c] * y[r][c];
-        }
-        dot = wsum(dot);
+            dot = wsum(dot);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int j = lane + 32 * c;
-            float ds = j < S && i < L ? 0.0f + y[r][c] * (g[r][c] - dot) : 0.0f;
-            if (a.mask && i < L && j < S && __ldg(a.mask + b * a.ms[0] + i * a.ms[1] + j * a.ms[2]) != 0) ds = 0.0f;
-            Ds[i * kLp + j] = a.scaled ? a.scale * ds : ds;  // through the scale's backward
+            for (int c = 0; c < 4; c++) {
+                const int j = lane + 32 * c;
+                float ds = j < S && i < L && !((mb >> c) & 1u) ? 0.0f + y[r][c] * (g[r][c] - dot) : 0.0f;
+                Ds[i * kLp + j] = a.scaled ? a.scale * ds : ds;  // through the scale's backward
+            }
         }
     }
     __syncthreads();
 
+    // dV = P_drop^T dO on warps 0-7 and dK = dS^T Q on warps 8-15, 16 output rows per warp
+    const int half = w >> 3, col0 = 16 * (w & 7);
     float acc[16];
-    if (dv) {  // dV = P_drop^T dO
-        cols_times_tile(Ps, Gs, L, acc);
+    if (half == 0 && dv) {
+        cols_times_tile<16>(Ps, Gs, L, col0, acc);
         if (lane < Dv)
 #pragma unroll
             for (int r = 0; r < 16; r++) {
-                const int j = 16 * w + r;
+                const int j = col0 + r;
                 if (j < S) {
                     float *p = dv + (b * a.S + j) * a.Dv + lane;
                     *p = acc_v ? *p + acc[r] : acc[r];
                 }
             }
     }
+    if (half == 1 && dkt) cols_times_tile<16>(Ds, Qs, L, col0, acc);
     if (dq) {  // dQ = dS K
-        rows_times_tile(Ds, Ks, (S + 3) & ~3, acc);
+        float aq[kRW];
+        rows_times_tile<kRW>(Ds, Ks, (S + 3) & ~3, row0, aq);
         if (lane < D)
 #pragma unroll
-            for (int r = 0; r < 16; r++) {
-                const int i = 16 * w + r;
+            for (int r = 0; r < kRW; r++) {
+                const int i = row0 + r;
                 if (i < L) {
                     float *p = dq + (b * a.L + i) * a.D + lane;
-                    *p = acc_q ? *p + acc[r] : acc[r];
+                    *p = acc_q ? *p + aq[r] : aq[r];
                 }
             }
     }
-    if (dkt) {  // dK = dS^T Q, written as K^T [D, S] through a transposed staging tile
-        cols_times_tile(Ds, Qs, L, acc);
+    if (dkt) {  // dK written as K^T [D, S] through a transposed staging tile
         __syncthreads();  // every warp is done with Ps (dV) before it is reused
         float *T = Ps;
+        if (half == 1)
 #pragma unroll
-        for (int r = 0; r < 16; r++) T[lane * kLt + 16 * w + r] = acc[r];
+            for (int r = 0; r < 16; r++) T[lane * kLt + col0 + r] = acc[r];
         __syncthreads();
         for (int idx = threadIdx.x; idx < D * S; idx += kAT) {
             const int dd = idx / S, j = idx - dd * S;

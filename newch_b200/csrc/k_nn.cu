@@ -12,6 +12,7 @@
 #include "k_math.cuh"
 
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/nc_ext.h"
 
@@ -903,8 +904,9 @@ __global__ void __launch_bounds__(256) k_bn_act_pool2x2(const float *__restrict_
                                                         const float *__restrict__ b, const float *__restrict__ mean,
                                                         const float *__restrict__ invstd, int act, float act_s,
                                                         float *__restrict__ y, int32_t *__restrict__ arg,
-                                                        uint32_t planes, uint32_t C, uint32_t W, uint32_t OH,
-                                                        uint32_t OW, FastDiv dow, FastDiv doh, FastDiv dc) {
+                                                        float *__restrict__ xarg, uint32_t planes, uint32_t C,
+                                                        uint32_t W, uint32_t OH, uint32_t OW, FastDiv dow,
+                                                        FastDiv doh, FastDiv dc) {
     const uint32_t total = planes * OH * OW;
     for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
         const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
@@ -917,13 +919,14 @@ __global__ void __launch_bounds__(256) k_bn_act_pool2x2(const float *__restrict_
         const float v0 = epi_fwd(act, act_s, p.x * a + dd), v1 = epi_fwd(act, act_s, p.y * a + dd);
         const float v2 = epi_fwd(act, act_s, q.x * a + dd), v3 = epi_fwd(act, act_s, q.y * a + dd);
         const int32_t i0 = (int32_t)(2 * oy * W + 2 * ox);
-        float best = v0;
+        float best = v0, bx = p.x;
         int32_t bi = i0;
-        if (v1 > best) best = v1, bi = i0 + 1;
-        if (v2 > best) best = v2, bi = i0 + (int32_t)W;
-        if (v3 > best) best = v3, bi = i0 + (int32_t)W + 1;
+        if (v1 > best) best = v1, bi = i0 + 1, bx = p.y;
+        if (v2 > best) best = v2, bi = i0 + (int32_t)W, bx = q.x;
+        if (v3 > best) best = v3, bi = i0 + (int32_t)W + 1, bx = q.y;
         y[t] = best;
         arg[t] = bi;
+        if (xarg) xarg[t] = bx;
     }
 }
 
@@ -932,13 +935,13 @@ extern "C" int nck_bn_pool2x2_ok(int64_t N, int64_t C, int64_t H, int64_t W) {
 }
 
 extern "C" void nck_bn_act_pool2x2(nck_dev *d, const float *x, const float *w, const float *b, const float *mean,
-                                   const float *invstd, int act, float act_s, float *y, int32_t *arg, int64_t N,
-                                   int64_t C, int64_t H, int64_t W) {
+                                   const float *invstd, int act, float act_s, float *y, int32_t *arg, float *xarg,
+                                   int64_t N, int64_t C, int64_t H, int64_t W) {
     const int64_t planes = N * C, OH = H / 2, OW = W / 2, total = planes * OH * OW;
     if (total <= 0) return;
-    Scope sc(d, "bn_act_pool", 0.0, 4.0 * planes * H * W + 8.0 * total);
+    Scope sc(d, "bn_act_pool", 0.0, 4.0 * planes * H * W + (xarg ? 12.0 : 8.0) * total);
     k_bn_act_pool2x2<<<grid_for(d, total), 256, 0, NCK_STREAM(d)>>>(
-        x, w, b, mean, invstd, act, act_s, y, arg, (uint32_t)planes, (uint32_t)C, (uint32_t)W, (uint32_t)OH,
+        x, w, b, mean, invstd, act, act_s, y, arg, xarg, (uint32_t)planes, (uint32_t)C, (uint32_t)W, (uint32_t)OH,
         (uint32_t)OW, make_fastdiv((uint32_t)OW), make_fastdiv((uint32_t)OH), make_fastdiv((uint32_t)C));
     NCK_LAUNCHED(d, 1);
 }
@@ -1201,6 +1204,60 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_sums(const float *__restric
     if (last_block_done(counter)) bn_bwd_finalize(part, C, N * HW, fin);
 }
 
+// The sums from the forward's x at the argmax (xarg, pooled layout): two contiguous streams per plane,
+// V-wide loads, the same per-element terms as the gathering kernel above.
+template <int V>
+__global__ void __launch_bounds__(256) k_bn_pool_bwd_sums_x(const float *__restrict__ xarg,
+                                                            const float *__restrict__ gp,
+                                                            const float *__restrict__ w, const float *__restrict__ b,
+                                                            const float *__restrict__ mean,
+                                                            const float *__restrict__ invstd, int act, float act_s,
+                                                            double *__restrict__ part, int64_t N, int64_t C,
+                                                            int64_t L, int64_t per_split, BnBwdFin fin,
+                                                            unsigned *counter) {
+    using VT = typename std::conditional<V == 4, float4, float>::type;
+    __shared__ double sm[64];
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const float mu = mean[c], is = invstd[c], ea = w[c] * is, ed = b[c] - mu * ea;
+    double g0 = 0.0, h0 = 0.0, g1 = 0.0, h1 = 0.0;
+    ChanWalk wk;
+    const int SV = (int)(L / V);
+    wk.init(SV, n1 > n0 ? n1 - n0 : 0);
+    const int64_t pbase = n0 * C + c;
+    while (wk.live()) {
+        VT gv[2], xv[2];
+        bool on[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            on[j] = wk.live();
+            if (on[j]) {
+                const int64_t off = (pbase + (int64_t)wk.na * C) * SV + wk.ia;
+                gv[j] = __ldg(reinterpret_cast<const VT *>(gp) + off);
+                xv[j] = __ldg(reinterpret_cast<const VT *>(xarg) + off);
+            }
+            wk.next();
+        }
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            if (!on[j]) continue;
+            const float *ge = reinterpret_cast<const float *>(&gv[j]), *xe = reinterpret_cast<const float *>(&xv[j]);
+#pragma unroll
+            for (int e = 0; e < V; e++) {
+                const float g = epi_grad(act, act_s, xe[e] * ea + ed, ge[e]);
+                if (e & 1) g1 += g, h1 += g * (xe[e] - mu) * is;
+                else g0 += g, h0 += g * (xe[e] - mu) * is;
+            }
+        }
+    }
+    double sg = g0 + g1, sgx = h0 + h1;
+    block_sum2(sg, sgx, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = sg;
+        part[(blockIdx.y * C + c) * 2 + 1] = sgx;
+    }
+    if (last_block_done(counter)) bn_bwd_finalize(part, C, N * L * 4, fin);
+}
+
 __global__ void __launch_bounds__(256) k_bn_pool_bwd_dx(const float *__restrict__ x, const float *__restrict__ gp,
                                                         const int32_t *__restrict__ arg, const float *__restrict__ w,
                                                         const float *__restrict__ b, const float *__restrict__ mean,
@@ -1242,21 +1299,31 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_dx(const float *__restrict_
 }
 
 extern "C" void nck_bn_pool_bwd(nck_dev *d, const float *x, const float *w, const float *b, const float *gpool,
-                                const int32_t *arg, const float *mean, const float *invstd, float *gx, float *gw,
-                                float *gb, int64_t N, int64_t C, int64_t H, int64_t W, int acc_gx, int act,
-                                float act_s) {
+                                const int32_t *arg, const float *xarg, const float *mean, const float *invstd,
+                                float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t H, int64_t W,
+                                int acc_gx, int act, float act_s) {
     const int64_t HW = H * W, OH = H / 2, OW = W / 2, L = OH * OW;
     Scope sc(d, "bn_pool_bwd", 0.0, 4.0 * N * C * (HW + 2 * L) + (gx ? (acc_gx ? 8.0 : 4.0) * N * C * HW : 0.0));
-    static int res = 0;
+    static int res = 0, res4 = 0, res1 = 0;
     if (!res) res = resident_blocks(d, k_bn_pool_bwd_sums, kThreads);
-    int64_t splits = bn_splits(res, N, C, L), per = (N + splits - 1) / splits;
+    if (!res4) res4 = resident_blocks(d, k_bn_pool_bwd_sums_x<4>, kThreads);
+    if (!res1) res1 = resident_blocks(d, k_bn_pool_bwd_sums_x<1>, kThreads);
+    const bool v4 = xarg && L % 4 == 0 && (((uintptr_t)xarg | (uintptr_t)gpool) & 15) == 0;
+    int64_t splits = bn_splits(xarg ? (v4 ? res4 : res1) : res, N, C, L), per = (N + splits - 1) / splits;
     splits = (N + per - 1) / per;
     double *part = (double *)d->scratch;
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     const BnBwdFin fin = {gw, gb, coef, (int)splits};
     dim3 g1((unsigned)C, (unsigned)splits);
-    k_bn_pool_bwd_sums<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, gpool, arg, w, b, mean, invstd, act, act_s, part, N, C, HW,
-                                                          L, per, fin, d->counters);
+    if (v4)
+        k_bn_pool_bwd_sums_x<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(xarg, gpool, w, b, mean, invstd, act, act_s, part, N,
+                                                                   C, L, per, fin, d->counters);
+    else if (xarg)
+        k_bn_pool_bwd_sums_x<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(xarg, gpool, w, b, mean, invstd, act, act_s, part, N,
+                                                                   C, L, per, fin, d->counters);
+    else
+        k_bn_pool_bwd_sums<<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, gpool, arg, w, b, mean, invstd, act, act_s, part, N, C,
+                                                              HW, L, per, fin, d->counters);
     int launched = 1;
     if (gx) {
         const int64_t total = N * C * L;

@@ -372,6 +372,8 @@ int nc__attn_dropout(nc_node *n, const uint32_t *bits);
  * for NC_CHAIN_MAX) with the chain's other nodes (whose own backward must not run) and returns their
  * count, else 0. */
 #define NC_CHAIN_MAX 6
+/* x at each window's argmax when a max pool ran over a BatchNorm recipe (ops_conv.c), else NULL */
+const float *nc__pool_xarg(const nc_node *n);
 int nc__fused_backward(nc_ctx *ctx, nc_node *n, nc_node **consumed);
 /* the values of n's output and inputs, for a backward that reads them: pending recipes computed */
 void nc__backward_inputs(nc_node *n);

@@ -201,19 +201,22 @@ void nck_bn_stats_train(nck_dev *d, const float *x, float *mean, float *invstd, 
 /* y = act(x * w * invstd + (b - mean * w * invstd)) per channel; act = NCK_UN_* kind or -1 (none) */
 void nck_bn_apply(nck_dev *d, const float *x, const float *w, const float *b, const float *mean, const float *invstd,
                   float *y, int64_t N, int64_t C, int64_t S, int act, float act_s);
-/* BatchNorm (given statistics) + activation + 2 x 2 / stride 2 max pooling in one pass (even H, W) */
+/* BatchNorm (given statistics) + activation + 2 x 2 / stride 2 max pooling in one pass (even H, W);
+ * xarg (may be NULL) receives x at each window's argmax, for the fused backward's sums */
 int nck_bn_pool2x2_ok(int64_t N, int64_t C, int64_t H, int64_t W);
 void nck_bn_act_pool2x2(nck_dev *d, const float *x, const float *w, const float *b, const float *mean,
-                        const float *invstd, int act, float act_s, float *y, int32_t *arg, int64_t N, int64_t C,
-                        int64_t H, int64_t W);
+                        const float *invstd, int act, float act_s, float *y, int32_t *arg, float *xarg, int64_t N,
+                        int64_t C, int64_t H, int64_t W);
 /* backward of act(BatchNorm(x)) given the activation output's gradient g (act < 0: plain BatchNorm) */
 void nck_bn_bwd_ex(nck_dev *d, const float *x, const float *w, const float *b, const float *g, const float *mean,
                    const float *invstd, float *gx, float *gw, float *gb, int64_t N, int64_t C, int64_t S, int training,
                    int acc_gx, int act, float act_s);
-/* backward of max_pool2x2(act(BatchNorm(x))) given the pooled gradient and argmax (training) */
+/* backward of max_pool2x2(act(BatchNorm(x))) given the pooled gradient and argmax (training); xarg:
+ * the forward's x at the argmax (NULL: gathered from x) */
 void nck_bn_pool_bwd(nck_dev *d, const float *x, const float *w, const float *b, const float *gpool,
-                     const int32_t *arg, const float *mean, const float *invstd, float *gx, float *gw, float *gb,
-                     int64_t N, int64_t C, int64_t H, int64_t W, int acc_gx, int act, float act_s);
+                     const int32_t *arg, const float *xarg, const float *mean, const float *invstd, float *gx,
+                     float *gw, float *gb, int64_t N, int64_t C, int64_t H, int64_t W, int acc_gx, int act,
+                     float act_s);
 void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *mean,
                       float *invstd, float *rm, float *rv, int64_t N, int64_t C, int64_t S, float mom, float eps,
                       int stage);

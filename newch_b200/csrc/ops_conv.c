@@ -362,15 +362,29 @@ static nc_status pool_infer(nc_node *n, nc_dtype *dt, int *nd, int64_t *shape) {
 
 /* 2 x 2 / stride 2 max pooling straight from the pending recipe of its input (BatchNorm and maybe
  * an activation, fusion.c): returns 1 when it did the pooling */
-static int pool_from_recipe(nc_node *n, int32_t *arg) {
+/* 2 x 2 / stride 2 max pooling of a pending BatchNorm (+ activation) output, straight from its input:
+ * the saved buffer holds the argmax and, after it, the input value there (for the fused backward) */
+static int pool_from_recipe(nc_node *n) {
     nc_tensor *x = n->in[0];
     const nc_deferred *d = nc__deferred_of(x);
     const int64_t *p = n->p.i;
-    if (!d || x->ndim != 4 || p[0] != 2 || p[1] != 2 || p[2] != 0 || p[3] != 0 || p[4] != 2 || p[5] != 2) return 0;
+    if (!d || d->kind != NC_DEF_BN || x->ndim != 4 || p[0] != 2 || p[1] != 2 || p[2] != 0 || p[3] != 0 || p[4] != 2 ||
+        p[5] != 2)
+        return 0;
     if (!nck_bn_pool2x2_ok(x->shape[0], x->shape[1], x->shape[2], x->shape[3])) return 0;
+    const int64_t L = nc_numel(n->out);
+    int32_t *arg = (int32_t *)nc__arena_alloc(x->ctx, (size_t)L * (sizeof(int32_t) + sizeof(float)));
+    if (!arg) return 0;
+    n->saved = arg;
     nck_bn_act_pool2x2(nc__k(x->ctx), d->x, d->w, d->b, d->mean, d->invstd, d->act, d->act_s, (float *)n->out->data,
-                       arg, x->shape[0], x->shape[1], x->shape[2], x->shape[3]);
+                       arg, (float *)(arg + L), x->shape[0], x->shape[1], x->shape[2], x->shape[3]);
     return 1;
+}
+
+const float *nc__pool_xarg(const nc_node *n) {
+    return n->op == &nc_op_max_pool2d && n->saved && n->p.i[6] == 1 ? (const float *)((const int32_t *)n->saved +
+                                                                                       nc_numel(n->out))
+                                                                    : NULL;
 }
 
 static nc_status pool_fwd(nc_node *n) {
@@ -379,10 +393,13 @@ static nc_status pool_fwd(nc_node *n) {
     int is_max = n->op->kind == POOL_MAX;
     int32_t *arg = NULL;
     if (is_max) {
+        if (nc_numel(n->out) && pool_from_recipe(n)) {
+            n->p.i[6] = 1; /* saved: argmax, then x there */
+            return NC_OK;
+        }
         arg = (int32_t *)nc__arena_alloc(x->ctx, (size_t)nc_numel(n->out) * sizeof(int32_t));
         if (!arg) return NC_ERR_OOM;
         n->saved = arg;
-        if (nc_numel(n->out) && pool_from_recipe(n, arg)) return NC_OK;
     }
     const float *X = nc__contig_f32(x);
     if (!X) return NC_ERR_OOM;

@@ -22,8 +22,8 @@ OUT = HERE / "ref_state.ncw"
 
 
 def ncw1_tensors():
-    """(name, array) pairs of the file: float32 of several ranks, int32, int8, uint8, a scalar and an
-    empty tensor."""
+    """(name, array) pairs of the file: float32 of several ranks, int32, int8, uint8, a one-element and
+    an empty tensor."""
     return [
         ("fc1.weight", seeded(9000, (6, 10))),
         ("fc1.bias", seeded(9001, (6,))),
@@ -31,7 +31,7 @@ def ncw1_tensors():
         ("steps", np.array([3, -7, 2**31 - 1], np.int32)),
         ("qweight", np.array([-127, 0, 5, 127, -1], np.int8)),
         ("bytes", np.arange(0, 250, 25, dtype=np.uint8)),
-        ("scalar", np.array(2.5, np.float32)),
+        ("scalar", np.array([2.5], np.float32)),
         ("empty", np.zeros((0, 4), np.float32)),
     ]
 
