@@ -279,8 +279,8 @@ int nc__is_persistent_mode(const nc_ctx *ctx) { return ctx->persistent_depth > 0
 
 /* ---- host <-> device copies ------------------------------------------------------------------- */
 
-#define NC_STAGE_BYTES ((size_t)8 << 20)
-#define NC_STAGE_SLOTS 8
+#define NC_STAGE_BYTES ((size_t)16 << 20)
+#define NC_STAGE_SLOTS 32
 
 void nc__upload(nc_ctx *ctx, void *dst, const void *src, size_t bytes) {
     if (!bytes || !ctx->device_ok) return;

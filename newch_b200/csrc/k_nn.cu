@@ -627,11 +627,18 @@ extern "C" const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t c
 }
 
 extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits,
-                                int64_t n, float p, const void *polys) {
+                                int64_t n, float p, const void *polys, const void *host_tabs) {
     if (n <= 0) return;
     Scope sc(d, y ? "dropout" : "dropout_mask", 0.0, (y ? 8.0 * n : 0.0) + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
+    if (polys && host_tabs) {
+        k_dropout_fwd_poly<<<(unsigned)blocks, kDropPolyThreads, 0, NCK_STREAM(d)>>>(
+            reinterpret_cast<const ulonglong4 *>(host_tabs), reinterpret_cast<const ulonglong4 *>(polys), x, y, bits,
+            n, p);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     if (polys) {
         // base states T^(64 j) s0, j < 4: 64, 128 and 192 transitions of the host's copy
         uint64_t st[4] = {state[0], state[1], state[2], state[3]};
@@ -1414,7 +1421,7 @@ __global__ void __launch_bounds__(256) k_ln_fwd_reg(const float *__restrict__ x,
 
 // Backward with the row in registers: dx in one read of x and g, and the weight / bias column sums
 // of the block's rows (lane-private running sums, then a fixed tree over the block's warps) as one
-// partial per block, combined in order by k_ln_bwd_wb_combine.
+// partial per block, combined in a fixed order by nck_combine_cols.
 template <int NV>
 __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float *__restrict__ x, const float *__restrict__ w,
                                                     const float *__restrict__ g, const float *__restrict__ stats,
@@ -1557,6 +1564,14 @@ __global__ void k_ln_bwd_wb_combine(const float *__restrict__ part, int splits, 
     }
 }
 
+// the weight / bias sums from the per-split partials (split k: D weight sums, then D bias sums); a
+// missing output is skipped by summing only the half that exists
+static void ln_wb_combine(nck_dev *d, const float *part, int splits, int64_t D, float *gw, float *gb) {
+    if (gw && gb) nck_combine_cols(d, part, 2 * D, splits, 2 * D, gw, D, gb);
+    else if (gw) nck_combine_cols(d, part, 2 * D, splits, D, gw, D, nullptr);
+    else if (gb) nck_combine_cols(d, part + D, 2 * D, splits, D, gb, D, nullptr);
+}
+
 extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
                            float *gw, float *gb, int64_t R, int64_t D) {
     Scope sc(d, "ln_bwd", 0.0, (gx ? 16.0 : 8.0) * R * D);
@@ -1578,11 +1593,8 @@ extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const flo
         else if (D == 512) k_ln_bwd_reg<4><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
         else k_ln_bwd_reg<8><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
         launched = 1;
-        if (want) {
-            k_ln_bwd_wb_combine<<<grid_for(d, D), kThreads, 0, NCK_STREAM(d)>>>(part, (int)blocks, D, gw, gb);
-            launched++;
-        }
         NCK_LAUNCHED(d, launched);
+        if (want) ln_wb_combine(d, part, (int)blocks, D, gw, gb);
         return;
     }
     if (gx) {
@@ -1601,8 +1613,10 @@ extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const flo
         float *part = (float *)d->scratch;
         dim3 grid((unsigned)col_blocks, (unsigned)splits), block(32, 8);
         k_ln_bwd_wb<<<grid, block, 0, NCK_STREAM(d)>>>(x, g, stats, part, R, D, per);
-        k_ln_bwd_wb_combine<<<grid_for(d, D), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, D, gw, gb);
-        launched += 2;
+        launched++;
+        NCK_LAUNCHED(d, launched);
+        ln_wb_combine(d, part, (int)splits, D, gw, gb);
+        return;
     }
     NCK_LAUNCHED(d, launched);
 }

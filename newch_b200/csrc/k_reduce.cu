@@ -246,6 +246,43 @@ __global__ void __launch_bounds__(1024) k_colsum_small(const float *__restrict__
     }
 }
 
+// Sums of `splits` partial rows (row r at part + r * ldp) per column, added to y[n] (n < n1) or
+// y2[n - n1] (n >= n1): a block of 32 warps takes 32 columns, warp w adds rows w, w + 32, ... in
+// order (loads four rows ahead), and the 32 warp sums are added in warp order. A fixed order for a
+// given split count, with a few loads in flight per warp instead of one thread walking every row.
+__global__ void __launch_bounds__(1024) k_combine_cols(const float *__restrict__ part, int64_t ldp, int splits,
+                                                       int64_t N, float *__restrict__ y, int64_t n1,
+                                                       float *__restrict__ y2) {
+    __shared__ float sm[32][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = blockIdx.x * 32 + lane;
+    float a = 0.0f;
+    if (n < N) {
+        int r = w;
+        for (; r + 96 < splits; r += 128) {
+            const float v0 = __ldcg(part + (int64_t)r * ldp + n), v1 = __ldcg(part + (int64_t)(r + 32) * ldp + n);
+            const float v2 = __ldcg(part + (int64_t)(r + 64) * ldp + n), v3 = __ldcg(part + (int64_t)(r + 96) * ldp + n);
+            a += v0, a += v1, a += v2, a += v3;
+        }
+        for (; r < splits; r += 32) a += __ldcg(part + (int64_t)r * ldp + n);
+    }
+    sm[w][lane] = a;
+    __syncthreads();
+    if (w == 0 && n < N) {
+        float s = 0.0f;
+        for (int k = 0; k < 32; k++) s += sm[k][lane];
+        if (n < n1) y[n] += s;
+        else y2[n - n1] += s;
+    }
+}
+
+extern "C" void nck_combine_cols(nck_dev *d, const float *part, int64_t ldp, int splits, int64_t N, float *y,
+                                 int64_t n1, float *y2) {
+    if (N <= 0 || splits <= 0) return;
+    k_combine_cols<<<(unsigned)((N + 31) / 32), 1024, 0, NCK_STREAM(d)>>>(part, ldp, splits, N, y, n1, y2);
+    NCK_LAUNCHED(d, 1);
+}
+
 extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N) {
     if (M <= 0 || N <= 0) return;
     Scope sc(d, "colsum");
@@ -267,8 +304,8 @@ extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M,
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)col_blocks, (unsigned)splits), block(32, kColRows);
     k_colsum_partial<<<grid, block, 0, NCK_STREAM(d)>>>(x, part, M, N, rows_per);
-    k_colsum_combine<<<grid_for(d, N), kThreads, 0, NCK_STREAM(d)>>>(part, gy, N, (int)splits);
-    NCK_LAUNCHED(d, 2);
+    NCK_LAUNCHED(d, 1);
+    nck_combine_cols(d, part, N, (int)splits, N, gy, N, nullptr);
 }
 
 // ---- sum of squares (double) ---------------------------------------------------------------------------

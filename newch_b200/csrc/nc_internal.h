@@ -209,7 +209,7 @@ struct nc_ctx {
     /* pinned staging ring for small uploads */
     unsigned char *stage;
     size_t stage_cap, stage_pos;
-    void *stage_events[8];
+    void *stage_events[32];
     int stage_slot;
 
     /* data parallel */
@@ -256,6 +256,8 @@ void nc__rng_skip(nc_ctx *ctx, uint64_t n);
 int nc__rng_device_init(nc_ctx *ctx);
 const uint64_t *nc__rng_run_polys(int64_t count);          /* x^(64 k) mod P, k < count (host) */
 const void *nc__rng_dropout_table(nc_ctx *ctx, int64_t n); /* the same on the device, or NULL */
+/* the dropout kernel's Horner window tables for the current state, on the device (32 KiB), or NULL */
+const void *nc__rng_dropout_tabs(nc_ctx *ctx);
 
 void nc__detect_cpu(nc_cpu_info *info);
 

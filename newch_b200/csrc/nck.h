@@ -119,6 +119,10 @@ void nck_masked_fill_fwd(nck_dev *d, const nck_bcast *bc, const float *x, const 
 void nck_masked_fill_bwd(nck_dev *d, const nck_bcast *bc, const float *g, const int32_t *m, float *gx);
 
 /* ---- reductions ---------------------------------------------------------------------------- */
+/* y[n] (n < n1) or y2[n - n1] (n >= n1) += sum over r < splits of part[r * ldp + n], in a fixed order
+ * (the combine step of split column reductions) */
+void nck_combine_cols(nck_dev *d, const float *part, int64_t ldp, int splits, int64_t N, float *y, int64_t n1,
+                      float *y2);
 /* x viewed as [outer, R, inner], contiguous. mean: scale = 1/R. */
 void nck_reduce_sum(nck_dev *d, const float *x, float *y, int64_t outer, int64_t R, int64_t inner, float scale);
 void nck_reduce_sum_i32(nck_dev *d, const int32_t *x, int32_t *y, int64_t outer, int64_t R, int64_t inner);
@@ -148,9 +152,10 @@ void nck_nll_fwd(nck_dev *d, const float *x, const int32_t *lab, float *loss, in
 void nck_nll_bwd(nck_dev *d, const int32_t *lab, const float *gloss, float *gi, int64_t N, int64_t C, int sum);
 /* inverted dropout with the engine's xoshiro256** stream: draw i (0-based from `state`) decides element i;
  * x = y = NULL draws the keep mask only */
-/* polys: the device table of run polynomials (nck_rng_polys) or NULL to jump by matrices */
+/* polys: the device table of run polynomials (nck_rng_polys) or NULL to jump by matrices; tabs: the
+ * launch's Horner window tables built by the host (NULL: a one-block kernel builds them first) */
 void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float *y, uint32_t *bits, int64_t n,
-                     float p, const void *polys);
+                     float p, const void *polys, const void *tabs);
 /* device copy of x^(64 k) mod P for k < count from the host table (uploaded once, grown on demand) */
 const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t count);
 void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p, int acc);

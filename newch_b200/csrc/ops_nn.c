@@ -159,7 +159,11 @@ static nc_status dropout_fwd(nc_node *n) {
     if (nc__attn_dropout_ok(n->in[0])) { /* attention probabilities: draw the mask only, extend the recipe */
         uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
         if (!bits) return NC_ERR_OOM;
-        if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, NULL, NULL, bits, N, n->p.f[0], nc__rng_dropout_table(ctx, N));
+        if (N) {
+            const void *polys = nc__rng_dropout_table(ctx, N);
+            nck_dropout_fwd(nc__k(ctx), ctx->rng, NULL, NULL, bits, N, n->p.f[0], polys,
+                            polys ? nc__rng_dropout_tabs(ctx) : NULL);
+        }
         nc__rng_skip(ctx, (uint64_t)N);
         n->saved = bits;
         if (nc__attn_dropout(n, bits)) return NC_OK;
@@ -169,8 +173,11 @@ static nc_status dropout_fwd(nc_node *n) {
     const float *x = nc__contig_f32(n->in[0]);
     uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
     if (!x || !bits) return NC_ERR_OOM;
-    if (N) nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0],
-                           nc__rng_dropout_table(ctx, N));
+    if (N) {
+        const void *polys = nc__rng_dropout_table(ctx, N);
+        nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0], polys,
+                        polys ? nc__rng_dropout_tabs(ctx) : NULL);
+    }
     nc__rng_skip(ctx, (uint64_t)N);
     n->saved = bits;
     return NC_OK;

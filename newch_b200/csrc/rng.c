@@ -257,6 +257,35 @@ const uint64_t *nc__rng_run_polys(int64_t count) {
 /* Device table of run polynomials covering n draws (runs of 64), uploaded once and grown on demand;
  * NULL when n is beyond the table's cap (2^27 draws) or the table is unavailable, and the dropout
  * kernel then jumps by matrices instead. */
+/* The Horner window tables of the polynomial dropout kernel for the context's current state, on the
+ * device: with the base states b_j = T^(64 j) s (j < 4), entry (j, w, v) is the XOR over the set
+ * bits t of v of T^(4 w + t) b_j (w, v < 16), 32 bytes each, 32 KiB in all. T^i b_j is the state
+ * 64 j + i steps past s, so 256 steps of a copy of the state give every term. Built here instead of
+ * by a one-block kernel in front of every dropout launch; the block comes from the step arena and
+ * reaches the device through the pinned staging ring. */
+const void *nc__rng_dropout_tabs(nc_ctx *ctx) {
+    uint64_t states[256][4];          /* 8 KiB */
+    uint64_t tab[4 * 16 * 16][4];     /* 32 KiB, copied into the staging ring before the return */
+    uint64_t st[4];
+    memcpy(st, ctx->rng, sizeof st);
+    for (int i = 0; i < 256; i++) {
+        memcpy(states[i], st, sizeof st);
+        step(st);
+    }
+    for (int e = 0; e < 4 * 16 * 16; e++) {
+        const int j = e >> 8, w = (e >> 4) & 15, v = e & 15;
+        uint64_t a[4] = {0, 0, 0, 0};
+        for (int t = 0; t < 4; t++)
+            if ((v >> t) & 1)
+                for (int q = 0; q < 4; q++) a[q] ^= states[64 * j + 4 * w + t][q];
+        memcpy(tab[e], a, sizeof a);
+    }
+    void *dev = nc__arena_alloc(ctx, sizeof tab);
+    if (!dev) return NULL;
+    nc__upload(ctx, dev, tab, sizeof tab);
+    return dev;
+}
+
 const void *nc__rng_dropout_table(nc_ctx *ctx, int64_t n) {
     if (n <= 0 || n > ((int64_t)1 << 27)) return NULL;
     const char *jump = getenv("NC_DROPOUT_JUMP"); /* "matrix": always the matrix-jump kernel */

@@ -6,7 +6,8 @@ into four 64-bit words r_j evaluated on the base states T^(64 j) s0 (Horner's ru
 windows on the device). This test compiles rng.c with stubs for its device calls and checks, against
 plain sequential stepping of the generator (the reference's own stream, engine/src/core/ctx.c:414-435):
 P has degree 256, q_k(T) v = T^(64 k) v for runs near the start and far into a 2^20-draw tensor, and
-the four-word split with base states gives the same state."""
+the four-word split with base states gives the same state, as do the host-built 4-bit window tables
+the kernel reads (nc__rng_dropout_tabs)."""
 
 from __future__ import annotations
 
@@ -24,6 +25,9 @@ HARNESS = r"""
 int nck_rng_tables_upload(nck_dev *d, const uint64_t *t, size_t b) { return 0; }
 const void *nck_rng_polys(nck_dev *d, const uint64_t *h, int64_t c) { return 0; }
 void nc__error(nc_ctx *ctx, nc_status st, const char *fmt, ...) {}
+static uint64_t g_arena[1024][4], g_dev[1024][4];
+void *nc__arena_alloc(nc_ctx *ctx, size_t bytes) { return bytes <= sizeof g_arena ? (void *)g_arena : 0; }
+void nc__upload(nc_ctx *ctx, void *dst, const void *src, size_t bytes) { memcpy(g_dev, src, bytes); }
 
 static void steps(uint64_t *s, long n) { for (long i = 0; i < n; i++) step(s); }
 
@@ -55,6 +59,17 @@ int main(void) {
             steps(b, 64);
         }
         if (memcmp(acc, s, sizeof acc)) { printf("FAIL split %ld\n", k); return 1; }
+        /* the host-built window tables (nc__rng_dropout_tabs) evaluated as the kernel does */
+        static nc_ctx ctx;
+        memcpy(ctx.rng, v, sizeof v);
+        if (nc__rng_dropout_tabs(&ctx) != (const void *)g_arena) { printf("FAIL tabs\n"); return 1; }
+        uint64_t w4[4] = {0, 0, 0, 0};
+        for (int j = 0; j < 4; j++)
+            for (int nn = 0; nn < 16; nn++) {
+                const uint64_t *e = g_dev[j * 256 + nn * 16 + ((q[4 * k + j] >> (4 * nn)) & 15)];
+                for (int q2 = 0; q2 < 4; q2++) w4[q2] ^= e[q2];
+            }
+        if (memcmp(w4, s, sizeof w4)) { printf("FAIL windows %ld\n", k); return 1; }
     }
     printf("OK\n");
     return 0;
