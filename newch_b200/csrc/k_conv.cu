@@ -759,6 +759,164 @@ __global__ void k_dw_dw_combine(const float *__restrict__ part, int splits, int6
     }
 }
 
+// ---- 3 x 3, stride 1, dilation 1, output rows a multiple of 4 wide: strips of four outputs -------
+// A thread takes four consecutive outputs of a row: the 3 x 6 input window they share is read once
+// (L1-cached loads, zero outside the image) instead of staged behind block barriers, and the four
+// outputs keep the per-element arithmetic of the tiled kernels above (forward: the bias, then the taps
+// row-major; input gradient: kernel rows from the last up, columns ascending), so results are the
+// same bit for bit. The weight gradient keeps one running sum per tap over the thread's strips, plane
+// by plane, its four outputs in column order.
+
+struct Strip3 {
+    uint32_t planes, OH, OW4;  // strips: planes * OH * OW4
+    FastDiv dow4, doh;
+};
+
+__device__ __forceinline__ void strip_pos(const Strip3 &g, uint32_t t, uint32_t &plane, int &oy, int &ox) {
+    const uint32_t r = g.dow4.div(t), q = t - r * g.OW4;
+    plane = g.doh.div(r);
+    oy = (int)(r - plane * g.OH), ox = (int)(4 * q);
+}
+
+// rows r0 .. r0 + 2, columns c0 .. c0 + 5 of a plane (H x W), zero outside
+__device__ __forceinline__ void window36(const float *__restrict__ p, int H, int W, int r0, int c0, float (&v)[3][6]) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const int y = r0 + i;
+        const bool rok = y >= 0 && y < H;
+#pragma unroll
+        for (int j = 0; j < 6; j++) {
+            const int x = c0 + j;
+            v[i][j] = rok && x >= 0 && x < W ? __ldg(p + (int64_t)y * W + x) : 0.0f;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_dw3_fwd(nck_conv g, Strip3 st, const float *__restrict__ x,
+                                                 const float *__restrict__ w, const float *__restrict__ b,
+                                                 float *__restrict__ y) {
+    const uint32_t total = st.planes * st.OH * st.OW4;
+    const int H = (int)g.H, W = (int)g.W, OW = (int)g.OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        uint32_t plane;
+        int oy, ox;
+        strip_pos(st, t, plane, oy, ox);
+        const int c = (int)(plane % (uint32_t)g.C);
+        float wk[9];
+#pragma unroll
+        for (int k = 0; k < 9; k++) wk[k] = __ldg(w + c * 9 + k);
+        float v[3][6];
+        window36(x + (int64_t)plane * H * W, H, W, oy - g.ph, ox - g.pw, v);
+        const float bias = b ? __ldg(b + c) : 0.0f;
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            float acc = bias;
+#pragma unroll
+            for (int ki = 0; ki < 3; ki++)
+#pragma unroll
+                for (int kj = 0; kj < 3; kj++) acc = fmaf(wk[ki * 3 + kj], v[ki][e + kj], acc);
+            o[e] = acc;
+        }
+        *reinterpret_cast<float4 *>(y + (int64_t)plane * g.OH * OW + (int64_t)oy * OW + ox) =
+            make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// input gradient: strips of the input plane (H x W, W a multiple of 4); gy rows iy + ph - ki
+__global__ void __launch_bounds__(256) k_dw3_dx(nck_conv g, Strip3 st, const float *__restrict__ gy,
+                                                const float *__restrict__ w, float *__restrict__ gx, int acc_in) {
+    const uint32_t total = st.planes * st.OH * st.OW4;
+    const int H = (int)g.H, W = (int)g.W, OH = (int)g.OH, OW = (int)g.OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        uint32_t plane;
+        int iy, ix;
+        strip_pos(st, t, plane, iy, ix);
+        const int c = (int)(plane % (uint32_t)g.C);
+        float wk[9];
+#pragma unroll
+        for (int k = 0; k < 9; k++) wk[k] = __ldg(w + c * 9 + k);
+        // v[i][j] = gy[iy + ph - 2 + i][ix + pw - 2 + j]: tap (ki, kj) of output e reads v[2 - ki][e + 2 - kj]
+        float v[3][6];
+        window36(gy + (int64_t)plane * OH * OW, OH, OW, iy + g.ph - 2, ix + g.pw - 2, v);
+        float *dst = gx + (int64_t)plane * H * W + (int64_t)iy * W + ix;
+        float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (acc_in) {
+            const float4 a = *reinterpret_cast<const float4 *>(dst);
+            o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            float acc = o[e];
+#pragma unroll
+            for (int ki = 2; ki >= 0; ki--)
+#pragma unroll
+                for (int kj = 0; kj < 3; kj++) acc = fmaf(wk[ki * 3 + kj], v[2 - ki][e + 2 - kj], acc);
+            o[e] = acc;
+        }
+        *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// weight and bias gradient partials: block (c, split) over the planes of its samples
+__global__ void __launch_bounds__(256) k_dw3_dw_partial(nck_conv g, Strip3 st, const float *__restrict__ x,
+                                                        const float *__restrict__ gy, float *__restrict__ part,
+                                                        int64_t per_split) {
+    __shared__ float red[8][NCK_DW_MAX_TAPS + 1];
+    const int c = blockIdx.x;
+    const int64_t n0 = blockIdx.y * per_split, n1 = min(g.N, n0 + per_split);
+    const int H = (int)g.H, W = (int)g.W, OW = (int)g.OW;
+    const uint32_t strips = st.OH * st.OW4;
+    float acc[9], bsum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 9; k++) acc[k] = 0.0f;
+    for (int64_t nn = n0; nn < n1; nn++) {
+        const int64_t plane = nn * g.C + c;
+        const float *xp = x + plane * H * W, *gp = gy + plane * (int64_t)g.OH * OW;
+        for (uint32_t q = threadIdx.x; q < strips; q += blockDim.x) {
+            const uint32_t oy = st.dow4.div(q);
+            const int ox = (int)(4 * (q - oy * st.OW4));
+            const float4 g4 = __ldg(reinterpret_cast<const float4 *>(gp + (int64_t)oy * OW + ox));
+            float v[3][6];
+            window36(xp, H, W, (int)oy - g.ph, ox - g.pw, v);
+            const float ge[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+#pragma unroll
+                for (int ki = 0; ki < 3; ki++)
+#pragma unroll
+                    for (int kj = 0; kj < 3; kj++) acc[ki * 3 + kj] = fmaf(v[ki][e + kj], ge[e], acc[ki * 3 + kj]);
+                bsum += ge[e];
+            }
+        }
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int k = 0; k <= 9; k++) {
+        float v = k < 9 ? acc[k] : bsum;
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[wid][k < 9 ? k : NCK_DW_MAX_TAPS] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 9 || threadIdx.x == NCK_DW_MAX_TAPS) {
+        float s = 0.0f;
+        for (int q = 0; q < (int)(blockDim.x >> 5); q++) s += red[q][threadIdx.x];
+        part[((int64_t)blockIdx.y * g.C + c) * (NCK_DW_MAX_TAPS + 1) + threadIdx.x] = s;
+    }
+}
+
+bool dw3_ok(const nck_conv *g, int64_t rows, int64_t cols) {
+    return g->KH == 3 && g->KW == 3 && g->sh == 1 && g->sw == 1 && g->dh == 1 && g->dw == 1 && cols % 4 == 0 &&
+           g->N * g->C * rows * cols < ((int64_t)1 << 31) && g->ph <= 2 && g->pw <= 2;
+}
+
+Strip3 strip3(int64_t planes, int64_t rows, int64_t cols) {
+    Strip3 s;
+    s.planes = (uint32_t)planes, s.OH = (uint32_t)rows, s.OW4 = (uint32_t)(cols / 4);
+    s.dow4 = make_fastdiv(s.OW4), s.doh = make_fastdiv(s.OH);
+    return s;
+}
+
 // rows per tile so that a tile has about kDwTileOut outputs; staged rows and width for it
 DwPlan dw_plan_out(const nck_conv *g) {
     DwPlan p;
@@ -797,6 +955,12 @@ extern "C" void nck_dw_fwd(nck_dev *d, const nck_conv *g, const float *x, const 
     const int64_t total = g->N * g->C * g->OH * g->OW;
     if (total <= 0) return;
     Scope sc(d, "dw_fwd", 2.0 * total * g->KH * g->KW, 4.0 * (g->N * g->C * g->H * g->W + total));
+    if (dw3_ok(g, g->OH, g->OW) && (((uintptr_t)x | (uintptr_t)y) & 15) == 0) {
+        const Strip3 st = strip3(g->N * g->C, g->OH, g->OW);
+        k_dw3_fwd<<<grid_for(d, total / 4), 256, 0, NCK_STREAM(d)>>>(*g, st, x, w, b, y);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     const DwPlan pl = dw_plan_out(g);
     const size_t smem = dw_smem(pl);
     const int64_t blocks = g->N * g->C * pl.tiles;
@@ -813,6 +977,12 @@ extern "C" void nck_dw_dx(nck_dev *d, const nck_conv *g, const float *gy, const 
     if (total <= 0) return;
     Scope sc(d, "dw_dx", 2.0 * g->N * g->C * g->OH * g->OW * g->KH * g->KW,
              4.0 * (g->N * g->C * g->OH * g->OW + (acc ? 2 : 1) * total));
+    if (dw3_ok(g, g->H, g->W) && (((uintptr_t)gy | (uintptr_t)gx) & 15) == 0) {
+        const Strip3 st = strip3(g->N * g->C, g->H, g->W);
+        k_dw3_dx<<<grid_for(d, total / 4), 256, 0, NCK_STREAM(d)>>>(*g, st, gy, w, gx, acc);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     nck_conv t = *g;
     t.OH = g->H, t.OW = g->W;
     DwPlan pl = dw_plan_out(&t); /* rows of the input plane per tile */
@@ -837,6 +1007,23 @@ extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const f
     if (g->N * g->C <= 0 || KK <= 0 || KK > NCK_DW_MAX_TAPS) return;
     Scope sc(d, "dw_dw", 2.0 * g->N * g->C * g->OH * g->OW * KK,
              4.0 * (g->N * g->C * (g->H * g->W + g->OH * g->OW)));
+    float *part = (float *)d->scratch;
+    if (dw3_ok(g, g->OH, g->OW) && ((uintptr_t)gy & 15) == 0) {
+        static int res = 0;
+        if (!res) res = resident_blocks(d, k_dw3_dw_partial, 256);
+        int64_t splits = (res + g->C - 1) / g->C;
+        if (splits > g->N) splits = g->N;
+        if (splits < 1) splits = 1;
+        const int64_t per = (g->N + splits - 1) / splits;
+        splits = (g->N + per - 1) / per;
+        const Strip3 st = strip3(1, g->OH, g->OW);
+        dim3 grid((unsigned)g->C, (unsigned)splits);
+        k_dw3_dw_partial<<<grid, 256, 0, NCK_STREAM(d)>>>(*g, st, x, gy, part, per);
+        k_dw_dw_combine<<<grid_for(d, g->C * (KK + 1)), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, g->C, KK, gw,
+                                                                                     gb);
+        NCK_LAUNCHED(d, 2);
+        return;
+    }
     const DwPlan pl = dw_plan_out(g);
     const size_t smem = sizeof(float) * (size_t)pl.srows * pl.scols;
     const bool k3 = g->KH == 3 && g->KW == 3;
@@ -850,7 +1037,6 @@ extern "C" void nck_dw_dw(nck_dev *d, const nck_conv *g, const float *x, const f
     if (splits < 1) splits = 1;
     const int64_t per = (g->N + splits - 1) / splits;
     splits = (g->N + per - 1) / per;
-    float *part = (float *)d->scratch;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid((unsigned)g->C, (unsigned)splits);
     kp<<<grid, kDwThreads, smem, NCK_STREAM(d)>>>(*g, x, gy, part, per, pl, make_fastdiv((uint32_t)g->OW));

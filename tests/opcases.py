@@ -45,6 +45,14 @@ def case_conv_depthwise(e):
     return _conv(e, (2, 3, 7, 6), (3, 1, 3, 3), True, (1, 1), (1, 1), (1, 1), 3, 40)
 
 
+def case_conv_depthwise_w8(e):  # rows a multiple of 4 wide: the strip kernels
+    return _conv(e, (3, 5, 9, 8), (5, 1, 3, 3), True, (1, 1), (1, 1), (1, 1), 5, 42)
+
+
+def case_conv_depthwise_valid(e):  # no padding: strip forward and weight gradient, tiled input gradient
+    return _conv(e, (2, 3, 10, 10), (3, 1, 3, 3), True, (1, 1), (0, 0), (1, 1), 3, 43)
+
+
 def case_conv_depthwise_s2(e):
     return _conv(e, (2, 4, 9, 8), (4, 1, 3, 3), False, (2, 2), (1, 1), (2, 1), 4, 45)
 

@@ -25,6 +25,8 @@ CONV = {
     "conv_dilation": dict(stride=(1, 1), pad=(2, 1), dil=(2, 1), groups=1),
     "conv_depthwise": dict(stride=(1, 1), pad=(1, 1), dil=(1, 1), groups=3),
     "conv_depthwise_s2": dict(stride=(2, 2), pad=(1, 1), dil=(2, 1), groups=4),
+    "conv_depthwise_w8": dict(stride=(1, 1), pad=(1, 1), dil=(1, 1), groups=5),
+    "conv_depthwise_valid": dict(stride=(1, 1), pad=(0, 0), dil=(1, 1), groups=3),
     "conv_pointwise": dict(stride=(1, 1), pad=(0, 0), dil=(1, 1), groups=1),
     "conv_im2col": dict(stride=(1, 1), pad=(1, 1), dil=(1, 1), groups=1),
     "conv_stem": dict(stride=(2, 2), pad=(1, 1), dil=(1, 1), groups=1),
