@@ -156,6 +156,7 @@ class Run:
 
     def __init__(self, lib, trace_name: str, rank: int, world: int, pg, pinned: bool = False):
         self.lib = lib
+        self.name = trace_name
         self.trace = replay.Trace(trace_name)
         self.rep = replay.Replayer(lib, self.trace, seed_offset=dist_host.shard_seed_offset(rank), pinned=pinned)
         self.rep.run(0, 1)  # nc_init
@@ -227,10 +228,11 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     else:
         achieved = by / max(cnt, 1) / (per_launch_ms / 1e3) / 1e9
         peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+    # DRAM bytes per call of this scope in this workload, from one-kernel ncu captures (profiles/)
     traffic = None
     tf = REPO / "profiles" / "traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get(name)
+        traffic = json.loads(tf.read_text()).get(run.name, {}).get(name)
     kernels = sorted(table, key=lambda t: -t[1])[:16]
     sec = max(per_launch_ms, 1e-9) / 1e3
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
