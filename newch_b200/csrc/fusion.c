@@ -69,6 +69,7 @@ void nc__materialize(nc_tensor *owner) {
     nc_ctx *ctx = owner->ctx;
     unlink_deferred(ctx, d); /* first: the launch below reads no recipe */
     if (d->kind == NC_DEF_ATTN) nck_attn_probs(nc__k(ctx), &d->at, (float *)owner->data);
+    else if (d->kind == NC_DEF_UNARY) nck_unary_fwd(nc__k(ctx), d->act, d->act_s, d->x, (float *)owner->data, d->N);
     else
         nck_bn_apply(nc__k(ctx), d->x, d->w, d->b, d->mean, d->invstd, (float *)owner->data, d->N, d->C, d->S,
                      d->act, d->act_s);
@@ -92,6 +93,29 @@ void nc__deferred_flush(nc_ctx *ctx) {
 void nc__deferred_reset(nc_ctx *ctx) {
     for (nc_deferred *d = ctx->deferred_head; d; d = d->next) d->owner->deferred = NULL;
     ctx->deferred_head = NULL;
+}
+
+/* ---- activations consumed on the fly --------------------------------------------------------- */
+
+int nc__defer_unary(nc_tensor *out, nc_tensor *x, int act, float act_s) {
+    nc_ctx *ctx = out->ctx;
+    if (!ctx->fuse || ctx->fwd_on_tape || nc__deferred_of(x) || !nc_is_contiguous(x) || x->dtype != NC_F32) return 0;
+    nc_deferred *d = (nc_deferred *)nc__meta_alloc(ctx, sizeof(nc_deferred), 0);
+    if (!d) return 0;
+    memset(d, 0, sizeof *d);
+    d->owner = out, d->src[0] = nc__owner(x), d->kind = NC_DEF_UNARY;
+    d->x = (const float *)nc__dev(x), d->act = act, d->act_s = act_s, d->N = nc_numel(x);
+    d->next = ctx->deferred_head;
+    ctx->deferred_head = d;
+    out->deferred = d;
+    return 1;
+}
+
+int nc__unary_recipe(const nc_tensor *t, const float **x, int *act, float *act_s) {
+    const nc_deferred *d = nc__deferred_of(t);
+    if (!d || d->kind != NC_DEF_UNARY) return 0;
+    *x = d->x, *act = d->act, *act_s = d->act_s;
+    return 1;
 }
 
 /* ---- attention chains --------------------------------------------------------------------------- */

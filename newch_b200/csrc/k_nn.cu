@@ -568,6 +568,47 @@ __global__ void __launch_bounds__(kDropPolyThreads) k_dropout_fwd_poly(const ulo
     drop_block_write(x, y, bits, n, p, mb);
 }
 
+// One thread per run: thread t of block b evaluates the whole polynomial of run k = 128 b + t (its
+// four words, 64 window lookups) into the run's start state and makes the run's 64 draws itself, so no
+// lane steps the generator past draws another lane makes. Same runs, mask words and outputs as the
+// kernels above.
+__global__ void __launch_bounds__(kDropThreads) k_dropout_fwd_run(const ulonglong4 *__restrict__ gtab,
+                                                                  const ulonglong4 *__restrict__ polys,
+                                                                  const float *__restrict__ x, float *__restrict__ y,
+                                                                  uint32_t *__restrict__ bits, int64_t n, float p) {
+    __shared__ uint32_t mb[kDropBlock / 32];
+    __shared__ ulonglong4 tab[4][16][16];
+    for (int e = threadIdx.x; e < 4 * 16 * 16; e += blockDim.x) (&tab[0][0][0])[e] = gtab[e];
+    __syncthreads();
+    const int64_t k = (int64_t)blockIdx.x * kDropThreads + threadIdx.x;
+    uint32_t w0 = 0, w1 = 0;
+    if (k * kDropDraws < n) {
+        const ulonglong4 q = polys[k];
+        const unsigned long long words[4] = {q.x, q.y, q.z, q.w};
+        unsigned long long a[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int nn = 0; nn < 16; nn++) {
+                const ulonglong4 t = tab[j][nn][(words[j] >> (4 * nn)) & 15];
+                a[0] ^= t.x, a[1] ^= t.y, a[2] ^= t.z, a[3] ^= t.w;
+            }
+#pragma unroll 8
+        for (int i = 0; i < kDropDraws; i++) {
+            const unsigned long long r = rotl64(a[1] * 5ull, 7) * 9ull;
+            xo_step(a);
+            const float u = (float)(r >> 40) * (1.0f / 16777216.0f);
+            const uint32_t keep = u >= p ? 1u : 0u;
+            if (i < 32) w0 |= keep << i;
+            else w1 |= keep << (i - 32);
+        }
+    }
+    mb[2 * threadIdx.x] = w0;
+    mb[2 * threadIdx.x + 1] = w1;
+    __syncthreads();
+    drop_block_write(x, y, bits, n, p, mb);
+}
+
 __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
                                                               float *__restrict__ y, uint32_t *__restrict__ bits,
                                                               int64_t n, float p) {
@@ -633,7 +674,7 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
     if (polys && host_tabs) {
-        k_dropout_fwd_poly<<<(unsigned)blocks, kDropPolyThreads, 0, NCK_STREAM(d)>>>(
+        k_dropout_fwd_run<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(
             reinterpret_cast<const ulonglong4 *>(host_tabs), reinterpret_cast<const ulonglong4 *>(polys), x, y, bits,
             n, p);
         NCK_LAUNCHED(d, 1);

@@ -10,6 +10,7 @@
 
 #include "k_common.cuh"
 #include "k_tcgen05.cuh"
+#include "k_unary.cuh"
 
 using namespace nck;
 
@@ -33,8 +34,86 @@ __global__ void k_quantize_rows(const float *__restrict__ x, int8_t *__restrict_
     }
 }
 
+// One block per row of 1024 NV columns, the row in registers (NV float4 per thread): one read of x,
+// the activation (act >= 0: a NCK_UN_* kind applied to x first, as the unary kernel computes it)
+// evaluated once per element, the row's amax by a warp tree and a block tree (a maximum: any order
+// gives the same value), then the same scale, reciprocal, rounding and clamp as k_quantize_rows.
+template <int M, int NV>
+__global__ void __launch_bounds__(256) k_quantize_rows_reg(const float *__restrict__ x, int act, float act_s,
+                                                           int8_t *__restrict__ q, float *__restrict__ scale,
+                                                           int64_t cols) {
+    __shared__ float red[8];
+    const int64_t r = blockIdx.x;
+    const float4 *p = reinterpret_cast<const float4 *>(x + r * cols);
+    float4 v[NV];
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+        v[k] = __ldcs(p + threadIdx.x + 256 * k);
+        if (act >= 0) {
+            v[k].x = unary_f<M>(act, act_s, v[k].x), v[k].y = unary_f<M>(act, act_s, v[k].y);
+            v[k].z = unary_f<M>(act, act_s, v[k].z), v[k].w = unary_f<M>(act, act_s, v[k].w);
+        }
+        amax = fmaxf(amax, fabsf(v[k].x)), amax = fmaxf(amax, fabsf(v[k].y));
+        amax = fmaxf(amax, fabsf(v[k].z)), amax = fmaxf(amax, fabsf(v[k].w));
+    }
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+    const float sc = amax > 0.0f ? amax / 127.0f : 1.0f;
+    const float inv = 1.0f / sc;
+    char4 *qr = reinterpret_cast<char4 *>(q + r * cols);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+        const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        signed char o[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float t = rintf(e[i] * inv);
+            o[i] = (signed char)(t > 127.0f ? 127.0f : t < -127.0f ? -127.0f : t);
+        }
+        qr[threadIdx.x + 256 * k] = make_char4(o[0], o[1], o[2], o[3]);
+    }
+    if (threadIdx.x == 0) scale[r] = sc;
+}
+
+extern "C" int nck_quantize_rows_act_ok(int64_t cols) {
+    return cols == 1024 || cols == 2048 || cols == 4096 || cols == 8192;
+}
+
+extern "C" void nck_quantize_rows_act(nck_dev *d, const float *x, int act, float act_s, int8_t *q, float *scale,
+                                      int64_t rows, int64_t cols) {
+    if (rows <= 0) return;
+    Scope sc(d, act >= 0 ? "act_quantize_rows" : "quantize_rows", 0.0, 5.0 * rows * cols + 4.0 * rows);
+    const bool aligned = (((uintptr_t)x | (uintptr_t)q) & 15) == 0;
+    if (!aligned || !nck_quantize_rows_act_ok(cols)) {
+        /* the general kernel has no activation: this form is only used for act < 0 */
+        k_quantize_rows<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, q, scale, rows, cols);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
+    const bool libm = d->math_mode == MATH_LIBM;
+#define NCK_QR(NV)                                                                                          \
+    (libm ? k_quantize_rows_reg<MATH_LIBM, NV> : k_quantize_rows_reg<MATH_POLY, NV>)<<<(unsigned)rows, 256, 0, \
+                                                                                    NCK_STREAM(d)>>>(           \
+        x, act, act_s, q, scale, cols)
+    if (cols == 1024) NCK_QR(1);
+    else if (cols == 2048) NCK_QR(2);
+    else if (cols == 4096) NCK_QR(4);
+    else NCK_QR(8);
+#undef NCK_QR
+    NCK_LAUNCHED(d, 1);
+}
+
 extern "C" void nck_quantize_rows(nck_dev *d, const float *x, int8_t *q, float *scale, int64_t rows, int64_t cols) {
     if (rows <= 0) return;
+    if ((((uintptr_t)x | (uintptr_t)q) & 15) == 0 && nck_quantize_rows_act_ok(cols)) {
+        nck_quantize_rows_act(d, x, -1, 0.0f, q, scale, rows, cols);
+        return;
+    }
     Scope sc(d, "quantize_rows", 0.0, 5.0 * rows * cols + 4.0 * rows);
     k_quantize_rows<<<grid_for(d, rows * 32), kThreads, 0, NCK_STREAM(d)>>>(x, q, scale, rows, cols);
     NCK_LAUNCHED(d, 1);

@@ -334,7 +334,7 @@ void nc__dp_rng_step_end(nc_ctx *ctx);
  * reads the recipe and pools straight from x; anything else that touches the data materialises it
  * first (nc__dev and the host paths call nc__materialize). In backward, a pool or activation over
  * such a chain runs the whole chain's backward in one fused BatchNorm backward. */
-enum { NC_DEF_BN = 0, NC_DEF_ATTN = 1 };
+enum { NC_DEF_BN = 0, NC_DEF_ATTN = 1, NC_DEF_UNARY = 2 };
 typedef struct nc_deferred {
     nc_tensor *owner;              /* the tensor whose values are pending */
     nc_tensor *src[3];             /* owners whose data feeds the recipe (NULL: unused) */
@@ -346,6 +346,7 @@ typedef struct nc_deferred {
     float act_s;
     /* NC_DEF_ATTN: a tensor of the scores -> mask -> softmax -> dropout chain (at.stage says which) */
     nck_attn at;
+    /* NC_DEF_UNARY: act(x) over N = numel contiguous elements (x, act, act_s above) */
     struct nc_deferred *next;
 } nc_deferred;
 
@@ -363,6 +364,11 @@ void nc__deferred_flush(nc_ctx *ctx);  /* materialise every pending recipe */
 void nc__deferred_reset(nc_ctx *ctx);  /* step end: forget every recipe (their storage is reset) */
 /* Attention chains (fusion.c). Each returns 1 when it took the op (out is a recipe, or was computed
  * by the fused kernel), 0 when the op runs its own kernels. */
+/* out := act(x) as a recipe (no tape: an inference forward), for a consumer that applies act itself
+ * (the int8 linear's quantization); 1 when deferred */
+int nc__defer_unary(nc_tensor *out, nc_tensor *x, int act, float act_s);
+/* t's pending unary recipe (its input data, kind, parameter), or 0 */
+int nc__unary_recipe(const nc_tensor *t, const float **x, int *act, float *act_s);
 int nc__attn_bmm(nc_node *n);                       /* scores q @ k^T, or probabilities @ v */
 int nc__attn_mask(nc_node *n);                      /* masked_fill of the scores */
 int nc__attn_softmax(nc_node *n);                   /* softmax of the (masked) scores */

@@ -380,6 +380,11 @@ void nck_optim_step(nck_dev *d, const nck_opt_hyper *h, const nck_param_seg *dse
                     int nchunk, int64_t total, const unsigned char *present);
 
 /* ---- int8 quantization -------------------------------------------------------------------------- */
+/* rows of act(x) quantized as nck_quantize_rows does (act: a NCK_UN_* kind applied on the fly, -1 none);
+ * act >= 0 needs nck_quantize_rows_act_ok(cols) and 16-byte aligned x and q */
+int nck_quantize_rows_act_ok(int64_t cols);
+void nck_quantize_rows_act(nck_dev *d, const float *x, int act, float act_s, int8_t *q, float *scale, int64_t rows,
+                           int64_t cols);
 void nck_quantize_rows(nck_dev *d, const float *x, int8_t *q, float *scale, int64_t rows, int64_t cols);
 /* y[r, o] = (float)acc * xs[r] * ws[o] + b[o], acc = sum_k xq[r,k] * wq[o,k] (exact int32) */
 void nck_qlinear(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, const float *b,

@@ -112,6 +112,10 @@ static nc_status unary_fwd(nc_node *n) {
         return NC_OK;
     /* a scale of pending attention scores joins the chain */
     if (n->op->kind == NCK_UN_SCALE && nc__attn_scale(n, n->p.f[0])) return NC_OK;
+    /* without a tape, a GELU output waits for its reader: the int8 linear quantizes it on the fly */
+    if ((n->op->kind == NCK_UN_GELU || n->op->kind == NCK_UN_GELU_TANH) && nc__defer_unary(n->out, n->in[0],
+                                                                                         n->op->kind, n->p.f[0]))
+        return NC_OK;
     const float *x = nc__contig_f32(n->in[0]);
     if (!x) return NC_ERR_OOM;
     nck_unary_fwd(nc__k(n->out->ctx), n->op->kind, n->p.f[0], x, (float *)n->out->data, nc_numel(n->out));

@@ -54,18 +54,24 @@ static nc_status qlinear_fwd(nc_node *n) {
         nc__error(ctx, NC_ERR_ARG, "linear_int8: weight must be contiguous");
         return NC_ERR_ARG;
     }
-    const float *X = nc__contig_f32(x), *ws = nc__contig_f32(n->in[2]);
+    /* a pending activation of the input (GELU between int8 layers) is applied while quantizing */
+    const float *X = NULL;
+    int act = -1;
+    float act_s = 0.0f;
+    if (!(nc__unary_recipe(x, &X, &act, &act_s) && nck_quantize_rows_act_ok(in))) act = -1, X = nc__contig_f32(x);
+    const float *ws = nc__contig_f32(n->in[2]);
     const float *b = n->n_in > 3 ? nc__contig_f32(n->in[3]) : NULL;
     int8_t *xq = (int8_t *)nc__arena_alloc(ctx, (size_t)(M * in) + 16);
     float *xs = (float *)nc__arena_alloc(ctx, (size_t)(M ? M : 1) * sizeof(float));
     if (!X || !ws || (n->n_in > 3 && !b) || !xq || !xs) return NC_ERR_OOM;
     if (!M || !out) return NC_OK;
-    nck_quantize_rows(nc__k(ctx), X, xq, xs, M, in);
+    if (act >= 0) nck_quantize_rows_act(nc__k(ctx), X, act, act_s, xq, xs, M, in);
+    else nck_quantize_rows(nc__k(ctx), X, xq, xs, M, in);
     nck_qlinear(nc__k(ctx), xq, xs, (const int8_t *)nc__dev(wq), ws, b, (float *)n->out->data, M, out, in, NULL);
     return NC_OK;
 }
 
-const nc_op_def nc_op_linear_int8 = {"linear_int8", NC_OPF_NONDIFF, 0, qlinear_infer, NULL, qlinear_fwd, NULL};
+const nc_op_def nc_op_linear_int8 = {"linear_int8", NC_OPF_NONDIFF | NC_OPF_RECIPE, 0, qlinear_infer, NULL, qlinear_fwd, NULL};
 
 nc_tensor *nc_linear_int8(nc_tensor *x, nc_tensor *wq, nc_tensor *w_scale, nc_tensor *bias) {
     nc_tensor *in[4] = {x, wq, w_scale, bias};

@@ -536,6 +536,26 @@ def case_int8(e):
     return {"w": w, "x": x, "b": b, "q": e.np(q), "scale": e.np(s), "y": e.np(y)}
 
 
+def case_int8_gelu_chain(e):
+    """Inference (no tape) int8 MLP block: linear_int8 -> GELU -> linear_int8, 1024 features: the B200
+    engine quantizes the pending GELU output on the fly (no fp32 GELU tensor is written unless read)."""
+    e.L.nc_set_grad_enabled(e.ctx, 0)
+    out = {}
+    x = seeded(255, (33, 1024))
+    h = e.t(x)
+    for i, (o, k) in enumerate(((1024, 1024), (10, 1024))):
+        w = seeded(256 + i, (o, k), 0.05)
+        b = seeded(258 + i, (o,), 0.1)
+        sp = capi.ptr_array([None])
+        q = e.check(e.L.nc_quantize_rows(e.t(w), sp))
+        h = e.check(e.L.nc_linear_int8(h, q, sp[0], e.t(b)))
+        if i == 0:
+            h = e.check(e.L.nc_gelu(h, 0))
+    out.update(x=x, y=e.np(h))
+    e.L.nc_set_grad_enabled(e.ctx, 1)
+    return out
+
+
 def _adam(e, decoupled, seed):
     w0 = seeded(seed, (50,))
     w = e.param(w0)

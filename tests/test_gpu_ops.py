@@ -24,6 +24,7 @@ EXACT = {
     "dropout": {"y1", "y2", "dx"},
     "random": {"uniform"},
     "int8": {"q", "scale", "y"},
+    "int8_gelu_chain": {"x", "y"},
     "reductions": {"argmax_1", "max_0_y", "max_1_y", "max_2_y", "max_all_y", "max_0_dx", "max_1_dx", "max_2_dx",
                    "max_all_dx"},
     "maxpool_2x2": {"y"},
@@ -82,7 +83,7 @@ def test_libm_math_mode(how, monkeypatch):
 
 @pytest.mark.parametrize("case", ["bn_relu_pool", "bn_pool", "bn_hardswish", "bn_relu6_pool", "bn_relu_reused",
                                   "bn_relu_pool_odd", "attention_chain", "attention_mha", "attention_mha_128",
-                                  "attention_sdpa", "attention_unmasked", "attention_probs_read"])
+                                  "attention_sdpa", "attention_unmasked", "attention_probs_read", "int8_gelu_chain"])
 def test_chains_unfused(case, monkeypatch):
     """NC_FUSE=0: the BatchNorm and attention chains through the unfused kernels (every intermediate
     written), held to the same goldens as the fused default (test_op_matches_reference)."""
