@@ -352,12 +352,13 @@ static void linear_bwd(nc_node *n) {
             gemm_launch(x->ctx, d.rows, d.in, d.out, G, row_major(W, d.in), (float *)gx->data, d.in, acc ? 1.0f : 0.0f,
                         NULL, 1, 0, 0, 0, 0);
     }
-    if (nc__needs_grad(w)) { /* dW += dY^T X */
+    if (nc__needs_grad(w)) { /* dW += dY^T X (stored when the gradient is fresh: no fill, no read of C) */
         const float *X = nc__contig_f32(x);
-        nc_tensor *gw = X ? nc__grad_buf(w) : NULL;
+        int acc = 1;
+        nc_tensor *gw = X ? nc__grad_buf_acc(w, &acc) : NULL;
         if (gw)
-            gemm_launch(x->ctx, d.out, d.in, d.rows, mat_t(G), row_major(X, d.in), (float *)gw->data, d.in, 1.0f, NULL, 1,
-                        0, 0, 0, 0);
+            gemm_launch(x->ctx, d.out, d.in, d.rows, mat_t(G), row_major(X, d.in), (float *)gw->data, d.in,
+                        acc ? 1.0f : 0.0f, NULL, 1, 0, 0, 0, 0);
     }
     if (b && nc__needs_grad(b)) { /* db += column sums of dY */
         nc_tensor *gb = nc__grad_buf(b);
