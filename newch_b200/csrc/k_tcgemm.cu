@@ -15,9 +15,10 @@
 //   warp 5     MMA issuer (one thread): 4 MMAs of K = 8 per stage, commits each stage back to the
 //              loader and each finished tile to the epilogue
 //   warps 6-13 3xTF32 only: write the remainder of every staged fp32 tile below its TF32 head (the
-//              top 19 bits, which the MMA reads from the staged tile itself), rounded to TF32; the
-//              MMA thread then
-//              accumulates head*head + head*rest + rest*head
+//              top 19 bits, which the MMA reads from the staged tile itself), rounded to TF32; the Q
+//              remainder lands right after the Q head, so the MMA thread issues two MMAs per K step:
+//              P_head x [Q_head | Q_rest] into a 2*BN-wide accumulator, then P_rest x Q_head into its
+//              first half; the epilogue adds the halves
 // Two accumulators in TMEM let the epilogue of one tile overlap the main loop of the next.
 //
 // Every mbarrier wait gives up after 2 s of device time and records an error in the status word; a
@@ -58,7 +59,8 @@ struct TcParams {
 };
 
 // Barriers sit in the first KiB of dynamic shared memory; the stage buffers follow, 1 KiB aligned:
-// [P stages][Q stages] and in 3xTF32 mode [P rests][Q rests], `stages` of each.
+// [P stages][Q stages] and in 3xTF32 mode [P rests]; in 3xTF32 mode a Q stage holds the head tile
+// followed by its remainder (2 * BN rows).
 struct Bars {
     uint64_t full[kMaxStages], empty[kMaxStages], ready[kMaxStages];
     uint64_t tfull[2], tempty[2], mma_done;
@@ -92,6 +94,14 @@ __device__ __forceinline__ Unit unit_of(const TcParams &p, int64_t u) {
     return w;
 }
 
+// 3xTF32: the accumulator's second half (P_h Q_r) added to the first (P_h Q_h + P_r Q_h), column by column
+__device__ __forceinline__ void add_cross(uint32_t taddr, uint32_t (&r)[16]) {
+    uint32_t r2[16];
+    tmem_ld16(taddr, r2);
+#pragma unroll
+    for (int j = 0; j < 16; j++) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(r2[j]));
+}
+
 template <bool THREE, bool BETA>
 __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm(const __grid_constant__ CUtensorMap tmP,
                                                                  const __grid_constant__ CUtensorMap tmQ, TcParams p) {
@@ -99,14 +109,14 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
     unsigned char *base = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                             ~(uintptr_t)1023);
     Bars &s = *reinterpret_cast<Bars *>(base);
-    const int S = p.stages, sbq = p.BN * TK;
+    const int S = p.stages, sbq = p.BN * TK, sbq2 = THREE ? 2 * sbq : sbq;
     float *const ring_a = reinterpret_cast<float *>(base + 1024);
     float *const ring_b = ring_a + S * kStageA;
-    float *const rest_a = ring_b + S * sbq;  // 3xTF32 only
-    float *const rest_b = rest_a + S * kStageA;
+    float *const rest_a = ring_b + S * sbq2;  // 3xTF32 only
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int BN = p.BN;
-    const uint32_t tcols = BN * 2 <= 32 ? 32 : BN * 2 <= 64 ? 64 : BN * 2 <= 128 ? 128 : 256;
+    const int AW = THREE ? 2 * BN : BN;  // accumulator columns per tile
+    const uint32_t tcols = tmem_cols(AW);
     const uint32_t stage_bytes = (uint32_t)(TM + BN) * TK * 4;
 
     if (tid == 0) {
@@ -156,12 +166,12 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                         }
                     }
                     if (!p.q_mn) {
-                        if (p.q_bat) tma_3d(ring_b + st * sbq, &tmQ, kk, (int)w.q0, b, &s.full[st]);
-                        else tma_2d(ring_b + st * sbq, &tmQ, kk, (int)w.q0, &s.full[st]);
+                        if (p.q_bat) tma_3d(ring_b + st * sbq2, &tmQ, kk, (int)w.q0, b, &s.full[st]);
+                        else tma_2d(ring_b + st * sbq2, &tmQ, kk, (int)w.q0, &s.full[st]);
                     } else {
                         for (int j = 0; j < BN / 32; j++) {
-                            if (p.q_bat) tma_3d(ring_b + st * sbq + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, b, &s.full[st]);
-                            else tma_2d(ring_b + st * sbq + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
+                            if (p.q_bat) tma_3d(ring_b + st * sbq2 + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, b, &s.full[st]);
+                            else tma_2d(ring_b + st * sbq2 + j * 1024, &tmQ, (int)w.q0 + 32 * j, kk, &s.full[st]);
                         }
                     }
                     if (++st == S) st = 0, ph ^= 1;
@@ -177,12 +187,13 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ---- MMA issuer ----------------------------------------------------------------------------
-            const uint32_t idesc = idesc_tf32(p.p_mn, p.q_mn, BN);
+            // the Q head and rest are adjacent: one operand 2*BN wide (K-major: 2*BN rows of 128 B;
+            // MN-major: 2*BN/32 blocks of 4 KiB, the block stride of the descriptor)
+            const uint32_t idesc = idesc_tf32(p.p_mn, p.q_mn, BN), idesc2 = idesc_tf32(p.p_mn, p.q_mn, 2 * BN);
             const uint64_t dA = stage_desc(smem_u32(ring_a), p.p_mn, 0), dB = stage_desc(smem_u32(ring_b), p.q_mn, 0);
-            const uint32_t stA = (uint32_t)(kStageA * 4) >> 4, stB = (uint32_t)(sbq * 4) >> 4;
+            const uint32_t stA = (uint32_t)(kStageA * 4) >> 4, stB = (uint32_t)(sbq2 * 4) >> 4;
             const uint32_t kA = p.p_mn ? 64u : 2u, kB = p.q_mn ? 64u : 2u;  // 8 K rows (MN-major) or 32 B
             const uint64_t restA = (uint64_t)((smem_u32(rest_a) - smem_u32(ring_a)) >> 4);
-            const uint64_t restB = (uint64_t)((smem_u32(rest_b) - smem_u32(ring_b)) >> 4);
             int64_t it = 0, local = 0;
             int st = 0;
             uint32_t ph = 0;
@@ -204,10 +215,11 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                     for (int k = 0; k < TK / 8; k++) {
                         const uint32_t accum = (t > 0 || k > 0) ? 1u : 0u;
                         const uint64_t ak = a0 + (uint64_t)(k * kA), bk = b0 + (uint64_t)(k * kB);
-                        mma_tf32(d, ak, bk, idesc, accum);
                         if (THREE) {
-                            mma_tf32(d, ak, bk + restB, idesc, 1u);
-                            mma_tf32(d, ak + restA, bk, idesc, 1u);
+                            mma_tf32(d, ak, bk, idesc2, accum);     // [P_h Q_h | P_h Q_r]
+                            mma_tf32(d, ak + restA, bk, idesc, 1u);  // += P_r Q_h in the first half
+                        } else {
+                            mma_tf32(d, ak, bk, idesc, accum);
                         }
                     }
                     mma_commit(&s.empty[st]);  // the loader may refill this stage once these MMAs read it
@@ -237,7 +249,7 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                 for (int i = t2; i < TM * TK / 4; i += kSplitThreads) {
                     al[i] = tf32_rest4(ah[i]);
                 }
-                float4 *bh = reinterpret_cast<float4 *>(ring_b + st * sbq), *bl = reinterpret_cast<float4 *>(rest_b + st * sbq);
+                float4 *bh = reinterpret_cast<float4 *>(ring_b + st * sbq2), *bl = bh + sbq / 4;
                 for (int i = t2; i < nb; i += kSplitThreads) {
                     bl[i] = tf32_rest4(bh[i]);
                 }
@@ -273,6 +285,7 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                         cv[jj] = (live && j < p.Cq) ? out[j * ldo + i] : 0.0f;
                     }
                     tmem_ld16(taddr, r);
+                    if (THREE) add_cross(taddr + (uint32_t)BN, r);
                     if (!live) continue;
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) {
@@ -286,6 +299,7 @@ __global__ void __launch_bounds__(THREE ? kThreads3x : kThreadsTf32, 1) k_tcgemm
                     continue;
                 }
                 tmem_ld16(taddr, r);
+                if (THREE) add_cross(taddr + (uint32_t)BN, r);
                 if (!live) continue;
 #pragma unroll
                 for (int jj = 0; jj < 16; jj++) {
