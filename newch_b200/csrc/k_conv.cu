@@ -509,6 +509,104 @@ static void direct3_dw_launch(nck_dev *d, const nck_conv *g, const float *x, con
     NCK_LAUNCHED(d, 2);
 }
 
+// Weight (and bias) gradient of a few-tap convolution (groups 1, C*KH*KW + 1 <= 32, OC <= 64) as a
+// contraction over positions: a block takes a slice of the (image, position) items in tiles of 64;
+// per tile the receptive fields (column k < C*KH*KW, then a column of ones for the bias) and dY of
+// every output channel are staged in shared memory, each read from global memory once, and lane k of
+// warp w adds dY[p][oc] * col[p][k] for the warp's OCT channels, positions in order. One partial per
+// block ([OC][C*KH*KW] weights, then [OC] bias sums); k_direct_dw_combine adds the slices in order.
+constexpr int kDwTP = 64;  // positions per tile
+
+template <int OCT>
+__global__ void __launch_bounds__(256) k_conv_dw_cols(nck_conv g, const float *__restrict__ x,
+                                                      const float *__restrict__ gy, float *__restrict__ part,
+                                                      int64_t per_split) {
+    __shared__ Taps taps;
+    __shared__ float cols[kDwTP][33];
+    __shared__ float dys[kDwTP][8 * OCT + 1];
+    const int CKK = (int)(g.C * g.KH * g.KW), OC = (int)g.OC;
+    const int L = (int)(g.OH * g.OW), OW = (int)g.OW, H = (int)g.H, W = (int)g.W;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, oc0 = warp * OCT;
+    build_taps(g, CKK, taps);
+    float acc[OCT];
+#pragma unroll
+    for (int o = 0; o < OCT; o++) acc[o] = 0.0f;
+    const int64_t total = g.N * (int64_t)L, p0 = blockIdx.x * per_split;
+    const int64_t p1 = p0 + per_split < total ? p0 + per_split : total;
+    __syncthreads();
+    for (int64_t t0 = p0; t0 < p1; t0 += kDwTP) {
+        const int np = (int)(p1 - t0 < kDwTP ? p1 - t0 : kDwTP);
+        // receptive fields: thread (q, k-half) gathers half the taps of position q
+        for (int e = threadIdx.x; e < kDwTP * 32; e += blockDim.x) {
+            const int q = e >> 5, k = e & 31;
+            float v = 0.0f;
+            if (q < np) {
+                const int64_t p = t0 + q, n = p / L;
+                const int l = (int)(p - n * L), oy = l / OW, ox = l - oy * OW;
+                if (k < CKK) {
+                    const int iy = oy * g.sh + taps.dy[k], ix = ox * g.sw + taps.dx[k];
+                    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                        v = __ldg(x + n * g.C * (int64_t)H * W + (int64_t)(oy * g.sh) * W + ox * g.sw + taps.off[k]);
+                } else if (k == CKK) {
+                    v = 1.0f;  // the bias column
+                }
+            }
+            cols[q][k] = v;
+        }
+        // dY of every channel at the tile's positions (runs of positions are contiguous per channel)
+        for (int e = threadIdx.x; e < kDwTP * 8 * OCT; e += blockDim.x) {
+            const int oc = e / kDwTP, q = e - oc * kDwTP;
+            float v = 0.0f;
+            if (q < np && oc < OC) {
+                const int64_t p = t0 + q, n = p / L;
+                v = __ldg(gy + (n * OC + oc) * (int64_t)L + (p - n * L));
+            }
+            dys[q][oc] = v;
+        }
+        __syncthreads();
+        for (int q = 0; q < np; q++) {
+            const float cv = cols[q][lane];
+#pragma unroll
+            for (int o = 0; o < OCT; o++) acc[o] = fmaf(dys[q][oc0 + o], cv, acc[o]);
+        }
+        __syncthreads();
+    }
+    float *dst = part + (int64_t)blockIdx.x * OC * (CKK + 1);
+#pragma unroll
+    for (int o = 0; o < OCT; o++) {
+        const int oc = oc0 + o;
+        if (oc >= OC) continue;
+        if (lane < CKK) dst[oc * CKK + lane] = acc[o];
+        else if (lane == CKK) dst[OC * CKK + oc] = acc[o];
+    }
+}
+
+static bool dw_cols_ok(const nck_conv *g) {
+    return g->G == 1 && g->C * g->KH * g->KW + 1 <= 32 && g->OC <= 64 && g->N * g->OH * g->OW < ((int64_t)1 << 31);
+}
+
+static void dw_cols_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb) {
+    const int64_t CKK = g->C * g->KH * g->KW, total = g->N * g->OH * g->OW, wsz = g->OC * (CKK + 1);
+    const bool wide = g->OC > 32;
+    static int res4 = 0, res8 = 0;
+    if (!wide && !res4) res4 = resident_blocks(d, k_conv_dw_cols<4>, 256);
+    if (wide && !res8) res8 = resident_blocks(d, k_conv_dw_cols<8>, 256);
+    int64_t splits = wide ? res8 : res4;
+    const int64_t maxs = (int64_t)(d->scratch_bytes / sizeof(float)) / wsz;
+    if (splits > maxs) splits = maxs;
+    if (splits > (total + kDwTP - 1) / kDwTP) splits = (total + kDwTP - 1) / kDwTP;
+    if (splits < 1) splits = 1;
+    int64_t per = (total + splits - 1) / splits;
+    per = (per + kDwTP - 1) / kDwTP * kDwTP;
+    splits = (total + per - 1) / per;
+    float *part = (float *)d->scratch;
+    if (wide) k_conv_dw_cols<8><<<(unsigned)splits, 256, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
+    else k_conv_dw_cols<4><<<(unsigned)splits, 256, 0, NCK_STREAM(d)>>>(*g, x, gy, part, per);
+    k_direct_dw_combine<<<grid_for(d, wsz * 32), kThreads, 0, NCK_STREAM(d)>>>(part, (int)splits, wsz, gw,
+                                                                               g->OC * CKK, gb);
+    NCK_LAUNCHED(d, 2);
+}
+
 template <int KT, int OCW>
 static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw) {
     const int64_t OCg = g->OC / g->G, CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;
@@ -540,6 +638,10 @@ extern "C" int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x,
              4.0 * (g->N * g->C * g->H * g->W + g->N * g->OC * L + 2 * g->OC * CKK));
     if (direct3_ok(g)) {
         direct3_dw_launch(d, g, x, gy, gw, gb);
+        return gb != nullptr;
+    }
+    if (dw_cols_ok(g)) {
+        dw_cols_launch(d, g, x, gy, gw, gb);
         return gb != nullptr;
     }
     if (CKK <= 9) direct_dw_launch<9, 8>(d, g, x, gy, gw);
