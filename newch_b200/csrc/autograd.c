@@ -371,8 +371,10 @@ void nc_clear_grad(nc_tensor *t) {
 void nc_release_temp(nc_tensor *t) {
     if (!t || (t->flags & (NC_TF_PERSISTENT | NC_TF_ON_TAPE)) || !(t->flags & NC_TF_OWNS_DATA) || !t->data) return;
     nc_ctx *ctx = t->ctx;
-    nc__deferred_release(t);
-    nc__arena_free(ctx, t->data, t->bytes);
+    if (!nc__deferred_adopt(t)) { /* else a pending recipe still reads the block and frees it later */
+        nc__deferred_release(t);
+        nc__arena_free(ctx, t->data, t->bytes);
+    }
     t->data = NULL;
     t->coh = 0;
     nc_tensor *g = t->grad;

@@ -63,13 +63,38 @@ static void unlink_deferred(nc_ctx *ctx, nc_deferred *d) {
     d->owner->deferred = NULL;
 }
 
+/* an adopted source block goes back to the arena (after the last launch that reads it is enqueued) */
+static void free_adopted(nc_ctx *ctx, nc_deferred *d) {
+    if (!d->adopt) return;
+    nc__arena_free(ctx, d->adopt, d->adopt_bytes);
+    d->adopt = NULL;
+}
+
+int nc__deferred_adopt(nc_tensor *owner) {
+    nc_ctx *ctx = owner->ctx;
+    if (owner->deferred) return 0;
+    nc_deferred *only = NULL;
+    for (nc_deferred *d = ctx->deferred_head; d; d = d->next) {
+        if (d->src[0] != owner && d->src[1] != owner && d->src[2] != owner) continue;
+        if (only || d->kind != NC_DEF_UNARY || d->adopt || d->x != (const float *)owner->data) return 0;
+        only = d;
+    }
+    if (!only) return 0;
+    only->adopt = owner->data, only->adopt_bytes = owner->bytes;
+    only->src[0] = NULL;
+    return 1;
+}
+
 void nc__materialize(nc_tensor *owner) {
     nc_deferred *d = owner->deferred;
     if (!d) return;
     nc_ctx *ctx = owner->ctx;
     unlink_deferred(ctx, d); /* first: the launch below reads no recipe */
     if (d->kind == NC_DEF_ATTN) nck_attn_probs(nc__k(ctx), &d->at, (float *)owner->data);
-    else if (d->kind == NC_DEF_UNARY) nck_unary_fwd(nc__k(ctx), d->act, d->act_s, d->x, (float *)owner->data, d->N);
+    else if (d->kind == NC_DEF_UNARY) {
+        nck_unary_fwd(nc__k(ctx), d->act, d->act_s, d->x, (float *)owner->data, d->N);
+        free_adopted(ctx, d);
+    }
     else
         nck_bn_apply(nc__k(ctx), d->x, d->w, d->b, d->mean, d->invstd, (float *)owner->data, d->N, d->C, d->S,
                      d->act, d->act_s);
@@ -83,7 +108,11 @@ void nc__deferred_release(nc_tensor *owner) {
         if ((d->src[0] == owner || d->src[1] == owner || d->src[2] == owner) && d->owner != owner)
             nc__materialize(d->owner);
     }
-    if (owner->deferred) unlink_deferred(ctx, owner->deferred);
+    if (owner->deferred) {
+        nc_deferred *d = owner->deferred;
+        unlink_deferred(ctx, d);
+        free_adopted(ctx, d);
+    }
 }
 
 void nc__deferred_flush(nc_ctx *ctx) {

@@ -346,7 +346,10 @@ typedef struct nc_deferred {
     float act_s;
     /* NC_DEF_ATTN: a tensor of the scores -> mask -> softmax -> dropout chain (at.stage says which) */
     nck_attn at;
-    /* NC_DEF_UNARY: act(x) over N = numel contiguous elements (x, act, act_s above) */
+    /* NC_DEF_UNARY: act(x) over N = numel contiguous elements (x, act, act_s above); adopt: the
+     * source's arena block when the caller released the source first (freed with the recipe) */
+    void *adopt;
+    size_t adopt_bytes;
     struct nc_deferred *next;
 } nc_deferred;
 
@@ -367,6 +370,9 @@ void nc__deferred_reset(nc_ctx *ctx);  /* step end: forget every recipe (their s
 /* out := act(x) as a recipe (no tape: an inference forward), for a consumer that applies act itself
  * (the int8 linear's quantization); 1 when deferred */
 int nc__defer_unary(nc_tensor *out, nc_tensor *x, int act, float act_s);
+/* owner (a temporary being released) feeds only a pending unary recipe: the recipe takes over its
+ * data block (freed when the recipe is computed or dropped); 1 when it did */
+int nc__deferred_adopt(nc_tensor *owner);
 /* t's pending unary recipe (its input data, kind, parameter), or 0 */
 int nc__unary_recipe(const nc_tensor *t, const float **x, int *act, float *act_s);
 int nc__attn_bmm(nc_node *n);                       /* scores q @ k^T, or probabilities @ v */

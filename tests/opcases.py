@@ -550,7 +550,9 @@ def case_int8_gelu_chain(e):
         q = e.check(e.L.nc_quantize_rows(e.t(w), sp))
         h = e.check(e.L.nc_linear_int8(h, q, sp[0], e.t(b)))
         if i == 0:
+            pre = h
             h = e.check(e.L.nc_gelu(h, 0))
+            e.L.nc_release_temp(pre)  # as newch's inference loop does: the GELU input goes first
     out.update(x=x, y=e.np(h))
     e.L.nc_set_grad_enabled(e.ctx, 1)
     return out
