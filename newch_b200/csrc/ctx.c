@@ -283,8 +283,12 @@ int nc__is_persistent_mode(const nc_ctx *ctx) { return ctx->persistent_depth > 0
 #define NC_STAGE_SLOTS 32
 
 void nc__upload(nc_ctx *ctx, void *dst, const void *src, size_t bytes) {
+    nc__upload_on(ctx, ctx->dev.stream, dst, src, bytes);
+}
+
+void nc__upload_on(nc_ctx *ctx, void *stream, void *dst, const void *src, size_t bytes) {
     if (!bytes || !ctx->device_ok) return;
-    cudaStream_t s = (cudaStream_t)ctx->dev.stream;
+    cudaStream_t s = (cudaStream_t)stream;
     size_t slot_bytes = ctx->stage_cap / NC_STAGE_SLOTS;
     if (ctx->stage && bytes <= slot_bytes) {
         /* small uploads go through a pinned ring so the caller's buffer is free on return and
@@ -437,6 +441,7 @@ void nc_free_ctx(nc_ctx *ctx) {
     if (ctx->device_ok) {
         cudaStream_t s = (cudaStream_t)ctx->dev.stream;
         cudaStreamSynchronize(s);
+        nc__rng_side_free(ctx);
         nc__dp_free(ctx);
         for (int i = 0; i < ctx->n_dchunks; i++) cudaFreeAsync(ctx->dchunks[i].base, s);
         for (size_t i = 0; i < ctx->pmem_cap; i++)
@@ -468,6 +473,7 @@ void nc_free_ctx(nc_ctx *ctx) {
 
 void nc_step_end(nc_ctx *ctx) {
     nc__deferred_reset(ctx);
+    nc__rng_side_step_end(ctx);
     if (ctx->bn_n) nc__dp_bn_flush(ctx, 0); /* statistics staged in a step no optimizer step closed */
     nc__dp_rng_step_end(ctx);
     for (int i = 0; i < ctx->n_dchunks; i++) ctx->dchunks[i].used = 0;

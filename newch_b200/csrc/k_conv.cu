@@ -630,6 +630,8 @@ static void direct_dw_launch(nck_dev *d, const nck_conv *g, const float *x, cons
 
 extern "C" int nck_conv_direct3_ok(const nck_conv *g) { return direct3_ok(g); }
 
+extern "C" int nck_conv_direct_dw_bias_ok(const nck_conv *g) { return direct3_ok(g) || dw_cols_ok(g); }
+
 extern "C" int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw,
                                   float *gb) {
     int64_t CKK = (g->C / g->G) * g->KH * g->KW, L = g->OH * g->OW;

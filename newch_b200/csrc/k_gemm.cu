@@ -229,7 +229,19 @@ __global__ void __launch_bounds__(256) k_sgemm_small_thread(GemmP p, int64_t nou
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t ob = t / MN, rm = t - ob * MN, m = rm / p.N, n = rm - m * p.N;
         float acc = 0.0f;
-        for (int64_t r = 0; r < R; r++) acc = small_fma(p, ob, m, n, r, acc);
+        int64_t r = 0;
+        if (!p.reduce) {
+            // four terms' operands loaded before their multiply-adds (added in order: r ascending)
+            const int64_t ba = p.sA ? ob : 0, bb = p.sB ? ob : 0;
+            for (; r + 4 <= R; r += 4) {
+                float a[4], b[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) a[u] = op_a(p, ba, m, r + u), b[u] = op_b(p, bb, r + u, n);
+#pragma unroll
+                for (int u = 0; u < 4; u++) acc = fmaf(a[u], b[u], acc);
+            }
+        }
+        for (; r < R; r++) acc = small_fma(p, ob, m, n, r, acc);
         float *c = p.C + ob * p.sC + m * p.ldc + n;
         *c = epi(p, acc, m, n, c);
     }

@@ -709,6 +709,45 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
     NCK_LAUNCHED(d, 1);
 }
 
+// y = x * (keep ? 1 / (1 - p) : 0) from a drawn keep mask: float4 items with all of a thread's loads
+// in flight before its stores, the same product as the drawing kernels' output pass
+__global__ void __launch_bounds__(256) k_dropout_apply(const float *__restrict__ x, const uint32_t *__restrict__ bits,
+                                                       float *__restrict__ y, int64_t n, float p, int vec) {
+    const float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+    const int64_t n4 = vec ? n / 4 : 0, stride = (int64_t)gridDim.x * blockDim.x;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float4 *y4 = reinterpret_cast<float4 *>(y);
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * stride) {
+        float4 v[4];
+        uint32_t m[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t i = i0 + u * stride;
+            if (i < n4) v[u] = __ldcs(x4 + i), m[u] = (__ldg(bits + (i >> 3)) >> ((i & 7) * 4)) & 15u;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t i = i0 + u * stride;
+            if (i >= n4) break;
+            v[u].x *= (m[u] & 1u) ? keepv : 0.0f;
+            v[u].y *= (m[u] & 2u) ? keepv : 0.0f;
+            v[u].z *= (m[u] & 4u) ? keepv : 0.0f;
+            v[u].w *= (m[u] & 8u) ? keepv : 0.0f;
+            __stcs(y4 + i, v[u]);
+        }
+    }
+    for (int64_t e = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += stride)
+        y[e] = x[e] * ((__ldg(bits + (e >> 5)) >> (e & 31)) & 1u ? keepv : 0.0f);
+}
+
+extern "C" void nck_dropout_apply(nck_dev *d, const float *x, const uint32_t *bits, float *y, int64_t n, float p) {
+    if (n <= 0) return;
+    Scope sc(d, "dropout", 0.0, 8.0 * n + n / 8.0);
+    const int vec = (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+    k_dropout_apply<<<grid_for(d, vec ? n / 16 + 1 : n), 256, 0, NCK_STREAM(d)>>>(x, bits, y, n, p, vec);
+    NCK_LAUNCHED(d, 1);
+}
+
 __global__ void k_dropout_bwd(const float *__restrict__ g, const uint32_t *__restrict__ bits, float *__restrict__ gi,
                               int64_t n, float p, int acc) {
     float keepv = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
@@ -948,22 +987,6 @@ extern "C" void nck_bn_fwd_train(nck_dev *d, const float *x, const float *w, con
 // store it) straight from the BatchNorm input: each element of a window is normalised and activated
 // in registers (the same arithmetic as k_bn_norm), so the full-size normalised and activated tensors
 // are never written. Even H and W (every window whole).
-// a pooled element's window position: plane, output row and column, the window's first input index
-struct PoolPos {
-    uint32_t pl, c, oy, ox;
-};
-
-__device__ __forceinline__ PoolPos pool_pos(uint32_t t, uint32_t C, uint32_t OW, const FastDiv &dow,
-                                            const FastDiv &doh, const FastDiv &dc, uint32_t OH) {
-    PoolPos q;
-    const uint32_t r = dow.div(t);
-    q.ox = t - r * OW, q.pl = doh.div(r), q.oy = r - q.pl * OH;
-    q.c = q.pl - dc.div(q.pl) * C;
-    return q;
-}
-
-constexpr int kPoolIlp = 4;  // windows per thread with every load issued before the first is used
-
 __global__ void __launch_bounds__(256) k_bn_act_pool2x2(const float *__restrict__ x, const float *__restrict__ w,
                                                         const float *__restrict__ b, const float *__restrict__ mean,
                                                         const float *__restrict__ invstd, int act, float act_s,
@@ -971,37 +994,26 @@ __global__ void __launch_bounds__(256) k_bn_act_pool2x2(const float *__restrict_
                                                         float *__restrict__ xarg, uint32_t planes, uint32_t C,
                                                         uint32_t W, uint32_t OH, uint32_t OW, FastDiv dow,
                                                         FastDiv doh, FastDiv dc) {
-    const uint32_t total = planes * OH * OW, stride = gridDim.x * blockDim.x;
-    for (uint32_t t0 = blockIdx.x * blockDim.x + threadIdx.x; t0 < total; t0 += kPoolIlp * stride) {
-        float2 p[kPoolIlp], q[kPoolIlp];
-        PoolPos pos[kPoolIlp];
-#pragma unroll
-        for (int u = 0; u < kPoolIlp; u++) {
-            const uint32_t t = t0 + u * stride;
-            if (t >= total) break;
-            pos[u] = pool_pos(t, C, OW, dow, doh, dc, OH);
-            const float *r0 = x + (size_t)pos[u].pl * (2 * OH) * W + (size_t)(2 * pos[u].oy) * W + 2 * pos[u].ox;
-            p[u] = __ldg(reinterpret_cast<const float2 *>(r0));
-            q[u] = __ldg(reinterpret_cast<const float2 *>(r0 + W));
-        }
-#pragma unroll
-        for (int u = 0; u < kPoolIlp; u++) {
-            const uint32_t t = t0 + u * stride;
-            if (t >= total) break;
-            const uint32_t c = pos[u].c;
-            const float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
-            const float v0 = epi_fwd(act, act_s, p[u].x * a + dd), v1 = epi_fwd(act, act_s, p[u].y * a + dd);
-            const float v2 = epi_fwd(act, act_s, q[u].x * a + dd), v3 = epi_fwd(act, act_s, q[u].y * a + dd);
-            const int32_t i0 = (int32_t)(2 * pos[u].oy * W + 2 * pos[u].ox);
-            float best = v0, bx = p[u].x;
-            int32_t bi = i0;
-            if (v1 > best) best = v1, bi = i0 + 1, bx = p[u].y;
-            if (v2 > best) best = v2, bi = i0 + (int32_t)W, bx = q[u].x;
-            if (v3 > best) best = v3, bi = i0 + (int32_t)W + 1, bx = q[u].y;
-            y[t] = best;
-            arg[t] = bi;
-            if (xarg) xarg[t] = bx;
-        }
+    const uint32_t total = planes * OH * OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
+        const uint32_t c = pl - dc.div(pl) * C;
+        const float a = __ldg(w + c) * __ldg(invstd + c), dd = __ldg(b + c) - __ldg(mean + c) * a;
+        const uint32_t H = 2 * OH;
+        const float *r0 = x + (size_t)pl * H * W + (size_t)(2 * oy) * W + 2 * ox;
+        const float2 p = __ldg(reinterpret_cast<const float2 *>(r0));
+        const float2 q = __ldg(reinterpret_cast<const float2 *>(r0 + W));
+        const float v0 = epi_fwd(act, act_s, p.x * a + dd), v1 = epi_fwd(act, act_s, p.y * a + dd);
+        const float v2 = epi_fwd(act, act_s, q.x * a + dd), v3 = epi_fwd(act, act_s, q.y * a + dd);
+        const int32_t i0 = (int32_t)(2 * oy * W + 2 * ox);
+        float best = v0, bx = p.x;
+        int32_t bi = i0;
+        if (v1 > best) best = v1, bi = i0 + 1, bx = p.y;
+        if (v2 > best) best = v2, bi = i0 + (int32_t)W, bx = q.x;
+        if (v3 > best) best = v3, bi = i0 + (int32_t)W + 1, bx = q.y;
+        y[t] = best;
+        arg[t] = bi;
+        if (xarg) xarg[t] = bx;
     }
 }
 
@@ -1341,51 +1353,35 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_dx(const float *__restrict_
                                                         float *__restrict__ gx, int acc, uint32_t planes, uint32_t C,
                                                         uint32_t W, uint32_t OH, uint32_t OW, FastDiv dow,
                                                         FastDiv doh, FastDiv dc) {
-    const uint32_t total = planes * OH * OW, stride = gridDim.x * blockDim.x;
-    for (uint32_t t0 = blockIdx.x * blockDim.x + threadIdx.x; t0 < total; t0 += kPoolIlp * stride) {
-        float2 p[kPoolIlp], q[kPoolIlp];
-        float gv[kPoolIlp];
-        int32_t av[kPoolIlp];
-        PoolPos pos[kPoolIlp];
+    const uint32_t total = planes * OH * OW;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const uint32_t r = dow.div(t), ox = t - r * OW, pl = doh.div(r), oy = r - pl * OH;
+        const uint32_t c = pl - dc.div(pl) * C;
+        const float mu = __ldg(mean + c), is = __ldg(invstd + c), k = __ldg(w + c) * is;
+        const float ea = k, ed = __ldg(b + c) - mu * ea;
+        const float mg = __ldg(coef + 2 * c), mgx = __ldg(coef + 2 * c + 1);
+        const size_t base = (size_t)pl * (2 * OH) * W + (size_t)(2 * oy) * W + 2 * ox;
+        const float2 p = __ldg(reinterpret_cast<const float2 *>(x + base));
+        const float2 q = __ldg(reinterpret_cast<const float2 *>(x + base + W));
+        const int32_t a = __ldg(arg + t) - (int32_t)(2 * oy * W + 2 * ox); // 0, 1, W or W + 1
+        const float xs[4] = {p.x, p.y, q.x, q.y};
+        const int32_t at[4] = {0, 1, (int32_t)W, (int32_t)W + 1};
+        const float gval = __ldg(gp + t);
+        float o[4];
 #pragma unroll
-        for (int u = 0; u < kPoolIlp; u++) {
-            const uint32_t t = t0 + u * stride;
-            if (t >= total) break;
-            pos[u] = pool_pos(t, C, OW, dow, doh, dc, OH);
-            const size_t base = (size_t)pos[u].pl * (2 * OH) * W + (size_t)(2 * pos[u].oy) * W + 2 * pos[u].ox;
-            p[u] = __ldg(reinterpret_cast<const float2 *>(x + base));
-            q[u] = __ldg(reinterpret_cast<const float2 *>(x + base + W));
-            av[u] = __ldg(arg + t);
-            gv[u] = __ldg(gp + t);
+        for (int e = 0; e < 4; e++) {
+            const float ge = at[e] == a ? epi_grad(act, act_s, xs[e] * ea + ed, gval) : 0.0f;
+            o[e] = k * (ge - mg - (xs[e] - mu) * is * mgx);
         }
-#pragma unroll
-        for (int u = 0; u < kPoolIlp; u++) {
-            const uint32_t t = t0 + u * stride;
-            if (t >= total) break;
-            const uint32_t c = pos[u].c, oy = pos[u].oy, ox = pos[u].ox;
-            const float mu = __ldg(mean + c), is = __ldg(invstd + c), k = __ldg(w + c) * is;
-            const float ea = k, ed = __ldg(b + c) - mu * ea;
-            const float mg = __ldg(coef + 2 * c), mgx = __ldg(coef + 2 * c + 1);
-            const size_t base = (size_t)pos[u].pl * (2 * OH) * W + (size_t)(2 * oy) * W + 2 * ox;
-            const int32_t a = av[u] - (int32_t)(2 * oy * W + 2 * ox);  // 0, 1, W or W + 1
-            const float xs[4] = {p[u].x, p[u].y, q[u].x, q[u].y};
-            const int32_t at[4] = {0, 1, (int32_t)W, (int32_t)W + 1};
-            float o[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float ge = at[e] == a ? epi_grad(act, act_s, xs[e] * ea + ed, gv[u]) : 0.0f;
-                o[e] = k * (ge - mg - (xs[e] - mu) * is * mgx);
-            }
-            float2 *d0 = reinterpret_cast<float2 *>(gx + base), *d1 = reinterpret_cast<float2 *>(gx + base + W);
-            if (acc) {
-                const float2 uu = *d0, vv = *d1;
-                o[0] = uu.x + o[0], o[1] = uu.y + o[1], o[2] = vv.x + o[2], o[3] = vv.y + o[3];
-            } else {
-                o[0] = 0.0f + o[0], o[1] = 0.0f + o[1], o[2] = 0.0f + o[2], o[3] = 0.0f + o[3];
-            }
-            *d0 = make_float2(o[0], o[1]);
-            *d1 = make_float2(o[2], o[3]);
+        float2 *d0 = reinterpret_cast<float2 *>(gx + base), *d1 = reinterpret_cast<float2 *>(gx + base + W);
+        if (acc) {
+            const float2 u = *d0, v = *d1;
+            o[0] = u.x + o[0], o[1] = u.y + o[1], o[2] = v.x + o[2], o[3] = v.y + o[3];
+        } else {
+            o[0] = 0.0f + o[0], o[1] = 0.0f + o[1], o[2] = 0.0f + o[2], o[3] = 0.0f + o[3];
         }
+        *d0 = make_float2(o[0], o[1]);
+        *d1 = make_float2(o[2], o[3]);
     }
 }
 

@@ -206,8 +206,16 @@ __global__ void k_colsum_partial(const float *__restrict__ x, float *__restrict_
     int64_t n = blockIdx.x * 32 + threadIdx.x;
     int64_t m0 = blockIdx.y * rows_per_split, m1 = m0 + rows_per_split < M ? m0 + rows_per_split : M;
     float acc = 0.0f;
-    if (n < N)
-        for (int64_t m = m0 + threadIdx.y; m < m1; m += kColRows) acc += x[m * N + n];
+    if (n < N) {
+        // four rows' loads in flight, added in row order
+        int64_t m = m0 + threadIdx.y;
+        for (; m + 3 * kColRows < m1; m += 4 * kColRows) {
+            const float v0 = __ldg(x + m * N + n), v1 = __ldg(x + (m + kColRows) * N + n);
+            const float v2 = __ldg(x + (m + 2 * kColRows) * N + n), v3 = __ldg(x + (m + 3 * kColRows) * N + n);
+            acc += v0, acc += v1, acc += v2, acc += v3;
+        }
+        for (; m < m1; m += kColRows) acc += __ldg(x + m * N + n);
+    }
     sm[threadIdx.y][threadIdx.x] = acc;
     __syncthreads();
     if (threadIdx.y == 0 && n < N) {

@@ -424,10 +424,8 @@ extern "C" int nck_gemm_tc(nck_dev *d, const nck_gemm_args *a) {
         if (splits > a->batch) splits = a->batch;
     } else if (tiles * nout < sms) {
         // no more units than SMs: one unit over the grid would run as a second wave on its own
-        // at least 8 K-stages per slice: shorter slices spend their time filling the pipeline, and
-        // every extra slice is another partial tile for the combine to read
         splits = sms / (tiles * nout);
-        int64_t cap = (a->K + 8 * TK - 1) / (8 * TK);
+        int64_t cap = (a->K + 4 * TK - 1) / (4 * TK);
         if (splits > cap) splits = cap;
     }
     if (splits > maxpart) splits = maxpart;

@@ -219,6 +219,15 @@ struct nc_ctx {
     void *ev_main;       /* cudaEvent_t: main-stream point a reduce waits for */
     void *ev_comm;       /* cudaEvent_t: comm-stream point the main stream waits for */
     int comm_pending;    /* reduces enqueued on comm_stream since the last join */
+    /* dropout keep masks drawn on a side stream (rng.c): they depend on no tensor, so they run while
+     * the main stream is still busy with earlier work; the main stream waits before each consumer */
+    void *side_stream;   /* cudaStream_t, created on first use; NULL: masks drawn on the main stream */
+    void *ev_side;       /* cudaEvent_t: a mask is drawn */
+    void *ev_step;       /* cudaEvent_t: recorded at nc_step_end, waited for by the next step's masks */
+    unsigned char *side_pool; /* device block for the step's masks and tables (bump, reset at step end) */
+    size_t side_cap, side_used;
+    int side_fresh;      /* no mask drawn yet this step: wait for ev_step first */
+    int side_off;        /* NC_RNG_SIDE=0, or set-up failed */
     struct nc_optim *optims; /* optimizers of this context (intrusive list) */
     /* data parallel BatchNorm: each training forward stages its batch (mean, unbiased variance) here;
      * nc__dp_bn_flush gathers every rank's and applies the running-statistic updates in rank order */
@@ -258,11 +267,22 @@ const uint64_t *nc__rng_run_polys(int64_t count);          /* x^(64 k) mod P, k 
 const void *nc__rng_dropout_table(nc_ctx *ctx, int64_t n); /* the same on the device, or NULL */
 /* the dropout kernel's Horner window tables for the current state, on the device (32 KiB), or NULL */
 const void *nc__rng_dropout_tabs(nc_ctx *ctx);
+/* the window tables for state s0 on the host: 1024 entries of four words */
+void nc__rng_build_tabs(const uint64_t s0[4], uint64_t (*tab)[4]);
 
 void nc__detect_cpu(nc_cpu_info *info);
 
 /* host <-> device */
 void nc__upload(nc_ctx *ctx, void *dst, const void *src, size_t bytes);
+/* the same on another stream of the context (void * = cudaStream_t) */
+void nc__upload_on(nc_ctx *ctx, void *stream, void *dst, const void *src, size_t bytes);
+/* Draws the keep mask of the stream's next n draws (threshold p) on the side stream into a block of
+ * the step's side pool and makes the main stream wait for it; *bits receives the block. Returns 0
+ * (nothing drawn) when the side stream is off, per-kernel timing is on or the pool is full: the
+ * caller draws on the main stream. The caller advances the stream past the n draws either way. */
+int nc__rng_side_mask(nc_ctx *ctx, int64_t n, float p, uint32_t **bits);
+void nc__rng_side_step_end(nc_ctx *ctx);
+void nc__rng_side_free(nc_ctx *ctx);
 void nc__download(nc_ctx *ctx, void *dst, const void *src, size_t bytes); /* synchronous */
 
 /* ---- tensor helpers --------------------------------------------------------------------------- */

@@ -159,6 +159,8 @@ void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float *x, float 
 /* device copy of x^(64 k) mod P for k < count from the host table (uploaded once, grown on demand) */
 const void *nck_rng_polys(nck_dev *d, const uint64_t *host, int64_t count);
 void nck_dropout_bwd(nck_dev *d, const float *g, const uint32_t *bits, float *gi, int64_t n, float p, int acc);
+/* y = x * (keep ? 1 / (1 - p) : 0) from a keep mask drawn by nck_dropout_fwd (x = y = NULL) */
+void nck_dropout_apply(nck_dev *d, const float *x, const uint32_t *bits, float *y, int64_t n, float p);
 
 /* Attention over B independent heads: scores S = Q K^T (FFMA, d in order), masked_fill where the mask is
  * nonzero, row softmax, inverted dropout, and the product with V. Operands are strided views, element
@@ -311,6 +313,8 @@ int nck_convtap(nck_dev *d, int mode, const nck_conv *g, const nck_tapgeom *t, c
 int nck_conv_direct_dw(nck_dev *d, const nck_conv *g, const float *x, const float *gy, float *gw, float *gb);
 /* whether nck_conv_direct_dw takes the 3x3 one-channel kernel (and can add the bias gradient) */
 int nck_conv_direct3_ok(const nck_conv *g);
+/* nck_conv_direct_dw also sums the bias gradient for this geometry (when given gb) */
+int nck_conv_direct_dw_bias_ok(const nck_conv *g);
 /* depthwise (groups == C == OC): shared-memory plane tiles; nck_dw_ok says whether a geometry fits
  * them (at most NCK_DW_MAX_TAPS taps, tiles within shared memory) */
 #define NCK_DW_MAX_TAPS 25

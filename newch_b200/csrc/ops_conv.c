@@ -99,7 +99,11 @@ static int is_depthwise(const nck_conv *g) { return g->G == g->C && g->OC == g->
 static int is_pointwise(const nck_conv *g) {
     return g->KH == 1 && g->KW == 1 && g->sh == 1 && g->sw == 1 && g->ph == 0 && g->pw == 0;
 }
-static int use_direct(const nck_conv *g) { return (g->C / g->G) * g->KH * g->KW <= 32 && g->OC / g->G <= 64; }
+/* few taps per group: the direct kernels (a 1x1 convolution over 16 or more channels is a GEMM of
+ * real depth and goes to the tensor cores instead) */
+static int use_direct(const nck_conv *g) {
+    return (g->C / g->G) * g->KH * g->KW <= 32 && g->OC / g->G <= 64 && !(is_pointwise(g) && g->C / g->G >= 16);
+}
 
 /* samples per im2col chunk: the unfolded buffer stays under 256 MiB */
 static int64_t chunk_samples(const nck_conv *g) {
@@ -248,7 +252,7 @@ static void conv_bwd(nc_node *n) {
     const int direct_dw = gw && use_direct(&g) && !is_depthwise(&g);
     const int tap = !is_depthwise(&g) && !is_pointwise(&g) && ((gw && !direct_dw) || gx) &&
                     nck_convtap_plan(nc__k(ctx), &g, &tg);
-    float *gb_direct = gb && direct_dw && nck_conv_direct3_ok(&g) ? (float *)gb->data : NULL;
+    float *gb_direct = gb && direct_dw && nck_conv_direct_dw_bias_ok(&g) ? (float *)gb->data : NULL;
     float *gb_tap = gb && !gb_direct && tap && nck_tap_pack_colsum_ok(nc__k(ctx), &tg, tg.OCp) ? (float *)gb->data : NULL;
     /* depthwise: the weight-gradient pass also sums the bias gradient */
     float *gb_dw = gb && gw && is_depthwise(&g) ? (float *)gb->data : NULL;

@@ -157,13 +157,15 @@ static nc_status dropout_fwd(nc_node *n) {
     int64_t N = nc_numel(n->out);
     int64_t words = (N + 31) / 32 + 1;
     if (nc__attn_dropout_ok(n->in[0])) { /* attention probabilities: draw the mask only, extend the recipe */
-        uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
-        if (!bits) return NC_ERR_OOM;
-        if (N) {
+        uint32_t *bits = NULL;
+        if (N && !nc__rng_side_mask(ctx, N, n->p.f[0], &bits)) {
+            bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
+            if (!bits) return NC_ERR_OOM;
             const void *polys = nc__rng_dropout_table(ctx, N);
             nck_dropout_fwd(nc__k(ctx), ctx->rng, NULL, NULL, bits, N, n->p.f[0], polys,
                             polys ? nc__rng_dropout_tabs(ctx) : NULL);
         }
+        if (!bits && !(bits = (uint32_t *)nc__arena_alloc(ctx, sizeof(uint32_t)))) return NC_ERR_OOM;
         nc__rng_skip(ctx, (uint64_t)N);
         n->saved = bits;
         if (nc__attn_dropout(n, bits)) return NC_OK;
@@ -171,12 +173,18 @@ static nc_status dropout_fwd(nc_node *n) {
         return NC_ERR_OOM;
     }
     const float *x = nc__contig_f32(n->in[0]);
-    uint32_t *bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
-    if (!x || !bits) return NC_ERR_OOM;
-    if (N) {
-        const void *polys = nc__rng_dropout_table(ctx, N);
-        nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0], polys,
-                        polys ? nc__rng_dropout_tabs(ctx) : NULL);
+    if (!x) return NC_ERR_OOM;
+    uint32_t *bits = NULL;
+    if (N && nc__rng_side_mask(ctx, N, n->p.f[0], &bits)) { /* mask drawn on the side stream */
+        nck_dropout_apply(nc__k(ctx), x, bits, (float *)n->out->data, N, n->p.f[0]);
+    } else {
+        bits = (uint32_t *)nc__arena_alloc(ctx, (size_t)words * sizeof(uint32_t));
+        if (!bits) return NC_ERR_OOM;
+        if (N) {
+            const void *polys = nc__rng_dropout_table(ctx, N);
+            nck_dropout_fwd(nc__k(ctx), ctx->rng, x, (float *)n->out->data, bits, N, n->p.f[0], polys,
+                            polys ? nc__rng_dropout_tabs(ctx) : NULL);
+        }
     }
     nc__rng_skip(ctx, (uint64_t)N);
     n->saved = bits;

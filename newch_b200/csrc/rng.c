@@ -263,11 +263,10 @@ const uint64_t *nc__rng_run_polys(int64_t count) {
  * 64 j + i steps past s, so 256 steps of a copy of the state give every term. Built here instead of
  * by a one-block kernel in front of every dropout launch; the block comes from the step arena and
  * reaches the device through the pinned staging ring. */
-const void *nc__rng_dropout_tabs(nc_ctx *ctx) {
-    uint64_t states[256][4];          /* 8 KiB */
-    uint64_t tab[4 * 16 * 16][4];     /* 32 KiB, copied into the staging ring before the return */
+void nc__rng_build_tabs(const uint64_t s0[4], uint64_t (*tab)[4]) {
+    uint64_t states[256][4]; /* 8 KiB */
     uint64_t st[4];
-    memcpy(st, ctx->rng, sizeof st);
+    memcpy(st, s0, sizeof st);
     for (int i = 0; i < 256; i++) {
         memcpy(states[i], st, sizeof st);
         step(st);
@@ -280,6 +279,11 @@ const void *nc__rng_dropout_tabs(nc_ctx *ctx) {
                 for (int q = 0; q < 4; q++) a[q] ^= states[64 * j + 4 * w + t][q];
         memcpy(tab[e], a, sizeof a);
     }
+}
+
+const void *nc__rng_dropout_tabs(nc_ctx *ctx) {
+    uint64_t tab[4 * 16 * 16][4]; /* 32 KiB, copied into the staging ring before the return */
+    nc__rng_build_tabs(ctx->rng, tab);
     void *dev = nc__arena_alloc(ctx, sizeof tab);
     if (!dev) return NULL;
     nc__upload(ctx, dev, tab, sizeof tab);

@@ -92,3 +92,18 @@ def test_chains_unfused(case, monkeypatch):
     for k in out:
         ref = GOLD[f"{case}/{k}"]
         assert rel_err(out[k], ref) <= TOL, (case, k)
+
+
+@pytest.mark.parametrize("case", ["dropout", "attention_chain", "attention_mha_128"])
+def test_masks_on_the_main_stream(case, monkeypatch):
+    """NC_RNG_SIDE=0: dropout masks drawn on the main stream instead of the side stream, held to the
+    same goldens (bit-exact where test_op_matches_reference is)."""
+    monkeypatch.setenv("NC_RNG_SIDE", "0")
+    out = run_case("b200", case)
+    exact = EXACT.get(case, set())
+    for k in out:
+        ref = GOLD[f"{case}/{k}"]
+        if k in exact:
+            assert np.array_equal(out[k], ref, equal_nan=True), (case, k)
+        else:
+            assert rel_err(out[k], ref) <= TOL, (case, k)
