@@ -61,6 +61,8 @@ DATA = {"cfg1": "synthetic (seeded uint8 images [B,1,28,28], 10 uniform labels)"
         "cfg5": "synthetic (seeded N(0,1) activations [8192,1024])"}
 SETUP_DRIVER = "recorded newch call sequence replayed through the nc.h C ABI"
 L2_NOTE = "flushed between timed steps (256 MiB write, outside the timed events)"
+INPUTS_NOTE = ("value: the step's host-data uploads (nc_from_data) made once before the timed region, inputs "
+               "resident in HBM; e2e: every step uploads its batch from pinned host memory and reads its result")
 
 
 def config_dict(cfg: str, world: int) -> dict:
@@ -130,8 +132,22 @@ def load_peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "sm_max_mhz": d.get("sm_max_mhz", 1965.0),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "sm_max_mhz": 1965.0, "src": "fallback"}
+
+
+def compute_roof(scope: str, peaks: dict):
+    """The arithmetic roof of a timed scope: (TFLOP/s, bound, how it is derived). The tensor roofs scale
+    the measured bf16 GEMM by the dense-rate ratios of the B200's tensor cores (TF32 1/2, int8 2x);
+    CUDA-core kernels (FFMA) take 128 fp32 FMAs per clock per SM on 148 SMs at the maximum clock."""
+    b = peaks["bf16_tflops"]
+    if scope.startswith("qgemm_i8"):
+        return 2.0 * b, "tensor", "int8 tensor roof = 2 x measured bf16 (dense-rate ratio)"
+    if "tf32" in scope or scope.startswith("conv_tap"):
+        return 0.5 * b, "tensor", ("tf32 tensor roof = measured bf16 / 2 (dense-rate ratio); 3xTF32 issues three "
+                                   "TF32 products per fp32 product, so its useful-FLOP ceiling is a third of it")
+    return 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12, "fp32", "fp32 CUDA-core roof (148 SMs x 128 FMA/clk)"
 
 
 def step_io_bytes(trace: replay.Trace, start: int, end: int):
@@ -154,7 +170,8 @@ class Run:
     """A trace replayed on the B200 engine: prologue and recorded steps once, then the last recorded
     step repeated."""
 
-    def __init__(self, lib, trace_name: str, rank: int, world: int, pg, pinned: bool = False):
+    def __init__(self, lib, trace_name: str, rank: int, world: int, pg, pinned: bool = False,
+                 resident: bool = False):
         self.lib = lib
         self.name = trace_name
         self.trace = replay.Trace(trace_name)
@@ -168,6 +185,9 @@ class Run:
         steps = self.trace.steps()
         self.rep.run(1, steps[-1][1])  # model set-up and every recorded step
         self.step = steps[-1]
+        # resident: the repeated step's host-data uploads (nc_from_data) are made once here, so the
+        # timed steps start with their inputs in HBM
+        self.resident_bytes = self.rep.make_resident(*self.step) if resident else 0
 
     def one(self):
         self.rep.run(*self.step)
@@ -220,14 +240,15 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     per_launch_ms = ms / max(cnt, 1)
     # the binding roof: a kernel with FLOPs is tensor-bound only when its arithmetic takes longer at the
     # tensor peak than its algorithmic bytes take at the HBM peak
-    t_tensor = fl / (peaks["bf16_tflops"] * 1e12)
+    cpeak, cbound, cnote = compute_roof(name, peaks)
+    t_compute = fl / (cpeak * 1e12)
     t_hbm = by / (peaks["hbm_gbs"] * 1e9)
-    if fl > 0 and t_tensor >= t_hbm:
+    if fl > 0 and t_compute >= t_hbm:
         achieved = fl / max(cnt, 1) / (per_launch_ms / 1e3) / 1e12
-        peak, unit, bound = peaks["bf16_tflops"], "TFLOP/s", "tensor"
+        peak, unit, bound, note = round(cpeak, 1), "TFLOP/s", cbound, cnote
     else:
         achieved = by / max(cnt, 1) / (per_launch_ms / 1e3) / 1e9
-        peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        peak, unit, bound, note = peaks["hbm_gbs"], "GB/s", "hbm", "measured HBM copy bandwidth"
     # DRAM bytes per call of this scope in this workload, from one-kernel ncu captures (profiles/)
     traffic = None
     tf = REPO / "profiles" / "traffic.json"
@@ -236,7 +257,7 @@ def roofline(run: Run, peaks: dict, steps: int = 3) -> dict:
     kernels = sorted(table, key=lambda t: -t[1])[:16]
     sec = max(per_launch_ms, 1e-9) / 1e3
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-            "frac": round(achieved / peak, 4), "traffic": traffic, "peak_src": peaks["src"] + " (MEASURED_PEAKS.json)",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "peak_src": peaks["src"] + " (MEASURED_PEAKS.json): " + note,
             "algorithmic_bytes_per_launch": round(by / max(cnt, 1)), "flops_per_launch": round(fl / max(cnt, 1)),
             "achieved_gbs": round(by / max(cnt, 1) / sec / 1e9, 1),
             "achieved_tflops": round(fl / max(cnt, 1) / sec / 1e12, 2),
@@ -286,7 +307,7 @@ def measure(lib, cfg: str, rank: int, world: int, pg, local: int, steps: int, wa
     import torch
     import torch.distributed as dist
     batch = BATCH.get(cfg, 1)
-    run = Run(lib, cfg, rank, world, pg)
+    run = Run(lib, cfg, rank, world, pg, resident=True)
     stream = torch.cuda.ExternalStream(lib.nc_ext_stream(run.ctx), device=torch.device("cuda", local))
     for _ in range(warmup):
         run.one()
@@ -309,10 +330,11 @@ def measure(lib, cfg: str, rank: int, world: int, pg, local: int, steps: int, wa
     res = {"value": round(batch * world * steps / secs, 3), "unit": UNIT.get(cfg, "samples/s"),
            "ms_per_step": round(1e3 * secs / steps, 4), "steps": steps, "warmup": warmup,
            "gpu_launches": int(launches), "gemm": lib.nc_ext_gemm_mode(run.ctx).decode(),
-           "config": config_dict(cfg, world)}
+           "config": config_dict(cfg, world), "resident_input_bytes": run.resident_bytes}
     if extras:
+        # end to end: the step's batch uploaded from pinned host memory through the public calls
         et = E2E_TRACE.get(cfg, cfg)
-        erun = run if et == cfg else Run(lib, et, rank, world, pg, pinned=True)
+        erun = Run(lib, et, rank, world, pg, pinned=True)
         estream = torch.cuda.ExternalStream(lib.nc_ext_stream(erun.ctx), device=torch.device("cuda", local))
         for _ in range(max(warmup, 3)):
             erun.one()
@@ -326,8 +348,8 @@ def measure(lib, cfg: str, rank: int, world: int, pg, local: int, steps: int, wa
                       "d2h_bytes_per_step": d2h, "trace": et, "steps": ek,
                       "timing": "host wall clock around each step's public calls, to the device finishing",
                       "value_device_events": round(batch * world * ek / edev, 3)}
-        if erun is not run:
-            lib.nc_free_ctx(erun.ctx)
+        lib.nc_ext_synchronize(erun.ctx)
+        lib.nc_free_ctx(erun.ctx)
         # every rank steps (each step all-reduces gradients); rank 0 reports its kernel table
         res["roofline"] = roofline(run, load_peaks())
         res["cpu_baseline"] = None
@@ -412,7 +434,7 @@ def main() -> int:
                "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA.get(cfg, "synthetic"),
                "config": config_dict(cfg, world),
-               "setup": {"gemm": head["gemm"], "l2": L2_NOTE, "driver": SETUP_DRIVER},
+               "setup": {"gemm": head["gemm"], "l2": L2_NOTE, "driver": SETUP_DRIVER, "inputs": INPUTS_NOTE},
                "gpu_launches": head["gpu_launches"], "clocks": clk.summary(), "e2e": head.get("e2e"),
                "roofline": head.get("roofline"), "cpu_baseline": head.get("cpu_baseline"), "configs": others}
         print(json.dumps(out), flush=True)

@@ -124,6 +124,8 @@ class Replayer:
         self.params_after: list = []
         self.param_shapes: list = []  # shapes of the optimizer's parameters, taken when it is created
         self._steps_done = 0
+        self._resident: dict = {}  # call index -> device tensor made once (make_resident)
+        self._resident_ptrs: set = set()
         self._fns = {name: getattr(lib, name) for name in {c[0] for c in trace.calls}}
         self._prepared = [self._prepare(i, c) for i, c in enumerate(trace.calls)]
 
@@ -191,13 +193,42 @@ class Replayer:
         out_h = extra.get("out_h") if isinstance(extra, dict) else None
         return (fn, name, conv, ret_h, ret_null, out_h)
 
+    def make_resident(self, start: int, end: int) -> int:
+        """Inputs resident on the device: every nc_from_data call of calls [start, end) that uploads host
+        data is made once now, between nc_persistent_begin/end, and later runs of the range hand its
+        tensor to the following calls instead of uploading again (its releases inside the range are
+        skipped). Returns the bytes made resident."""
+        ctx, total = self.ctx, 0
+        for i in range(start, end):
+            fn, name, conv, ret_h, ret_null, out_h = self._prepared[i]
+            if name != "nc_from_data" or ret_h is None or not any(isinstance(a, dict) and "b" in a
+                                                                  for a in self.trace.calls[i][1]):
+                continue
+            self.lib.nc_persistent_begin(ctx)
+            try:
+                self.run(i, i + 1)
+            finally:
+                self.lib.nc_persistent_end(ctx)
+            self._resident[i] = self.h[ret_h]
+            total += int(self.lib.nc_numel(self.h[ret_h])) * {0: 4, 1: 4, 2: 2, 3: 1, 4: 1}[
+                int(self.lib.nc_get_dtype(self.h[ret_h]))]
+        self._resident_ptrs = set(self._resident.values())
+        return total
+
     # -- execution --------------------------------------------------------------------------
     def run(self, start: int = 0, end: int | None = None) -> None:
         h = self.h
         prepared = self._prepared
+        resident, rptrs = self._resident, self._resident_ptrs
         end = len(prepared) if end is None else end
         for i in range(start, end):
             fn, name, conv, ret_h, ret_null, out_h = prepared[i]
+            if resident:
+                if i in resident:
+                    h[ret_h] = resident[i]
+                    continue
+                if name in ("nc_release", "nc_release_temp") and conv and conv[0][0] == 1 and h[conv[0][1]] in rptrs:
+                    continue
             vals = []
             outbuf = None
             for kind, v in conv:

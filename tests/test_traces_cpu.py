@@ -56,3 +56,24 @@ def test_trace_structure(name):
                 assert a["h"] in made or a["h"] in inside
         if isinstance(c[2], dict) and "h" in c[2]:
             inside.add(c[2]["h"])
+
+
+@pytest.mark.parametrize("name", ["cfg3_small", "cfg5_small"])
+def test_resident_inputs_replay_the_same_step(name):
+    """The benchmark's resident-input mode (the repeated step's nc_from_data uploads made once, before
+    timing) gives the step the same results as uploading every time."""
+    lib = capi.load(REF_LIB)
+    t = replay.Trace(name)
+    s = t.steps()[-1]
+    runs = []
+    for resident in (False, True):
+        r = replay.Replayer(lib, t)
+        r.run(0, s[1])
+        made = r.make_resident(*s) if resident else 0
+        assert (made > 0) == resident
+        n0 = len(r.items), len(r.outputs)
+        for _ in range(2):
+            r.run(*s)
+        runs.append(([v for _, v in r.items[n0[0]:]], [b for _, b in r.outputs[n0[1]:]]))
+        lib.nc_free_ctx(r.ctx)
+    assert runs[0] == runs[1]
