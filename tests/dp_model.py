@@ -2,10 +2,13 @@
 parity test (tests/test_gpu_dp.py): the reference engine runs it with gradient accumulation over the
 ranks' micro-batches, each B200 rank runs its own micro-batch of every step.
 
-Model (config 2's first block at a small size): Conv2d(1, 8, 3, p=1)+bias -> BatchNorm2d(8) -> ReLU ->
+Model (config 2's first block at a small size): Conv2d(1, 8, 3, p=1, no bias) -> BatchNorm2d(8) -> ReLU ->
 MaxPool2d(2) -> flatten -> Dropout(0.25) -> Linear(1568, 10) -> cross_entropy; AdamW lr 1e-3,
 weight decay 0.01. Initial weights come from the context's seeded stream, so every engine and every
-rank starts from the same ones.
+rank starts from the same ones. The convolution has no bias: a bias in front of BatchNorm gets only a
+rounding-noise gradient, Adam moves it by lr times the sign of that noise, and the BatchNorm running
+mean tracks the bias, so it would compare the two engines' rounding noise rather than the data-parallel
+update.
 
 Run as a script, it is one B200 rank of a data-parallel group (the engine joins the group from the
 NC_RANK / NC_WORLD_SIZE / NC_NCCL_ID_FILE environment at nc_init) and writes its results to the
@@ -46,7 +49,7 @@ def _uniform_param(e: Eng, shape, bound):
 def build(e: Eng):
     L = e.L
     L.nc_persistent_begin(e.ctx)
-    p = {"conv_w": _uniform_param(e, (C1, 1, 3, 3), 1 / 3), "conv_b": _uniform_param(e, (C1,), 1 / 3),
+    p = {"conv_w": _uniform_param(e, (C1, 1, 3, 3), 1 / 3),
          "bn_w": e.check(L.nc_parameter(e.ctx, e.t(np.ones(C1, np.float32)), *capi.shape_arg((C1,)))),
          "bn_b": e.check(L.nc_parameter(e.ctx, None, *capi.shape_arg((C1,)))),
          "fc_w": _uniform_param(e, (10, FLAT), FLAT ** -0.5), "fc_b": _uniform_param(e, (10,), FLAT ** -0.5)}
@@ -60,7 +63,7 @@ def build(e: Eng):
 
 def forward_loss(e: Eng, p, stats, x, y):
     L = e.L
-    h = e.check(L.nc_conv2d_ex(e.t(x), p["conv_w"], p["conv_b"], 1, 1, 1, 1, 1, 1, 1))
+    h = e.check(L.nc_conv2d_ex(e.t(x), p["conv_w"], None, 1, 1, 1, 1, 1, 1, 1))
     h = e.check(L.nc_batch_norm(h, p["bn_w"], p["bn_b"], stats["bn_rm"], stats["bn_rv"], 1, 0.1, 1e-5))
     h = e.check(L.nc_max_pool2d(e.check(L.nc_relu(h)), 2, 2, 2, 2, 0, 0))
     h = e.check(L.nc_reshape(h, *capi.shape_arg((B, FLAT))))

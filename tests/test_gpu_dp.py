@@ -9,9 +9,8 @@ The engine reproduces each piece: rank r's dropout draws start where the referen
 draws start (nc_ext_dp_rng_stride), gradients are averaged over ranks before the update, and every
 rank applies all ranks' BatchNorm statistics to its running statistics in rank order.
 
-Runs when the box has at least two GPUs (skipped otherwise). CUDA-core GEMMs (NC_GEMM=ffma): losses
-and running statistics to 1e-5, parameters normwise to 1e-5 except the convolution bias in front of
-BatchNorm (no gradient; Adam moves it by the sign of rounding noise, at most lr per step).
+Runs when the box has at least two GPUs (skipped otherwise). CUDA-core GEMMs (NC_GEMM=ffma): losses,
+running statistics and every parameter to 1e-5 (normwise).
 """
 
 from __future__ import annotations
@@ -74,7 +73,6 @@ def test_two_ranks_match_reference_accumulation(tmp_path):
             assert rel_err(got[k], ref[k]) <= 1e-5, (r, k, got[k], ref[k])
         for k in ("conv_w", "bn_w", "bn_b", "fc_w", "fc_b"):
             assert rel_err(got[k], ref[k]) <= 1e-5, (r, k, rel_err(got[k], ref[k]))
-        assert np.all(np.abs(got["conv_b"] - ref["conv_b"]) <= 2 * 1e-3 * dp_model.STEPS + 1e-6)
     # every rank holds the same model
     for k in ranks[0]:
         if k != "losses":
