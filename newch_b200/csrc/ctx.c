@@ -383,6 +383,11 @@ nc_ctx *nc_init(const nc_config *cfg) {
         ctx->dev.gemm_small = !gs || strcmp(gs, "0") != 0;
         const char *qg = getenv("NC_QGEMM");
         ctx->dev.qgemm_tc = !qg || strcmp(qg, "dp4a") != 0;
+        /* BatchNorm channel reductions fed by bulk copies: by default the statistics pass over planes of
+         * at least 4 KiB (measured faster there); NC_BN_BULK=0 never, =8 / =16 every eligible pass in
+         * 8 / 16 KiB stages */
+        const char *bb = getenv("NC_BN_BULK");
+        ctx->dev.bn_bulk_stage = !bb ? -16384 : !strcmp(bb, "0") ? 0 : !strcmp(bb, "8") ? 8192 : 16384;
         /* exp / sigmoid / tanh / erf: newch's AVX2-tier polynomials unless the reference tier's C
          * library forms are asked for (force_reference, as newch selects its reference tier) */
         const char *fz = getenv("NC_FUSE");

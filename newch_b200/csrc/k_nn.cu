@@ -9,6 +9,7 @@
 
 #include "k_act.cuh"
 #include "k_common.cuh"
+#include "k_tcgen05.cuh"
 #include "k_math.cuh"
 
 #include <mutex>
@@ -941,9 +942,283 @@ static int64_t bn_splits(int64_t resident, int64_t N, int64_t C, int64_t S) {
 }
 
 
+// backward sums -> weight / bias gradients and the two means the input gradient needs
+struct BnBwdFin {
+    float *gw, *gb, *coef;
+    int splits;
+};
+
+__device__ void bn_bwd_finalize(const double *part, int64_t C, int64_t M, const BnBwdFin &f) {
+    for (int64_t c = threadIdx.x >> 3; c < C; c += blockDim.x >> 3) {
+        double sg, sgx;
+        sum_splits8(part, f.splits, C, c, sg, sgx);
+        if ((threadIdx.x & 7) == 0) {
+            if (f.gw) f.gw[c] += (float)sgx;
+            if (f.gb) f.gb[c] += (float)sg;
+            f.coef[2 * c] = (float)(sg / (double)M);
+            f.coef[2 * c + 1] = (float)(sgx / (double)M);
+        }
+    }
+}
+
+// ---- channel reductions fed by bulk copies --------------------------------------------------------------
+//
+// The statistics and backward-sum passes read whole planes of one channel (S contiguous floats per
+// sample and channel). In these kernels one thread streams the block's planes into a ring of
+// shared-memory stages with cp.async.bulk (no multicast; one mbarrier per stage counts the bytes),
+// kBnRing stages ahead of the block's threads, which reduce each stage from shared memory. A block
+// keeps up to kBnRing * 16 KiB of loads in flight without holding registers for them (the register-fed
+// kernels above keep 64 bytes per thread in flight, short of what HBM needs under their occupancy).
+// Used when a plane is a multiple of 16 bytes and fits a stage. The waits are bounded like the
+// tensor-core pipelines': a block that gives up reports NCK_ERR_PIPELINE, lets its copies land (again
+// bounded) and stops.
+constexpr int kBnRing = 4, kBnStageMax = 16384;
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+                 : "memory");
+}
+
+// planes [n0, n1) of channel c of NT tensors [N][C][S], PP planes of each per stage, each plane in a
+// slot of SP floats. al: every plane starts on a 16-byte boundary and S is a multiple of 4 (SP = S,
+// the stage is one contiguous run of floats). Otherwise each plane's copy starts at the 16-byte
+// boundary at or below it and ends at the one at or above its end (SP = S + 3 rounded up to 4; the
+// plane then sits lead(t, s, j) floats into its slot): device blocks are 256-byte aligned and sized
+// in whole 256-byte units, so these few bytes around a plane lie inside its tensor's allocation.
+template <int NT>
+struct PlaneRing {
+    const float *src[NT];
+    int64_t C, S, n0, n1, c;
+    int PP, SP, al;
+    float *buf;  // kBnRing stages of NT * PP * SP floats
+    uint64_t *full;
+    __device__ int64_t stages() const { return n1 > n0 ? (n1 - n0 + PP - 1) / PP : 0; }
+    __device__ const float *stage(int slot, int t) const { return buf + ((int64_t)slot * NT + t) * PP * SP; }
+    __device__ int planes(int64_t s) const {
+        const int64_t left = n1 - (n0 + s * PP);
+        return (int)(left < PP ? left : PP);
+    }
+    __device__ const float *plane_src(int t, int64_t s, int j) const { return src[t] + ((n0 + s * PP + j) * C + c) * S; }
+    // floats between the slot's start and the plane's first element
+    __device__ int lead(int t, int64_t s, int j) const { return al ? 0 : (int)(((uintptr_t)plane_src(t, s, j) >> 2) & 3); }
+    // one thread: stage s of the walk into its ring slot
+    __device__ void issue(int64_t s) const {
+        const int slot = (int)(s % kBnRing), np = planes(s);
+        uint32_t total = 0;
+        for (int t = 0; t < NT; t++)
+            for (int j = 0; j < np; j++) {
+                const uintptr_t p = (uintptr_t)plane_src(t, s, j), a = p & ~(uintptr_t)15;
+                total += al ? (uint32_t)(S * 4) : (uint32_t)(((p + S * 4 + 15) & ~(uintptr_t)15) - a);
+            }
+        tc::mbar_expect_tx(&full[slot], total);
+        for (int t = 0; t < NT; t++)
+            for (int j = 0; j < np; j++) {
+                const uintptr_t p = (uintptr_t)plane_src(t, s, j), a = p & ~(uintptr_t)15;
+                const uint32_t bytes = al ? (uint32_t)(S * 4) : (uint32_t)(((p + S * 4 + 15) & ~(uintptr_t)15) - a);
+                bulk_g2s(buf + ((int64_t)slot * NT + t) * PP * SP + (int64_t)j * SP, (const void *)a, bytes, &full[slot]);
+            }
+    }
+    // every thread: the ring's barriers, then the first stages in flight
+    __device__ void start() const {
+        if (threadIdx.x == 0) {
+            for (int i = 0; i < kBnRing; i++) tc::mbar_init(&full[i], 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int64_t s = 0; s < kBnRing && s < stages(); s++) issue(s);
+    }
+    // after a failed wait at stage s: the copies issued past it land (bounded) before the block exits
+    __device__ void drain(int64_t s, int *status) const {
+        if (threadIdx.x != 0) return;
+        const int64_t end = s + kBnRing < stages() ? s + kBnRing : stages();
+        for (int64_t j = s; j < end; j++)
+            if (!tc::mbar_wait(&full[j % kBnRing], (uint32_t)((j / kBnRing) & 1), status)) break;
+    }
+};
+
+// per-channel statistics from bulk-copied planes (the same partials and finalize as k_bn_stats)
+__global__ void __launch_bounds__(256) k_bn_stats_bulk(const float *__restrict__ x, double *__restrict__ part,
+                                                       int64_t N, int64_t C, int64_t S, int64_t per_split, int PP,
+                                                       int SP, int al, FastDiv dS, BnFwdFin fin, unsigned *counter,
+                                                       int *status) {
+    extern __shared__ __align__(128) float bn_ring[];
+    __shared__ __align__(8) uint64_t full[kBnRing];
+    __shared__ double sm[64];
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    PlaneRing<1> r{{x}, C, S, n0, n1, c, PP, SP, al, bn_ring, full};
+    r.start();
+    double s0 = 0.0, q0 = 0.0, s1 = 0.0, q1 = 0.0;
+    const int64_t ns = r.stages();
+    for (int64_t st = 0; st < ns; st++) {
+        const int slot = (int)(st % kBnRing);
+        const bool got = tc::mbar_wait(&full[slot], (uint32_t)((st / kBnRing) & 1), status);
+        if (got && al) {
+            const float4 *p = reinterpret_cast<const float4 *>(r.stage(slot, 0));
+            const int n4 = r.planes(st) * (int)(S / 4);
+            for (int i = threadIdx.x; i < n4; i += 2 * blockDim.x) {
+                const float4 a = p[i];
+                s0 += (double)a.x, q0 += (double)a.x * a.x, s0 += (double)a.y, q0 += (double)a.y * a.y;
+                s0 += (double)a.z, q0 += (double)a.z * a.z, s0 += (double)a.w, q0 += (double)a.w * a.w;
+                if (i + (int)blockDim.x < n4) {
+                    const float4 b = p[i + blockDim.x];
+                    s1 += (double)b.x, q1 += (double)b.x * b.x, s1 += (double)b.y, q1 += (double)b.y * b.y;
+                    s1 += (double)b.z, q1 += (double)b.z * b.z, s1 += (double)b.w, q1 += (double)b.w * b.w;
+                }
+            }
+        } else if (got) {
+            const float *p = r.stage(slot, 0);
+            const int n = r.planes(st) * (int)S;
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int j = (int)dS.div((uint32_t)i);
+                const double a = (double)p[j * SP + r.lead(0, st, j) + (i - j * (int)S)];
+                if (i & 256) s1 += a, q1 += a * a;
+                else s0 += a, q0 += a * a;
+            }
+        }
+        if (!__syncthreads_and(got)) {
+            r.drain(st, status);
+            return;
+        }
+        if (threadIdx.x == 0 && st + kBnRing < ns) r.issue(st + kBnRing);
+    }
+    double s = s0 + s1, ss = q0 + q1;
+    block_sum2(s, ss, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = s;
+        part[(blockIdx.y * C + c) * 2 + 1] = ss;
+    }
+    if (last_block_done(counter)) bn_fwd_finalize(part, C, N * S, fin);
+}
+
+// backward sums from bulk-copied planes of x (or, after a pool, x at the argmax) and of the gradient:
+// the same per-element terms, partials and finalize as k_bn_bwd_sums / k_bn_pool_bwd_sums_x; M is the
+// element count of the statistics
+__global__ void __launch_bounds__(256) k_bn_sums_bulk(const float *__restrict__ x, const float *__restrict__ g,
+                                                      const float *__restrict__ mean, const float *__restrict__ invstd,
+                                                      double *__restrict__ part, int64_t N, int64_t C, int64_t S,
+                                                      int64_t per_split, int PP, int SP, int al, FastDiv dS,
+                                                      int64_t M, BnBwdFin fin, unsigned *counter, int *status,
+                                                      const float *__restrict__ wt, const float *__restrict__ bs,
+                                                      int act, float act_s) {
+    extern __shared__ __align__(128) float bn_ring[];
+    __shared__ __align__(8) uint64_t full[kBnRing];
+    __shared__ double sm[64];
+    const int64_t c = blockIdx.x, n0 = blockIdx.y * per_split, n1 = n0 + per_split < N ? n0 + per_split : N;
+    const float mu = mean[c], is = invstd[c];
+    const float ea = act >= 0 ? wt[c] * is : 0.0f, ed = act >= 0 ? bs[c] - mu * ea : 0.0f;
+    PlaneRing<2> r{{x, g}, C, S, n0, n1, c, PP, SP, al, bn_ring, full};
+    r.start();
+    double g0 = 0.0, h0 = 0.0, g1 = 0.0, h1 = 0.0;
+    const int64_t ns = r.stages();
+    for (int64_t st = 0; st < ns; st++) {
+        const int slot = (int)(st % kBnRing);
+        const bool got = tc::mbar_wait(&full[slot], (uint32_t)((st / kBnRing) & 1), status);
+        if (got && !al) {
+            const float *px = r.stage(slot, 0), *pg = r.stage(slot, 1);
+            const int n = r.planes(st) * (int)S;
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int j = (int)dS.div((uint32_t)i), e = i - j * (int)S;
+                const float xv = px[j * SP + r.lead(0, st, j) + e];
+                float gv = pg[j * SP + r.lead(1, st, j) + e];
+                if (act >= 0) gv = epi_grad(act, act_s, xv * ea + ed, gv);
+                if (i & 256) g1 += gv, h1 += gv * (xv - mu) * is;
+                else g0 += gv, h0 += gv * (xv - mu) * is;
+            }
+        } else if (got) {
+            const float *px = r.stage(slot, 0), *pg = r.stage(slot, 1);
+            const int n = r.planes(st) * (int)S;
+            for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {
+                const float4 xv = *reinterpret_cast<const float4 *>(px + i);
+                float4 gv = *reinterpret_cast<const float4 *>(pg + i);
+                if (act >= 0) {
+                    gv.x = epi_grad(act, act_s, xv.x * ea + ed, gv.x), gv.y = epi_grad(act, act_s, xv.y * ea + ed, gv.y);
+                    gv.z = epi_grad(act, act_s, xv.z * ea + ed, gv.z), gv.w = epi_grad(act, act_s, xv.w * ea + ed, gv.w);
+                }
+                g0 += gv.x, h0 += gv.x * (xv.x - mu) * is, g1 += gv.y, h1 += gv.y * (xv.y - mu) * is;
+                g0 += gv.z, h0 += gv.z * (xv.z - mu) * is, g1 += gv.w, h1 += gv.w * (xv.w - mu) * is;
+            }
+        }
+        if (!__syncthreads_and(got)) {
+            r.drain(st, status);
+            return;
+        }
+        if (threadIdx.x == 0 && st + kBnRing < ns) r.issue(st + kBnRing);
+    }
+    double sg = g0 + g1, sgx = h0 + h1;
+    block_sum2(sg, sgx, sm);
+    if (threadIdx.x == 0) {
+        part[(blockIdx.y * C + c) * 2] = sg;
+        part[(blockIdx.y * C + c) * 2 + 1] = sgx;
+    }
+    if (last_block_done(counter)) bn_bwd_finalize(part, C, M, fin);
+}
+
+// the ring layout of the bulk-fed kernels for NT tensors with S floats per plane: planes per stage
+// (0: not eligible: planes shorter than 4 floats or longer than a stage), slot floats, aligned case
+struct BnBulk {
+    int PP, SP, al;
+    FastDiv dS;
+};
+
+static BnBulk bn_bulk_plan(const nck_dev *d, int64_t S, int NT, const void *p, const void *q) {
+    BnBulk b = {0, 0, 0, make_fastdiv(1)};
+    // default policy (stage < 0): the statistics pass (NT = 1) over planes of at least 4 KiB, where the
+    // bulk feed measured faster (cfg3's 32 x 32 planes); the backward sums stay register-fed
+    const int auto_ = d->bn_bulk_stage < 0;
+    if (d->bn_bulk_stage == 0 || S < 4 || S >= ((int64_t)1 << 20) || (auto_ && (NT != 1 || S < 1024))) return b;
+    b.al = (S & 3) == 0 && (((uintptr_t)p | (uintptr_t)q) & 15) == 0;
+    b.SP = (int)(b.al ? S : (S + 3 + 3) / 4 * 4);
+    const int stage = d->bn_bulk_stage < 0 ? -d->bn_bulk_stage : d->bn_bulk_stage;
+    int64_t pp = (stage < kBnStageMax ? stage : kBnStageMax) / NT / ((int64_t)b.SP * 4);
+    if (pp > 64) pp = 64;
+    b.PP = (int)pp;
+    b.dS = make_fastdiv((uint32_t)S);
+    return b;
+}
+
+static size_t bn_bulk_smem(const BnBulk &b, int NT) { return (size_t)kBnRing * NT * b.PP * b.SP * sizeof(float); }
+
+// one wave of (channel, run of samples) blocks for a bulk-fed kernel
+template <typename K>
+static void bn_bulk_grid(nck_dev *d, K kernel, size_t smem, int64_t N, int64_t C, int64_t S, int64_t &splits,
+                         int64_t &per) {
+    static int attr = 0;
+    static size_t seen_smem[4];
+    static int seen_res[4], nseen = 0;
+    if (!attr) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBnRing * kBnStageMax);
+        attr = 1;
+    }
+    int res = 0;  // resident blocks, cached per ring size (the occupancy query is a host call)
+    for (int i = 0; i < nseen && !res; i++)
+        if (seen_smem[i] == smem) res = seen_res[i];
+    if (!res) {
+        res = resident_blocks(d, kernel, 256, smem);
+        const int slot = nseen < 4 ? nseen++ : 3;
+        seen_smem[slot] = smem, seen_res[slot] = res;
+    }
+    splits = bn_splits(res, N, C, S);
+    per = (N + splits - 1) / splits;
+    splits = (N + per - 1) / per;
+}
+
 extern "C" void nck_bn_stats_train(nck_dev *d, const float *x, float *mean, float *invstd, float *rm, float *rv,
                                    int64_t N, int64_t C, int64_t S, float mom, float eps, int stage) {
     Scope sc(d, "bn_fwd", 0.0, 4.0 * N * C * S);
+    const BnBulk bb = bn_bulk_plan(d, S, 1, x, x);
+    if (bb.PP) {
+        const size_t smem = bn_bulk_smem(bb, 1);
+        int64_t splits, per;
+        bn_bulk_grid(d, k_bn_stats_bulk, smem, N, C, S, splits, per);
+        const BnFwdFin fin = {mean, invstd, rm, rv, mom, eps, (int)splits, stage};
+        k_bn_stats_bulk<<<dim3((unsigned)C, (unsigned)splits), 256, smem, NCK_STREAM(d)>>>(
+            x, (double *)d->scratch, N, C, S, per, bb.PP, bb.SP, bb.al, bb.dS, fin, d->counters, d->status);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     const bool v4 = bn_vec4(S, x, x, x);
     static int res4 = 0, res1 = 0;
     if (v4 && !res4) res4 = resident_blocks(d, k_bn_stats<4>, kThreads);
@@ -1081,25 +1356,6 @@ extern "C" void nck_bn_fwd_eval(nck_dev *d, const float *x, const float *w, cons
 
 // backward sums per channel: sg = sum g, sgx = sum g * xhat (float products, double sums); same
 // walk as the statistics kernel
-// backward sums -> weight / bias gradients and the two means the input gradient needs
-struct BnBwdFin {
-    float *gw, *gb, *coef;
-    int splits;
-};
-
-__device__ void bn_bwd_finalize(const double *part, int64_t C, int64_t M, const BnBwdFin &f) {
-    for (int64_t c = threadIdx.x >> 3; c < C; c += blockDim.x >> 3) {
-        double sg, sgx;
-        sum_splits8(part, f.splits, C, c, sg, sgx);
-        if ((threadIdx.x & 7) == 0) {
-            if (f.gw) f.gw[c] += (float)sgx;
-            if (f.gb) f.gb[c] += (float)sg;
-            f.coef[2 * c] = (float)(sg / (double)M);
-            f.coef[2 * c + 1] = (float)(sgx / (double)M);
-        }
-    }
-}
-
 // act >= 0: g is the gradient of act(BatchNorm output); the BatchNorm output's own gradient is formed
 // on the fly from x (the activation's backward fused in)
 template <int V>
@@ -1205,16 +1461,26 @@ extern "C" void nck_bn_bwd_ex(nck_dev *d, const float *x, const float *w, const 
                               int64_t C, int64_t S, int training, int acc_gx, int act, float act_s) {
     Scope sc(d, act < 0 ? "bn_bwd" : "bn_act_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * N * C * S);
     const bool v4 = bn_vec4(S, x, g, gx ? (const void *)gx : (const void *)x);
+    const BnBulk bb = bn_bulk_plan(d, S, 2, x, g);
     static int res4 = 0, res1 = 0;
-    if (v4 && !res4) res4 = resident_blocks(d, k_bn_bwd_sums<4>, kThreads);
-    if (!v4 && !res1) res1 = resident_blocks(d, k_bn_bwd_sums<1>, kThreads);
-    int64_t splits = bn_splits(v4 ? res4 : res1, N, C, S), per = (N + splits - 1) / splits;
-    splits = (N + per - 1) / per;
+    int64_t splits, per;
+    if (bb.PP) {
+        bn_bulk_grid(d, k_bn_sums_bulk, bn_bulk_smem(bb, 2), N, C, S, splits, per);
+    } else {
+        if (v4 && !res4) res4 = resident_blocks(d, k_bn_bwd_sums<4>, kThreads);
+        if (!v4 && !res1) res1 = resident_blocks(d, k_bn_bwd_sums<1>, kThreads);
+        splits = bn_splits(v4 ? res4 : res1, N, C, S), per = (N + splits - 1) / splits;
+        splits = (N + per - 1) / per;
+    }
     double *part = (double *)d->scratch;
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     dim3 g1((unsigned)C, (unsigned)splits);
     const BnBwdFin fin = {gw, gb, coef, (int)splits};
-    if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters, w, b, act, act_s);
+    if (bb.PP)
+        k_bn_sums_bulk<<<g1, 256, bn_bulk_smem(bb, 2), NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, bb.PP,
+                                                                       bb.SP, bb.al, bb.dS, N * S, fin, d->counters,
+                                                                       d->status, w, b, act, act_s);
+    else if (v4) k_bn_bwd_sums<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters, w, b, act, act_s);
     else k_bn_bwd_sums<1><<<g1, kThreads, 0, NCK_STREAM(d)>>>(x, g, mean, invstd, part, N, C, S, per, fin, d->counters, w,
                                                                b, act, act_s);
     int launched = 1;
@@ -1396,13 +1662,23 @@ extern "C" void nck_bn_pool_bwd(nck_dev *d, const float *x, const float *w, cons
     if (!res4) res4 = resident_blocks(d, k_bn_pool_bwd_sums_x<4>, kThreads);
     if (!res1) res1 = resident_blocks(d, k_bn_pool_bwd_sums_x<1>, kThreads);
     const bool v4 = xarg && L % 4 == 0 && (((uintptr_t)xarg | (uintptr_t)gpool) & 15) == 0;
-    int64_t splits = bn_splits(xarg ? (v4 ? res4 : res1) : res, N, C, L), per = (N + splits - 1) / splits;
-    splits = (N + per - 1) / per;
+    const BnBulk bb = xarg ? bn_bulk_plan(d, L, 2, xarg, gpool) : BnBulk{0, 0, 0, make_fastdiv(1)};
+    int64_t splits, per;
+    if (bb.PP) {
+        bn_bulk_grid(d, k_bn_sums_bulk, bn_bulk_smem(bb, 2), N, C, L, splits, per);
+    } else {
+        splits = bn_splits(xarg ? (v4 ? res4 : res1) : res, N, C, L), per = (N + splits - 1) / splits;
+        splits = (N + per - 1) / per;
+    }
     double *part = (double *)d->scratch;
     float *coef = (float *)((char *)d->scratch + (size_t)splits * C * 2 * sizeof(double));
     const BnBwdFin fin = {gw, gb, coef, (int)splits};
     dim3 g1((unsigned)C, (unsigned)splits);
-    if (v4)
+    if (bb.PP)
+        k_bn_sums_bulk<<<g1, 256, bn_bulk_smem(bb, 2), NCK_STREAM(d)>>>(xarg, gpool, mean, invstd, part, N, C, L, per,
+                                                                       bb.PP, bb.SP, bb.al, bb.dS, N * L * 4, fin,
+                                                                       d->counters, d->status, w, b, act, act_s);
+    else if (v4)
         k_bn_pool_bwd_sums_x<4><<<g1, kThreads, 0, NCK_STREAM(d)>>>(xarg, gpool, w, b, mean, invstd, act, act_s, part, N,
                                                                    C, L, per, fin, d->counters);
     else if (xarg)
@@ -1506,7 +1782,7 @@ template <int NV>
 __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float *__restrict__ x, const float *__restrict__ w,
                                                     const float *__restrict__ g, const float *__restrict__ stats,
                                                     float *__restrict__ gx, float *__restrict__ part, int64_t R,
-                                                    int want_wb) {
+                                                    int want_wb, int acc_gx) {
     constexpr int D = 128 * NV;
     __shared__ float red[8][128];  // one 128-column slice at a time
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1543,7 +1819,7 @@ __global__ void __launch_bounds__(256) k_ln_bwd_reg(const float *__restrict__ x,
 #pragma unroll
             for (int k = 0; k < NV; k++) {
                 const int i = lane + 32 * k;
-                float4 a = o[i];
+                float4 a = acc_gx ? o[i] : make_float4(0.f, 0.f, 0.f, 0.f);  // a fresh buffer is stored
                 a.x += rstd * (gi[k].x - mg - xh[k].x * mgx), a.y += rstd * (gi[k].y - mg - xh[k].y * mgx);
                 a.z += rstd * (gi[k].z - mg - xh[k].z * mgx), a.w += rstd * (gi[k].w - mg - xh[k].w * mgx);
                 o[i] = a;
@@ -1588,7 +1864,8 @@ extern "C" void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const flo
 }
 
 __global__ void k_ln_bwd_dx(const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ g,
-                            const float *__restrict__ stats, float *__restrict__ gx, int64_t R, int64_t D) {
+                            const float *__restrict__ stats, float *__restrict__ gx, int64_t R, int64_t D,
+                            int acc_gx) {
     int lane = threadIdx.x & 31;
     int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t r = warp; r < R; r += nw) {
@@ -1606,7 +1883,7 @@ __global__ void k_ln_bwd_dx(const float *__restrict__ x, const float *__restrict
         float *o = gx + r * D;
         for (int64_t i = lane; i < D; i += 32) {
             float xhat = (p[i] - mean) * rstd, gi = w ? q[i] * w[i] : q[i];
-            o[i] += rstd * (gi - mg - xhat * mgx);
+            o[i] = (acc_gx ? o[i] : 0.0f) + rstd * (gi - mg - xhat * mgx);
         }
     }
 }
@@ -1653,8 +1930,8 @@ static void ln_wb_combine(nck_dev *d, const float *part, int splits, int64_t D, 
 }
 
 extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
-                           float *gw, float *gb, int64_t R, int64_t D) {
-    Scope sc(d, "ln_bwd", 0.0, (gx ? 16.0 : 8.0) * R * D);
+                           float *gw, float *gb, int64_t R, int64_t D, int acc_gx) {
+    Scope sc(d, "ln_bwd", 0.0, (gx ? (acc_gx ? 16.0 : 12.0) : 8.0) * R * D);
     int launched = 0;
     const bool vec = (D == 128 || D == 256 || D == 512 || D == 1024) &&
                      (((uintptr_t)x | (uintptr_t)g | (uintptr_t)gx | (uintptr_t)w) & 15) == 0;
@@ -1668,17 +1945,17 @@ extern "C" void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const flo
         if (blocks < 1) blocks = 1;
         float *part = (float *)d->scratch;
         const int want = gw || gb;
-        if (D == 128) k_ln_bwd_reg<1><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
-        else if (D == 256) k_ln_bwd_reg<2><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
-        else if (D == 512) k_ln_bwd_reg<4><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
-        else k_ln_bwd_reg<8><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want);
+        if (D == 128) k_ln_bwd_reg<1><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want, acc_gx);
+        else if (D == 256) k_ln_bwd_reg<2><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want, acc_gx);
+        else if (D == 512) k_ln_bwd_reg<4><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want, acc_gx);
+        else k_ln_bwd_reg<8><<<(unsigned)blocks, 256, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, part, R, want, acc_gx);
         launched = 1;
         NCK_LAUNCHED(d, launched);
         if (want) ln_wb_combine(d, part, (int)blocks, D, gw, gb);
         return;
     }
     if (gx) {
-        k_ln_bwd_dx<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, R, D);
+        k_ln_bwd_dx<<<grid_for(d, R * 32), kThreads, 0, NCK_STREAM(d)>>>(x, w, g, stats, gx, R, D, acc_gx);
         launched++;
     }
     if (gw || gb) {

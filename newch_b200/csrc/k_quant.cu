@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(256) k_qgemm(const int8_t *__restrict__ A, con
 namespace {
 using namespace tc;
 
-constexpr int kQBN = 128, kQStageP = TM * 128, kQThreads = 6 * 32;  // stage bytes of the weight tile
+constexpr int kQStageP = TM * 128, kQThreads = 6 * 32;  // stage bytes of the weight tile
 
 struct QtcParams {
     int64_t M, N, K;
@@ -225,6 +225,7 @@ struct QBars {
     uint32_t tmem;
 };
 
+template <int kQBN>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm_tc(const __grid_constant__ CUtensorMap tmW,
                                                            const __grid_constant__ CUtensorMap tmX, QtcParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -322,16 +323,26 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm_tc(const __grid_constant
             const bool live = n < p.N;
             const float wsn = live ? p.ws[n] : 0.0f, bn = (live && p.bias) ? p.bias[n] : 0.0f;
             for (int c0 = 0; c0 < kQBN; c0 += 16) {
-                uint32_t r[16];
-                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)acc * (tcols / 2) + (uint32_t)c0, r);
-                if (!live) continue;
+                // the chunk's 16 row scales are read before the accumulator and the stores (a store to y
+                // could alias xs for the compiler, which would otherwise re-read xs after every store)
+                float xv[16];
 #pragma unroll
                 for (int jj = 0; jj < 16; jj++) {
                     const int64_t m = q0 + c0 + jj;
-                    if (m < p.M) {
+                    xv[jj] = m < p.M ? __ldg(p.xs + m) : 0.0f;
+                }
+                uint32_t r[16];
+                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)acc * (tcols / 2) + (uint32_t)c0, r);
+                if (!live) continue;
+                float *yo = p.y + (q0 + c0) * p.N + n;
+                int32_t *ao = p.acc_out ? p.acc_out + (q0 + c0) * p.N + n : nullptr;
+                const int nj = p.M - (q0 + c0) < 16 ? (int)(p.M - (q0 + c0)) : 16;
+#pragma unroll
+                for (int jj = 0; jj < 16; jj++) {
+                    if (jj < nj) {
                         const int32_t a = (int32_t)r[jj];
-                        if (p.acc_out) p.acc_out[m * p.N + n] = a;
-                        p.y[m * p.N + n] = (float)a * p.xs[m] * wsn + bn;
+                        if (ao) ao[jj * p.N] = a;
+                        yo[jj * p.N] = (float)a * xv[jj] * wsn + bn;
                     }
                 }
             }
@@ -345,6 +356,10 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm_tc(const __grid_constant
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols));
 }
 
+template <int kQBN>
+int qgemm_tc_launch(nck_dev *d, const int8_t *wq, const int8_t *xq, const float *xs, const float *ws, const float *b,
+                    float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out);
+
 // 1 when launched on the tensor cores; 0 when the operands do not fit TMA (K not a multiple of 16
 // bytes, unaligned bases) or the product is tiny, and the dp4a kernel is used
 int qgemm_tc(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, const float *b,
@@ -352,11 +367,21 @@ int qgemm_tc(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, co
     if (!d->qgemm_tc || K % 16 || (((uintptr_t)xq | (uintptr_t)wq) & 15) || M * N < 4096 || M >= ((int64_t)1 << 31) ||
         N >= ((int64_t)1 << 31) || K >= ((int64_t)1 << 31))
         return 0;
+    // activation rows per tile: 256 for tall products (each weight panel staged from L2 once per 256
+    // rows instead of 128, halving the panel traffic per MMA), 128 otherwise
+    if (M >= 2048) return qgemm_tc_launch<256>(d, wq, xq, xs, ws, b, y, M, N, K, acc_out);
+    return qgemm_tc_launch<128>(d, wq, xq, xs, ws, b, y, M, N, K, acc_out);
+}
+
+template <int kQBN>
+int qgemm_tc_launch(nck_dev *d, const int8_t *wq, const int8_t *xq, const float *xs, const float *ws, const float *b,
+                    float *y, int64_t M, int64_t N, int64_t K, int32_t *acc_out) {
     CUtensorMap mw, mx;
     if (!make_map_u8(&mw, wq, K, N, K, 128, TM) || !make_map_u8(&mx, xq, K, M, K, 128, kQBN)) return 0;
     static int attr = 0;
     if (!attr) {
-        if (cudaFuncSetAttribute(k_qgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) != cudaSuccess) {
+        if (cudaFuncSetAttribute(k_qgemm_tc<kQBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit) !=
+            cudaSuccess) {
             cudaGetLastError();
             return 0;
         }
@@ -372,7 +397,7 @@ int qgemm_tc(nck_dev *d, const int8_t *xq, const float *xs, const int8_t *wq, co
     const size_t smem = 2048 + (size_t)p.stages * per;
     const int64_t sms = d->sm_count > 0 ? d->sm_count : 148;
     const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
-    k_qgemm_tc<<<grid, kQThreads, smem, NCK_STREAM(d)>>>(mw, mx, p);
+    k_qgemm_tc<kQBN><<<grid, kQThreads, smem, NCK_STREAM(d)>>>(mw, mx, p);
     if (cudaGetLastError() != cudaSuccess) *(volatile int *)d->status_host = NCK_ERR_LAUNCH;
     NCK_LAUNCHED(d, 1);
     return 1;

@@ -159,22 +159,46 @@ extern "C" void nck_reduce_max(nck_dev *d, const float *x, float *y, int32_t *ar
 
 // ---- gradients --------------------------------------------------------------------------------------
 
+// gi (+)= scale * g broadcast over the reduced extent R. acc == 0: gi is a fresh buffer and is
+// stored (scale * g, what accumulating into zeros gives). R a multiple of 4 with inner == 1: float4
+// items, each inside one broadcast run, with 32-bit fast division.
+template <bool ACC>
 __global__ void k_reduce_sum_bwd(const float *__restrict__ g, float *__restrict__ gi, int64_t outer, int64_t R,
-                                 int64_t inner, float scale) {
-    int64_t n = outer * R * inner;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+                                 int64_t inner, float scale, int vec, FastDiv dR) {
+    const int64_t n = outer * R * inner, stride = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {
+        float4 *g4 = reinterpret_cast<float4 *>(gi);
+        for (int64_t t4 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t4 < n / 4; t4 += stride) {
+            const float v = scale * __ldg(g + dR.div((uint32_t)(4 * t4)));
+            float4 o;
+            if (ACC) {
+                o = g4[t4];
+                o.x = o.x + v, o.y = o.y + v, o.z = o.z + v, o.w = o.w + v;
+            } else {
+                o = make_float4(v, v, v, v);
+            }
+            g4[t4] = o;
+        }
+        return;
+    }
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += stride) {
         int64_t i = t % inner, o = t / (R * inner);
         float gv = g[o * inner + i];
-        gi[t] = inner == 1 ? gi[t] + scale * gv : fmaf(scale, gv, gi[t]);
+        if (ACC) gi[t] = inner == 1 ? gi[t] + scale * gv : fmaf(scale, gv, gi[t]);
+        else gi[t] = scale * gv;
     }
 }
 
 extern "C" void nck_reduce_sum_bwd(nck_dev *d, const float *g, float *gi, int64_t outer, int64_t R, int64_t inner,
-                                   float scale) {
+                                   float scale, int acc) {
     int64_t n = outer * R * inner;
     if (n <= 0) return;
-    Scope sc(d, "reduce_sum_bwd");
-    k_reduce_sum_bwd<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(g, gi, outer, R, inner, scale);
+    Scope sc(d, "reduce_sum_bwd", 0.0, 4.0 * (outer * inner + (acc ? 2.0 : 1.0) * n));
+    const int vec = inner == 1 && R % 4 == 0 && ((uintptr_t)gi & 15) == 0 && n < ((int64_t)1 << 32);
+    const FastDiv dR = make_fastdiv((uint32_t)(vec ? R : 1));
+    const int64_t items = vec ? n / 4 : n;
+    if (acc) k_reduce_sum_bwd<true><<<grid_for(d, items), kThreads, 0, NCK_STREAM(d)>>>(g, gi, outer, R, inner, scale, vec, dR);
+    else k_reduce_sum_bwd<false><<<grid_for(d, items), kThreads, 0, NCK_STREAM(d)>>>(g, gi, outer, R, inner, scale, vec, dR);
     NCK_LAUNCHED(d, 1);
 }
 

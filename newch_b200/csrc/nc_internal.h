@@ -228,6 +228,7 @@ struct nc_ctx {
     size_t side_cap, side_used;
     int side_fresh;      /* no mask drawn yet this step: wait for ev_step first */
     int side_off;        /* NC_RNG_SIDE=0, or set-up failed */
+    int side_all;        /* NC_RNG_SIDE=1: every mask on the side stream, whatever its size */
     struct nc_optim *optims; /* optimizers of this context (intrusive list) */
     /* data parallel BatchNorm: each training forward stages its batch (mean, unbiased variance) here;
      * nc__dp_bn_flush gathers every rank's and applies the running-statistic updates in rank order */

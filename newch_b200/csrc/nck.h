@@ -29,6 +29,8 @@ typedef struct nck_dev {
     int conv_tap;      /* 1: stride-1 convolutions run as tap-shifted GEMMs (default; NC_CONV=unfolded|implicit: 0) */
     int gemm_small;    /* 1: small products take the one-thread / one-warp-per-output kernels (NC_GEMM_SMALL=0: off) */
     int qgemm_tc;      /* 1: int8 GEMMs on tcgen05 kind::i8 where TMA allows (NC_QGEMM=dp4a: CUDA cores) */
+    int bn_bulk_stage; /* bulk-fed BatchNorm reductions: stage bytes; < 0: statistics of planes >= 4 KiB only
+                        * (the default); 0: none (NC_BN_BULK=0) */
     int math_mode;     /* NCK_MATH_*: how exp / sigmoid / tanh / erf are evaluated */
     nck_timer *timer;  /* per-kernel CUDA-event timing, NULL when off */
     void *scratch;     /* device scratch for split reductions (owned by the context) */
@@ -133,7 +135,7 @@ void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M, int64_t N)
 /* gy[n] += sum over m of x[m * ld + n], one launch (for matrices of a few million elements at most) */
 void nck_colsum_ld(nck_dev *d, const float *x, int64_t ld, float *gy, int64_t M, int64_t N);
 void nck_reduce_sum_bwd(nck_dev *d, const float *g, float *gi, int64_t outer, int64_t R, int64_t inner,
-                        float scale);
+                        float scale, int acc); /* acc == 0: gi is fresh and is stored */
 void nck_reduce_max_bwd(nck_dev *d, const float *g, const int32_t *arg, float *gi, int64_t outer, int64_t R,
                         int64_t inner);
 /* fills *out (double, device) with sum of squares of n floats; accumulates when `accumulate` */
@@ -249,7 +251,7 @@ void nck_bn_bwd(nck_dev *d, const float *x, const float *w, const float *g, cons
 void nck_ln_fwd(nck_dev *d, const float *x, const float *w, const float *b, float *y, float *stats, int64_t R,
                 int64_t D, float eps);
 void nck_ln_bwd(nck_dev *d, const float *x, const float *w, const float *g, const float *stats, float *gx,
-                float *gw, float *gb, int64_t R, int64_t D);
+                float *gw, float *gb, int64_t R, int64_t D, int acc_gx); /* acc_gx == 0: gx is fresh, stored */
 
 /* ---- gather / scatter ------------------------------------------------------------------------ */
 void nck_index_select(nck_dev *d, const void *x, const int32_t *idx, void *y, int64_t B, int64_t N,

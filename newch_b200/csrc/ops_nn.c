@@ -425,12 +425,14 @@ static void layer_norm_bwd(nc_node *n) {
     const float *X = nc__contig_f32(x), *w = wt ? nc__contig_f32(wt) : NULL;
     int64_t D = ln_dim(n), R = D ? nc_numel(x) / D : 0;
     if (!X || (wt && !w)) return;
-    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf(x) : NULL;
+    int acc = 1;  /* the input gradient is written whole: a fresh buffer is stored */
+    nc_tensor *gx = nc__needs_grad(x) ? nc__grad_buf_acc(x, &acc) : NULL;
     nc_tensor *gw = wt && nc__needs_grad(wt) ? nc__grad_buf(wt) : NULL;
     nc_tensor *gb = bt && nc__needs_grad(bt) ? nc__grad_buf(bt) : NULL;
     if (R)
         nck_ln_bwd(nc__k(x->ctx), X, w, (const float *)n->out->grad->data, (const float *)n->saved,
-                   gx ? (float *)gx->data : NULL, gw ? (float *)gw->data : NULL, gb ? (float *)gb->data : NULL, R, D);
+                   gx ? (float *)gx->data : NULL, gw ? (float *)gw->data : NULL, gb ? (float *)gb->data : NULL, R, D,
+                   acc);
 }
 
 const nc_op_def nc_op_layer_norm = {"layer_norm", 0, 0, layer_norm_infer, NULL, layer_norm_fwd, layer_norm_bwd};

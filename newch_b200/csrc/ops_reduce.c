@@ -96,7 +96,10 @@ static nc_status reduce_fwd(nc_node *n) {
 }
 
 static void reduce_bwd(nc_node *n) {
-    nc_tensor *gt = nc__grad_buf(n->in[0]);
+    int acc = 1;
+    /* a sum or mean writes every element of its input's gradient: a fresh buffer is stored, not
+     * zero-filled and accumulated */
+    nc_tensor *gt = n->op->kind == RED_MAX ? nc__grad_buf(n->in[0]) : nc__grad_buf_acc(n->in[0], &acc);
     if (!gt) return;
     const int64_t outer = n->p.i[P_OUTER], R = n->p.i[P_EXTENT], inner = n->p.i[P_INNER];
     const float *g = (const float *)n->out->grad->data;
@@ -105,7 +108,7 @@ static void reduce_bwd(nc_node *n) {
         nck_reduce_max_bwd(k, g, (const int32_t *)n->saved, (float *)gt->data, outer, R, inner);
     else
         nck_reduce_sum_bwd(k, g, (float *)gt->data, outer, R, inner,
-                           n->op->kind == RED_MEAN ? 1.0f / (float)(R > 0 ? R : 1) : 1.0f);
+                           n->op->kind == RED_MEAN ? 1.0f / (float)(R > 0 ? R : 1) : 1.0f, acc);
 }
 
 const nc_op_def nc_op_sum = {"sum", NC_OPF_REDUCTION, RED_SUM, reduce_infer, NULL, reduce_fwd, reduce_bwd};

@@ -11,8 +11,9 @@
  * block, reset at nc_step_end), never from the step arena, whose blocks the main stream may still be
  * reading when the side stream would write them. The first draw of a step waits for an event that
  * nc_step_end records on the main stream, so a step's masks never overwrite the previous step's while
- * its backward still reads them. With per-kernel timing on (the benchmark's kernel table), or
- * NC_RNG_SIDE=0, or when the pool is full, masks are drawn on the main stream instead.
+ * its backward still reads them. With per-kernel timing on (the benchmark's kernel table), for masks
+ * under NC_SIDE_MIN_DRAWS (unless NC_RNG_SIDE=1), with NC_RNG_SIDE=0, or when the pool is full, masks
+ * are drawn on the main stream instead.
  */
 #include "nc_internal.h"
 
@@ -23,14 +24,23 @@
 #define NC_SIDE_POOL_BYTES ((size_t)64 << 20)
 #define NC_SIDE_TABS_BYTES ((size_t)4 * 16 * 16 * 32)
 
-static int side_ready(nc_ctx *ctx) {
+/* Masks below this many draws are drawn on the main stream by the fused draw-and-apply kernel: one
+ * launch and no events, where the host's cost of the side path (tables, events, two launches) exceeded
+ * the overlap it buys (cfg2's 64k-draw mask: 2.7% slower with it; cfg4's 2-8M-draw masks: 3.3% faster). */
+#define NC_SIDE_MIN_DRAWS ((int64_t)1 << 20)
+
+static int side_ready(nc_ctx *ctx, int64_t n) {
     if (ctx->side_off || !ctx->device_ok) return 0;
-    if (ctx->side_stream) return 1;
-    const char *e = getenv("NC_RNG_SIDE");
-    if (e && !strcmp(e, "0")) {
-        ctx->side_off = 1;
-        return 0;
+    if (!ctx->side_stream) {
+        const char *e = getenv("NC_RNG_SIDE"); /* 0: never, 1: every mask, unset: masks of >= 1M draws */
+        if (e && !strcmp(e, "0")) {
+            ctx->side_off = 1;
+            return 0;
+        }
+        ctx->side_all = e && !strcmp(e, "1");
     }
+    if (n < NC_SIDE_MIN_DRAWS && !ctx->side_all) return 0;
+    if (ctx->side_stream) return 1;
     cudaStream_t s = NULL;
     cudaEvent_t a = NULL, b = NULL;
     void *pool = NULL;
@@ -60,7 +70,7 @@ static void *side_alloc(nc_ctx *ctx, size_t bytes) {
 }
 
 int nc__rng_side_mask(nc_ctx *ctx, int64_t n, float p, uint32_t **bits) {
-    if (n <= 0 || ctx->dev.timer || !side_ready(ctx)) return 0;
+    if (n <= 0 || ctx->dev.timer || !side_ready(ctx, n)) return 0;
     const void *polys = nc__rng_dropout_table(ctx, n);
     if (!polys) return 0; /* beyond the polynomial tables: the main-stream kernel jumps by matrices */
     const size_t words = (size_t)(n + 31) / 32 + 1;

@@ -456,6 +456,17 @@ int nc_copy_from(nc_tensor *t, const void *src, size_t src_bytes) {
         return 0;
     }
     nc_tensor *o = nc__owner(t);
+    if (o->bytes <= NC_MIRROR_SMALL && !o->deferred && (need == o->bytes || (o->coh & NC_COH_HOST_VALID))) {
+        /* a small owner (a scalar such as BatchNorm's batch counter): the bytes go to its host mirror,
+         * marked as not yet on the device; the next device use uploads them (nc__dev), and a tensor
+         * that only the host reads never pays a copy */
+        char *h = (char *)mirror_of(o);
+        if (h) {
+            memcpy(h + ((char *)t->data - (char *)o->data), src, need);
+            o->coh = NC_COH_HOST_VALID | NC_COH_HOST_DIRTY;
+            return 1;
+        }
+    }
     nc__dev(t); /* earlier host writes must not land after this copy */
     nc__upload(t->ctx, t->data, src, need);
     if (o->host || o->bytes <= NC_MIRROR_SMALL) {

@@ -94,11 +94,27 @@ def test_chains_unfused(case, monkeypatch):
         assert rel_err(out[k], ref) <= TOL, (case, k)
 
 
+@pytest.mark.parametrize("case", ["batch_norm_train", "bn_relu_pool", "bn_pool", "bn_hardswish", "bn_relu6_pool",
+                                  "bn_relu_reused", "bn_relu_pool_odd"])
+@pytest.mark.parametrize("stage", ["0", "8", "16"])
+def test_bn_reductions_other_forms(case, stage, monkeypatch):
+    """NC_BN_BULK=0 (register-fed BatchNorm statistics and backward sums), =8 and =16 (every eligible
+    pass fed by bulk copies in 8 / 16 KiB stages, aligned and unaligned planes): the same goldens as
+    the default policy (test_op_matches_reference)."""
+    monkeypatch.setenv("NC_BN_BULK", stage)
+    out = run_case("b200", case)
+    for k in out:
+        ref = GOLD[f"{case}/{k}"]
+        assert rel_err(out[k], ref) <= TOL, (case, k)
+
+
 @pytest.mark.parametrize("case", ["dropout", "attention_chain", "attention_mha_128"])
-def test_masks_on_the_main_stream(case, monkeypatch):
-    """NC_RNG_SIDE=0: dropout masks drawn on the main stream instead of the side stream, held to the
-    same goldens (bit-exact where test_op_matches_reference is)."""
-    monkeypatch.setenv("NC_RNG_SIDE", "0")
+@pytest.mark.parametrize("side", ["0", "1"])
+def test_masks_on_either_stream(case, side, monkeypatch):
+    """NC_RNG_SIDE=0: dropout masks drawn on the main stream; =1: every mask drawn on the side stream
+    (by default only masks of at least 1M draws are); both held to the same goldens (bit-exact where
+    test_op_matches_reference is)."""
+    monkeypatch.setenv("NC_RNG_SIDE", side)
     out = run_case("b200", case)
     exact = EXACT.get(case, set())
     for k in out:
