@@ -278,30 +278,66 @@ __global__ void k_strided64(Strided v, const T *__restrict__ src, T *__restrict_
     }
 }
 
+// four items per thread per pass, all their loads issued before the first store
 template <typename T, int MODE>
 __global__ void k_strided32(Strided32 v, const T *__restrict__ src, T *__restrict__ dst, uint32_t n) {
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const uint32_t o = strided_offset32(v, i);
-        if (MODE == 0) dst[i] = src[o];
-        else if (MODE == 1) dst[o] += src[i];
-        else dst[o] = src[i];
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += 4 * stride) {
+        uint32_t o[4];
+        T a[4], b[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * stride;
+            if (i < n) {
+                o[u] = strided_offset32(v, i);
+                if (MODE == 0) a[u] = src[o[u]];
+                else a[u] = src[i];
+                if (MODE == 1) b[u] = dst[o[u]];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * stride;
+            if (i < n) {
+                if (MODE == 0) dst[i] = a[u];
+                else if (MODE == 1) dst[o[u]] = b[u] + a[u];
+                else dst[o[u]] = a[u];
+            }
+        }
     }
 }
 
-// float4 items: v describes the view in items of 4 floats (the innermost dim divided by 4)
+// float4 items: v describes the view in items of 4 floats (the innermost dim divided by 4); four
+// items per thread per pass, all their loads issued before the first store
 template <int MODE>
 __global__ void k_strided32_v4(Strided32 v, const float4 *__restrict__ src, float4 *__restrict__ dst, uint32_t n4) {
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
-        const uint32_t o = strided_offset32(v, i);
-        if (MODE == 0) {
-            dst[i] = __ldg(src + o);
-        } else if (MODE == 1) {
-            float4 a = dst[o];
-            const float4 b = __ldg(src + i);
-            a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
-            dst[o] = a;
-        } else {
-            dst[o] = __ldg(src + i);
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < n4; i0 += 4 * stride) {
+        uint32_t o[4];
+        float4 a[4], b[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * stride;
+            if (i < n4) {
+                o[u] = strided_offset32(v, i);
+                a[u] = MODE == 0 ? __ldg(src + o[u]) : __ldg(src + i);
+                if (MODE == 1) b[u] = dst[o[u]];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * stride;
+            if (i < n4) {
+                if (MODE == 0) {
+                    dst[i] = a[u];
+                } else if (MODE == 1) {
+                    float4 c = b[u];
+                    c.x += a[u].x, c.y += a[u].y, c.z += a[u].z, c.w += a[u].w;
+                    dst[o[u]] = c;
+                } else {
+                    dst[o[u]] = a[u];
+                }
+            }
         }
     }
 }

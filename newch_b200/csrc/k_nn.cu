@@ -1577,11 +1577,13 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_sums_x(const float *__restr
     const int SV = (int)(L / V);
     wk.init(SV, n1 > n0 ? n1 - n0 : 0);
     const int64_t pbase = n0 * C + c;
+    // items in flight per thread: two float4, or eight floats for planes that are not float4 multiples
+    constexpr int U = V == 4 ? 2 : 8;
     while (wk.live()) {
-        VT gv[2], xv[2];
-        bool on[2];
+        VT gv[U], xv[U];
+        bool on[U];
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < U; j++) {
             on[j] = wk.live();
             if (on[j]) {
                 const int64_t off = (pbase + (int64_t)wk.na * C) * SV + wk.ia;
@@ -1591,7 +1593,7 @@ __global__ void __launch_bounds__(256) k_bn_pool_bwd_sums_x(const float *__restr
             wk.next();
         }
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < U; j++) {
             if (!on[j]) continue;
             const float *ge = reinterpret_cast<const float *>(&gv[j]), *xe = reinterpret_cast<const float *>(&xv[j]);
 #pragma unroll
