@@ -249,6 +249,44 @@ __global__ void k_colsum_partial(const float *__restrict__ x, float *__restrict_
     }
 }
 
+// float4 columns: a block of (32, kColRows) threads takes 128 columns; thread (x, y) adds rows
+// y, y + kColRows, ... of columns 4x .. 4x + 3 with four rows' loads in flight, in row order; the
+// kColRows partial sums are added in order
+__global__ void k_colsum_partial4(const float *__restrict__ x, float *__restrict__ part, int64_t M, int64_t N,
+                                  int64_t rows_per_split) {
+    __shared__ float4 sm[kColRows][32];
+    const int64_t n = blockIdx.x * 128 + 4 * threadIdx.x;
+    const int64_t m0 = blockIdx.y * rows_per_split, m1 = m0 + rows_per_split < M ? m0 + rows_per_split : M;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n < N) {
+        int64_t m = m0 + threadIdx.y;
+        for (; m + 3 * kColRows < m1; m += 4 * kColRows) {
+            const float4 v0 = __ldg(reinterpret_cast<const float4 *>(x + m * N + n));
+            const float4 v1 = __ldg(reinterpret_cast<const float4 *>(x + (m + kColRows) * N + n));
+            const float4 v2 = __ldg(reinterpret_cast<const float4 *>(x + (m + 2 * kColRows) * N + n));
+            const float4 v3 = __ldg(reinterpret_cast<const float4 *>(x + (m + 3 * kColRows) * N + n));
+            acc.x += v0.x, acc.y += v0.y, acc.z += v0.z, acc.w += v0.w;
+            acc.x += v1.x, acc.y += v1.y, acc.z += v1.z, acc.w += v1.w;
+            acc.x += v2.x, acc.y += v2.y, acc.z += v2.z, acc.w += v2.w;
+            acc.x += v3.x, acc.y += v3.y, acc.z += v3.z, acc.w += v3.w;
+        }
+        for (; m < m1; m += kColRows) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + m * N + n));
+            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        }
+    }
+    sm[threadIdx.y][threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.y == 0 && n < N) {
+        float4 t = sm[0][threadIdx.x];
+        for (int k = 1; k < kColRows; k++) {
+            const float4 u = sm[k][threadIdx.x];
+            t.x += u.x, t.y += u.y, t.z += u.z, t.w += u.w;
+        }
+        *reinterpret_cast<float4 *>(part + blockIdx.y * N + n) = t;
+    }
+}
+
 __global__ void k_colsum_combine(const float *__restrict__ part, float *__restrict__ gy, int64_t N, int splits) {
     for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N; n += (int64_t)gridDim.x * blockDim.x) {
         float s = gy[n];
@@ -324,8 +362,11 @@ extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M,
         NCK_LAUNCHED(d, 1);
         return;
     }
-    int64_t col_blocks = (N + 31) / 32;
-    int64_t want = (int64_t)d->sm_count * 4;
+    // float4 columns (N a multiple of 4, 16-byte rows) and about eight blocks per SM: enough loads in
+    // flight for HBM; otherwise one float per thread
+    const bool v4 = N % 4 == 0 && ((uintptr_t)x & 15) == 0;
+    int64_t col_blocks = v4 ? (N + 127) / 128 : (N + 31) / 32;
+    int64_t want = (int64_t)d->sm_count * (v4 ? 8 : 4);
     int64_t splits = want / col_blocks;
     if (splits < 1) splits = 1;
     if (splits > M / 64 + 1) splits = M / 64 + 1;
@@ -335,7 +376,8 @@ extern "C" void nck_colsum_acc(nck_dev *d, const float *x, float *gy, int64_t M,
     splits = (M + rows_per - 1) / rows_per;
     float *part = (float *)d->scratch;
     dim3 grid((unsigned)col_blocks, (unsigned)splits), block(32, kColRows);
-    k_colsum_partial<<<grid, block, 0, NCK_STREAM(d)>>>(x, part, M, N, rows_per);
+    if (v4) k_colsum_partial4<<<grid, block, 0, NCK_STREAM(d)>>>(x, part, M, N, rows_per);
+    else k_colsum_partial<<<grid, block, 0, NCK_STREAM(d)>>>(x, part, M, N, rows_per);
     NCK_LAUNCHED(d, 1);
     nck_combine_cols(d, part, N, (int)splits, N, gy, N, nullptr);
 }
