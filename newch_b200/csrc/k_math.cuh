@@ -47,18 +47,39 @@ __device__ __forceinline__ float poly_exp(float x0) {
     return x0 != x0 ? x0 : r;
 }
 
+// poly_exp for arguments that are <= 0 or NaN (erf's exp(-x^2)): the same operations and results
+// without the upper clamp and the 2^128 scaling, which such arguments never reach
+__device__ __forceinline__ float poly_exp_nonpos(float x0) {
+    const float lo = -87.3365448f;
+    float x = fmaxf(x0, lo);  // NaN maps to lo here and is restored at the end
+    float fx = floorf(fmaf(x, 1.44269504088896341f, 0.5f));
+    x = fmaf(-fx, 0.693359375f, x);
+    x = fmaf(-fx, -2.12194440e-4f, x);
+    float y = 1.9875691500e-4f;
+    y = fmaf(y, x, 1.3981999507e-3f);
+    y = fmaf(y, x, 8.3334519073e-3f);
+    y = fmaf(y, x, 4.1665795894e-2f);
+    y = fmaf(y, x, 1.6666665459e-1f);
+    y = fmaf(y, x, 5.0000001201e-1f);
+    y = fmaf(y, x * x, x + 1.0f);
+    const int n = (int)fx;  // fx is integral and within [-126, 0]
+    float r = y * __int_as_float((n + 127) << 23);
+    if (x0 < lo) r = 0.0f;
+    return x0 != x0 ? x0 : r;
+}
+
 __device__ __forceinline__ float copysign_bits(float mag, float sgn) {
     return __int_as_float(__float_as_int(mag) | (__float_as_int(sgn) & (int)0x80000000));
 }
 
 // 1 / (1 + e^(0 - x))
-__device__ __forceinline__ float poly_sigmoid(float x) { return 1.0f / (1.0f + poly_exp(0.0f - x)); }
+__device__ __forceinline__ float poly_sigmoid(float x) { return __frcp_rn(1.0f + poly_exp(0.0f - x)); }
 
 // |x| < 1/4: x + x^3 (t3 + z (t5 + z (t7 + z t9))), z = x^2 (odd Taylor terms, no cancellation);
 // otherwise (1 - e) / (1 + e) with e = exp(-2 |x|), given the sign of x.
 __device__ __forceinline__ float poly_tanh(float x) {
     const float ax = fabsf(x);
-    const float e = poly_exp(ax * -2.0f);
+    const float e = poly_exp_nonpos(ax * -2.0f);
     const float big = copysign_bits((1.0f - e) / (1.0f + e), x);
     const float z = x * x;
     float p = fmaf(0.021869489f, z, -0.053968254f);
@@ -72,12 +93,12 @@ __device__ __forceinline__ float poly_tanh(float x) {
 // the sign of x restored.
 __device__ __forceinline__ float poly_erf(float x) {
     const float ax = fabsf(x);
-    const float t = 1.0f / fmaf(ax, 0.3275911f, 1.0f);
+    const float t = __frcp_rn(fmaf(ax, 0.3275911f, 1.0f));  // the correctly rounded 1 / d, as 1.0f / d
     float p = fmaf(1.061405429f, t, -1.453152027f);
     p = fmaf(p, t, 1.421413741f);
     p = fmaf(p, t, -0.284496736f);
     p = fmaf(p, t, 0.254829592f);
-    const float e = poly_exp(0.0f - ax * ax);
+    const float e = poly_exp_nonpos(0.0f - ax * ax);
     const float r = fmaf(-(p * t), e, 1.0f);
     return copysign_bits(r, x);
 }
