@@ -441,29 +441,49 @@ __global__ void __launch_bounds__(256) k_direct3_dw_partial(nck_conv g, const fl
         for (int k = 0; k < 10; k++) acc[o][k] = 0.0f;
     const uint32_t RG = (uint32_t)(OH + 3) / 4, total = (uint32_t)g.N * RG * (uint32_t)OW, p0 = blockIdx.x * per_split;
     const uint32_t p1 = p0 + per_split < total ? p0 + per_split : total;
-    for (uint32_t t = p0 + threadIdx.x; t < p1; t += blockDim.x) {
-        const uint32_t r = dow.div(t), ox = t - r * (uint32_t)OW, n = drg.div(r), oy0 = 4 * (r - n * RG);
-        float win[3][6];
-        window3x4(x + (int64_t)n * H * W, H, W, g.ph, g.pw, (int)oy0, (int)ox, win);
-        const int rows = OH - (int)oy0 < 4 ? OH - (int)oy0 : 4;
-        const float *gp = gy + ((int64_t)n * OC * OH + oy0) * OW + ox;
+    // two items per pass: both items' dY loads (and windows) are issued before either is multiplied,
+    // and their products enter the sums in item order (the same order as one item per pass)
+    for (uint32_t t0 = p0 + threadIdx.x; t0 < p1; t0 += 2 * blockDim.x) {
+        float win[2][3][6], gv[2][OCW][4];
 #pragma unroll
-        for (int o = 0; o < OCW; o++) {
-            float gv[4];
+        for (int u = 0; u < 2; u++) {
+            const uint32_t t = t0 + u * blockDim.x;
+            if (t >= p1) {
 #pragma unroll
-            for (int d = 0; d < 4; d++)
-                gv[d] = (o0 + o < OC && d < rows) ? __ldg(gp + ((int64_t)(o0 + o) * OH + d) * OW) : 0.0f;
+                for (int o = 0; o < OCW; o++)
 #pragma unroll
-            for (int ki = 0; ki < 3; ki++)
+                    for (int d = 0; d < 4; d++) gv[u][o][d] = 0.0f;
 #pragma unroll
-                for (int kj = 0; kj < 3; kj++) {
-                    float a = acc[o][ki * 3 + kj];
+                for (int i = 0; i < 3; i++)
 #pragma unroll
-                    for (int d = 0; d < 4; d++) a = fmaf(gv[d], win[kj][d + ki], a);
-                    acc[o][ki * 3 + kj] = a;
-                }
-            acc[o][9] += (gv[0] + gv[1]) + (gv[2] + gv[3]);
+                    for (int j = 0; j < 6; j++) win[u][i][j] = 0.0f;
+                continue;
+            }
+            const uint32_t r = dow.div(t), ox = t - r * (uint32_t)OW, n = drg.div(r), oy0 = 4 * (r - n * RG);
+            window3x4(x + (int64_t)n * H * W, H, W, g.ph, g.pw, (int)oy0, (int)ox, win[u]);
+            const int rows = OH - (int)oy0 < 4 ? OH - (int)oy0 : 4;
+            const float *gp = gy + ((int64_t)n * OC * OH + oy0) * OW + ox;
+#pragma unroll
+            for (int o = 0; o < OCW; o++)
+#pragma unroll
+                for (int d = 0; d < 4; d++)
+                    gv[u][o][d] = (o0 + o < OC && d < rows) ? __ldg(gp + ((int64_t)(o0 + o) * OH + d) * OW) : 0.0f;
         }
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+#pragma unroll
+            for (int o = 0; o < OCW; o++) {
+#pragma unroll
+                for (int ki = 0; ki < 3; ki++)
+#pragma unroll
+                    for (int kj = 0; kj < 3; kj++) {
+                        float a = acc[o][ki * 3 + kj];
+#pragma unroll
+                        for (int d = 0; d < 4; d++) a = fmaf(gv[u][o][d], win[u][kj][d + ki], a);
+                        acc[o][ki * 3 + kj] = a;
+                    }
+                acc[o][9] += (gv[u][o][0] + gv[u][o][1]) + (gv[u][o][2] + gv[u][o][3]);
+            }
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
