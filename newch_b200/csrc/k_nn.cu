@@ -610,6 +610,45 @@ __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd_run(const ulonglon
     drop_block_write(x, y, bits, n, p, mb);
 }
 
+// Mask only, two runs per thread: thread t jumps to run 2 t by the window tables (the polynomial of
+// run 2 t) and makes the 128 draws of runs 2 t and 2 t + 1 in sequence, so the jump (64 table reads)
+// is paid once per 128 draws; the four mask words go straight to global memory. The same draws and
+// mask words as the kernels above.
+__global__ void __launch_bounds__(kDropThreads) k_dropout_mask_run2(const ulonglong4 *__restrict__ gtab,
+                                                                    const ulonglong4 *__restrict__ polys,
+                                                                    uint32_t *__restrict__ bits, int64_t n, float p) {
+    __shared__ ulonglong4 tab[4][16][16];
+    for (int e = threadIdx.x; e < 4 * 16 * 16; e += blockDim.x) (&tab[0][0][0])[e] = gtab[e];
+    __syncthreads();
+    const int64_t t = (int64_t)blockIdx.x * kDropThreads + threadIdx.x, k = 2 * t;
+    if (k * kDropDraws >= n) return;
+    const ulonglong4 q = polys[k];
+    const unsigned long long words[4] = {q.x, q.y, q.z, q.w};
+    unsigned long long a[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int nn = 0; nn < 16; nn++) {
+            const ulonglong4 e = tab[j][nn][(words[j] >> (4 * nn)) & 15];
+            a[0] ^= e.x, a[1] ^= e.y, a[2] ^= e.z, a[3] ^= e.w;
+        }
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll 8
+    for (int i = 0; i < 2 * kDropDraws; i++) {
+        const unsigned long long r = rotl64(a[1] * 5ull, 7) * 9ull;
+        xo_step(a);
+        const float u = (float)(r >> 40) * (1.0f / 16777216.0f);
+        w[i >> 5] |= (u >= p ? 1u : 0u) << (i & 31);
+    }
+    const int64_t nw = (n + 31) / 32, w0 = 4 * t;
+    if (w0 + 4 <= nw) {
+        *reinterpret_cast<uint4 *>(bits + w0) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        for (int j = 0; j < 4; j++)
+            if (w0 + j < nw) bits[w0 + j] = w[j];
+    }
+}
+
 __global__ void __launch_bounds__(kDropThreads) k_dropout_fwd(ulonglong4 s0, const float *__restrict__ x,
                                                               float *__restrict__ y, uint32_t *__restrict__ bits,
                                                               int64_t n, float p) {
@@ -674,6 +713,14 @@ extern "C" void nck_dropout_fwd(nck_dev *d, const uint64_t state[4], const float
     Scope sc(d, y ? "dropout" : "dropout_mask", 0.0, (y ? 8.0 * n : 0.0) + n / 8.0);
     ulonglong4 s0 = make_ulonglong4(state[0], state[1], state[2], state[3]);
     int64_t blocks = (n + kDropBlock - 1) / kDropBlock;
+    if (polys && host_tabs && !y && n >= ((int64_t)1 << 21) && ((uintptr_t)bits & 15) == 0) {
+        /* a large mask on its own: two runs per thread */
+        const int64_t threads = (n + 2 * kDropDraws - 1) / (2 * kDropDraws);
+        k_dropout_mask_run2<<<(unsigned)((threads + kDropThreads - 1) / kDropThreads), kDropThreads, 0, NCK_STREAM(d)>>>(
+            reinterpret_cast<const ulonglong4 *>(host_tabs), reinterpret_cast<const ulonglong4 *>(polys), bits, n, p);
+        NCK_LAUNCHED(d, 1);
+        return;
+    }
     if (polys && host_tabs) {
         k_dropout_fwd_run<<<(unsigned)blocks, kDropThreads, 0, NCK_STREAM(d)>>>(
             reinterpret_cast<const ulonglong4 *>(host_tabs), reinterpret_cast<const ulonglong4 *>(polys), x, y, bits,

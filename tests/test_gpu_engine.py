@@ -334,7 +334,7 @@ def test_int8_gemm_paths_bit_exact(path, M, N, K, monkeypatch):
 
 
 @pytest.mark.parametrize("jump", ["poly", "matrix"])
-@pytest.mark.parametrize("n", [1, 31, 16384, 16385, 100000, 1 << 20])
+@pytest.mark.parametrize("n", [1, 31, 16384, 16385, 100000, 1 << 20, (1 << 21) + 77, 3 << 20])
 def test_dropout_masks_match_reference_stream(n, jump, monkeypatch):
     """Device jump-ahead reproduces the reference stream for any length, and the host stream
     continues where the kernel stopped. Both jump kernels: by run polynomials (the default) and by
