@@ -272,6 +272,38 @@ __global__ void __launch_bounds__(256) k_sgemm_small_warp(GemmP p, int64_t nout)
     }
 }
 
+// long reductions (R >= 2048): a block of 256 threads per output, thread t taking terms t, t + 256, ...
+// over four running sums; the lanes' sums go through a fixed shuffle tree and the eight warps' are
+// added in order
+__global__ void __launch_bounds__(256) k_sgemm_small_block(GemmP p, int64_t nout) {
+    __shared__ float red[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t MN = p.M * p.N, total = nout * MN, R = p.reduce ? p.batch * p.K : p.K;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        const int64_t ob = t / MN, rm = t - ob * MN, m = rm / p.N, n = rm - m * p.N;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int64_t r = threadIdx.x;
+        for (; r + 768 < R; r += 1024) {
+            a0 = small_fma(p, ob, m, n, r, a0);
+            a1 = small_fma(p, ob, m, n, r + 256, a1);
+            a2 = small_fma(p, ob, m, n, r + 512, a2);
+            a3 = small_fma(p, ob, m, n, r + 768, a3);
+        }
+        for (; r < R; r += 256) a0 = small_fma(p, ob, m, n, r, a0);
+        float acc = (a0 + a1) + (a2 + a3);
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float s = red[0];
+            for (int k = 1; k < 8; k++) s += red[k];
+            float *c = p.C + ob * p.sC + m * p.ldc + n;
+            *c = epi(p, s, m, n, c);
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace
 
 extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
@@ -298,6 +330,8 @@ extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (small) {
         const int64_t R = p.reduce ? a->batch * a->K : a->K, outs = nout_s * a->M * a->N;
         if (R <= 64) k_sgemm_small_thread<<<grid_for(d, outs), 256, 0, NCK_STREAM(d)>>>(p, nout_s);
+        else if (R >= 2048 && outs <= 4 * (int64_t)d->sm_count * 8)
+            k_sgemm_small_block<<<(unsigned)outs, 256, 0, NCK_STREAM(d)>>>(p, nout_s);
         else k_sgemm_small_warp<<<grid_for(d, outs * 32), 256, 0, NCK_STREAM(d)>>>(p, nout_s);
         NCK_LAUNCHED(d, 1);
         return;

@@ -376,7 +376,7 @@ typedef struct {
     float lr, momentum, weight_decay, beta1, beta2, eps, gs, bc1, bc2;
     int eps_inside_sqrt;
 } nck_opt_hyper;
-#define NCK_OPT_CHUNK 4096 /* elements per block */
+#define NCK_OPT_CHUNK 1024 /* elements per block: one float4 per thread (a 422k-parameter model: ~400 blocks) */
 /* fills chunks (when not NULL) for the segments; returns how many there are */
 int nck_optim_chunks(const nck_param_seg *segs, int nseg, nck_opt_chunk *chunks);
 /* One launch over device-resident tables: dsegs[nseg], dchunks[nchunk]; total = elements in all
