@@ -158,6 +158,30 @@ def _bn_chain(e, seed, shape, act, pool, reuse=False):
     return res
 
 
+def case_conv3_bn_relu_pool(e):
+    """Conv2d(1, C, 3, padding 1) of an image (no gradient) -> BatchNorm -> ReLU -> 2 x 2 max pool: the
+    B200 engine computes the convolution's weight and bias gradients inside the chain's fused backward."""
+    img = e.t(seeded(760, (5, 1, 10, 12), 1.0))
+    cw = e.param(seeded(761, (6, 1, 3, 3), 0.3))
+    cb = e.param(seeded(762, (6,), 0.1))
+    x = e.check(e.L.nc_conv2d_ex(img, cw, cb, 1, 1, 1, 1, 1, 1, 1))
+    w = e.param(seeded(763, (6,)))
+    b = e.param(seeded(764, (6,)))
+    e.L.nc_persistent_begin(e.ctx)
+    rm = e.t(np.zeros(6, np.float32))
+    rv = e.t(np.ones(6, np.float32))
+    e.L.nc_persistent_end(e.ctx)
+    y = e.check(e.L.nc_batch_norm(x, w, b, rm, rv, 1, 0.1, 1e-5))
+    out = e.check(e.L.nc_max_pool2d(e.check(e.L.nc_relu(y)), 2, 2, 2, 2, 0, 0))
+    G = seeded(765, e.shape(out))
+    res = {"y": e.np(out), "G": G}
+    e.backward_with(out, G)
+    # the convolution bias feeds BatchNorm, so its gradient is rounding noise around zero (compared on
+    # the trace workloads with their exemption for such biases, not against a golden value here)
+    res.update(dcw=e.grad(cw), dw=e.grad(w), db=e.grad(b), rm=e.np(rm), rv=e.np(rv))
+    return res
+
+
 def case_bn_relu_pool(e):
     return _bn_chain(e, 700, (4, 6, 10, 12), "relu", True)
 

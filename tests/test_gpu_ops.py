@@ -82,7 +82,7 @@ def test_libm_math_mode(how, monkeypatch):
 
 
 @pytest.mark.parametrize("case", ["bn_relu_pool", "bn_pool", "bn_hardswish", "bn_relu6_pool", "bn_relu_reused",
-                                  "bn_relu_pool_odd", "attention_chain", "attention_mha", "attention_mha_128",
+                                  "bn_relu_pool_odd", "conv3_bn_relu_pool", "attention_chain", "attention_mha", "attention_mha_128",
                                   "attention_sdpa", "attention_unmasked", "attention_probs_read", "int8_gelu_chain"])
 def test_chains_unfused(case, monkeypatch):
     """NC_FUSE=0: the BatchNorm and attention chains through the unfused kernels (every intermediate

@@ -77,3 +77,18 @@ def test_resident_inputs_replay_the_same_step(name):
         runs.append(([v for _, v in r.items[n0[0]:]], [b for _, b in r.outputs[n0[1]:]]))
         lib.nc_free_ctx(r.ctx)
     assert runs[0] == runs[1]
+
+
+def test_smoke_parameter_check_on_the_reference():
+    """__graft_entry__.smoke()'s final-parameter check (byte-kept and summarized outputs) gives zero on the
+    reference engine's own replay of the smoke trace."""
+    import sys as _sys
+    from pathlib import Path as _P
+    _sys.path.insert(0, str(_P(__file__).resolve().parent.parent))
+    import __graft_entry__ as ge
+    lib = capi.load(REF_LIB)
+    t = replay.Trace("cfg1_small")
+    r = replay.Replayer(lib, t)
+    r.run_all()
+    assert ge.param_error(t, r.outputs) == 0.0
+    lib.nc_free_ctx(r.ctx)
