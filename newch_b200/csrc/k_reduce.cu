@@ -23,6 +23,35 @@ __global__ void k_rowsum(const float *__restrict__ x, float *__restrict__ y, int
     }
 }
 
+// short rows (R a multiple of 4, at most 128, 16-byte aligned): LPR lanes per row (R / 4 rounded up
+// to a power of two), one float4 each, a tree over the row's lanes; a warp takes 32 / LPR rows per pass
+// and four passes' loads are issued before their sums
+template <int LPR>
+__global__ void k_rowsum_short(const float *__restrict__ x, float *__restrict__ y, int64_t rows, int R, float scale) {
+    constexpr int RPW = 32 / LPR;  // rows per warp pass
+    const int lane = threadIdx.x & 31, sub = lane % LPR, rw = lane / LPR;
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const bool col = 4 * sub < R;
+    for (int64_t r0 = warp * RPW; r0 < rows; r0 += 4 * nwarps * RPW) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t r = r0 + (int64_t)u * nwarps * RPW + rw;
+            v[u] = (r < rows && col) ? __ldg(reinterpret_cast<const float4 *>(x + r * R) + sub)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int64_t r = r0 + (int64_t)u * nwarps * RPW + rw;
+            float s = (v[u].x + v[u].y) + (v[u].z + v[u].w);
+#pragma unroll
+            for (int o = LPR / 2; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (sub == 0 && r < rows) y[r] = scale * s;
+        }
+    }
+}
+
 // inner > 1: one thread per (outer, inner) column, rows added in order with the scale fused
 __global__ void k_colsum_strided(const float *__restrict__ x, float *__restrict__ y, int64_t outer, int64_t R,
                                  int64_t inner, float scale) {
@@ -102,7 +131,18 @@ extern "C" void nck_reduce_sum(nck_dev *d, const float *x, float *y, int64_t out
             return;
         }
     }
-    if (inner == 1) {
+    if (inner == 1 && R % 4 == 0 && R <= 128 && ((uintptr_t)x & 15) == 0) {
+        const int lpr = R <= 4 ? 1 : R <= 8 ? 2 : R <= 16 ? 4 : R <= 32 ? 8 : R <= 64 ? 16 : 32;
+        const int64_t warps = (n * lpr + 31) / 32, items = (warps + 3) / 4 * 32;
+#define NCK_RS(L) k_rowsum_short<L><<<grid_for(d, items), kThreads, 0, NCK_STREAM(d)>>>(x, y, n, (int)R, scale)
+        if (lpr == 1) NCK_RS(1);
+        else if (lpr == 2) NCK_RS(2);
+        else if (lpr == 4) NCK_RS(4);
+        else if (lpr == 8) NCK_RS(8);
+        else if (lpr == 16) NCK_RS(16);
+        else NCK_RS(32);
+#undef NCK_RS
+    } else if (inner == 1) {
         k_rowsum<<<grid_for(d, n * 32), kThreads, 0, NCK_STREAM(d)>>>(x, y, n, R, scale);
     } else {
         k_colsum_strided<<<grid_for(d, n), kThreads, 0, NCK_STREAM(d)>>>(x, y, outer, R, inner, scale);
