@@ -206,7 +206,7 @@ __global__ void k_sgemm_combine(GemmP p, int64_t nout) {
 
 // ---- small problems ---------------------------------------------------------------------------------
 //
-// Products with few outputs (at most 64k) and little work (at most 16M multiply-adds), where 128 x 128
+// Products with few outputs (at most 64k) and little work (at most 4M multiply-adds), where 128 x 128
 // tiles would leave most SMs idle: one thread per output when the reduction (K, times the batch when
 // it is summed) is short, else one warp per output with the lanes taking strided runs of it and a
 // fixed shuffle tree. Exact fp32 in every GEMM mode.
@@ -310,7 +310,7 @@ extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (a->M <= 0 || a->N <= 0 || a->batch <= 0) return;
     const int64_t nout_s = a->reduce_batch && a->batch > 1 ? 1 : a->batch;
     const bool small = d->gemm_small && a->M * a->N * nout_s <= ((int64_t)1 << 16) &&
-                       a->M * a->N * a->K * a->batch <= ((int64_t)1 << 24);
+                       a->M * a->N * a->K * a->batch <= ((int64_t)1 << 22);
     if (!small && d->gemm_mode != NCK_GEMM_FFMA && nck_gemm_tc(d, a)) return;
     double nA = a->sA ? (double)a->batch : 1.0, nB = a->sB ? (double)a->batch : 1.0;
     double nC = (a->reduce_batch ? 1.0 : (double)a->batch) * (a->beta != 0.0f ? 2.0 : 1.0);

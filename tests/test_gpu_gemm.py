@@ -100,7 +100,7 @@ def test_conv_weight_grad_batch_reduction_large(mode):
                                    (37, 19, 70), (64, 196, 288)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_small_products(mode, monkeypatch, M, N, K, ta, tb):
-    """Products with at most 64k outputs and 16M multiply-adds take the small kernels (one thread per
+    """Products with at most 64k outputs and 4M multiply-adds take the small kernels (one thread per
     output for a reduction of at most 64, else one warp per output), exact fp32 in every mode: the
     FFMA tolerance applies whatever NC_GEMM says. Forward and both gradients (dA, dB are small too)."""
     monkeypatch.setenv("NC_GEMM_SMALL", "1")
