@@ -134,6 +134,40 @@ static void gemm_fwd(nc_ctx *ctx, const nck_conv *g, const float *W, const float
 /* what the forward left for the backward: x unfolded (whole batch in one chunk) or x packed for the
  * tap-shifted path */
 enum { SAVED_COL = 1, SAVED_TAP = 2 };
+
+/* Off the tape nothing keeps the packed input for a backward, so the packed copy (channels padded
+ * to 32, two planes for 3xTF32) need not hold the whole batch: samples per pack, keeping the
+ * workspace at most half the output's size (4 MiB at least). On the tape the whole batch. */
+static int64_t tap_chunk(const nc_ctx *ctx, const nck_conv *g, const nck_tapgeom *tg) {
+    if (ctx->fwd_on_tape) return g->N;
+    const int64_t per = tg->Hp * tg->Wp * tg->Cp * tg->planes * (int64_t)sizeof(float);
+    int64_t budget = g->N * g->OC * g->OH * g->OW * (int64_t)sizeof(float) / 2;
+    if (budget < ((int64_t)4 << 20)) budget = (int64_t)4 << 20;
+    const int64_t nb = budget / per;
+    return nb < 1 ? 1 : nb > g->N ? g->N : nb;
+}
+
+/* the tap convolution a chunk of samples at a time through one packed buffer (stream order makes
+ * each pack wait for the previous chunk's GEMM); 0 if the tap kernel turned a chunk down, in which
+ * case the caller's next path rewrites the whole output */
+static int tap_fwd_chunked(nc_ctx *ctx, const nck_conv *g, const nck_tapgeom *tg, const float *X, const float *Wt,
+                           const float *B, float *Y) {
+    const int64_t nb = tap_chunk(ctx, g, tg);
+    float *wp = (float *)nc__arena_alloc(ctx, (size_t)(g->OC * tg->T * tg->Cp * tg->planes) * sizeof(float));
+    float *xp = (float *)nc__arena_alloc(ctx, (size_t)(nb * tg->Hp * tg->Wp * tg->Cp * tg->planes) * sizeof(float));
+    if (!wp || !xp) return 0;
+    nck_tap_pack_w(nc__k(ctx), g, tg, Wt, wp, 0);
+    const int64_t xs = g->C * g->H * g->W, ys = g->OC * g->OH * g->OW;
+    for (int64_t n0 = 0; n0 < g->N; n0 += nb) {
+        nck_conv gc = *g;
+        gc.N = g->N - n0 < nb ? g->N - n0 : nb;
+        nck_tapgeom tc;
+        if (!nck_convtap_plan(nc__k(ctx), &gc, &tc)) return 0;
+        nck_tap_pack(nc__k(ctx), X + n0 * xs, gc.N, g->C, g->H, g->W, &tc, g->ph, g->pw, tc.Cp, xp, NULL);
+        if (!nck_convtap(nc__k(ctx), 0, &gc, &tc, xp, wp, Y + n0 * ys, B, 0)) return 0;
+    }
+    return 1;
+}
 typedef struct {
     int kind;
     float *buf;
@@ -161,7 +195,9 @@ static nc_status conv_fwd(nc_node *n) {
         return NC_OK;
     }
     nck_tapgeom tg;
-    if (nck_convtap_plan(nc__k(ctx), &g, &tg)) {
+    if (nck_convtap_plan(nc__k(ctx), &g, &tg) && tap_chunk(ctx, &g, &tg) < g.N) {
+        if (tap_fwd_chunked(ctx, &g, &tg, X, Wt, B, Y)) return NC_OK;
+    } else if (nck_convtap_plan(nc__k(ctx), &g, &tg)) {
         /* x packed once; the backward's weight gradient reads the same packed copy */
         conv_saved *sv = (conv_saved *)nc__meta_alloc(ctx, sizeof(conv_saved), 0);
         float *xp = (float *)nc__arena_alloc(ctx, (size_t)(tg.Nv * tg.Cp * tg.planes) * sizeof(float));

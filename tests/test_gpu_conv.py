@@ -117,3 +117,34 @@ def test_conv_large_batch_against_unfolded_path(monkeypatch):
             res[m] = (out, e.grad(x), e.grad(w), e.grad(b))
     for a, r in zip(res["3xtf32"], res["ffma"]):
         assert rel_err(a, r) < TOL["3xtf32"]
+
+
+@pytest.mark.parametrize("xs,oc", [((64, 16, 28, 28), 16), ((37, 24, 20, 20), 40)])
+def test_conv_off_the_tape_packs_a_few_samples_at_a_time(xs, oc, conv_path):
+    """A forward nothing will differentiate (no input needs a gradient) keeps no packed copy for a
+    backward, so the tap-shifted path packs a few samples at a time (ragged last chunk here): the
+    output is bit-identical to the whole-batch forward on the tape, and the arena's peak stays below
+    the output plus half of it (4 MiB at least) plus the packed weights, where the whole-batch pack
+    (channels padded to 32, two planes) would be several times the output. The other paths: values."""
+    import ncoracle as O
+
+    ws = (oc, xs[1], 3, 3)
+    X, W, B = seeded(13, xs), seeded(14, ws, 0.3), seeded(15, (oc,))
+    with Eng("b200") as e:
+        x, w, b = e.param(X), e.param(W), e.param(B)
+        on_tape = e.np(e.check(e.L.nc_conv2d_ex(x, w, b, 1, 1, 1, 1, 1, 1, 1)))
+        e.step_end()
+        xc, wc, bc = e.t(X, persistent=True), e.t(W, persistent=True), e.t(B, persistent=True)
+        before = e.L.nc_get_mem_stats(e.ctx).arena_bytes_in_use
+        e.L.nc_reset_peak(e.ctx)
+        y = e.check(e.L.nc_conv2d_ex(xc, wc, bc, 1, 1, 1, 1, 1, 1, 1))
+        assert not e.L.nc_requires_grad(y)
+        off_tape = e.np(y)
+        peak = e.L.nc_get_mem_stats(e.ctx).arena_peak_bytes - before
+        assert e.ok(), e.err()
+    out_bytes = off_tape.nbytes
+    wpack = oc * 9 * 32 * ((xs[1] + 31) // 32) * 2 * 4
+    if conv_path == "tap":
+        assert peak <= out_bytes + max(out_bytes // 2, 4 << 20) + wpack + (1 << 20), peak
+        assert np.array_equal(off_tape, on_tape)
+    assert rel_err(off_tape, O.conv2d(X, W, B, pad=(1, 1))) < TOL["3xtf32"]
