@@ -208,8 +208,9 @@ __global__ void k_sgemm_combine(GemmP p, int64_t nout) {
 //
 // Products with few outputs (at most 64k) and little work (at most 4M multiply-adds), where 128 x 128
 // tiles would leave most SMs idle: one thread per output when the reduction (K, times the batch when
-// it is summed) is short, else one warp per output with the lanes taking strided runs of it and a
-// fixed shuffle tree. Exact fp32 in every GEMM mode.
+// it is summed) is short, a block per 32 columns of one row when A is transposed and the reduction
+// long, else one warp per output with the lanes taking strided runs of it and a fixed shuffle tree
+// (a block per output for very long reductions). Exact fp32 in every GEMM mode.
 
 __device__ __forceinline__ float op_a(const GemmP &p, int64_t b, int64_t m, int64_t k) {
     return __ldg(p.A + b * p.sA + (p.ta ? k * p.lda + m : m * p.lda + k));
@@ -272,6 +273,37 @@ __global__ void __launch_bounds__(256) k_sgemm_small_warp(GemmP p, int64_t nout)
     }
 }
 
+// Transposed-A products with a long reduction (a weight gradient dY^T X, one batch entry): both
+// operands are rows of the reduction index, so the lanes take 32 consecutive columns n (one coalesced
+// row segment of B, one broadcast element of A per row) and the block's eight warps interleaved rows
+// r = w, w + 8, ... over eight running sums; the sums are added in a fixed tree, the warps' in order.
+__global__ void __launch_bounds__(256) k_sgemm_small_rows(GemmP p) {
+    __shared__ float red[8][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t ngrp = (p.N + 31) / 32, m = blockIdx.x / ngrp, n = (blockIdx.x - m * ngrp) * 32 + lane;
+    const bool live = n < p.N;
+    const float *a = p.A + m, *b = p.B + (live ? n : 0);
+    const int64_t R = p.K, lda = p.lda, ldb = p.ldb;
+    float s[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    int64_t r = warp;
+    for (; r + 56 < R; r += 64) {
+        float av[8], bv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) av[u] = __ldg(a + (r + 8 * u) * lda), bv[u] = __ldg(b + (r + 8 * u) * ldb);
+#pragma unroll
+        for (int u = 0; u < 8; u++) s[u] = fmaf(av[u], bv[u], s[u]);
+    }
+    for (; r < R; r += 8) s[0] = fmaf(__ldg(a + r * lda), __ldg(b + r * ldb), s[0]);
+    red[warp][lane] = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+    __syncthreads();
+    if (warp == 0 && live) {
+        float t = red[0][lane];
+        for (int w = 1; w < 8; w++) t += red[w][lane];
+        float *c = p.C + m * p.ldc + n;
+        *c = epi(p, t, m, n, c);
+    }
+}
+
 // long reductions (R >= 2048): a block of 256 threads per output, thread t taking terms t, t + 256, ...
 // over four running sums; the lanes' sums go through a fixed shuffle tree and the eight warps' are
 // added in order
@@ -330,6 +362,8 @@ extern "C" void nck_gemm(nck_dev *d, const nck_gemm_args *a) {
     if (small) {
         const int64_t R = p.reduce ? a->batch * a->K : a->K, outs = nout_s * a->M * a->N;
         if (R <= 64) k_sgemm_small_thread<<<grid_for(d, outs), 256, 0, NCK_STREAM(d)>>>(p, nout_s);
+        else if (a->ta && !a->tb && a->batch == 1 && a->N >= 32 && R >= 256)
+            k_sgemm_small_rows<<<(unsigned)(a->M * ((a->N + 31) / 32)), 256, 0, NCK_STREAM(d)>>>(p);
         else if (R >= 2048 && outs <= 4 * (int64_t)d->sm_count * 8)
             k_sgemm_small_block<<<(unsigned)outs, 256, 0, NCK_STREAM(d)>>>(p, nout_s);
         else k_sgemm_small_warp<<<grid_for(d, outs * 32), 256, 0, NCK_STREAM(d)>>>(p, nout_s);

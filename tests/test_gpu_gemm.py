@@ -97,12 +97,14 @@ def test_conv_weight_grad_batch_reduction_large(mode):
 
 
 @pytest.mark.parametrize("M,N,K", [(10, 128, 512), (512, 10, 128), (512, 128, 10), (8, 8, 8192), (1, 1, 1),
-                                   (37, 19, 70), (64, 196, 288)])
+                                   (37, 19, 70), (64, 196, 288), (24, 45, 777)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_small_products(mode, monkeypatch, M, N, K, ta, tb):
     """Products with at most 64k outputs and 4M multiply-adds take the small kernels (one thread per
-    output for a reduction of at most 64, else one warp per output), exact fp32 in every mode: the
-    FFMA tolerance applies whatever NC_GEMM says. Forward and both gradients (dA, dB are small too)."""
+    output for a reduction of at most 64; a block per 32 columns of a row for a transposed A and a
+    reduction of at least 256, ragged columns and rows included; else one warp per output), exact fp32
+    in every mode: the FFMA tolerance applies whatever NC_GEMM says. Forward and both gradients (dA, dB
+    are small too)."""
     monkeypatch.setenv("NC_GEMM_SMALL", "1")
     A = seeded(M * 7 + K, (K, M) if ta else (M, K))
     B = seeded(N * 13 + K, (N, K) if tb else (K, N))
@@ -152,3 +154,16 @@ def test_small_linear_bias_and_batch_sum():
         dwc = e.grad(w)
     _, dw_ref, _ = O.conv2d_grads(Xc, Wc, Gc)
     assert rel_err(dwc, dw_ref) < 1e-5
+
+
+def test_small_weight_gradient_accumulates():
+    """A Linear weight gradient over a long batch (dY^T X: transposed A, 600 rows, 45 columns, the
+    row-streaming small kernel) written by the first backward and added into by the second."""
+    X, W = seeded(21, (600, 45)), seeded(22, (10, 45), 0.2)
+    with Eng("b200") as e:
+        x, w = e.param(X), e.param(W)
+        G = seeded(23, (600, 10))
+        for _ in range(2):
+            e.backward_with(e.check(e.L.nc_linear_fn(x, w, None)), G)
+        dw = e.grad(w)
+    assert rel_err(dw, 2 * G.astype(np.float64).T @ X.astype(np.float64)) < 1e-5
